@@ -1,0 +1,356 @@
+#!/usr/bin/env python3
+"""Benchmark: TriangleMix paged sparse prefill attention on B200.
+
+Workload (one "step" = one prefill attention layer, BASELINE configs 0/3):
+  Qwen3-8B geometry (Hq=32, Hkv=8, D=128, page 128), bf16 N(0,1) inputs with
+  torch.Generator seed 0, random-permutation block table over 2x pages.
+  Default: 8192-token prompt processed as one 8192-token chunk ("prefill_8k").
+  --seq-len 32768 --query-tokens 8192 gives the 32K point of config 3.
+
+Multi-GPU (torchrun, one rank per GPU): KV-head partition.  Rank r owns kv
+heads [r*8/N, (r+1)*8/N) (query heads x4) of every layer; the job is N
+layers, so each rank runs 8 kv-head-layers per step (per-GPU work fixed,
+"scaling": "weak").  No collective touches the data path.
+
+Output: one JSON line on rank 0 (see keys in main()).
+  value        effective TFLOP/s over all ranks (unmasked QK^T + PV pairs)
+  e2e          same metric through the torch operator with pinned host
+               buffers, H2D of inputs and D2H of the output inside the timing
+  roofline     dominant kernel vs measured bf16 tensor peak
+  cpu_baseline oracle (port of the reference's torch CPU oracle) on a
+               bounded row sample, rank 0 only
+--impl reference times that CPU oracle on this host instead (rank 0 only).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+QUERY_HEADS, KV_HEADS, HEAD_DIM, PAGE = 32, 8, 128, 128
+SCALE = HEAD_DIM ** -0.5
+METRIC = "TriangleMix prefill attn ms/layer + effective TFLOP/s @8K/32K; TTFT, 1-8 B200"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+L2_FLUSH_BYTES = 256 << 20
+
+
+def effective_pairs(query_start: int, tq: int, seq: int, prompt: int) -> int:
+    """Sum over rows of |key set| (closed form of the reference key sets)."""
+    sb, se = 521, max(0, prompt - 128)
+    total = 0
+    for q in range(query_start, query_start + tq):
+        if sb <= q < se:
+            total += 8 + 513
+        else:
+            total += min(q + 1, seq)
+    return total
+
+
+def make_inputs(tq: int, seq: int, seed: int, kv_lo: int, kv_hi: int):
+    """Seeded host inputs; the head slice [kv_lo, kv_hi) of a full 8-head layer."""
+    gen = torch.Generator().manual_seed(seed)
+    logical = math.ceil(seq / PAGE)
+    physical = 2 * logical
+    perm = torch.randperm(physical, generator=gen)[:logical]
+    table = perm.to(torch.int32).view(1, -1).contiguous()
+    q = torch.randn(tq, QUERY_HEADS, HEAD_DIM, generator=gen).to(torch.bfloat16)
+    k = torch.randn(physical, PAGE, KV_HEADS, HEAD_DIM, generator=gen).to(torch.bfloat16)
+    v = torch.randn(physical, PAGE, KV_HEADS, HEAD_DIM, generator=gen).to(torch.bfloat16)
+    q = q[:, 4 * kv_lo:4 * kv_hi].contiguous()
+    k = k[:, :, kv_lo:kv_hi].contiguous()
+    v = v[:, :, kv_lo:kv_hi].contiguous()
+    return q, k, v, table
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+def load_peaks() -> tuple[dict, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        return json.loads(path.read_text()), "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def cpu_baseline(tq: int, seq: int, query_start: int, prompt: int, budget_s: float) -> dict:
+    """Time the oracle (port of the reference's CPU oracle) on a row sample."""
+    from oracle.triangle_oracle import oracle_attention_rowwise, prepare_logical_kv
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    q, k, v, table = make_inputs(tq, seq, 0, 0, KV_HEADS)
+    t0 = time.perf_counter()
+    lkv = prepare_logical_kv(k, v, table, seq)
+    t_gather = time.perf_counter() - t0
+    # A seeded random permutation of the rows: any prefix is a uniform sample
+    # of dense-prefix, sparse-middle and dense-tail rows.
+    order = torch.randperm(tq, generator=torch.Generator().manual_seed(1)).tolist()
+    rows, pairs, start, t_rows = [], 0, time.perf_counter(), 0.0
+    for i in range(0, tq, 32):
+        chunk = order[i:i + 32]
+        t0 = time.perf_counter()
+        oracle_attention_rowwise(q, k, v, table, query_start, seq, prompt, SCALE, rows=chunk,
+                                 logical_kv=lkv)
+        t_rows += time.perf_counter() - t0
+        pairs += sum(effective_pairs(query_start + r, 1, seq, prompt) for r in chunk)
+        rows.extend(chunk)
+        if time.perf_counter() - start > budget_s:
+            break
+    # The one cache gather is charged pro rata to the sampled rows.
+    t_compute = t_rows + t_gather * len(rows) / tq
+    flops = 4.0 * HEAD_DIM * QUERY_HEADS * pairs
+    return {"value": flops / t_compute / 1e12, "unit": "TFLOP/s (effective)", "cores": threads,
+            "kind": "port", "seconds": round(t_compute, 3),
+            "sample": f"{len(rows)} of {tq} query rows (seeded uniform sample), all 32 heads, "
+                      f"torch fp32 per-row gather+softmax, {threads} threads"}
+
+
+def run_reference_arm(args, rank: int) -> None:
+    if rank != 0:
+        return
+    tq, seq = args.query_tokens, args.seq_len
+    q0 = seq - tq
+    vals = []
+    for _ in range(args.warmup + args.steps):
+        vals.append(cpu_baseline(tq, seq, q0, seq, args.cpu_budget))
+    timed = vals[args.warmup:]
+    value = sum(v["value"] for v in timed) / len(timed)
+    pairs = effective_pairs(q0, tq, seq, seq)
+    ms = 4.0 * HEAD_DIM * QUERY_HEADS * pairs / (value * 1e12) * 1e3
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s (effective)",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+            "data": "synthetic", "config": workload_config(args),
+            "cpu_baseline": {**timed[-1], "value": value},
+            "e2e": {"value": value, "unit": "TFLOP/s (effective)", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(args) -> dict:
+    name = "prefill_8k" if args.seq_len == 8192 else f"prefill_{args.seq_len // 1024}k_q{args.query_tokens}"
+    return {"workload": name, "seq_len": args.seq_len, "query_tokens": args.query_tokens,
+            "query_start": args.seq_len - args.query_tokens, "prompt_len": args.seq_len,
+            "geometry": "Qwen3-8B attention (Hq=32, Hkv=8, D=128, page 128)",
+            "parallelism": f"kv-head partition x{args.gpus}", "layers_per_step": args.gpus,
+            "l2": "flushed between timed steps (256 MiB write)"}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
+    ap.add_argument("--seq-len", type=int, default=8192)
+    ap.add_argument("--query-tokens", type=int, default=None)
+    ap.add_argument("--cpu-budget", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    if args.query_tokens is None:
+        args.query_tokens = min(args.seq_len, 8192)
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        ap.error(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    if args.impl == "reference":
+        run_reference_arm(args, rank)
+        return
+
+    from __graft_entry__ import load_package
+
+    tm = load_package()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    tq, seq = args.query_tokens, args.seq_len
+    q0 = seq - tq
+    heads_per_rank = KV_HEADS // world
+    layers = world  # weak scaling: N layers per step for N ranks
+    # Each rank: `layers` layers x its kv-head slice.  Distinct seeds per layer.
+    rank_inputs = []
+    for layer in range(layers):
+        q, k, v, table = make_inputs(tq, seq, layer, rank * heads_per_rank, (rank + 1) * heads_per_rank)
+        rank_inputs.append((q, k, v, table))
+    dev_inputs = [tuple(t.to(dev) for t in x) for x in rank_inputs]
+    outs = [torch.empty_like(x[0]) for x in dev_inputs]
+    plan = tm._native.make_plan(tq, q0, seq, seq, heads_per_rank, 0, SCALE)
+    ws = (torch.empty(plan.workspace_bytes, dtype=torch.uint8, device=dev)
+          if plan.workspace_bytes else None)
+    stream = torch.cuda.current_stream(dev)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+
+    def step():
+        for (q, k, v, table), out in zip(dev_inputs, outs):
+            tm._native.paged_attention(q, k, v, table, out, q0, seq, seq, SCALE, kv_heads=heads_per_rank,
+                                       workspace=ws, stream=stream.cuda_stream)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    for _ in range(args.warmup):
+        flush.fill_(1.0)
+        step()
+    torch.cuda.synchronize(dev)
+    status = tm._native.device_status(local)
+    if status:
+        raise RuntimeError(f"device status {status:#x} after warm-up")
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize(dev)
+    for i in range(args.steps):
+        flush.fill_(float(i))  # evict L2 between steps (outside the timed events)
+        starts[i].record(stream)
+        step()
+        ends[i].record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    clocks = sampler.stop()
+    times = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    ms_rank = sum(times) / len(times)
+    kernel_ms = ms_rank / layers
+    if world > 1:
+        t = torch.tensor([ms_rank], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms_step = float(t.item())
+    else:
+        ms_step = ms_rank
+    pairs = effective_pairs(q0, tq, seq, seq)
+    flops_layer = 4.0 * HEAD_DIM * QUERY_HEADS * pairs  # all 32 heads
+    value = flops_layer * layers / (ms_step * 1e-3) / 1e12
+
+    # End-to-end through the torch operator with pinned host buffers.
+    e2e = None
+    if not args.no_e2e and world == 1:
+        tm.load_adapter()
+        hq, hk, hv, ht = (t.pin_memory() for t in rank_inputs[0])
+        hout = torch.empty_like(hq).pin_memory()
+        h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, ht))
+        d2h = hout.numel() * hout.element_size()
+
+        def e2e_step():
+            dq, dk, dv, dt = (t.to(dev, non_blocking=True) for t in (hq, hk, hv, ht))
+            o = torch.ops.trianglemix_reference.triangle_paged_sparse_attention(dq, dk, dv, dt, q0, seq,
+                                                                                seq, SCALE)
+            hout.copy_(o, non_blocking=True)
+
+        for _ in range(args.warmup):
+            e2e_step()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        e2e_ms = e0.elapsed_time(e1) / args.steps
+        e2e = {"value": flops_layer / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s (effective)",
+               "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "path": "torch.ops.trianglemix_reference.triangle_paged_sparse_attention"}
+    status = tm._native.device_status(local)
+    if status:
+        raise RuntimeError(f"device status {status:#x} after timing")
+
+    peaks, peak_kind = load_peaks()
+    achieved = flops_layer * heads_per_rank / KV_HEADS / (kernel_ms * 1e-3) / 1e12
+    roofline = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
+                "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"], "traffic": None,
+                "peak_source": f"{peak_kind} bf16_tflops (burst)",
+                "kernel": "tpsa_paged_kernel<false>", "kernel_ms": kernel_ms,
+                "algorithmic": "4*128*heads*pairs effective FLOPs per launch"}
+    line = {"metric": METRIC, "value": value, "unit": "TFLOP/s (effective)", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "ms_per_layer": ms_step / layers, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) bf16)",
+            "config": workload_config(args), "gpu_launches": args.steps * layers,
+            "clocks": clocks, "roofline": roofline, "e2e": e2e,
+            "plan": {"grid": plan.grid, "items": plan.total_items, "split_tiles": plan.split_tiles,
+                     "tiles": plan.total_tiles}}
+    if rank == 0 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(tq, seq, q0, seq, args.cpu_budget)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

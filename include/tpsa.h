@@ -1,0 +1,220 @@
+/*
+ * tpsa.h - C ABI of the B200 (sm_100a) TriangleMix paged sparse prefill
+ * attention library, libtpsa.so.
+ *
+ * The ABI uses plain pointers, integers and POD structs only.  Every entry
+ * point is host code; the compute entry points enqueue work on the caller's
+ * CUDA stream (passed as `void*`, i.e. a cudaStream_t, NULL = legacy default
+ * stream) and return without synchronising.
+ *
+ * Semantics per query row q (absolute position) of one request:
+ *   sparse row  (521 <= q < prompt_len - 128): keys [0, 8) U [q - 512, q]
+ *   dense row   (otherwise):                   keys [0, min(q + 1, seq_len))
+ * All keys of a row share one softmax; output is bf16.
+ *
+ * Reference interfaces replaced (paths are inside the reference project):
+ *   operator/torch_adapter/triangle_paged_attention_torch.cpp:101-178
+ *       triangle_paged_sparse_attention[_out]  -> tpsa_paged_attention
+ *   operator/torch_adapter/triangle_paged_attention_torch.cpp:180-261
+ *       triangle_paged_sparse_attention_workspace_size -> tpsa_workspace_size
+ *   operator/op_host/triangle_paged_sparse_attention.cpp:122-327
+ *       optiling::TilingFunc (shape gate + task geometry) -> tpsa_make_plan
+ *   operator/op_kernel/triangle_schedule.h:74-142
+ *       SplitQueryTile / BuildTileSchedule -> tpsa_plan_item / tpsa_plan_tile
+ */
+#ifndef TPSA_H_
+#define TPSA_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define TPSA_API __attribute__((visibility("default")))
+#else
+#define TPSA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TPSA_ABI_VERSION 1
+
+/* Fixed geometry (reference operator/op_kernel/triangle_schedule.h:14-21). */
+#define TPSA_QUERY_HEADS 32
+#define TPSA_KV_HEADS 8
+#define TPSA_HEAD_DIM 128
+#define TPSA_PAGE_SIZE 128
+#define TPSA_SINK_TOKENS 8
+#define TPSA_LOCAL_WINDOW 512
+#define TPSA_DENSE_TAIL 128
+#define TPSA_QUERY_TILE 32 /* reference attribute value; accepted, not used */
+
+typedef enum tpsa_status {
+  TPSA_OK = 0,
+  TPSA_ERR_INVALID_ARGUMENT = 1, /* a shape / attribute gate failed      */
+  TPSA_ERR_WORKSPACE = 2,        /* workspace missing or too small        */
+  TPSA_ERR_CUDA = 3,             /* a CUDA runtime or driver call failed  */
+  TPSA_ERR_UNSUPPORTED_DEVICE = 4, /* current device is not sm_100       */
+  TPSA_ERR_DEVICE_FAULT = 5,     /* the device status word is non-zero    */
+} tpsa_status;
+
+/* Device status word bits (tpsa_device_status). */
+#define TPSA_DEVICE_WAIT_TIMEOUT 0x1u /* a pipeline wait hit its bound      */
+#define TPSA_DEVICE_BAD_PAGE 0x2u     /* block_table held an out-of-range page */
+
+/*
+ * Launch plan: how one call is cut into work items.  A work item is
+ * (64-token query block, kv head, key-tile range); dense-tail blocks with many
+ * key tiles are split into several items whose partial results are merged
+ * inside the same launch.  Computed on the host by tpsa_make_plan.
+ */
+typedef struct tpsa_plan {
+  int32_t query_tokens;  /* Tq                                         */
+  int32_t query_start;   /* absolute position of query row 0           */
+  int32_t seq_len;       /* query_start + Tq                           */
+  int32_t sparse_begin;  /* 521                                        */
+  int32_t sparse_end;    /* min(max(0, prompt_len - 128), seq_len)     */
+  int32_t kv_heads;      /* kv heads held by this cache / call         */
+  int32_t num_blocks;    /* ceil(Tq / 64)                              */
+  int32_t tail_block0;   /* first block holding a dense-tail row       */
+  int32_t tail_items;    /* items of blocks [tail_block0, num_blocks)  */
+  int32_t total_items;   /* all work items                             */
+  int32_t split_tiles;   /* max key tiles per item for tail blocks     */
+  int32_t grid;          /* persistent CTAs launched                   */
+  int64_t workspace_bytes; /* scratch needed by tpsa_paged_attention   */
+  int64_t total_tiles;   /* key tiles summed over all items            */
+  float scale;           /* softmax scale                              */
+  float scale_log2;      /* scale * log2(e)                            */
+} tpsa_plan;
+
+typedef struct tpsa_item {
+  int32_t block;      /* query block index (rows 64*block ...)      */
+  int32_t kv_head;    /* kv head (query heads 4*kv_head .. +3)      */
+  int32_t split;      /* split index within the block               */
+  int32_t num_splits; /* number of items the block's keys are cut into */
+  int32_t tile_begin; /* first key tile of this item (block-local)   */
+  int32_t tile_end;   /* one past the last key tile                  */
+} tpsa_item;
+
+/* ABI version of the loaded library (TPSA_ABI_VERSION at build time). */
+TPSA_API int32_t tpsa_abi_version(void);
+
+/* Static description of a status code. */
+TPSA_API const char* tpsa_status_string(tpsa_status status);
+
+/* Message of the last failed host-side check on this thread ("" if none). */
+TPSA_API const char* tpsa_last_error(void);
+
+/*
+ * Validate the scalar attributes and build the launch plan.  `sm_count` <= 0
+ * means "query the current device".  Mirrors the reference TilingFunc gates
+ * (operator/op_host/triangle_paged_sparse_attention.cpp:192-238):
+ * query_start >= 0, seq_len > 0, prompt_len >= seq_len,
+ * query_start + query_tokens == seq_len, scale finite and > 0.
+ */
+TPSA_API tpsa_status tpsa_make_plan(int64_t query_tokens, int64_t query_start,
+                           int64_t seq_len, int64_t prompt_len,
+                           int32_t kv_heads, int32_t sm_count, float scale,
+                           tpsa_plan* plan);
+
+/* Work item `item` (0 <= item < plan->total_items), in launch order. */
+TPSA_API tpsa_status tpsa_plan_item(const tpsa_plan* plan, int32_t item,
+                           tpsa_item* out);
+
+/*
+ * Key tile `tile` of query block `block`: keys [*key_begin, *key_begin +
+ * *key_count), never crossing a page; *needs_mask is 1 when some row of the
+ * block excludes some key of the tile (causal / window / sink boundary).
+ */
+TPSA_API tpsa_status tpsa_plan_tile(const tpsa_plan* plan, int32_t block, int32_t tile,
+                           int32_t* key_begin, int32_t* key_count,
+                           int32_t* needs_mask);
+
+/*
+ * Scratch bytes tpsa_paged_attention needs on the current device for these
+ * attributes (0 when no block is split).  Replaces
+ * triangle_paged_sparse_attention_workspace_size (reference
+ * operator/torch_adapter/triangle_paged_attention_torch.cpp:180-261).
+ */
+TPSA_API tpsa_status tpsa_workspace_size(int64_t query_tokens, int64_t query_start,
+                                int64_t seq_len, int64_t prompt_len,
+                                uint64_t* bytes);
+
+/*
+ * TriangleMix paged sparse prefill attention, one request, one launch.
+ * Replaces aclnnTrianglePagedSparseAttention behind the reference's
+ * triangle_paged_sparse_attention[.out] (reference
+ * operator/torch_adapter/triangle_paged_attention_torch.cpp:101-178).
+ *
+ *   query        bf16 [query_tokens, 32, 128], contiguous, device memory
+ *   key_cache    bf16 [num_pages, 128, 8, 128] (BSND pages), contiguous
+ *   value_cache  bf16, same shape as key_cache
+ *   block_table  int32 [1, table_cols]; logical page -> physical page
+ *   out          bf16 [query_tokens, 32, 128], caller-owned, not aliasing
+ *                any input; written in place
+ *   workspace    device scratch of at least tpsa_workspace_size() bytes,
+ *                256-byte aligned; may be NULL when that size is 0.  Its
+ *                contents need not be initialised; calls sharing one
+ *                workspace must be ordered on one stream.
+ *   stream       cudaStream_t
+ *
+ * Gates (reference op_host :133-238): table_cols >= ceil(seq_len / 128),
+ * num_pages > 0, query_start + query_tokens == seq_len, prompt_len >= seq_len,
+ * seq_len <= 2^30.  Physical page ids are checked on the device: an id
+ * outside [0, num_pages) reads zeros and sets TPSA_DEVICE_BAD_PAGE.
+ * Returns without synchronising; no device memory is allocated.
+ */
+TPSA_API tpsa_status tpsa_paged_attention(const void* query, const void* key_cache,
+                                 const void* value_cache,
+                                 const int32_t* block_table, void* out,
+                                 int64_t query_tokens, int64_t num_pages,
+                                 int64_t table_cols, int64_t query_start,
+                                 int64_t seq_len, int64_t prompt_len,
+                                 float scale, void* workspace,
+                                 uint64_t workspace_bytes, void* stream);
+
+/*
+ * Same computation for a head-sharded cache: this call owns `kv_heads`
+ * (1, 2, 4 or 8) kv heads and the 4 * kv_heads query heads that read them,
+ * i.e. query [Tq, 4*kv_heads, 128] and caches [num_pages, 128, kv_heads,
+ * 128].  Used by the 1/2/4/8-GPU KV-head partition; no reference
+ * counterpart (the reference forces tensor-parallel callers to fall back,
+ * package/src/vllm_ascend_trianglemix/plugin.py:1251-1253).
+ */
+TPSA_API tpsa_status tpsa_paged_attention_heads(
+    const void* query, const void* key_cache, const void* value_cache,
+    const int32_t* block_table, void* out, int64_t query_tokens,
+    int64_t num_pages, int64_t table_cols, int64_t query_start,
+    int64_t seq_len, int64_t prompt_len, float scale, int32_t kv_heads,
+    void* workspace, uint64_t workspace_bytes, void* stream);
+
+/*
+ * Debug variant that runs the identical kernel and additionally records,
+ * for every (query row, query head), the key indices that entered its
+ * softmax: bit k of visited[(row * 4*kv_heads + head) * words_per_row +
+ * k / 32], words_per_row = ceil(seq_len / 32).  `visited` must be zeroed by
+ * the caller; `tile_counter` (2 x uint64, zeroed by the caller) receives the
+ * number of key tiles and of keys loaded.  Test infrastructure for the
+ * visited-key-set contract; not a production entry point.
+ */
+TPSA_API tpsa_status tpsa_paged_attention_visit(
+    const void* query, const void* key_cache, const void* value_cache,
+    const int32_t* block_table, void* out, int64_t query_tokens,
+    int64_t num_pages, int64_t table_cols, int64_t query_start,
+    int64_t seq_len, int64_t prompt_len, float scale, int32_t kv_heads,
+    void* workspace, uint64_t workspace_bytes, uint32_t* visited,
+    uint64_t* tile_counter, void* stream);
+
+/*
+ * Read and clear the device status word of `device` (TPSA_DEVICE_* bits).
+ * Synchronises that device.  A non-zero word means a launch since the last
+ * read hit a bounded wait or an out-of-range page id.
+ */
+TPSA_API tpsa_status tpsa_device_status(int32_t device, uint32_t* status_bits);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* TPSA_H_ */

@@ -1,0 +1,214 @@
+"""ctypes binding of libtpsa.so (the C ABI declared in include/tpsa.h).
+
+The library is built in-tree by ``build.py``.  Nothing here falls back to a
+CPU or PyTorch implementation: if the library is missing, every call raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+PKG_DIR = Path(__file__).resolve().parent
+LIB_PATH = PKG_DIR / "libtpsa.so"
+ADAPTER_PATH = PKG_DIR / "_tpsa_torch.so"
+
+TPSA_OK = 0
+STATUS_NAMES = {
+    0: "TPSA_OK",
+    1: "TPSA_ERR_INVALID_ARGUMENT",
+    2: "TPSA_ERR_WORKSPACE",
+    3: "TPSA_ERR_CUDA",
+    4: "TPSA_ERR_UNSUPPORTED_DEVICE",
+    5: "TPSA_ERR_DEVICE_FAULT",
+}
+DEVICE_WAIT_TIMEOUT = 0x1
+DEVICE_BAD_PAGE = 0x2
+
+# Every symbol include/tpsa.h declares.
+EXPORTED_SYMBOLS = (
+    "tpsa_abi_version",
+    "tpsa_status_string",
+    "tpsa_last_error",
+    "tpsa_make_plan",
+    "tpsa_plan_item",
+    "tpsa_plan_tile",
+    "tpsa_workspace_size",
+    "tpsa_paged_attention",
+    "tpsa_paged_attention_heads",
+    "tpsa_paged_attention_visit",
+    "tpsa_device_status",
+)
+
+
+class Plan(ctypes.Structure):
+    _fields_ = [
+        ("query_tokens", ctypes.c_int32),
+        ("query_start", ctypes.c_int32),
+        ("seq_len", ctypes.c_int32),
+        ("sparse_begin", ctypes.c_int32),
+        ("sparse_end", ctypes.c_int32),
+        ("kv_heads", ctypes.c_int32),
+        ("num_blocks", ctypes.c_int32),
+        ("tail_block0", ctypes.c_int32),
+        ("tail_items", ctypes.c_int32),
+        ("total_items", ctypes.c_int32),
+        ("split_tiles", ctypes.c_int32),
+        ("grid", ctypes.c_int32),
+        ("workspace_bytes", ctypes.c_int64),
+        ("total_tiles", ctypes.c_int64),
+        ("scale", ctypes.c_float),
+        ("scale_log2", ctypes.c_float),
+    ]
+
+
+class Item(ctypes.Structure):
+    _fields_ = [
+        ("block", ctypes.c_int32),
+        ("kv_head", ctypes.c_int32),
+        ("split", ctypes.c_int32),
+        ("num_splits", ctypes.c_int32),
+        ("tile_begin", ctypes.c_int32),
+        ("tile_end", ctypes.c_int32),
+    ]
+
+
+class TpsaError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"{STATUS_NAMES.get(status, status)}: {message}")
+        self.status = status
+
+
+_LOCK = threading.Lock()
+_LIB: ctypes.CDLL | None = None
+
+_i32, _i64, _u64, _f32, _vp = ctypes.c_int32, ctypes.c_int64, ctypes.c_uint64, ctypes.c_float, ctypes.c_void_p
+_ATTN = [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _f32]
+
+
+def lib() -> ctypes.CDLL:
+    """Load libtpsa.so once (raises if it has not been built)."""
+    global _LIB
+    with _LOCK:
+        if _LIB is not None:
+            return _LIB
+        if not LIB_PATH.exists():
+            raise RuntimeError(f"{LIB_PATH} is missing; build it with build.py")
+        h = ctypes.CDLL(str(LIB_PATH))
+        h.tpsa_abi_version.restype = _i32
+        h.tpsa_status_string.argtypes = [ctypes.c_int]
+        h.tpsa_status_string.restype = ctypes.c_char_p
+        h.tpsa_last_error.restype = ctypes.c_char_p
+        h.tpsa_make_plan.argtypes = [_i64, _i64, _i64, _i64, _i32, _i32, _f32, ctypes.POINTER(Plan)]
+        h.tpsa_plan_item.argtypes = [ctypes.POINTER(Plan), _i32, ctypes.POINTER(Item)]
+        h.tpsa_plan_tile.argtypes = [ctypes.POINTER(Plan), _i32, _i32, ctypes.POINTER(_i32),
+                                     ctypes.POINTER(_i32), ctypes.POINTER(_i32)]
+        h.tpsa_workspace_size.argtypes = [_i64, _i64, _i64, _i64, ctypes.POINTER(_u64)]
+        h.tpsa_paged_attention.argtypes = _ATTN + [_vp, _u64, _vp]
+        h.tpsa_paged_attention_heads.argtypes = _ATTN + [_i32, _vp, _u64, _vp]
+        h.tpsa_paged_attention_visit.argtypes = _ATTN + [_i32, _vp, _u64, _vp, _vp, _vp]
+        h.tpsa_device_status.argtypes = [_i32, ctypes.POINTER(ctypes.c_uint32)]
+        for name in ("tpsa_make_plan", "tpsa_plan_item", "tpsa_plan_tile", "tpsa_workspace_size",
+                     "tpsa_paged_attention", "tpsa_paged_attention_heads",
+                     "tpsa_paged_attention_visit", "tpsa_device_status"):
+            getattr(h, name).restype = ctypes.c_int
+        _LIB = h
+        return h
+
+
+def check(status: int) -> None:
+    if status != TPSA_OK:
+        msg = lib().tpsa_last_error().decode() or lib().tpsa_status_string(status).decode()
+        raise TpsaError(status, msg)
+
+
+def make_plan(query_tokens: int, query_start: int, seq_len: int, prompt_len: int,
+              kv_heads: int = 8, sm_count: int = 0, scale: float = 128 ** -0.5) -> Plan:
+    plan = Plan()
+    check(lib().tpsa_make_plan(query_tokens, query_start, seq_len, prompt_len, kv_heads, sm_count,
+                               scale, ctypes.byref(plan)))
+    return plan
+
+
+def plan_item(plan: Plan, item: int) -> Item:
+    out = Item()
+    check(lib().tpsa_plan_item(ctypes.byref(plan), item, ctypes.byref(out)))
+    return out
+
+
+def plan_tile(plan: Plan, block: int, tile: int) -> tuple[int, int, bool]:
+    k0, w, m = _i32(), _i32(), _i32()
+    check(lib().tpsa_plan_tile(ctypes.byref(plan), block, tile, ctypes.byref(k0), ctypes.byref(w),
+                               ctypes.byref(m)))
+    return k0.value, w.value, bool(m.value)
+
+
+def workspace_size(query_tokens: int, query_start: int, seq_len: int, prompt_len: int) -> int:
+    out = _u64()
+    check(lib().tpsa_workspace_size(query_tokens, query_start, seq_len, prompt_len, ctypes.byref(out)))
+    return out.value
+
+
+def device_status(device: int = 0) -> int:
+    bits = ctypes.c_uint32()
+    st = lib().tpsa_device_status(device, ctypes.byref(bits))
+    if st not in (TPSA_OK, 5):
+        check(st)
+    return bits.value
+
+
+def paged_attention(query, key_cache, value_cache, block_table, out, query_start: int,
+                    seq_len: int, prompt_len: int, scale: float, *, kv_heads: int | None = None,
+                    workspace=None, stream=None, visited=None, tile_counter=None) -> None:
+    """Launch through the C ABI with torch CUDA tensors (no checks beyond the ABI's)."""
+    import torch
+
+    if stream is None:
+        stream = torch.cuda.current_stream(query.device).cuda_stream
+    h = lib()
+    ws_ptr = workspace.data_ptr() if workspace is not None else None
+    ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
+    common = (query.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(), block_table.data_ptr(),
+              out.data_ptr(), query.shape[0], key_cache.shape[0], block_table.shape[-1],
+              query_start, seq_len, prompt_len, scale)
+    if visited is not None:
+        check(h.tpsa_paged_attention_visit(*common, kv_heads or key_cache.shape[2], ws_ptr, ws_bytes,
+                                           visited.data_ptr(), tile_counter.data_ptr(), stream))
+    elif kv_heads is not None:
+        check(h.tpsa_paged_attention_heads(*common, kv_heads, ws_ptr, ws_bytes, stream))
+    else:
+        check(h.tpsa_paged_attention(*common, ws_ptr, ws_bytes, stream))
+
+
+_ADAPTER_LOADED: str | None = None
+
+
+def load_adapter(path: str | Path | None = None) -> str:
+    """Load the torch op adapter once per process (refuses a second path)."""
+    import torch
+
+    global _ADAPTER_LOADED
+    resolved = str(Path(path or ADAPTER_PATH).resolve())
+    with _LOCK:
+        if _ADAPTER_LOADED is not None:
+            if _ADAPTER_LOADED != resolved:
+                raise RuntimeError(
+                    f"TriangleMix adapter is already loaded from {_ADAPTER_LOADED}; refusing {resolved}")
+            return resolved
+        if not Path(resolved).is_file():
+            raise FileNotFoundError(f"TriangleMix Torch adapter does not exist: {resolved}")
+        torch.ops.load_library(resolved)
+        try:
+            torch.ops.trianglemix.triangle_paged_sparse_attention.out
+        except (AttributeError, RuntimeError) as err:
+            raise RuntimeError(
+                "TriangleMix adapter did not register trianglemix::triangle_paged_sparse_attention.out"
+            ) from err
+        _ADAPTER_LOADED = resolved
+        return resolved
+
+
+def adapter_loaded() -> bool:
+    with _LOCK:
+        return _ADAPTER_LOADED is not None
