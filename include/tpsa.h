@@ -133,7 +133,8 @@ TPSA_API tpsa_status tpsa_plan_tile(const tpsa_plan* plan, int32_t block, int32_
 
 /*
  * Scratch bytes tpsa_paged_attention needs on the current device for these
- * attributes (0 when no block is split).  Replaces
+ * attributes: 2 KiB of scheduler control words, plus the partial results of
+ * split dense-tail blocks when the plan splits any.  Replaces
  * triangle_paged_sparse_attention_workspace_size (reference
  * operator/torch_adapter/triangle_paged_attention_torch.cpp:180-261).
  */
@@ -154,9 +155,10 @@ TPSA_API tpsa_status tpsa_workspace_size(int64_t query_tokens, int64_t query_sta
  *   out          bf16 [query_tokens, 32, 128], caller-owned, not aliasing
  *                any input; written in place
  *   workspace    device scratch of at least tpsa_workspace_size() bytes,
- *                256-byte aligned; may be NULL when that size is 0.  Its
- *                contents need not be initialised; calls sharing one
- *                workspace must be ordered on one stream.
+ *                256-byte aligned, never NULL.  Its contents need not be
+ *                initialised: each call clears the 2 KiB of control words
+ *                with cudaMemsetAsync on `stream` before the kernel.  Calls
+ *                sharing one workspace must be ordered on one stream.
  *   stream       cudaStream_t
  *
  * Gates (reference op_host :133-238): table_cols >= ceil(seq_len / 128),

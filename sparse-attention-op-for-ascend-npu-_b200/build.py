@@ -49,16 +49,33 @@ def _run(cmd: list[str]) -> None:
         raise RuntimeError(f"build step failed ({' '.join(cmd[:3])} ...):\n{res.stdout}\n{res.stderr}")
 
 
-def build_lib(force: bool = False, verbose_ptxas: bool = False) -> Path:
+def _check_ptxas_report(text: str) -> None:
+    """The kernel must compile without local-memory spills (softmax rows live
+    in registers; a spill puts local-memory traffic on the critical path)."""
+    import re
+
+    found = re.findall(r"Compiling entry function '\w*tpsa_paged_kernel\w*' for 'sm_100a'\n"
+                       r"(?:.*\n)*?\s*(\d+) bytes stack frame, (\d+) bytes spill stores", text)
+    if not found:
+        raise RuntimeError("could not read the ptxas report of tpsa_paged_kernel")
+    spills = [int(st) for _, st in found]
+    if any(spills):
+        raise RuntimeError(f"tpsa_paged_kernel spills registers ({spills} bytes)")
+
+
+def build_lib(force: bool = False) -> Path:
     sources = [CSRC / "tpsa_kernel.cu", CSRC / "tpsa_schedule.h", CSRC / "sm100_ptx.cuh",
                INCLUDE / "tpsa.h"]
     if not force and _newer(LIB, sources):
         return LIB
     tmp = LIB.with_suffix(".so.tmp")
-    cmd = [_nvcc(), *NVCC_FLAGS, "-shared", "-o", str(tmp), str(CSRC / "tpsa_kernel.cu")]
-    if verbose_ptxas:
-        cmd.insert(1, "-Xptxas=-v")
-    _run(cmd)
+    cmd = [_nvcc(), *NVCC_FLAGS, "-Xptxas=-v", "-shared", "-o", str(tmp),
+           str(CSRC / "tpsa_kernel.cu")]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"nvcc failed:\n{res.stdout}\n{res.stderr}")
+    _check_ptxas_report(res.stdout + res.stderr)
+    (PKG_DIR / "ptxas_report.txt").write_text(res.stdout + res.stderr)
     tmp.replace(LIB)
     return LIB
 

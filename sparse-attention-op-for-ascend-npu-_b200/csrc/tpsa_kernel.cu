@@ -7,23 +7,37 @@
 // BSND paged cache through the block table and writing bf16 output into the
 // caller's buffer.
 //
-// CTA organisation (one CTA per SM, 320 threads):
-//   warp 0      TMA producer: Q block (4 boxes), K/V key tiles (64-row boxes)
-//   warp 1      tcgen05 MMA issuer (lane 0) and TMEM owner
-//   warps 2-5   softmax + epilogue of M tile 0 (query heads 4h, 4h+1)
-//   warps 6-9   softmax + epilogue of M tile 1 (query heads 4h+2, 4h+3)
-// A work item is (64-token query block, kv head, key-tile range).  Its 256
-// rows (64 tokens x 4 GQA heads) are two M=128 tiles; both read the same
-// K/V tile from shared memory, so every K/V byte loaded serves 4 heads.
+// CTA pairs.  The kernel runs as clusters of two CTAs on two SMs that share
+// every tensor-core instruction (tcgen05 cta_group::2, M = 256):
+//   * a work item is (64-token query block, kv head, key-tile range); its
+//     256 rows (64 tokens x 4 GQA heads) are split between the pair: CTA r
+//     owns query heads {4h + 2r, 4h + 2r + 1} (128 rows, one M half);
+//   * each key tile [k0, k0 + w) is split between the pair as the MMA wants
+//     its B operand split along N: CTA r loads keys [k0 + r*w/2, +w/2) of K
+//     (for S = Q K^T) and d-half r of V (for O = P V), so every K/V byte is
+//     loaded once per pair and serves 4 query heads.
+// Roles (384 threads per CTA):
+//   warp 0      TMA producer; in CTA 0 also the work scheduler (a global
+//               counter, longest items first), which hands items to CTA 1
+//               through its shared memory
+//   warp 1      CTA 0: tcgen05 MMA issuer; both: TMEM owner
+//   warps 4-11  softmax + epilogue of this CTA's 128 rows: warpgroup 0
+//               (warps 4-7) takes the first half of every S tile's columns
+//               and of O's, warpgroup 1 (warps 8-11) the second half; row
+//               maxima and sums are exchanged through shared memory
+// Tensor memory per CTA (fp32 columns): S0 [0,128), S1 [128,256),
+// O [256,384).  S is double-buffered by key tile, so QK(n+1) runs while the
+// softmax of tile n is computed; P (bf16 pairs) overwrites the first half of
+// its S buffer and PV(n) reads it from there.  MMA issue order per item:
+//   QK(0), QK(1), PV(0), QK(2), PV(1), QK(3), ...
+// The O rescale for a grown row max is lazy (only when the max grows by
+// more than 2^8) and done by the softmax warps in tensor memory.
 //
-// Tensor memory (512 columns, fp32):
-//   [  0,128) S0 / P0   [128,256) S1 / P1   [256,384) O0   [384,512) O1
-// P (bf16 pairs) overwrites the first half of its S tile after the softmax
-// warps have read S.  Per M tile the MMA order is
-//   QK(n) -> softmax(n) -> PV(n) -> QK(n+1)
-// and the two M tiles alternate, so one tile's softmax overlaps the other's
-// MMAs.  The O rescale for a grown row max is lazy (only when the max grows
-// by more than 2^8) and is done by the softmax warps in tensor memory.
+// Softmax arithmetic: scores are scaled into the log2 domain with one fused
+// multiply-add, exponentiated with ex2.approx (MUFU) for 3 of every 4 column
+// pairs and with poly_exp2 (FMA pipe) for the fourth, summed in fp32, and
+// rounded to bf16 (round-to-nearest-even) for the PV product, as the
+// reference does (vendor block_epilogue_online_softmax.hpp:886-906).
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -41,53 +55,113 @@ namespace tpsa {
 
 __device__ uint32_t g_device_status = 0;
 
+// Optional event trace of cluster 0 (build with -DTPSA_TRACE; compiled out of
+// the library otherwise).  Each tracing thread owns one buffer and a register
+// counter, so a trace point is two plain stores and a clock read.
+#ifdef TPSA_TRACE
+constexpr uint32_t kTraceRoles = 4;
+constexpr uint32_t kTraceCap = 1u << 14;
+__device__ unsigned long long g_trace[kTraceRoles][kTraceCap][2];
+__device__ uint32_t g_trace_n[kTraceRoles];
+#define TPSA_TRACE_STATE uint32_t tr_n_ = 0
+#define TPSA_SM_TR(ev)                                                             \
+  do {                                                                             \
+    if (blockIdx.x < 2 && threadIdx.x == 128 && trn < kTraceCap) {              \
+      g_trace[trole][trn][0] = static_cast<unsigned long long>(ev) << 32;          \
+      g_trace[trole][trn][1] = clock64();                                          \
+      ++trn;                                                                       \
+      g_trace_n[trole] = trn;                                                      \
+    }                                                                              \
+  } while (0)
+#define TPSA_TR(role, ev, arg)                                                    \
+  do {                                                                            \
+    if (blockIdx.x < 2 && tr_n_ < kTraceCap) {                                    \
+      g_trace[role][tr_n_][0] = (static_cast<unsigned long long>(ev) << 32) |     \
+                                static_cast<uint32_t>(arg);                        \
+      g_trace[role][tr_n_][1] = clock64();                                        \
+      ++tr_n_;                                                                    \
+      g_trace_n[role] = tr_n_;                                                    \
+    }                                                                             \
+  } while (0)
+#else
+#define TPSA_TRACE_STATE \
+  do {                   \
+  } while (0)
+#define TPSA_TR(role, ev, arg) \
+  do {                         \
+  } while (0)
+#define TPSA_SM_TR(ev) \
+  do {                 \
+  } while (0)
+#endif
+
 namespace {
 
-constexpr int kNumThreads = 320;
-constexpr int kStages = 2;
+constexpr int kNumThreads = 384;
+constexpr int kSoftmaxWarps = 8;  // two warpgroups, each half of the S columns
 constexpr uint32_t kTmemCols = 512;
 constexpr uint64_t kWaitTimeoutNs = 1000000000ull;  // 1 s per wait
+constexpr uint64_t kAbortSettleNs = 200000ull;      // let in-flight TMA land
 constexpr float kRescaleLog2 = 8.0f;  // lazy O rescale threshold (log2 units)
+constexpr uint16_t kPairMask = 0x3;
 
-// Shared memory (offsets from a 1024-byte aligned base).
-constexpr uint32_t kHalfBytes = 128 * 128;        // 128 rows x 64 bf16
-constexpr uint32_t kQBytes = 4 * kHalfBytes;      // [m tile][d half]
-constexpr uint32_t kStageBytes = 2 * kHalfBytes;  // [d half]
-constexpr uint32_t kOffQ = 0;
-constexpr uint32_t kOffK = kOffQ + kQBytes;
-constexpr uint32_t kOffV = kOffK + kStages * kStageBytes;
-constexpr uint32_t kOffBar = kOffV + kStages * kStageBytes;
+// Shared memory per CTA (offsets from a 1024-byte aligned base).
+constexpr uint32_t kQHalfBytes = 128 * 128;        // 128 rows x 64 bf16
+constexpr uint32_t kQBytes = 2 * kQHalfBytes;      // one Q buffer (2 d-halves)
+constexpr uint32_t kRingSlotBytes = 16384;         // one K or V half-tile
+constexpr uint32_t kKHalfBytes = 8192;             // d-half of a K half-tile
+constexpr int kRing = 9;                           // K/V half-tile slots
+constexpr uint32_t kOffQ = 0;                      // 2 Q buffers
+constexpr uint32_t kOffKV = kOffQ + 2 * kQBytes;
+constexpr uint32_t kOffBar = kOffKV + kRing * kRingSlotBytes;
 
 enum BarId : uint32_t {
-  kBarQFull = 0,
-  kBarQEmpty,
-  kBarKFull,                      // + stage
-  kBarKEmpty = kBarKFull + kStages,
-  kBarVFull = kBarKEmpty + kStages,
-  kBarVEmpty = kBarVFull + kStages,
-  kBarSFull = kBarVEmpty + kStages,  // + m tile
-  kBarPFull = kBarSFull + 2,
-  kBarOFull = kBarPFull + 2,
-  kBarOEmpty = kBarOFull + 2,
-  kBarSplitWritten = kBarOEmpty + 2,
-  kBarSplitDecided,
-  kBarDrain,
+  kBarQFull = 0,                          // [2] CTA 0: both Q halves landed
+  kBarQEmpty = kBarQFull + 2,             // [2] both CTAs: Q buffer free
+  kBarKVFull = kBarQEmpty + 2,            // [kRing] CTA 0: both halves landed
+  kBarKVEmpty = kBarKVFull + kRing,       // [kRing] both: slot free
+  kBarSFull = kBarKVEmpty + kRing,        // [2] both: S buffer computed
+  kBarPFull = kBarSFull + 2,              // CTA 0: P of a tile in TMEM (8 warps)
+  kBarPvDone = kBarPFull + 1,             // both: PV of a tile completed
+  kBarOEmpty = kBarPvDone + 1,            // CTA 0: O read by both epilogues
+  kBarItemFull = kBarOEmpty + 1,          // [2] both: item index written
+  kBarItemEmpty = kBarItemFull + 2,       // [2] CTA 0: item index consumed
+  kBarSplitWritten = kBarItemEmpty + 2,   // per CTA: split partial written
+  kBarSplitDecided = kBarSplitWritten + 1,
+  kBarTail = kBarSplitDecided + 1,        // per CTA: V tail tile landed
+  kBarDrain = kBarTail + 1,               // CTA 0: all MMAs complete
+  kBarWgX = kBarDrain + 1,                // per CTA: softmax warpgroups exchanged
   kNumBars
 };
+// Arrivals: p_full and o_empty take one per softmax warp of both CTAs;
+// item_empty takes the MMA issuer and 4 softmax warps of CTA 0 plus the
+// producer and 4 softmax warps of CTA 1.
+constexpr uint32_t kPairWarpArrivals = 2 * kSoftmaxWarps;
+constexpr uint32_t kItemConsumers = 2 * (1 + kSoftmaxWarps);
 
-constexpr uint32_t kOffTmemSlot = kOffBar + kNumBars * 8;
+constexpr uint32_t kOffItemSlots = kOffBar + kNumBars * 8;  // 2 x int32
+constexpr uint32_t kOffTmemSlot = kOffItemSlots + 8;
 constexpr uint32_t kOffAbort = kOffTmemSlot + 4;
 constexpr uint32_t kOffSplitLast = kOffAbort + 4;
-constexpr uint32_t kSmemUsed = kOffSplitLast + 4;
+// Row-max / row-sum exchange between the two softmax warpgroups:
+// float [2 buffers][2 warpgroups][128 rows].
+constexpr uint32_t kOffXchg = (kOffSplitLast + 4 + 15) & ~15u;
+constexpr uint32_t kSmemUsed = kOffXchg + 2 * 2 * 128 * 4;
 constexpr uint32_t kSmemBytes = kSmemUsed + 1024;  // alignment slack
 static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+
+// Workspace control words (first kControlBytes of the workspace, zeroed by
+// the launcher): [0] next work item, [64..] one split counter per
+// (tail block, kv head, pair rank).
+constexpr int kCtlNextItem = 0;
+constexpr int kCtlSplitBase = 64;
 
 struct KernelArgs {
   tpsa_plan plan;
   const int32_t* block_table;
   __nv_bfloat16* out;
   float* scratch;      // split partials (tail_items slots)
-  int32_t* split_ctr;  // one counter per (tail block, kv head)
+  int32_t* ctl;        // control words
   int32_t num_pages;
   int32_t words_per_row;       // visit mode
   uint32_t* visited;           // visit mode
@@ -97,23 +171,38 @@ struct KernelArgs {
 struct Shared {
   uint8_t* base;
   uint32_t base_u32;
+  uint32_t rank;  // CTA rank in the pair
   __device__ uint32_t bar(uint32_t id) const { return base_u32 + kOffBar + 8 * id; }
+  // The same barrier in CTA 0 (shared::cluster address).
+  __device__ uint32_t bar0(uint32_t id) const { return ptx::mapa(bar(id), 0); }
   __device__ volatile int* abort_flag() const {
     return reinterpret_cast<volatile int*>(base + kOffAbort);
   }
+  __device__ volatile int32_t* item_slot(uint32_t i) const {
+    return reinterpret_cast<volatile int32_t*>(base + kOffItemSlots) + i;
+  }
+  __device__ uint32_t item_slot_addr(uint32_t i) const { return base_u32 + kOffItemSlots + 4 * i; }
 };
 
 __device__ __forceinline__ void raise_status(uint32_t bits) {
   atomicOr(&g_device_status, bits);
 }
 
-// Bounded wait: gives up after kWaitTimeoutNs or as soon as another role has
-// aborted; on timeout records TPSA_DEVICE_WAIT_TIMEOUT and aborts the CTA.
+// Bounded wait: gives up after kWaitTimeoutNs or as soon as another role of
+// this CTA has aborted; on timeout records TPSA_DEVICE_WAIT_TIMEOUT.
+// kCluster selects a cluster-scope acquire (only needed where the signal
+// carries the peer's st.shared::cluster stores: the item ring).
+template <bool kCluster>
+__device__ __forceinline__ bool try_wait_sel(uint32_t bar, uint32_t parity) {
+  return kCluster ? ptx::mbar_try_wait_cluster(bar, parity) : ptx::mbar_try_wait(bar, parity);
+}
+
+template <bool kCluster>
 __device__ __noinline__ bool wait_bar_slow(uint32_t bar, uint32_t parity,
                                            volatile int* abort_flag) {
   const uint64_t t0 = ptx::globaltimer_ns();
   while (true) {
-    if (ptx::mbar_try_wait(bar, parity)) return true;
+    if (try_wait_sel<kCluster>(bar, parity)) return true;
     if (*abort_flag) return false;
     if (ptx::globaltimer_ns() - t0 > kWaitTimeoutNs) {
       *abort_flag = 1;
@@ -123,14 +212,14 @@ __device__ __noinline__ bool wait_bar_slow(uint32_t bar, uint32_t parity,
   }
 }
 
-__device__ __forceinline__ bool wait_bar(const Shared& sh, uint32_t bar,
-                                         uint32_t parity) {
-  if (ptx::mbar_try_wait(bar, parity)) return true;
-  return wait_bar_slow(bar, parity, sh.abort_flag());
+template <bool kCluster = false>
+__device__ __forceinline__ bool wait_bar(const Shared& sh, uint32_t bar, uint32_t parity) {
+  if (try_wait_sel<kCluster>(bar, parity)) return true;
+  return wait_bar_slow<kCluster>(bar, parity, sh.abort_flag());
 }
 
-// Bounded wait used while draining after an abort (ignores the abort flag).
-__device__ __noinline__ void drain_bar(uint32_t bar, uint32_t parity) {
+// Bounded wait used while draining (ignores the abort flag).
+__device__ __forceinline__ void drain_bar(uint32_t bar, uint32_t parity) {
   const uint64_t t0 = ptx::globaltimer_ns();
   while (!ptx::mbar_try_wait(bar, parity)) {
     if (ptx::globaltimer_ns() - t0 > kWaitTimeoutNs) {
@@ -140,10 +229,29 @@ __device__ __noinline__ void drain_bar(uint32_t bar, uint32_t parity) {
   }
 }
 
-__device__ __forceinline__ float fast_exp2(float x) {
+__device__ __forceinline__ uint32_t ring_slot(uint32_t r) { return r % kRing; }
+__device__ __forceinline__ uint32_t ring_parity(uint32_t r) { return (r / kRing) & 1; }
+
+__device__ __forceinline__ float mufu_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// 2^x on the FMA/ALU pipes: x = n + f with n = round(x), f in [-1/2, 1/2];
+// 2^f by a degree-3 minimax polynomial (Remez fit, max relative error
+// 7.5e-5, coefficients from csrc/fit_exp2_poly.py); 2^n added to the
+// exponent field.  x is clamped at -127.5 so that 2^n underflows the
+// exponent for any x <= -127.5 (and -inf) and the integer max returns +0.
+__device__ __forceinline__ float poly_exp2(float x) {
+  x = fmaxf(x, -127.5f);
+  const float t = x + 12582912.0f;  // 1.5 * 2^23: round(x) in the low bits
+  const float f = x - (t - 12582912.0f);
+  float p = fmaf(0.0551716685f, f, 0.2426111251f);
+  p = fmaf(p, f, 0.6932609677f);
+  p = fmaf(p, f, 0.9999280572f);
+  const int32_t bits = __float_as_int(p) + (__float_as_int(t) << 23);
+  return __int_as_float(max(bits, 0));
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
@@ -151,34 +259,95 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// (a0, a1) * (b, b) + (c, c) as one packed f32x2 FMA.
+__device__ __forceinline__ void fma2(float a0, float a1, float b, float c, float& r0,
+                                     float& r1) {
+  uint64_t av, bv, cv, rv;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(av) : "f"(a0), "f"(a1));
+  asm("mov.b64 %0, {%1, %1};" : "=l"(bv) : "f"(b));
+  asm("mov.b64 %0, {%1, %1};" : "=l"(cv) : "f"(c));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(rv) : "l"(av), "l"(bv), "l"(cv));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r0), "=f"(r1) : "l"(rv));
+}
+
+// (s0, s1) += (a0, a1) as one packed f32x2 add.
+__device__ __forceinline__ void add2(float& s0, float& s1, float a0, float a1) {
+  uint64_t sv, av;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(sv) : "f"(s0), "f"(s1));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(av) : "f"(a0), "f"(a1));
+  asm("add.rn.f32x2 %0, %0, %1;" : "+l"(sv) : "l"(av));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(s0), "=f"(s1) : "l"(sv));
+}
+
+// ------------------------------------------------------------ scheduler ring
+// Item indices flow from CTA 0's producer to every consumer through a
+// 2-slot ring in each CTA's shared memory.  Consumers in CTA 0 release on
+// their own item_empty, consumers in CTA 1 on CTA 0's (remote arrive).
+__device__ __forceinline__ bool take_item(const Shared& sh, uint32_t n, int32_t* idx) {
+  const uint32_t slot = n % 2;
+  if (!wait_bar<true>(sh, sh.bar(kBarItemFull + slot), (n / 2) & 1)) return false;
+  *idx = *sh.item_slot(slot);
+  return true;
+}
+
+__device__ __forceinline__ void release_item(const Shared& sh, uint32_t n) {
+  ptx::mbar_arrive_cluster(sh.bar0(kBarItemEmpty + n % 2));
+}
+
 // ------------------------------------------------------------ producer
 __device__ void producer_role(const KernelArgs& a, const Shared& sh,
-                              const CUtensorMap* tq, const CUtensorMap* tk,
-                              const CUtensorMap* tv) {
+                              const CUtensorMap* tq, const CUtensorMap* tk64,
+                              const CUtensorMap* tk32, const CUtensorMap* tv) {
   const tpsa_plan& p = a.plan;
+  const uint32_t r = sh.rank;
   ptx::prefetch_tmap(tq);
-  ptx::prefetch_tmap(tk);
+  ptx::prefetch_tmap(tk64);
+  ptx::prefetch_tmap(tk32);
   ptx::prefetch_tmap(tv);
-  uint32_t kv_iter = 0, item_iter = 0;
-  uint32_t stage_arms[kStages] = {0, 0};
+  uint32_t ring = 0, q_iter = 0, tail_iter = 0;
   bool ok = true;
-  for (int32_t idx = blockIdx.x; ok && idx < p.total_items; idx += gridDim.x) {
+  TPSA_TRACE_STATE;
+  int32_t next = r == 0 ? atomicAdd(a.ctl + kCtlNextItem, 1) : 0;
+  for (uint32_t n = 0; ok; ++n) {
+    int32_t idx;
+    const uint32_t slot = n % 2;
+    if (r == 0) {
+      idx = next;
+      if (!wait_bar(sh, sh.bar(kBarItemEmpty + slot), ((n / 2) & 1) ^ 1)) break;
+      *sh.item_slot(slot) = idx;
+      ptx::st_cluster_u32(ptx::mapa(sh.item_slot_addr(slot), 1), static_cast<uint32_t>(idx));
+      ptx::mbar_arrive(sh.bar(kBarItemFull + slot));
+      ptx::mbar_arrive_cluster_release(ptx::mapa(sh.bar(kBarItemFull + slot), 1));
+      if (idx >= p.total_items) break;
+      next = atomicAdd(a.ctl + kCtlNextItem, 1);  // latency hidden by the loads below
+    } else {
+      if (!take_item(sh, n, &idx)) break;
+      release_item(sh, n);
+      if (idx >= p.total_items) break;
+    }
+    if (r == 0) TPSA_TR(0, 20, idx);
     const tpsa_item it = decode_item(p, idx);
     const BlockTiles bt = block_tiles(p, it.block);
-    if (item_iter > 0 && !wait_bar(sh, sh.bar(kBarQEmpty), (item_iter - 1) & 1)) {
-      ok = false;
-      break;
+
+    // Q: this CTA's 128 rows (64 tokens x query heads 4h + 2r, 4h + 2r + 1).
+    const uint32_t qb = q_iter % 2;
+    if (q_iter >= 2 && !wait_bar(sh, sh.bar(kBarQEmpty + qb), ((q_iter / 2) - 1) & 1)) break;
+    ptx::mbar_arrive_expect_tx_cluster(sh.bar0(kBarQFull + qb), kQBytes);
+    for (int dh = 0; dh < 2; ++dh) {
+      ptx::tma_load_3d_pair(sh.base_u32 + kOffQ + qb * kQBytes + dh * kQHalfBytes, tq, dh * 64,
+                            it.kv_head * kGroupSize + 2 * r, it.block * kBlockQ,
+                            sh.bar0(kBarQFull + qb));
     }
-    ptx::mbar_arrive_expect_tx(sh.bar(kBarQFull), kQBytes);
-    for (int mt = 0; mt < 2; ++mt) {
-      for (int dh = 0; dh < 2; ++dh) {
-        ptx::tma_load_3d(sh.base_u32 + kOffQ + (mt * 2 + dh) * kHalfBytes, tq,
-                         dh * 64, it.kv_head * kGroupSize + mt * 2,
-                         it.block * kBlockQ, sh.bar(kBarQFull));
-      }
-    }
-    ++item_iter;
-    for (int32_t t = it.tile_begin; t < it.tile_end; ++t) {
+    ++q_iter;
+    if (r == 0) TPSA_TR(0, 21, idx);
+
+    for (int32_t t = it.tile_begin; t < it.tile_end && ok; ++t) {
       int32_t k0, w;
       tile_keys(bt, t, &k0, &w);
       const int32_t page = __ldg(a.block_table + k0 / kPageSize);
@@ -189,196 +358,195 @@ __device__ void producer_role(const KernelArgs& a, const Shared& sh,
       } else {
         tok = page * kPageSize + (k0 % kPageSize);
       }
-      if (a.tiles != nullptr) {
+      if (a.tiles != nullptr && r == 0) {
         atomicAdd(a.tiles, 1ull);
         atomicAdd(a.tiles + 1, static_cast<unsigned long long>(w));
       }
-      const uint32_t s = kv_iter % kStages;
-      const uint32_t empty_parity = ((kv_iter / kStages) & 1) ^ 1;
-      const uint32_t bytes = static_cast<uint32_t>(w) * kHeadDim * 2;
-      if (!wait_bar(sh, sh.bar(kBarKEmpty + s), empty_parity)) {
-        ok = false;
-        break;
-      }
-      ptx::mbar_arrive_expect_tx(sh.bar(kBarKFull + s), bytes);
-      for (int dh = 0; dh < 2; ++dh) {
-        for (int sub = 0; sub < w / 64; ++sub) {
-          ptx::tma_load_3d(
-              sh.base_u32 + kOffK + s * kStageBytes + dh * kHalfBytes + sub * 8192,
-              tk, dh * 64, it.kv_head, tok + sub * 64, sh.bar(kBarKFull + s));
+      const int32_t half = w / 2;
+      // K half-tile: keys [k0 + r*half, +half), all 128 d (two d-halves).
+      {
+        const uint32_t s = ring_slot(ring);
+        if (!wait_bar(sh, sh.bar(kBarKVEmpty + s), ring_parity(ring) ^ 1)) { ok = false; break; }
+        ptx::mbar_arrive_expect_tx_cluster(sh.bar0(kBarKVFull + s),
+                                           static_cast<uint32_t>(half) * kHeadDim * 2);
+        const CUtensorMap* km = w == kTileKeys ? tk64 : tk32;
+        for (int dh = 0; dh < 2; ++dh) {
+          ptx::tma_load_3d_pair(sh.base_u32 + kOffKV + s * kRingSlotBytes + dh * kKHalfBytes, km,
+                                dh * 64, it.kv_head, tok + static_cast<int32_t>(r) * half,
+                                sh.bar0(kBarKVFull + s));
         }
+        ++ring;
       }
-      if (!wait_bar(sh, sh.bar(kBarVEmpty + s), empty_parity)) {
-        // K of this stage is armed; account for it in the drain below.
-        ++stage_arms[s];
-        ok = false;
-        break;
-      }
-      ptx::mbar_arrive_expect_tx(sh.bar(kBarVFull + s), bytes);
-      for (int dh = 0; dh < 2; ++dh) {
-        for (int sub = 0; sub < w / 64; ++sub) {
-          ptx::tma_load_3d(
-              sh.base_u32 + kOffV + s * kStageBytes + dh * kHalfBytes + sub * 8192,
-              tv, dh * 64, it.kv_head, tok + sub * 64, sh.bar(kBarVFull + s));
+      // V half-tile: keys [k0, k0 + w), d-half r.
+      {
+        const uint32_t s = ring_slot(ring);
+        if (!wait_bar(sh, sh.bar(kBarKVEmpty + s), ring_parity(ring) ^ 1)) { ok = false; break; }
+        const uint32_t vdst = sh.base_u32 + kOffKV + s * kRingSlotBytes;
+        const uint32_t bytes = static_cast<uint32_t>(w) * 64 * 2;
+        if (k0 + w <= p.seq_len) {
+          ptx::mbar_arrive_expect_tx_cluster(sh.bar0(kBarKVFull + s), bytes);
+          for (int sub = 0; sub < w / 64; ++sub) {
+            ptx::tma_load_3d_pair(vdst + sub * 8192, tv, static_cast<int32_t>(r) * 64,
+                                  it.kv_head, tok + sub * 64, sh.bar0(kBarKVFull + s));
+          }
+        } else {
+          // Keys at or beyond seq_len may be unwritten cache slots: load the
+          // tile here, zero those V rows so P = 0 never meets a NaN, then
+          // release it to the MMA issuer with a plain arrival.
+          ptx::mbar_arrive_expect_tx(sh.bar(kBarTail), bytes);
+          for (int sub = 0; sub < w / 64; ++sub) {
+            ptx::tma_load_3d(vdst + sub * 8192, tv, static_cast<int32_t>(r) * 64, it.kv_head,
+                             tok + sub * 64, sh.bar(kBarTail));
+          }
+          if (!wait_bar(sh, sh.bar(kBarTail), tail_iter & 1)) { ok = false; break; }
+          ++tail_iter;
+          for (int32_t row = p.seq_len - k0; row < w; ++row) {
+            uint4* dst = reinterpret_cast<uint4*>(sh.base + (vdst - sh.base_u32) + row * 128);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) dst[j] = make_uint4(0, 0, 0, 0);
+          }
+          ptx::fence_proxy_async_smem();
+          ptx::mbar_arrive_cluster(sh.bar0(kBarKVFull + s));
         }
+        ++ring;
       }
-      ++stage_arms[s];
-      ++kv_iter;
+      if (r == 0) TPSA_TR(0, 22, t);
     }
   }
-  // Every TMA load this thread issued must land before the CTA exits.
-  if (item_iter > 0) drain_bar(sh.bar(kBarQFull), (item_iter - 1) & 1);
-  for (uint32_t s = 0; s < kStages; ++s) {
-    if (stage_arms[s] > 0) {
-      drain_bar(sh.bar(kBarKFull + s), (stage_arms[s] - 1) & 1);
+  if (!ok || *sh.abort_flag()) {
+    // Aborted: give in-flight TMA loads time to land before the CTA exits.
+    const uint64_t t0 = ptx::globaltimer_ns();
+    while (ptx::globaltimer_ns() - t0 < kAbortSettleNs) {
     }
-  }
-  // V stages: the last armed phase of each stage (kv_iter counts V arms).
-  for (uint32_t s = 0; s < kStages; ++s) {
-    const uint32_t arms = kv_iter / kStages + (s < kv_iter % kStages ? 1 : 0);
-    if (arms > 0) drain_bar(sh.bar(kBarVFull + s), (arms - 1) & 1);
   }
 }
 
 // ------------------------------------------------------------ MMA issuer
-__device__ void mma_role(const KernelArgs& a, const Shared& sh, uint32_t tmem,
-                         int lane) {
+// The whole warp runs this role: operands are computed by every lane (they
+// are warp-uniform) and one elected lane issues each tcgen05 instruction.
+__device__ void mma_role(const KernelArgs& a, const Shared& sh, uint32_t tmem, int lane) {
   const tpsa_plan& p = a.plan;
-  constexpr uint32_t kIdescQK128 = ptx::idesc_bf16_f32(128, 128, 0);
-  constexpr uint32_t kIdescQK64 = ptx::idesc_bf16_f32(128, 64, 0);
-  constexpr uint32_t kIdescPV = ptx::idesc_bf16_f32(128, 128, 1);
-  uint32_t kv_iter = 0, item_iter = 0;
-  uint32_t p_parity[2] = {0, 0};
+  uint32_t ring = 0, q_iter = 0, g = 0, p_count = 0, item_iter = 0;
   bool ok = true;
+  TPSA_TRACE_STATE;
 
-  auto issue_qk = [&](int m, uint32_t stage, int32_t w) {
-    const uint32_t d = tmem + m * 128;
-    const uint32_t idesc = w == 128 ? kIdescQK128 : kIdescQK64;
+  auto warp_wait = [&](uint32_t bar, uint32_t parity) -> bool {
+    return __all_sync(0xffffffffu, wait_bar(sh, bar, parity));
+  };
+  // S(gt) = Q K(gt)^T into S buffer gt % 2 (M = 256 over the pair, N = w).
+  auto issue_qk = [&](uint32_t qb, uint32_t kslot, uint32_t gt, int32_t w) {
+    const uint32_t d = tmem + (gt % 2) * 128;
+    const uint32_t idesc = ptx::idesc_bf16_f32(256, static_cast<uint32_t>(w), 0);
+    const uint64_t qd = ptx::smem_desc_sw128(sh.base_u32 + kOffQ + qb * kQBytes, 16, 1024);
+    const uint64_t kd =
+        ptx::smem_desc_sw128(sh.base_u32 + kOffKV + kslot * kRingSlotBytes, 16, 1024);
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-      const uint32_t qa = sh.base_u32 + kOffQ + (m * 2 + k / 4) * kHalfBytes + (k % 4) * 32;
-      const uint32_t kb = sh.base_u32 + kOffK + stage * kStageBytes + (k / 4) * kHalfBytes + (k % 4) * 32;
-      ptx::umma_ss(d, ptx::smem_desc_sw128(qa, 16, 1024),
-                   ptx::smem_desc_sw128(kb, 16, 1024), idesc, k > 0 ? 1u : 0u);
+      // Descriptor start addresses are in 16-byte units.
+      const uint64_t qo = (k / 4) * (kQHalfBytes >> 4) + (k % 4) * 2;
+      const uint64_t ko = (k / 4) * (kKHalfBytes >> 4) + (k % 4) * 2;
+      ptx::umma_ss_pair_elect(d, qd + qo, kd + ko, idesc, k > 0 ? 1u : 0u);
     }
   };
-  auto issue_pv = [&](int m, uint32_t stage, int32_t w, bool first) {
-    const uint32_t d = tmem + 256 + m * 128;
-    const uint32_t pa = tmem + m * 128;
-    for (int k = 0; k < w / 16; ++k) {
-      const uint32_t vb = sh.base_u32 + kOffV + stage * kStageBytes + k * 16 * 128;
-      ptx::umma_ts(d, pa + k * 8, ptx::smem_desc_sw128(vb, kHalfBytes, 1024),
-                   kIdescPV, (first && k == 0) ? 0u : 1u);
-    }
-  };
-  // Keys at or beyond seq_len in the last tile may be unwritten cache slots;
-  // their V rows are zeroed so that P = 0 never meets a NaN.  Every lane
-  // first observes the V-full barrier (already complete) so the TMA bytes
-  // are ordered before its stores.
-  auto zero_v_tail = [&](uint32_t stage, uint32_t parity, int32_t k0, int32_t w) -> bool {
-    const int32_t valid = p.seq_len - k0;
-    if (valid >= w) return true;
-    if (!wait_bar(sh, sh.bar(kBarVFull + stage), parity)) return false;
-    for (int32_t r = valid; r < w; ++r) {
-      for (int dh = 0; dh < 2; ++dh) {
-        uint4* row = reinterpret_cast<uint4*>(sh.base + kOffV + stage * kStageBytes +
-                                              dh * kHalfBytes + r * 128);
-        if (lane < 8) row[lane] = make_uint4(0, 0, 0, 0);
+  // O += P(gt) V(gt): P from S buffer gt % 2 (bf16 pairs), V d-half per CTA.
+  auto issue_pv = [&](uint32_t vslot, uint32_t gt, int32_t w, bool first) {
+    const uint32_t d = tmem + 256;
+    const uint32_t pa = tmem + (gt % 2) * 128;
+    constexpr uint32_t idesc = ptx::idesc_bf16_f32(256, 128, 1);
+    const uint64_t vd = ptx::smem_desc_sw128(sh.base_u32 + kOffKV + vslot * kRingSlotBytes,
+                                             kKHalfBytes, 1024);
+    if (w == kTileKeys) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        ptx::umma_ts_pair_elect(d, pa + k * 8, vd + k * (2048 >> 4), idesc,
+                                (first && k == 0) ? 0u : 1u);
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        ptx::umma_ts_pair_elect(d, pa + k * 8, vd + k * (2048 >> 4), idesc,
+                                (first && k == 0) ? 0u : 1u);
       }
     }
-    ptx::fence_proxy_async_smem();
-    return true;
   };
 
-  for (int32_t idx = blockIdx.x; ok && idx < p.total_items; idx += gridDim.x) {
+  for (uint32_t n_item = 0; ok; ++n_item) {
+    int32_t idx = 0;
+    const bool got = take_item(sh, n_item, &idx);
+    if (!__all_sync(0xffffffffu, got)) break;
+    __syncwarp();
+    if (lane == 0) release_item(sh, n_item);
+    if (idx >= p.total_items) break;
+    if (lane == 0) TPSA_TR(1, 10, idx);
     const tpsa_item it = decode_item(p, idx);
     const BlockTiles bt = block_tiles(p, it.block);
     const int32_t ntiles = it.tile_end - it.tile_begin;
-    bool w_ok = true;
-    if (lane == 0) w_ok = wait_bar(sh, sh.bar(kBarQFull), item_iter & 1);
-    if (!__shfl_sync(0xffffffffu, w_ok, 0)) { ok = false; break; }
+    const uint32_t qb = q_iter % 2;
+    if (!warp_wait(sh.bar(kBarQFull + qb), (q_iter / 2) & 1)) break;
+    ++q_iter;
     ptx::tc_fence_after();
+    // Ring positions of this item's tiles: K(t) at base + 2t, V(t) at base + 2t + 1.
+    const uint32_t rbase = ring;
+    ring += 2 * static_cast<uint32_t>(ntiles);
 
-    int32_t k0, w;
-    tile_keys(bt, it.tile_begin, &k0, &w);
-    {
-      const uint32_t s = kv_iter % kStages;
-      if (lane == 0) w_ok = wait_bar(sh, sh.bar(kBarKFull + s), (kv_iter / kStages) & 1);
-      if (!__shfl_sync(0xffffffffu, w_ok, 0)) { ok = false; break; }
+    // QK for the first two tiles.
+    for (int32_t t = 0; t < 2 && t < ntiles && ok; ++t) {
+      int32_t k0, w;
+      tile_keys(bt, it.tile_begin + t, &k0, &w);
+      const uint32_t kr = rbase + 2 * t;
+      if (!warp_wait(sh.bar(kBarKVFull + ring_slot(kr)), ring_parity(kr))) { ok = false; break; }
       ptx::tc_fence_after();
-      if (lane == 0) {
-        issue_qk(0, s, w);
-        ptx::umma_commit(sh.bar(kBarSFull + 0));
-        issue_qk(1, s, w);
-        ptx::umma_commit(sh.bar(kBarSFull + 1));
-        ptx::umma_commit(sh.bar(kBarKEmpty + s));
-        if (ntiles == 1) ptx::umma_commit(sh.bar(kBarQEmpty));
-      }
-      __syncwarp();
+      issue_qk(qb, ring_slot(kr), g + t, w);
+      ptx::umma_commit_pair_mc_elect(sh.bar(kBarSFull + (g + t) % 2), kPairMask);
+      ptx::umma_commit_pair_mc_elect(sh.bar(kBarKVEmpty + ring_slot(kr)), kPairMask);
+      if (t == ntiles - 1) ptx::umma_commit_pair_mc_elect(sh.bar(kBarQEmpty + qb), kPairMask);
     }
     for (int32_t n = 0; n < ntiles && ok; ++n) {
-      const uint32_t s = (kv_iter + n) % kStages;
-      const uint32_t ph = ((kv_iter + n) / kStages) & 1;
-      if (lane == 0) w_ok = wait_bar(sh, sh.bar(kBarVFull + s), ph);
-      if (!__shfl_sync(0xffffffffu, w_ok, 0)) { ok = false; break; }
-      ptx::tc_fence_after();
-      if (!__all_sync(0xffffffffu, zero_v_tail(s, ph, k0, w))) { ok = false; break; }
-      int32_t k0n = 0, wn = 0;
-      const bool has_next = n + 1 < ntiles;
-      if (has_next) tile_keys(bt, it.tile_begin + n + 1, &k0n, &wn);
-      const uint32_t sn = (kv_iter + n + 1) % kStages;
-      const uint32_t phn = ((kv_iter + n + 1) / kStages) & 1;
-      for (int m = 0; m < 2 && ok; ++m) {
-        if (lane == 0) {
-          if (n == 0 && item_iter > 0) {
-            w_ok = wait_bar(sh, sh.bar(kBarOEmpty + m), (item_iter - 1) & 1);
-          }
-          if (w_ok) w_ok = wait_bar(sh, sh.bar(kBarPFull + m), p_parity[m]);
-          p_parity[m] ^= 1;
-        }
-        if (!__shfl_sync(0xffffffffu, w_ok, 0)) { ok = false; break; }
-        ptx::tc_fence_after();
-        if (lane == 0) {
-          issue_pv(m, s, w, n == 0);
-          if (n + 1 == ntiles) ptx::umma_commit(sh.bar(kBarOFull + m));
-        }
-        if (has_next) {
-          if (m == 0 && lane == 0) w_ok = wait_bar(sh, sh.bar(kBarKFull + sn), phn);
-          if (!__shfl_sync(0xffffffffu, w_ok, 0)) { ok = false; break; }
-          ptx::tc_fence_after();
-          if (lane == 0) {
-            issue_qk(m, sn, wn);
-            ptx::umma_commit(sh.bar(kBarSFull + m));
-            if (m == 1) {
-              ptx::umma_commit(sh.bar(kBarKEmpty + sn));
-              if (n + 2 == ntiles) ptx::umma_commit(sh.bar(kBarQEmpty));
-            }
-          }
-        }
-        __syncwarp();
+      int32_t k0, w;
+      tile_keys(bt, it.tile_begin + n, &k0, &w);
+      const uint32_t vr = rbase + 2 * n + 1;
+      if (lane == 0) TPSA_TR(1, 12, n);
+      if (!warp_wait(sh.bar(kBarKVFull + ring_slot(vr)), ring_parity(vr))) { ok = false; break; }
+      if (lane == 0) TPSA_TR(1, 13, n);
+      if (n == 0 && item_iter > 0 && !warp_wait(sh.bar(kBarOEmpty), (item_iter - 1) & 1)) {
+        ok = false;
+        break;
       }
-      if (lane == 0 && ok) ptx::umma_commit(sh.bar(kBarVEmpty + s));
-      __syncwarp();
-      k0 = k0n;
-      w = wn;
+      if (!warp_wait(sh.bar(kBarPFull), p_count & 1)) { ok = false; break; }
+      ++p_count;
+      if (lane == 0) TPSA_TR(1, 14, n);
+      ptx::tc_fence_after();
+      issue_pv(ring_slot(vr), g + n, w, n == 0);
+      if (lane == 0) TPSA_TR(1, 15, n);
+      ptx::umma_commit_pair_mc_elect(sh.bar(kBarKVEmpty + ring_slot(vr)), kPairMask);
+      ptx::umma_commit_pair_mc_elect(sh.bar(kBarPvDone), kPairMask);
+      if (lane == 0) TPSA_TR(1, 16, n);
+      if (n + 2 < ntiles) {
+        int32_t k2, w2;
+        tile_keys(bt, it.tile_begin + n + 2, &k2, &w2);
+        const uint32_t kr = rbase + 2 * (n + 2);
+        if (!warp_wait(sh.bar(kBarKVFull + ring_slot(kr)), ring_parity(kr))) { ok = false; break; }
+        if (lane == 0) TPSA_TR(1, 17, n + 2);
+        ptx::tc_fence_after();
+        issue_qk(qb, ring_slot(kr), g + n + 2, w2);
+        if (lane == 0) TPSA_TR(1, 18, n + 2);
+        ptx::umma_commit_pair_mc_elect(sh.bar(kBarSFull + (g + n + 2) % 2), kPairMask);
+        ptx::umma_commit_pair_mc_elect(sh.bar(kBarKVEmpty + ring_slot(kr)), kPairMask);
+        if (n + 2 == ntiles - 1) {
+          ptx::umma_commit_pair_mc_elect(sh.bar(kBarQEmpty + qb), kPairMask);
+        }
+      }
     }
-    kv_iter += ntiles;
+    g += static_cast<uint32_t>(ntiles);
     ++item_iter;
   }
-  // All MMAs issued by this thread complete before TMEM is released.
-  if (lane == 0) {
-    ptx::umma_commit(sh.bar(kBarDrain));
-    drain_bar(sh.bar(kBarDrain), 0);
-  }
+  // All MMAs issued by this warp complete before TMEM is released.
+  ptx::umma_commit_pair_elect(sh.bar(kBarDrain));
+  if (lane == 0) drain_bar(sh.bar(kBarDrain), 0);
   __syncwarp();
 }
 
 // ------------------------------------------------------------ softmax
-struct RowCtx {
-  int32_t tok;     // absolute position of this row's query token
-  int32_t sparse;  // row reads sink + window instead of the dense prefix
-};
-
 template <int W>
 __device__ __forceinline__ void load_s(uint32_t taddr, float (&s)[W]) {
   uint32_t r[W];
@@ -391,9 +559,10 @@ __device__ __forceinline__ void load_s(uint32_t taddr, float (&s)[W]) {
   for (int c = 0; c < W; ++c) s[c] = __uint_as_float(r[c]);
 }
 
-__device__ __forceinline__ void rescale_o(uint32_t o_addr, float factor) {
+// Multiplies this warpgroup's 64 O columns of the row by `factor`.
+__device__ __forceinline__ void rescale_o_half(uint32_t o_addr, float factor) {
 #pragma unroll 1
-  for (int c = 0; c < 4; ++c) {
+  for (int c = 0; c < 2; ++c) {
     uint32_t r[32];
     ptx::tmem_ld32(o_addr + 32 * c, r);
     ptx::tmem_wait_ld();
@@ -404,179 +573,331 @@ __device__ __forceinline__ void rescale_o(uint32_t o_addr, float factor) {
   ptx::tmem_wait_st();
 }
 
-// One key tile of one M tile: mask, online-softmax update, P -> TMEM.
-template <int W>
-__device__ __forceinline__ void softmax_tile(const tpsa_plan& p, uint32_t s_addr,
-                                             uint32_t o_addr, const RowCtx& rc,
-                                             int32_t k0, bool masked, bool first,
-                                             float& m_run, float& l_run,
-                                             uint32_t* visit_row,
-                                             int32_t words_per_row) {
-  float s[W];
-  load_s<W>(s_addr, s);
-  if (masked) {
-    const int32_t q = rc.tok < p.seq_len ? rc.tok : p.seq_len - 1;
-    const int32_t hi = q - k0 + 1;
-    const int32_t lo = rc.sparse ? q - kLocalWindow - k0 : -(1 << 30);
-    const int32_t sk = kSinkTokens - k0;
+// Masks columns of this warpgroup's part of a tile; column c holds key
+// k0c + c.
+template <int W, int MODE>
+__device__ __forceinline__ void apply_mask(float (&s)[W], int32_t q, bool sparse, int32_t k0c) {
+  const int32_t hi = q - k0c + 1;             // keep c < hi
+  const int32_t lo = q - kLocalWindow - k0c;  // keep c >= lo (sparse rows)
+  const int32_t sk = kSinkTokens - k0c;       // keep c < sk (sink keys)
+  if constexpr (MODE == kMaskCausal) {
+#pragma unroll
+    for (int c = 0; c < W; ++c) s[c] = c < hi ? s[c] : -INFINITY;
+  } else if constexpr (MODE == kMaskWindow) {
+#pragma unroll
+    for (int c = 0; c < W; ++c) s[c] = c >= lo ? s[c] : -INFINITY;
+  } else if constexpr (MODE == kMaskBand) {
+#pragma unroll
+    for (int c = 0; c < W; ++c) s[c] = (c >= lo && c < hi) ? s[c] : -INFINITY;
+  } else if constexpr (MODE == kMaskSink) {
+#pragma unroll
+    for (int c = 0; c < W; ++c) s[c] = c < sk ? s[c] : -INFINITY;
+  } else if constexpr (MODE == kMaskGeneral) {
+    const int32_t lo_g = sparse ? lo : -(1 << 30);
 #pragma unroll
     for (int c = 0; c < W; ++c) {
-      const bool v = (c < hi) && (c >= lo || c < sk);
+      const bool v = (c < hi) && (c >= lo_g || c < sk);
       s[c] = v ? s[c] : -INFINITY;
     }
   }
+}
+
+// Per-thread softmax state.  Both warpgroups of a row hold the same m_run;
+// each holds the partial row sum of its own columns.
+struct RowState {
+  float m_run;
+  float l_run;
+};
+
+// Exchanges one float per row between the two softmax warpgroups (the value
+// of warpgroup wg is published, the other one returned).  `xc` counts
+// exchanges; both warpgroups run the same sequence.
+__device__ __forceinline__ bool exchange(const Shared& sh, uint32_t& xc, int wg, int row,
+                                         int lane, float mine, float* other) {
+  volatile float* buf = reinterpret_cast<volatile float*>(sh.base + kOffXchg) + (xc & 1) * 256;
+  buf[wg * 128 + row] = mine;
+  __syncwarp();
+  if (lane == 0) ptx::mbar_arrive(sh.bar(kBarWgX));
+  const bool ok = wait_bar(sh, sh.bar(kBarWgX), xc & 1);
+  ++xc;
+  if (!__all_sync(0xffffffffu, ok)) return false;
+  *other = buf[(1 - wg) * 128 + row];
+  return true;
+}
+
+struct SoftmaxCtx {
+  const tpsa_plan* p;
+  const Shared* sh;
+  uint32_t s_addr;  // this warpgroup's first S column of the tile's buffer
+  uint32_t p_addr;  // this warpgroup's first P column (bf16 pairs)
+  uint32_t o_addr;  // this warpgroup's first O column
+  int wg, row, lane;
+  int32_t q;
+  bool sparse;
+};
+
+// One key tile, this warpgroup's W columns (W = w / 2): mask, joint row
+// max, online-softmax update, P -> TMEM.  `pv_needed`: PV completions to
+// observe before O may be rescaled (every PV issued before this tile).
+template <int W, int MODE>
+__device__ __forceinline__ bool softmax_tile(const SoftmaxCtx& cx, int32_t k0c, bool first,
+                                             uint32_t pv_needed, uint32_t& pv_seen,
+                                             uint32_t& xc, RowState& st, uint32_t* visit_row,
+                                             int32_t words_per_row, uint32_t trole,
+                                             uint32_t& trn) {
+  const tpsa_plan& p = *cx.p;
+  float s[W];
+  load_s<W>(cx.s_addr, s);
+  apply_mask<W, MODE>(s, cx.q, cx.sparse, k0c);
+  TPSA_SM_TR(2);
   if (visit_row != nullptr) {
 #pragma unroll
     for (int j = 0; j < W / 32; ++j) {
       uint32_t bits = 0;
 #pragma unroll
       for (int c = 0; c < 32; ++c) bits |= (s[32 * j + c] != -INFINITY ? 1u : 0u) << c;
-      const int32_t word = k0 / 32 + j;
+      const int32_t word = k0c / 32 + j;
       if (bits != 0 && word < words_per_row) atomicOr(visit_row + word, bits);
     }
   }
-  float mx = -INFINITY;
+  // Partial row max over this warpgroup's columns, then the joint max.
+  float mx0 = s[0], mx1 = s[2], mx2 = s[4], mx3 = s[6];
 #pragma unroll
-  for (int c = 0; c < W; ++c) mx = fmaxf(mx, s[c]);
-  const float m_new = fmaxf(m_run, mx);
-  const bool need = (m_new - m_run) * p.scale_log2 > kRescaleLog2;
+  for (int c = 0; c < W; c += 8) {
+    mx0 = max3(mx0, s[c], s[c + 1]);
+    mx1 = max3(mx1, s[c + 2], s[c + 3]);
+    mx2 = max3(mx2, s[c + 4], s[c + 5]);
+    mx3 = max3(mx3, s[c + 6], s[c + 7]);
+  }
+  float mx = fmaxf(max3(mx0, mx1, mx2), mx3);
+  // S of both halves is in registers before either warpgroup writes P over
+  // the other's S columns (the exchange orders the two).
+  ptx::tc_fence_before();
+  float mx_other;
+  if (!exchange(*cx.sh, xc, cx.wg, cx.row, cx.lane, mx, &mx_other)) return false;
+  ptx::tc_fence_after();
+  mx = fmaxf(mx, mx_other);
+  const float m_new = fmaxf(st.m_run, mx);
+  const bool need = (m_new - st.m_run) * p.scale_log2 > kRescaleLog2;
   if (__any_sync(0xffffffffu, need)) {
-    const float factor = need ? fast_exp2((m_run - m_new) * p.scale_log2) : 1.0f;
-    if (!first) rescale_o(o_addr, factor);
-    l_run *= factor;
-    if (need) m_run = m_new;
+    const float factor = need ? mufu_exp2((st.m_run - m_new) * p.scale_log2) : 1.0f;
+    if (!first) {
+      // O holds PVs of earlier tiles: they must have completed.
+      while (pv_seen < pv_needed) {
+        const bool ok = wait_bar(*cx.sh, cx.sh->bar(kBarPvDone), pv_seen & 1);
+        if (!__all_sync(0xffffffffu, ok)) return false;
+        ++pv_seen;
+      }
+      ptx::tc_fence_after();
+      rescale_o_half(cx.o_addr, factor);
+    }
+    st.l_run *= factor;
+    if (need) st.m_run = m_new;
   }
-  const float mb = m_run == -INFINITY ? 0.0f : m_run * p.scale_log2;
-  float sum = 0.0f;
-  uint32_t pk[W / 2];
+  const float neg_mb = st.m_run == -INFINITY ? 0.0f : -st.m_run * p.scale_log2;
+  TPSA_SM_TR(6);
+  float sum0 = 0.0f, sum1 = 0.0f;
 #pragma unroll
-  for (int c = 0; c < W / 2; ++c) {
-    const float e0 = fast_exp2(fmaf(s[2 * c], p.scale_log2, -mb));
-    const float e1 = fast_exp2(fmaf(s[2 * c + 1], p.scale_log2, -mb));
-    sum += e0 + e1;
-    pk[c] = pack_bf16x2(e0, e1);
-  }
-  l_run += sum;
+  for (int j = 0; j < W / 32; ++j) {
+    uint32_t pk[16];
 #pragma unroll
-  for (int j = 0; j < W / 64; ++j) {
-    ptx::tmem_st32(s_addr + 32 * j, *reinterpret_cast<uint32_t(*)[32]>(&pk[32 * j]));
+    for (int c = 0; c < 16; ++c) {
+      float x0, x1;
+      fma2(s[32 * j + 2 * c], s[32 * j + 2 * c + 1], p.scale_log2, neg_mb, x0, x1);
+      float e0, e1;
+      if ((c & 3) == 3) {
+        e0 = poly_exp2(x0);
+        e1 = poly_exp2(x1);
+      } else {
+        e0 = mufu_exp2(x0);
+        e1 = mufu_exp2(x1);
+      }
+      add2(sum0, sum1, e0, e1);
+      pk[c] = pack_bf16x2(e0, e1);
+    }
+    ptx::tmem_st16(cx.p_addr + 16 * j, pk);
   }
+  st.l_run += sum0 + sum1;
   ptx::tmem_wait_st();
+  TPSA_SM_TR(7);
+  return true;
 }
 
-__device__ __forceinline__ void store_row_bf16(__nv_bfloat16* dst, const float* v,
-                                               float scale) {
+// Normalises 64 O values and stores them as bf16 (128 bytes).
+__device__ __forceinline__ void store_half_bf16(__nv_bfloat16* dst, const uint32_t* v,
+                                                float scale) {
   uint4* d = reinterpret_cast<uint4*>(dst);
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
+  for (int j = 0; j < 8; ++j) {
     uint4 u;
-    u.x = pack_bf16x2(v[8 * j + 0] * scale, v[8 * j + 1] * scale);
-    u.y = pack_bf16x2(v[8 * j + 2] * scale, v[8 * j + 3] * scale);
-    u.z = pack_bf16x2(v[8 * j + 4] * scale, v[8 * j + 5] * scale);
-    u.w = pack_bf16x2(v[8 * j + 6] * scale, v[8 * j + 7] * scale);
+    u.x = pack_bf16x2(__uint_as_float(v[8 * j + 0]) * scale, __uint_as_float(v[8 * j + 1]) * scale);
+    u.y = pack_bf16x2(__uint_as_float(v[8 * j + 2]) * scale, __uint_as_float(v[8 * j + 3]) * scale);
+    u.z = pack_bf16x2(__uint_as_float(v[8 * j + 4]) * scale, __uint_as_float(v[8 * j + 5]) * scale);
+    u.w = pack_bf16x2(__uint_as_float(v[8 * j + 6]) * scale, __uint_as_float(v[8 * j + 7]) * scale);
     d[j] = u;
   }
 }
 
-__device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tmem,
-                             int m) {
+// One arrival per softmax warp on a CTA-0 barrier.
+__device__ __forceinline__ void warp_arrive0(const Shared& sh, uint32_t id, int lane) {
+  __syncwarp();
+  if (lane == 0) ptx::mbar_arrive_cluster(sh.bar0(id));
+}
+
+__device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tmem) {
   const tpsa_plan& p = a.plan;
+  const uint32_t r = sh.rank;
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
+  const int wg = (warp - 4) / 4;     // which half of the columns
   const int quad = warp % 4;
-  const int row = quad * 32 + lane;  // TMEM lane == row of the M tile
+  const int row = quad * 32 + lane;  // TMEM lane == row of this CTA's M half
   const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
-  const uint32_t s_addr = tmem + lane_base + m * 128;
-  const uint32_t o_addr = tmem + lane_base + 256 + m * 128;
   const int32_t hq = p.kv_heads * kGroupSize;
   const bool visit = a.visited != nullptr;
-  uint32_t s_parity = 0, o_parity = 0, split_iter = 0;
+  uint32_t g = 0, pv_seen = 0, split_iter = 0, xc = 0;
   volatile int* split_last = reinterpret_cast<volatile int*>(sh.base + kOffSplitLast);
+  uint32_t tr_sm = 0;  // trace counter (used only with TPSA_TRACE)
+#define tr_n_ tr_sm
+  SoftmaxCtx cx;
+  cx.p = &p;
+  cx.sh = &sh;
+  cx.wg = wg;
+  cx.row = row;
+  cx.lane = lane;
+  cx.o_addr = tmem + lane_base + 256 + wg * 64;
 
-  for (int32_t idx = blockIdx.x; idx < p.total_items; idx += gridDim.x) {
+  for (uint32_t n_item = 0;; ++n_item) {
+    int32_t idx = 0;
+    const bool got = take_item(sh, n_item, &idx);
+    if (!__all_sync(0xffffffffu, got)) break;
+    __syncwarp();
+    if (lane == 0) release_item(sh, n_item);
+    if (idx >= p.total_items) break;
     const tpsa_item it = decode_item(p, idx);
     const BlockTiles bt = block_tiles(p, it.block);
-    RowCtx rc;
-    rc.tok = bt.q_begin + row / 2;
-    rc.sparse = row_is_sparse(p, rc.tok) ? 1 : 0;
+    const int32_t tok = bt.q_begin + row / 2;
+    cx.q = tok < p.seq_len ? tok : p.seq_len - 1;
+    cx.sparse = row_is_sparse(p, tok);
     const int32_t qrow = it.block * kBlockQ + row / 2;  // row within the chunk
-    const int32_t head = it.kv_head * kGroupSize + m * 2 + (row & 1);
+    const int32_t head = it.kv_head * kGroupSize + 2 * static_cast<int32_t>(r) + (row & 1);
     const bool real_row = qrow < p.query_tokens;
     uint32_t* visit_row =
         (visit && real_row)
             ? a.visited + (static_cast<size_t>(qrow) * hq + head) * a.words_per_row
             : nullptr;
-    float m_run = -INFINITY, l_run = 0.0f;
+    RowState st{-INFINITY, 0.0f};
     bool ok = true;
-    for (int32_t t = it.tile_begin; t < it.tile_end; ++t) {
+    const int32_t ntiles = it.tile_end - it.tile_begin;
+    for (int32_t n = 0; n < ntiles; ++n) {
+      const uint32_t gt = g + static_cast<uint32_t>(n);
       int32_t k0, w;
-      tile_keys(bt, t, &k0, &w);
-      const bool masked = tile_needs_mask(p, bt, k0, w);
-      bool w_ok = wait_bar(sh, sh.bar(kBarSFull + m), s_parity);
-      s_parity ^= 1;
+      tile_keys(bt, it.tile_begin + n, &k0, &w);
+      const int32_t mode = tile_mask_mode(p, bt, k0, w);
+      const bool w_ok = wait_bar(sh, sh.bar(kBarSFull + gt % 2), (gt / 2) & 1);
       if (!__all_sync(0xffffffffu, w_ok)) { ok = false; break; }
+      if (row == 0 && wg == 0) TPSA_TR(2 + r, 1, n);
       ptx::tc_fence_after();
+      const uint32_t sbuf = tmem + lane_base + (gt % 2) * 128;
+      const int32_t half = w / 2;
+      cx.s_addr = sbuf + wg * half;
+      cx.p_addr = sbuf + wg * (half / 2);
+      const int32_t k0c = k0 + wg * half;
+      const bool first = n == 0;
+      bool t_ok = true;
+#define TPSA_TILE(WW, MM)                                                                   \
+  t_ok = softmax_tile<WW, MM>(cx, k0c, first, gt, pv_seen, xc, st, visit_row, a.words_per_row, \
+                              2 + r, tr_sm)
       if (w == 128) {
-        softmax_tile<128>(p, s_addr, o_addr, rc, k0, masked, t == it.tile_begin,
-                          m_run, l_run, visit_row, a.words_per_row);
+        switch (mode) {
+          case kMaskNone: TPSA_TILE(64, kMaskNone); break;
+          case kMaskCausal: TPSA_TILE(64, kMaskCausal); break;
+          case kMaskWindow: TPSA_TILE(64, kMaskWindow); break;
+          case kMaskBand: TPSA_TILE(64, kMaskBand); break;
+          default: TPSA_TILE(64, kMaskGeneral); break;
+        }
       } else {
-        softmax_tile<64>(p, s_addr, o_addr, rc, k0, masked, t == it.tile_begin,
-                         m_run, l_run, visit_row, a.words_per_row);
+        switch (mode) {
+          case kMaskNone: TPSA_TILE(32, kMaskNone); break;
+          case kMaskCausal: TPSA_TILE(32, kMaskCausal); break;
+          case kMaskWindow: TPSA_TILE(32, kMaskWindow); break;
+          case kMaskBand: TPSA_TILE(32, kMaskBand); break;
+          case kMaskSink: TPSA_TILE(32, kMaskSink); break;
+          default: TPSA_TILE(32, kMaskGeneral); break;
+        }
       }
+#undef TPSA_TILE
+      if (!t_ok) { ok = false; break; }
+      // Keep the pv_done barrier at most one phase ahead: observe PV(gt - 1),
+      // issued one tile earlier and normally complete by now.
+      while (pv_seen < gt) {
+        const bool pv_ok = wait_bar(sh, sh.bar(kBarPvDone), pv_seen & 1);
+        if (!__all_sync(0xffffffffu, pv_ok)) { ok = false; break; }
+        ++pv_seen;
+      }
+      if (!ok) break;
       ptx::tc_fence_before();
-      ptx::mbar_arrive(sh.bar(kBarPFull + m));
+      if (row == 0 && wg == 0) TPSA_TR(2 + r, 3, n);
+      warp_arrive0(sh, kBarPFull, lane);
     }
     if (!ok) break;
-    bool w_ok = wait_bar(sh, sh.bar(kBarOFull + m), o_parity);
-    o_parity ^= 1;
-    if (!__all_sync(0xffffffffu, w_ok)) break;
+    g += static_cast<uint32_t>(ntiles);
+    // O is final once the item's last PV completed.
+    while (pv_seen < g) {
+      const bool pv_ok = wait_bar(sh, sh.bar(kBarPvDone), pv_seen & 1);
+      if (!__all_sync(0xffffffffu, pv_ok)) { ok = false; break; }
+      ++pv_seen;
+    }
+    if (!ok) break;
     ptx::tc_fence_after();
+    // O leaves tensor memory first, so the next item's PV can start while
+    // this row is normalised and stored.
+    uint32_t o[64];
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      ptx::tmem_ld32(cx.o_addr + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&o[32 * c]));
+    }
+    ptx::tmem_wait_ld();
+    ptx::tc_fence_before();
+    warp_arrive0(sh, kBarOEmpty, lane);
+    float l_other;
+    if (!exchange(sh, xc, wg, row, lane, st.l_run, &l_other)) break;
+    const float l_total = st.l_run + l_other;
+    if (row == 0 && wg == 0) TPSA_TR(2 + r, 5, 0);
 
+    __nv_bfloat16* dst_row = a.out + (static_cast<size_t>(qrow) * hq + head) * kHeadDim;
     if (it.num_splits == 1) {
-      const float inv = 1.0f / l_run;
-      __nv_bfloat16* dst = a.out + (static_cast<size_t>(qrow) * hq + head) * kHeadDim;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        ptx::tmem_ld32(o_addr + 32 * c, r);
-        ptx::tmem_wait_ld();
-        if (real_row) store_row_bf16(dst + 32 * c, reinterpret_cast<const float*>(r), inv);
-      }
-      ptx::tc_fence_before();
-      ptx::mbar_arrive(sh.bar(kBarOEmpty + m));
+      if (real_row) store_half_bf16(dst_row + wg * 64, o, 1.0f / l_total);
       continue;
     }
 
     // Split item: publish (O, m, l) of this row, then the last split of the
-    // block merges all partials (log-sum-exp combine) and writes bf16.
+    // block (per CTA of the pair) merges all partials and writes bf16.
     float* slot = a.scratch + static_cast<size_t>(idx) * kSlotFloats;
-    const int32_t srow = m * kRowsPerTile + row;
-#pragma unroll 1
-    for (int c = 0; c < 4; ++c) {
-      uint32_t r[32];
-      ptx::tmem_ld32(o_addr + 32 * c, r);
-      ptx::tmem_wait_ld();
-      float4* d = reinterpret_cast<float4*>(slot + static_cast<size_t>(srow) * kHeadDim + 32 * c);
+    const int32_t srow = static_cast<int32_t>(r) * kRowsPerTile + row;
+    {
+      float4* d =
+          reinterpret_cast<float4*>(slot + static_cast<size_t>(srow) * kHeadDim + wg * 64);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        d[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                           __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+      for (int j = 0; j < 16; ++j) {
+        d[j] = make_float4(__uint_as_float(o[4 * j]), __uint_as_float(o[4 * j + 1]),
+                           __uint_as_float(o[4 * j + 2]), __uint_as_float(o[4 * j + 3]));
       }
     }
-    ptx::tc_fence_before();
-    ptx::mbar_arrive(sh.bar(kBarOEmpty + m));
-    slot[2 * kRowsPerTile * kHeadDim + srow] = m_run;
-    slot[2 * kRowsPerTile * (kHeadDim + 1) + srow] = l_run;
+    if (wg == 0) {
+      slot[2 * kRowsPerTile * kHeadDim + srow] = st.m_run;
+      slot[2 * kRowsPerTile * (kHeadDim + 1) + srow] = l_total;
+    }
     __threadfence();
-    ptx::mbar_arrive(sh.bar(kBarSplitWritten));
-    w_ok = wait_bar(sh, sh.bar(kBarSplitWritten), split_iter & 1);
+    __syncwarp();
+    if (lane == 0) ptx::mbar_arrive(sh.bar(kBarSplitWritten));
+    bool w_ok = wait_bar(sh, sh.bar(kBarSplitWritten), split_iter & 1);
     if (!__all_sync(0xffffffffu, w_ok)) break;
-    const int32_t ctr = (it.block - p.tail_block0) * p.kv_heads + it.kv_head;
-    if (m == 0 && row == 0) {
-      const int prev = atomicAdd(a.split_ctr + ctr, 1);
-      const int last = prev == it.num_splits - 1;
-      if (last) a.split_ctr[ctr] = 0;  // leave the counter clean
-      *split_last = last;
+    if (row == 0 && wg == 0) {
+      int32_t* ctr = a.ctl + kCtlSplitBase +
+                     ((it.block - p.tail_block0) * p.kv_heads + it.kv_head) * 2 + r;
+      const int prev = atomicAdd(ctr, 1);
+      *split_last = prev == it.num_splits - 1;
       ptx::mbar_arrive(sh.bar(kBarSplitDecided));
     }
     w_ok = wait_bar(sh, sh.bar(kBarSplitDecided), split_iter & 1);
@@ -585,33 +906,31 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
     if (!*split_last || !real_row) continue;
     __threadfence();
     const float* first_slot = a.scratch + static_cast<size_t>(idx - it.split) * kSlotFloats;
+    const size_t m_off = 2 * kRowsPerTile * kHeadDim + srow;
+    const size_t l_off = 2 * kRowsPerTile * (kHeadDim + 1) + srow;
     float mmax = -INFINITY;
     for (int32_t sp = 0; sp < it.num_splits; ++sp) {
-      const float* sl = first_slot + static_cast<size_t>(sp) * kSlotFloats;
-      mmax = fmaxf(mmax, __ldcg(sl + 2 * kRowsPerTile * kHeadDim + srow));
+      mmax = fmaxf(mmax, __ldcg(first_slot + sp * kSlotFloats + m_off));
     }
-    float wts[64];  // num_splits <= 64 enforced by the planner
     float lsum = 0.0f;
     for (int32_t sp = 0; sp < it.num_splits; ++sp) {
-      const float* sl = first_slot + static_cast<size_t>(sp) * kSlotFloats;
-      const float ms = __ldcg(sl + 2 * kRowsPerTile * kHeadDim + srow);
-      const float ls = __ldcg(sl + 2 * kRowsPerTile * (kHeadDim + 1) + srow);
-      const float wgt = ms == -INFINITY ? 0.0f : fast_exp2((ms - mmax) * p.scale_log2);
-      wts[sp & 63] = wgt;
-      lsum += wgt * ls;
+      const float* sl = first_slot + sp * kSlotFloats;
+      const float ms = __ldcg(sl + m_off);
+      if (ms != -INFINITY) lsum += mufu_exp2((ms - mmax) * p.scale_log2) * __ldcg(sl + l_off);
     }
     const float inv = 1.0f / lsum;
-    __nv_bfloat16* dst = a.out + (static_cast<size_t>(qrow) * hq + head) * kHeadDim;
 #pragma unroll 1
-    for (int c = 0; c < 4; ++c) {
+    for (int c = 0; c < 2; ++c) {
+      const int col = wg * 64 + 32 * c;
       float acc[32];
 #pragma unroll
       for (int j = 0; j < 32; ++j) acc[j] = 0.0f;
       for (int32_t sp = 0; sp < it.num_splits; ++sp) {
-        const float wgt = wts[sp & 63];
-        const float4* src = reinterpret_cast<const float4*>(
-            first_slot + static_cast<size_t>(sp) * kSlotFloats +
-            static_cast<size_t>(srow) * kHeadDim + 32 * c);
+        const float* sl = first_slot + sp * kSlotFloats;
+        const float ms = __ldcg(sl + m_off);
+        const float wgt = ms == -INFINITY ? 0.0f : mufu_exp2((ms - mmax) * p.scale_log2);
+        const float4* src =
+            reinterpret_cast<const float4*>(sl + static_cast<size_t>(srow) * kHeadDim + col);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const float4 v = __ldcg(src + j);
@@ -621,16 +940,25 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
           acc[4 * j + 3] += wgt * v.w;
         }
       }
-      store_row_bf16(dst + 32 * c, acc, inv);
+      uint4* d = reinterpret_cast<uint4*>(dst_row + col);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        d[j] = make_uint4(pack_bf16x2(acc[8 * j] * inv, acc[8 * j + 1] * inv),
+                          pack_bf16x2(acc[8 * j + 2] * inv, acc[8 * j + 3] * inv),
+                          pack_bf16x2(acc[8 * j + 4] * inv, acc[8 * j + 5] * inv),
+                          pack_bf16x2(acc[8 * j + 6] * inv, acc[8 * j + 7] * inv));
+      }
     }
   }
 }
+#undef tr_n_
 
 template <bool kVisit>
-__global__ void __launch_bounds__(kNumThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kNumThreads, 1)
     tpsa_paged_kernel(const __grid_constant__ KernelArgs args,
                       const __grid_constant__ CUtensorMap tmap_q,
-                      const __grid_constant__ CUtensorMap tmap_k,
+                      const __grid_constant__ CUtensorMap tmap_k64,
+                      const __grid_constant__ CUtensorMap tmap_k32,
                       const __grid_constant__ CUtensorMap tmap_v) {
   extern __shared__ uint8_t smem_raw[];
   Shared sh;
@@ -639,54 +967,57 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     const uint32_t aligned = (raw + 1023u) & ~1023u;
     sh.base = smem_raw + (aligned - raw);
     sh.base_u32 = aligned;
+    sh.rank = ptx::cluster_ctarank();
   }
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
 
   if (threadIdx.x == 0) {
-    ptx::mbar_init(sh.bar(kBarQFull), 1);
-    ptx::mbar_init(sh.bar(kBarQEmpty), 1);
-    for (int s = 0; s < kStages; ++s) {
-      ptx::mbar_init(sh.bar(kBarKFull + s), 1);
-      ptx::mbar_init(sh.bar(kBarKEmpty + s), 1);
-      ptx::mbar_init(sh.bar(kBarVFull + s), 1);
-      ptx::mbar_init(sh.bar(kBarVEmpty + s), 1);
+    for (int i = 0; i < 2; ++i) {
+      ptx::mbar_init(sh.bar(kBarQFull + i), 2);
+      ptx::mbar_init(sh.bar(kBarQEmpty + i), 1);
+      ptx::mbar_init(sh.bar(kBarSFull + i), 1);
+      ptx::mbar_init(sh.bar(kBarItemFull + i), 1);
+      ptx::mbar_init(sh.bar(kBarItemEmpty + i), kItemConsumers);
     }
-    for (int m = 0; m < 2; ++m) {
-      ptx::mbar_init(sh.bar(kBarSFull + m), 1);
-      ptx::mbar_init(sh.bar(kBarPFull + m), 128);
-      ptx::mbar_init(sh.bar(kBarOFull + m), 1);
-      ptx::mbar_init(sh.bar(kBarOEmpty + m), 128);
+    for (int s = 0; s < kRing; ++s) {
+      ptx::mbar_init(sh.bar(kBarKVFull + s), 2);
+      ptx::mbar_init(sh.bar(kBarKVEmpty + s), 1);
     }
-    ptx::mbar_init(sh.bar(kBarSplitWritten), 256);
+    ptx::mbar_init(sh.bar(kBarPFull), kPairWarpArrivals);
+    ptx::mbar_init(sh.bar(kBarPvDone), 1);
+    ptx::mbar_init(sh.bar(kBarOEmpty), kPairWarpArrivals);
+    ptx::mbar_init(sh.bar(kBarSplitWritten), kSoftmaxWarps);
     ptx::mbar_init(sh.bar(kBarSplitDecided), 1);
+    ptx::mbar_init(sh.bar(kBarTail), 1);
     ptx::mbar_init(sh.bar(kBarDrain), 1);
+    ptx::mbar_init(sh.bar(kBarWgX), kSoftmaxWarps);
     *sh.abort_flag() = 0;
     ptx::fence_mbar_init();
   }
   if (warp == 1) {
-    ptx::tmem_alloc(sh.base_u32 + kOffTmemSlot, kTmemCols);
-    ptx::tmem_relinquish();
+    ptx::tmem_alloc_pair(sh.base_u32 + kOffTmemSlot, kTmemCols);
+    ptx::tmem_relinquish_pair();
   }
   ptx::tc_fence_before();
-  __syncthreads();
+  ptx::cluster_sync();  // barriers of both CTAs initialised before any remote use
   ptx::tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sh.base + kOffTmemSlot);
 
   if (warp == 0) {
-    if (lane == 0) producer_role(args, sh, &tmap_q, &tmap_k, &tmap_v);
+    if (lane == 0) producer_role(args, sh, &tmap_q, &tmap_k64, &tmap_k32, &tmap_v);
     __syncwarp();
   } else if (warp == 1) {
-    mma_role(args, sh, tmem, lane);
-  } else {
-    softmax_role(args, sh, tmem, warp < 6 ? 0 : 1);
+    if (sh.rank == 0) mma_role(args, sh, tmem, lane);
+  } else if (warp >= 4) {
+    softmax_role(args, sh, tmem);
   }
 
   ptx::tc_fence_before();
-  __syncthreads();
+  ptx::cluster_sync();  // no remote traffic after this point; MMAs drained
   if (warp == 1) {
     ptx::tc_fence_after();
-    ptx::tmem_dealloc(tmem, kTmemCols);
+    ptx::tmem_dealloc_pair(tmem, kTmemCols);
   }
 }
 
@@ -707,6 +1038,7 @@ struct DeviceState {
   int sm_count = 0;
   int major = 0;
   bool attr_set = false;
+  int max_pairs = 0;  // co-resident CTA pairs (clusters of 2)
 };
 
 std::mutex g_mutex;
@@ -737,6 +1069,15 @@ tpsa_status device_state(DeviceState** out) {
     e = cudaFuncSetAttribute(tpsa_paged_kernel<true>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (st.sm_count / 2), 1, 1);
+    cfg.blockDim = dim3(kNumThreads, 1, 1);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    int clusters = 0;
+    e = cudaOccupancyMaxActiveClusters(&clusters, tpsa_paged_kernel<false>, &cfg);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveClusters");
+    if (clusters <= 0) return fail(TPSA_ERR_CUDA, "no CTA pair fits on this device");
+    st.max_pairs = clusters;
     st.attr_set = true;
   }
   *out = &st;
@@ -790,8 +1131,10 @@ tpsa_status encode_map(CUtensorMap* map, const void* base, uint64_t d1, uint64_t
   return TPSA_OK;
 }
 
+// `pairs`: CTA pairs (2-SM clusters) the launch runs; each pair runs one item
+// at a time.
 tpsa_status build_plan(int64_t query_tokens, int64_t query_start, int64_t seq_len,
-                       int64_t prompt_len, int32_t kv_heads, int32_t sm_count,
+                       int64_t prompt_len, int32_t kv_heads, int32_t pairs,
                        float scale, tpsa_plan* p) {
   if (p == nullptr) return fail(TPSA_ERR_INVALID_ARGUMENT, "plan pointer is NULL");
   if (!(kv_heads == 1 || kv_heads == 2 || kv_heads == 4 || kv_heads == 8)) {
@@ -812,7 +1155,7 @@ tpsa_status build_plan(int64_t query_tokens, int64_t query_start, int64_t seq_le
   if (prompt_len > static_cast<int64_t>(UINT32_MAX)) {
     return fail(TPSA_ERR_INVALID_ARGUMENT, "prompt lengths above UINT32_MAX are unsupported");
   }
-  if (sm_count <= 0) return fail(TPSA_ERR_INVALID_ARGUMENT, "sm_count must be positive");
+  if (pairs <= 0) return fail(TPSA_ERR_INVALID_ARGUMENT, "sm_count must be positive");
   std::memset(p, 0, sizeof(*p));
   p->query_tokens = static_cast<int32_t>(query_tokens);
   p->query_start = static_cast<int32_t>(query_start);
@@ -830,7 +1173,7 @@ tpsa_status build_plan(int64_t query_tokens, int64_t query_start, int64_t seq_le
   int64_t tiles = 0;
   for (int32_t b = 0; b < p->num_blocks; ++b) tiles += block_tiles(*p, b).count;
   tiles *= kv_heads;
-  const double target = static_cast<double>(tiles) / sm_count;
+  const double target = static_cast<double>(tiles) / pairs;
   int32_t split = static_cast<int32_t>(0.7 * target);
   if (split < kMinSplitTiles) split = kMinSplitTiles;
   // The in-kernel merge keeps per-split weights for at most 64 splits.
@@ -838,7 +1181,7 @@ tpsa_status build_plan(int64_t query_tokens, int64_t query_start, int64_t seq_le
     const int32_t c = block_tiles(*p, b).count;
     if (ceil_div(c, split) > 64) split = ceil_div(c, 64);
   }
-  if ((p->num_blocks - b0) * kv_heads > kMaxSplitCounters) split = 1 << 30;
+  if ((p->num_blocks - b0) * kv_heads * 2 > kMaxSplitCounters) split = 1 << 30;
   p->split_tiles = split;
   int64_t tail_items = 0;
   bool any_split = false;
@@ -849,9 +1192,9 @@ tpsa_status build_plan(int64_t query_tokens, int64_t query_start, int64_t seq_le
   }
   p->tail_items = static_cast<int32_t>(tail_items);
   p->total_items = static_cast<int32_t>(tail_items + static_cast<int64_t>(b0) * kv_heads);
-  p->grid = p->total_items < sm_count ? p->total_items : sm_count;
+  p->grid = 2 * (p->total_items < pairs ? p->total_items : pairs);
   p->total_tiles = tiles;
-  p->workspace_bytes = any_split ? kControlBytes + tail_items * kSlotBytes : 0;
+  p->workspace_bytes = kControlBytes + (any_split ? tail_items * kSlotBytes : 0);
   return TPSA_OK;
 }
 
@@ -879,53 +1222,52 @@ tpsa_status launch(const void* query, const void* key_cache, const void* value_c
   if (st != TPSA_OK) return st;
   KernelArgs args;
   std::memset(&args, 0, sizeof(args));
-  st = build_plan(query_tokens, query_start, seq_len, prompt_len, kv_heads, dev->sm_count,
+  st = build_plan(query_tokens, query_start, seq_len, prompt_len, kv_heads, dev->max_pairs,
                   scale, &args.plan);
   if (st != TPSA_OK) return st;
   const tpsa_plan& p = args.plan;
-  if (p.workspace_bytes > 0) {
-    if (workspace == nullptr || workspace_bytes < static_cast<uint64_t>(p.workspace_bytes)) {
-      return fail(TPSA_ERR_WORKSPACE, "workspace smaller than tpsa_workspace_size()");
-    }
-    if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0) {
-      return fail(TPSA_ERR_WORKSPACE, "workspace must be 256-byte aligned");
-    }
+  if (workspace == nullptr || workspace_bytes < static_cast<uint64_t>(p.workspace_bytes)) {
+    return fail(TPSA_ERR_WORKSPACE, "workspace smaller than tpsa_workspace_size()");
+  }
+  if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0) {
+    return fail(TPSA_ERR_WORKSPACE, "workspace must be 256-byte aligned");
   }
   for (const void* ptr : {query, key_cache, value_cache, static_cast<const void*>(out)}) {
     if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0) {
       return fail(TPSA_ERR_INVALID_ARGUMENT, "tensors must be 16-byte aligned");
     }
   }
-  CUtensorMap tq, tk, tv;
+  CUtensorMap tq, tk64, tk32, tv;
   const uint64_t hq = static_cast<uint64_t>(kv_heads) * kGroupSize;
+  const uint64_t cache_tokens = static_cast<uint64_t>(num_pages) * kPageSize;
   st = encode_map(&tq, query, hq, static_cast<uint64_t>(query_tokens), 2, kBlockQ);
   if (st != TPSA_OK) return st;
-  st = encode_map(&tk, key_cache, kv_heads, static_cast<uint64_t>(num_pages) * kPageSize, 1, 64);
+  st = encode_map(&tk64, key_cache, kv_heads, cache_tokens, 1, 64);
   if (st != TPSA_OK) return st;
-  st = encode_map(&tv, value_cache, kv_heads, static_cast<uint64_t>(num_pages) * kPageSize, 1,
-                  64);
+  st = encode_map(&tk32, key_cache, kv_heads, cache_tokens, 1, 32);
+  if (st != TPSA_OK) return st;
+  st = encode_map(&tv, value_cache, kv_heads, cache_tokens, 1, 64);
   if (st != TPSA_OK) return st;
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   args.block_table = block_table;
   args.out = static_cast<__nv_bfloat16*>(out);
   args.num_pages = static_cast<int32_t>(num_pages);
-  if (p.workspace_bytes > 0) {
-    args.split_ctr = static_cast<int32_t*>(workspace);
-    args.scratch = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kControlBytes);
-    cudaError_t e = cudaMemsetAsync(workspace, 0, kControlBytes, s);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(workspace)");
-  }
+  args.ctl = static_cast<int32_t*>(workspace);
+  args.scratch = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kControlBytes);
+  // The work-item counter and split counters start at zero every launch.
+  cudaError_t e = cudaMemsetAsync(workspace, 0, kControlBytes, s);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(workspace)");
   args.visited = visited;
   args.tiles = reinterpret_cast<unsigned long long*>(tile_counter);
   args.words_per_row = (p.seq_len + 31) / 32;
 
   if (visited != nullptr || tile_counter != nullptr) {
-    tpsa_paged_kernel<true><<<p.grid, kNumThreads, kSmemBytes, s>>>(args, tq, tk, tv);
+    tpsa_paged_kernel<true><<<p.grid, kNumThreads, kSmemBytes, s>>>(args, tq, tk64, tk32, tv);
   } else {
-    tpsa_paged_kernel<false><<<p.grid, kNumThreads, kSmemBytes, s>>>(args, tq, tk, tv);
+    tpsa_paged_kernel<false><<<p.grid, kNumThreads, kSmemBytes, s>>>(args, tq, tk64, tk32, tv);
   }
-  cudaError_t e = cudaGetLastError();
+  e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
   return TPSA_OK;
 }
@@ -958,14 +1300,14 @@ tpsa_status tpsa_make_plan(int64_t query_tokens, int64_t query_start, int64_t se
                            int64_t prompt_len, int32_t kv_heads, int32_t sm_count,
                            float scale, tpsa_plan* plan) {
   t_last_error.clear();
+  int32_t pairs = sm_count / 2;
   if (sm_count <= 0) {
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
-    e = cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, dev);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(SM count)");
+    DeviceState* dev = nullptr;
+    tpsa_status st = device_state(&dev);
+    if (st != TPSA_OK) return st;
+    pairs = dev->max_pairs;
   }
-  return build_plan(query_tokens, query_start, seq_len, prompt_len, kv_heads, sm_count, scale,
+  return build_plan(query_tokens, query_start, seq_len, prompt_len, kv_heads, pairs, scale,
                     plan);
 }
 
@@ -1045,6 +1387,22 @@ tpsa_status tpsa_paged_attention_visit(const void* query, const void* key_cache,
                 table_cols, query_start, seq_len, prompt_len, scale, kv_heads, workspace,
                 workspace_bytes, visited, tile_counter, stream);
 }
+
+#ifdef TPSA_TRACE
+// Copies role `role`'s events of the last launch into out (2 x uint64 each).
+TPSA_API uint32_t tpsa_debug_trace(uint32_t role, unsigned long long* out, uint32_t max_events) {
+  uint32_t n[kTraceRoles] = {0, 0, 0, 0};
+  cudaDeviceSynchronize();
+  if (role >= kTraceRoles) {  // softmax sub-phase buffers of CTA role - 4
+    return 0;
+  }
+  cudaMemcpyFromSymbol(n, g_trace_n, sizeof(n));
+  uint32_t c = n[role] < max_events ? n[role] : max_events;
+  cudaMemcpyFromSymbol(out, g_trace, sizeof(unsigned long long) * 2 * c,
+                       sizeof(unsigned long long) * 2 * kTraceCap * role);
+  return c;
+}
+#endif
 
 tpsa_status tpsa_device_status(int32_t device, uint32_t* status_bits) {
   t_last_error.clear();

@@ -47,8 +47,10 @@ constexpr int32_t kMaxSeqLen = 1 << 30;
 // Partial result of one split item: 256 rows x (128 O values + m + l), fp32.
 constexpr int64_t kSlotFloats = 2 * kRowsPerTile * (kHeadDim + 2);
 constexpr int64_t kSlotBytes = kSlotFloats * 4;
-constexpr int64_t kControlBytes = 1024;  // split counters, 256 x int32
-constexpr int32_t kMaxSplitCounters = 256;
+// Workspace control words: work-item counter + split counters (int32), one
+// per (dense-tail block, kv head, CTA of the pair).
+constexpr int64_t kControlBytes = 2048;
+constexpr int32_t kMaxSplitCounters = 448;  // (2048 - 64 * 4) / 4
 
 TPSA_HD int32_t ceil_div(int32_t a, int32_t b) { return (a + b - 1) / b; }
 TPSA_HD int32_t min_i(int32_t a, int32_t b) { return a < b ? a : b; }
@@ -62,6 +64,17 @@ struct BlockTiles {
   int32_t key_end;    // 64-aligned end of the contiguous key range
   int32_t count;      // number of key tiles
   int32_t all_dense;  // every row of the block is a dense row
+  int32_t all_sparse; // every row of the block is a sparse row
+};
+
+// Per-tile mask kinds (uniform over the tile's rows; chosen per tile).
+enum MaskMode : int32_t {
+  kMaskNone = 0,     // every row sees every key of the tile
+  kMaskCausal = 1,   // keep k <= q
+  kMaskWindow = 2,   // keep k >= q - 512 (sparse rows, tile holds no sink key)
+  kMaskBand = 3,     // keep q - 512 <= k <= q (sparse rows, no sink key)
+  kMaskSink = 4,     // the separate sink tile [0, 64): keep k < 8
+  kMaskGeneral = 5,  // per-row rule of key_visible
 };
 
 // Row q is sparse iff sparse_begin <= q < sparse_end (reference
@@ -78,6 +91,7 @@ TPSA_HD BlockTiles block_tiles(const tpsa_plan& p, int32_t block) {
   const int32_t sparse_hi = min_i(t.q_end, p.sparse_end);
   t.all_dense = sparse_lo >= sparse_hi ? 1 : 0;
   const bool all_sparse = t.q_begin >= p.sparse_begin && t.q_end <= p.sparse_end;
+  t.all_sparse = all_sparse ? 1 : 0;
   t.key_end = ceil_div(t.q_end, kKeyGrain) * kKeyGrain;
   t.sink = 0;
   t.key_begin = 0;
@@ -119,6 +133,21 @@ TPSA_HD bool tile_needs_mask(const tpsa_plan& p, const BlockTiles& t,
   if (t.all_dense) return false;
   const int32_t last_sparse = min_i(t.q_end, p.sparse_end) - 1;
   return k0 < last_sparse - kLocalWindow;  // window lower edge or sink gap
+}
+
+// Mask kind of tile [k0, k0 + w) for the rows of block t.
+TPSA_HD int32_t tile_mask_mode(const tpsa_plan& p, const BlockTiles& t, int32_t k0,
+                               int32_t w) {
+  if (!tile_needs_mask(p, t, k0, w)) return kMaskNone;
+  if (t.all_dense) return kMaskCausal;
+  if (!t.all_sparse) return kMaskGeneral;
+  if (k0 < kSinkTokens) {
+    return (t.sink && k0 == 0 && w == kKeyGrain) ? kMaskSink : kMaskGeneral;
+  }
+  const bool causal = k0 + w - 1 > t.q_begin;
+  const bool window = k0 < (t.q_end - 1) - kLocalWindow;
+  if (causal && window) return kMaskBand;
+  return causal ? kMaskCausal : kMaskWindow;
 }
 
 // Key k enters row q's softmax (reference triangle_v2_reference.py:193-232:

@@ -13,7 +13,7 @@ import numpy as np
 import pytest
 import torch
 
-from gpu_helpers import MAX_ABS, MEAN_ABS, assert_close, run_cabi
+from gpu_helpers import MAX_ABS, MEAN_ABS, assert_close, run_cabi, workspace_for
 from inputs import SCALE, baseline_inputs, inputs_digest, reference_case_inputs
 from oracle.triangle_oracle import count_pairs, oracle_attention, visited_bitmap
 
@@ -179,7 +179,8 @@ def test_bad_page_is_flagged_not_faulted(tm, cuda_device):
     bad[0, 2] = k.shape[0] + 5
     qd, kd, vd, td = (t.to(cuda_device) for t in (q, k, v, bad))
     out = torch.empty_like(qd)
-    tm._native.paged_attention(qd, kd, vd, td, out, 0, seq, seq, SCALE)
+    ws = workspace_for(tm, seq, 0, seq, seq, 8, cuda_device)
+    tm._native.paged_attention(qd, kd, vd, td, out, 0, seq, seq, SCALE, workspace=ws)
     torch.cuda.synchronize()
     status = tm._native.device_status(0)
     assert status & tm._native.DEVICE_BAD_PAGE

@@ -136,9 +136,10 @@ def test_items_partition_blocks_heads_and_tiles(tm, q0, tq, seq, prompt):
                     break
             assert parts[-1][2] == ntiles
         assert sum(costs) == plan.total_tiles
-        assert plan.grid == min(plan.total_items, SM)
-        if plan.workspace_bytes:
-            assert plan.workspace_bytes == 1024 + plan.tail_items * 256 * 130 * 4
+        assert plan.grid == 2 * min(plan.total_items, SM // 2)  # CTA pairs
+        split = any(tm._native.plan_item(plan, i).num_splits > 1 for i in range(plan.tail_items))
+        assert plan.workspace_bytes == 2048 + (plan.tail_items * 256 * 130 * 4 if split else 0)
+        assert (plan.num_blocks - plan.tail_block0) * kvh * 2 <= 448 or not split
 
 
 def test_long_tail_blocks_are_split_and_run_first(tm):
@@ -148,10 +149,11 @@ def test_long_tail_blocks_are_split_and_run_first(tm):
     longest = max(tm._native.plan_item(plan, i).tile_end - tm._native.plan_item(plan, i).tile_begin
                   for i in range(plan.total_items))
     assert longest <= plan.split_tiles
-    assert plan.total_tiles / SM >= longest
+    assert plan.total_tiles / (SM // 2) >= longest
 
 
-def test_workspace_size_zero_without_splits(tm):
-    # Intermediate chunk with no dense tail: nothing is split.
+def test_workspace_is_control_words_without_splits(tm):
+    # Intermediate chunk with no dense tail: nothing is split, only the
+    # scheduler's control words are needed.
     plan = tm._native.make_plan(2048, 2048, 4096, 8320, 8, SM)
-    assert plan.workspace_bytes == 0 and plan.tail_items == 0
+    assert plan.workspace_bytes == 2048 and plan.tail_items == 0
