@@ -28,6 +28,7 @@ import argparse
 import json
 import math
 import os
+import re
 import subprocess
 import sys
 import threading
@@ -58,8 +59,10 @@ def effective_pairs(query_start: int, tq: int, seq: int, prompt: int) -> int:
     return total
 
 
-def make_inputs(tq: int, seq: int, seed: int, kv_lo: int, kv_hi: int):
-    """Seeded host inputs; the head slice [kv_lo, kv_hi) of a full 8-head layer."""
+def make_inputs(tq: int, seq: int, seed: int, rank: int = 0, world: int = 1):
+    """Seeded host inputs of one full 8-head layer, sliced to this rank's KV heads."""
+    from __graft_entry__ import load_package
+
     gen = torch.Generator().manual_seed(seed)
     logical = math.ceil(seq / PAGE)
     physical = 2 * logical
@@ -68,9 +71,9 @@ def make_inputs(tq: int, seq: int, seed: int, kv_lo: int, kv_hi: int):
     q = torch.randn(tq, QUERY_HEADS, HEAD_DIM, generator=gen).to(torch.bfloat16)
     k = torch.randn(physical, PAGE, KV_HEADS, HEAD_DIM, generator=gen).to(torch.bfloat16)
     v = torch.randn(physical, PAGE, KV_HEADS, HEAD_DIM, generator=gen).to(torch.bfloat16)
-    q = q[:, 4 * kv_lo:4 * kv_hi].contiguous()
-    k = k[:, :, kv_lo:kv_hi].contiguous()
-    v = v[:, :, kv_lo:kv_hi].contiguous()
+    if world == 1:
+        return q, k, v, table
+    q, k, v, _ = load_package().sharding.shard_layer(q, k, v, rank, world)
     return q, k, v, table
 
 
@@ -135,13 +138,28 @@ def load_peaks() -> tuple[dict, str]:
     return dict(FALLBACK_PEAKS), "fallback"
 
 
+def profiled_traffic(workload: str, heads: int) -> dict | None:
+    """DRAM bytes per launch from the committed ncu summary of this workload.
+
+    The summary holds one ``traffic_bytes_per_launch: N`` line measured on the
+    full 8-head layer; a head slice moves proportionally fewer bytes.
+    """
+    path = ROOT / "profiles" / f"tpsa_paged_kernel_{workload}.md"
+    if not path.exists():
+        return None
+    m = re.search(r"^traffic_bytes_per_launch:\s*(\d+)", path.read_text(), re.M)
+    if m is None:
+        return None
+    return {"bytes": int(m.group(1)) * heads // KV_HEADS, "source": f"profiles/{path.name}"}
+
+
 def cpu_baseline(tq: int, seq: int, query_start: int, prompt: int, budget_s: float) -> dict:
     """Time the oracle (port of the reference's CPU oracle) on a row sample."""
     from oracle.triangle_oracle import oracle_attention_rowwise, prepare_logical_kv
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    q, k, v, table = make_inputs(tq, seq, 0, 0, KV_HEADS)
+    q, k, v, table = make_inputs(tq, seq, 0)
     t0 = time.perf_counter()
     lkv = prepare_logical_kv(k, v, table, seq)
     t_gather = time.perf_counter() - t0
@@ -243,7 +261,7 @@ def main() -> None:
     # Each rank: `layers` layers x its kv-head slice.  Distinct seeds per layer.
     rank_inputs = []
     for layer in range(layers):
-        q, k, v, table = make_inputs(tq, seq, layer, rank * heads_per_rank, (rank + 1) * heads_per_rank)
+        q, k, v, table = make_inputs(tq, seq, layer, rank, world)
         rank_inputs.append((q, k, v, table))
     dev_inputs = [tuple(t.to(dev) for t in x) for x in rank_inputs]
     outs = [torch.empty_like(x[0]) for x in dev_inputs]
@@ -332,10 +350,16 @@ def main() -> None:
     peaks, peak_kind = load_peaks()
     achieved = flops_layer * heads_per_rank / KV_HEADS / (kernel_ms * 1e-3) / 1e12
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
-                "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"], "traffic": None,
+                "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
+                "traffic": None,
                 "peak_source": f"{peak_kind} bf16_tflops (burst)",
                 "kernel": "tpsa_paged_kernel<false>", "kernel_ms": kernel_ms,
                 "algorithmic": "4*128*heads*pairs effective FLOPs per launch"}
+    traffic = profiled_traffic(workload_config(args)["workload"], heads_per_rank)
+    if traffic is not None:
+        roofline["traffic"] = traffic["bytes"]
+        roofline["traffic_unit"] = "bytes/launch (ncu dram read+write)"
+        roofline["traffic_source"] = traffic["source"]
     line = {"metric": METRIC, "value": value, "unit": "TFLOP/s (effective)", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
             "ms_per_layer": ms_step / layers, "higher_is_better": True, "scaling": "weak",

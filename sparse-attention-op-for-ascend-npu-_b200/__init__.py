@@ -13,7 +13,7 @@ Layers, bottom up:
   sharding.py           KV-head partition across 1/2/4/8 GPUs
 """
 
-from . import _native
+from . import _native, sharding
 from ._native import TpsaError, load_adapter
 from .kernel import (
     TriangleMixConfig,
@@ -50,4 +50,5 @@ __all__ = [
     "triangle_sparse_span",
     "triangle_streaming_start",
     "_native",
+    "sharding",
 ]
