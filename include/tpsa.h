@@ -209,6 +209,42 @@ TPSA_API tpsa_status tpsa_paged_attention_visit(
     uint64_t* tile_counter, void* stream);
 
 /*
+ * tpsa_paged_attention without a workspace argument: it allocates nothing.
+ * This entry point has no counterpart in the reference.
+ *
+ * Some callers cannot allocate device memory at the moment they run the
+ * operator: plain C or FFI hosts that bind this library without an
+ * allocator of their own, and serving runtimes that reserve all device memory
+ * up front, where an allocation in the middle of a step could fail or
+ * fragment the pool.  This variant keeps its scratch (the control words and
+ * the split-KV partials) in one module-global device array of at most
+ * 16 MiB per device.  That covers 8192-token query chunks over contexts up to
+ * 128K tokens.  A call whose plan needs more scratch returns
+ * TPSA_ERR_WORKSPACE with the required size in tpsa_last_error(); use
+ * tpsa_paged_attention with a caller workspace for those shapes.  The call
+ * makes no cudaMalloc or cudaFree and uses no allocating library routine.
+ *
+ * Set-up: the first call on a device (with that device current) looks up
+ * the array's device address with cudaGetSymbolAddress and caches it.  That
+ * lookup also makes the CUDA runtime load this library's device globals on
+ * the device.  Make the first call on each device before any stream capture.
+ *
+ * Sharing: every call on a device uses the same array, and the array keeps
+ * the previous call's contents.  Each call clears the control words that
+ * must start at zero (cudaMemsetAsync on `stream`).  The partial slots are
+ * written before they are read.  Calls that overlap on the GPU (launched on
+ * different streams without ordering, or from several host threads at once)
+ * race on the array and give wrong results, so order them on one stream.
+ *
+ * Arguments, gates and results are those of tpsa_paged_attention.
+ */
+TPSA_API tpsa_status tpsa_paged_attention_static_scratch(
+    const void* query, const void* key_cache, const void* value_cache,
+    const int32_t* block_table, void* out, int64_t query_tokens,
+    int64_t num_pages, int64_t table_cols, int64_t query_start,
+    int64_t seq_len, int64_t prompt_len, float scale, void* stream);
+
+/*
  * Read and clear the device status word of `device` (TPSA_DEVICE_* bits).
  * Synchronises that device.  A non-zero word means a launch since the last
  * read hit a bounded wait or an out-of-range page id.

@@ -39,6 +39,7 @@ EXPORTED_SYMBOLS = (
     "tpsa_paged_attention_heads",
     "tpsa_paged_attention_visit",
     "tpsa_device_status",
+    "tpsa_paged_attention_static_scratch",
 )
 
 
@@ -109,9 +110,11 @@ def lib() -> ctypes.CDLL:
         h.tpsa_paged_attention_heads.argtypes = _ATTN + [_i32, _vp, _u64, _vp]
         h.tpsa_paged_attention_visit.argtypes = _ATTN + [_i32, _vp, _u64, _vp, _vp, _vp]
         h.tpsa_device_status.argtypes = [_i32, ctypes.POINTER(ctypes.c_uint32)]
+        h.tpsa_paged_attention_static_scratch.argtypes = _ATTN + [_vp]
         for name in ("tpsa_make_plan", "tpsa_plan_item", "tpsa_plan_tile", "tpsa_workspace_size",
                      "tpsa_paged_attention", "tpsa_paged_attention_heads",
-                     "tpsa_paged_attention_visit", "tpsa_device_status"):
+                     "tpsa_paged_attention_visit", "tpsa_device_status",
+                     "tpsa_paged_attention_static_scratch"):
             getattr(h, name).restype = ctypes.c_int
         _LIB = h
         return h
@@ -179,6 +182,26 @@ def paged_attention(query, key_cache, value_cache, block_table, out, query_start
         check(h.tpsa_paged_attention_heads(*common, kv_heads, ws_ptr, ws_bytes, stream))
     else:
         check(h.tpsa_paged_attention(*common, ws_ptr, ws_bytes, stream))
+
+
+def paged_attention_static_scratch(query, key_cache, value_cache, block_table, out,
+                                   query_start: int, seq_len: int, prompt_len: int, scale: float,
+                                   *, stream=None) -> None:
+    """Launch the variant that allocates nothing (scratch in a module-global array).
+
+    For callers that cannot allocate device memory when they run the
+    operator.  Calls on one device share the scratch, so they must be ordered on one
+    stream. The first call on a device sets up the scratch address; make it
+    before any stream capture.
+    """
+    import torch
+
+    if stream is None:
+        stream = torch.cuda.current_stream(query.device).cuda_stream
+    check(lib().tpsa_paged_attention_static_scratch(
+        query.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(), block_table.data_ptr(),
+        out.data_ptr(), query.shape[0], key_cache.shape[0], block_table.shape[-1],
+        query_start, seq_len, prompt_len, scale, stream))
 
 
 _ADAPTER_LOADED: str | None = None

@@ -1272,6 +1272,47 @@ tpsa_status launch(const void* query, const void* key_cache, const void* value_c
   return TPSA_OK;
 }
 
+// ------------------------------------------------ static-scratch variant
+// Scratch for tpsa_paged_attention_static_scratch: the same control words and
+// split-KV partial slots that tpsa_paged_attention keeps in a caller-provided
+// workspace, in one module-global array per device instead.  Its maximum
+// size, 16 MiB, covers 8192-token query chunks over contexts up to 128K
+// tokens (10.2 MiB there).
+constexpr uint64_t kStaticScratchBytes = uint64_t{16} << 20;
+constexpr int kMaxScratchDevices = 64;
+std::mutex g_scratch_mutex;
+void* g_scratch_ptr[kMaxScratchDevices] = {};
+
+// Device address of the static scratch on the current device.  The first
+// call on a device looks the address up (cudaGetSymbolAddress, which also
+// makes the runtime load this module's device globals there) and caches it.
+tpsa_status static_scratch_address(void** ptr);
+
+}  // namespace
+
+static __device__ __align__(256) uint8_t g_static_scratch[kStaticScratchBytes];
+
+namespace {
+
+tpsa_status static_scratch_address(void** ptr) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxScratchDevices) {
+    return fail(TPSA_ERR_CUDA, "device ordinal out of range");
+  }
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (g_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_static_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(static scratch)");
+    if (p == nullptr) return fail(TPSA_ERR_CUDA, "static scratch has no device address");
+    g_scratch_ptr[dev] = p;
+  }
+  *ptr = g_scratch_ptr[dev];
+  return TPSA_OK;
+}
+
 }  // namespace
 }  // namespace tpsa
 
@@ -1386,6 +1427,36 @@ tpsa_status tpsa_paged_attention_visit(const void* query, const void* key_cache,
   return launch(query, key_cache, value_cache, block_table, out, query_tokens, num_pages,
                 table_cols, query_start, seq_len, prompt_len, scale, kv_heads, workspace,
                 workspace_bytes, visited, tile_counter, stream);
+}
+
+tpsa_status tpsa_paged_attention_static_scratch(const void* query, const void* key_cache,
+                                                const void* value_cache,
+                                                const int32_t* block_table, void* out,
+                                                int64_t query_tokens, int64_t num_pages,
+                                                int64_t table_cols, int64_t query_start,
+                                                int64_t seq_len, int64_t prompt_len, float scale,
+                                                void* stream) {
+  t_last_error.clear();
+  DeviceState* dev = nullptr;
+  tpsa_status st = device_state(&dev);
+  if (st != TPSA_OK) return st;
+  tpsa_plan p;
+  st = build_plan(query_tokens, query_start, seq_len, prompt_len, TPSA_KV_HEADS, dev->max_pairs,
+                  scale, &p);
+  if (st != TPSA_OK) return st;
+  if (static_cast<uint64_t>(p.workspace_bytes) > kStaticScratchBytes) {
+    return fail(TPSA_ERR_WORKSPACE,
+                "this call needs " + std::to_string(p.workspace_bytes) +
+                    " bytes of scratch; the static scratch holds " +
+                    std::to_string(kStaticScratchBytes) +
+                    " bytes (16 MiB): use tpsa_paged_attention with a caller workspace");
+  }
+  void* scratch = nullptr;
+  st = static_scratch_address(&scratch);
+  if (st != TPSA_OK) return st;
+  return launch(query, key_cache, value_cache, block_table, out, query_tokens, num_pages,
+                table_cols, query_start, seq_len, prompt_len, scale, TPSA_KV_HEADS, scratch,
+                kStaticScratchBytes, nullptr, nullptr, stream);
 }
 
 #ifdef TPSA_TRACE
