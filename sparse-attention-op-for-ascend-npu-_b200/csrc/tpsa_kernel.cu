@@ -21,17 +21,20 @@
 //               counter, longest items first), which hands items to CTA 1
 //               through its shared memory
 //   warp 1      CTA 0: tcgen05 MMA issuer; both: TMEM owner
-//   warps 4-11  softmax + epilogue of this CTA's 128 rows: warpgroup 0
-//               (warps 4-7) takes the first half of every S tile's columns
-//               and of O's, warpgroup 1 (warps 8-11) the second half; row
-//               maxima and sums are exchanged through shared memory
+//   warps 2-3   idle (they complete the control warpgroup for setmaxnreg)
+//   warps 4-11  two softmax warpgroups.  Key tile gt of the pair's global
+//               tile sequence belongs to warpgroup gt % 2, which keeps its
+//               own S buffer, O accumulator and row (max, sum) over whole
+//               128-column rows; the two partial results of an item are
+//               merged once at its end.  While one warpgroup exponentiates,
+//               the tensor pipe runs the other's QK and PV.
 // Tensor memory per CTA (fp32 columns): S0 [0,128), S1 [128,256),
-// O [256,384).  S is double-buffered by key tile, so QK(n+1) runs while the
-// softmax of tile n is computed; P (bf16 pairs) overwrites the first half of
+// O0 [256,384), O1 [384,512).  P (bf16 pairs) overwrites the first half of
 // its S buffer and PV(n) reads it from there.  MMA issue order per item:
 //   QK(0), QK(1), PV(0), QK(2), PV(1), QK(3), ...
-// The O rescale for a grown row max is lazy (only when the max grows by
-// more than 2^8) and done by the softmax warps in tensor memory.
+// so QK(n+1) (the other warpgroup's S) runs while tile n's softmax is
+// computed.  The O rescale for a grown row max is lazy (only when the max
+// grows by more than 2^8) and done by the softmax warps in tensor memory.
 //
 // Softmax arithmetic: scores are scaled into the log2 domain with one fused
 // multiply-add, exponentiated with ex2.approx (MUFU) for 3 of every 4 column
@@ -66,7 +69,7 @@ __device__ uint32_t g_trace_n[kTraceRoles];
 #define TPSA_TRACE_STATE uint32_t tr_n_ = 0
 #define TPSA_SM_TR(ev)                                                             \
   do {                                                                             \
-    if (blockIdx.x < 2 && threadIdx.x == 128 && trn < kTraceCap) {              \
+    if (blockIdx.x == 0 && (threadIdx.x == 128 || threadIdx.x == 256) && trn < kTraceCap) {              \
       g_trace[trole][trn][0] = static_cast<unsigned long long>(ev) << 32;          \
       g_trace[trole][trn][1] = clock64();                                          \
       ++trn;                                                                       \
@@ -98,7 +101,14 @@ __device__ uint32_t g_trace_n[kTraceRoles];
 namespace {
 
 constexpr int kNumThreads = 384;
-constexpr int kSoftmaxWarps = 8;  // two warpgroups, each half of the S columns
+constexpr int kSoftmaxWarps = 8;  // two warpgroups, alternate key tiles
+constexpr int kFirstSoftmaxWarp = 4;
+// Register split (setmaxnreg): the control warpgroup (warps 0-3) keeps 48
+// registers a thread, the two softmax warpgroups 224, within the launch's
+// 384 x 168: 128 x 48 + 256 x 224 = 63488.
+constexpr uint32_t kControlRegs = 48;
+constexpr uint32_t kSoftmaxRegs = 224;
+static_assert(128 * kControlRegs + 256 * kSoftmaxRegs <= 384 * 168, "register split");
 constexpr uint32_t kTmemCols = 512;
 constexpr uint64_t kWaitTimeoutNs = 1000000000ull;  // 1 s per wait
 constexpr uint64_t kAbortSettleNs = 200000ull;      // let in-flight TMA land
@@ -121,9 +131,9 @@ enum BarId : uint32_t {
   kBarKVFull = kBarQEmpty + 2,            // [kRing] CTA 0: both halves landed
   kBarKVEmpty = kBarKVFull + kRing,       // [kRing] both: slot free
   kBarSFull = kBarKVEmpty + kRing,        // [2] both: S buffer computed
-  kBarPFull = kBarSFull + 2,              // CTA 0: P of a tile in TMEM (8 warps)
-  kBarPvDone = kBarPFull + 1,             // both: PV of a tile completed
-  kBarOEmpty = kBarPvDone + 1,            // CTA 0: O read by both epilogues
+  kBarPFull = kBarSFull + 2,              // [2] CTA 0: P of a warpgroup's tile in TMEM
+  kBarPvDone = kBarPFull + 2,             // [2] both: PV of a warpgroup's tile completed
+  kBarOEmpty = kBarPvDone + 2,            // CTA 0: O0 and O1 read by both epilogues
   kBarItemFull = kBarOEmpty + 1,          // [2] both: item index written
   kBarItemEmpty = kBarItemFull + 2,       // [2] CTA 0: item index consumed
   kBarSplitWritten = kBarItemEmpty + 2,   // per CTA: split partial written
@@ -137,16 +147,17 @@ enum BarId : uint32_t {
 // item_empty takes the MMA issuer and 4 softmax warps of CTA 0 plus the
 // producer and 4 softmax warps of CTA 1.
 constexpr uint32_t kPairWarpArrivals = 2 * kSoftmaxWarps;
+constexpr uint32_t kPairWgArrivals = kSoftmaxWarps;  // 4 warps of one warpgroup x 2 CTAs
 constexpr uint32_t kItemConsumers = 2 * (1 + kSoftmaxWarps);
 
 constexpr uint32_t kOffItemSlots = kOffBar + kNumBars * 8;  // 2 x int32
 constexpr uint32_t kOffTmemSlot = kOffItemSlots + 8;
 constexpr uint32_t kOffAbort = kOffTmemSlot + 4;
 constexpr uint32_t kOffSplitLast = kOffAbort + 4;
-// Row-max / row-sum exchange between the two softmax warpgroups:
-// float [2 buffers][2 warpgroups][128 rows].
+// (row max, row sum) exchange between the two softmax warpgroups at the
+// end of an item: float [2 buffers][2 warpgroups][2 values][128 rows].
 constexpr uint32_t kOffXchg = (kOffSplitLast + 4 + 15) & ~15u;
-constexpr uint32_t kSmemUsed = kOffXchg + 2 * 2 * 128 * 4;
+constexpr uint32_t kSmemUsed = kOffXchg + 2 * 2 * 2 * 128 * 4;
 constexpr uint32_t kSmemBytes = kSmemUsed + 1024;  // alignment slack
 static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 
@@ -198,7 +209,7 @@ __device__ __forceinline__ bool try_wait_sel(uint32_t bar, uint32_t parity) {
 }
 
 template <bool kCluster>
-__device__ __noinline__ bool wait_bar_slow(uint32_t bar, uint32_t parity,
+__device__ __forceinline__ bool wait_bar_slow(uint32_t bar, uint32_t parity,
                                            volatile int* abort_flag) {
   const uint64_t t0 = ptx::globaltimer_ns();
   while (true) {
@@ -426,7 +437,7 @@ __device__ void producer_role(const KernelArgs& a, const Shared& sh,
 // are warp-uniform) and one elected lane issues each tcgen05 instruction.
 __device__ void mma_role(const KernelArgs& a, const Shared& sh, uint32_t tmem, int lane) {
   const tpsa_plan& p = a.plan;
-  uint32_t ring = 0, q_iter = 0, g = 0, p_count = 0, item_iter = 0;
+  uint32_t ring = 0, q_iter = 0, g = 0, item_iter = 0;
   bool ok = true;
   TPSA_TRACE_STATE;
 
@@ -448,9 +459,11 @@ __device__ void mma_role(const KernelArgs& a, const Shared& sh, uint32_t tmem, i
       ptx::umma_ss_pair_elect(d, qd + qo, kd + ko, idesc, k > 0 ? 1u : 0u);
     }
   };
-  // O += P(gt) V(gt): P from S buffer gt % 2 (bf16 pairs), V d-half per CTA.
+  // O(gt % 2) += P(gt) V(gt): P from S buffer gt % 2 (bf16 pairs), V d-half
+  // per CTA.  Tile gt belongs to softmax warpgroup gt % 2, which owns S and O
+  // buffer gt % 2.
   auto issue_pv = [&](uint32_t vslot, uint32_t gt, int32_t w, bool first) {
-    const uint32_t d = tmem + 256;
+    const uint32_t d = tmem + 256 + (gt % 2) * 128;
     const uint32_t pa = tmem + (gt % 2) * 128;
     constexpr uint32_t idesc = ptx::idesc_bf16_f32(256, 128, 1);
     const uint64_t vd = ptx::smem_desc_sw128(sh.base_u32 + kOffKV + vslot * kRingSlotBytes,
@@ -512,14 +525,15 @@ __device__ void mma_role(const KernelArgs& a, const Shared& sh, uint32_t tmem, i
         ok = false;
         break;
       }
-      if (!warp_wait(sh.bar(kBarPFull), p_count & 1)) { ok = false; break; }
-      ++p_count;
+      const uint32_t gt = g + static_cast<uint32_t>(n);
+      if (!warp_wait(sh.bar(kBarPFull + gt % 2), (gt / 2) & 1)) { ok = false; break; }
       if (lane == 0) TPSA_TR(1, 14, n);
       ptx::tc_fence_after();
-      issue_pv(ring_slot(vr), g + n, w, n == 0);
+      // Each warpgroup's first tile of the item overwrites its O buffer.
+      issue_pv(ring_slot(vr), gt, w, n < 2);
       if (lane == 0) TPSA_TR(1, 15, n);
       ptx::umma_commit_pair_mc_elect(sh.bar(kBarKVEmpty + ring_slot(vr)), kPairMask);
-      ptx::umma_commit_pair_mc_elect(sh.bar(kBarPvDone), kPairMask);
+      ptx::umma_commit_pair_mc_elect(sh.bar(kBarPvDone + gt % 2), kPairMask);
       if (lane == 0) TPSA_TR(1, 16, n);
       if (n + 2 < ntiles) {
         int32_t k2, w2;
@@ -559,10 +573,10 @@ __device__ __forceinline__ void load_s(uint32_t taddr, float (&s)[W]) {
   for (int c = 0; c < W; ++c) s[c] = __uint_as_float(r[c]);
 }
 
-// Multiplies this warpgroup's 64 O columns of the row by `factor`.
-__device__ __forceinline__ void rescale_o_half(uint32_t o_addr, float factor) {
+// Multiplies the 128 O columns of this thread's row by `factor`.
+__device__ __forceinline__ void rescale_o(uint32_t o_addr, float factor) {
 #pragma unroll 1
-  for (int c = 0; c < 2; ++c) {
+  for (int c = 0; c < 4; ++c) {
     uint32_t r[32];
     ptx::tmem_ld32(o_addr + 32 * c, r);
     ptx::tmem_wait_ld();
@@ -573,169 +587,167 @@ __device__ __forceinline__ void rescale_o_half(uint32_t o_addr, float factor) {
   ptx::tmem_wait_st();
 }
 
-// Masks columns of this warpgroup's part of a tile; column c holds key
-// k0c + c.
-template <int W, int MODE>
-__device__ __forceinline__ void apply_mask(float (&s)[W], int32_t q, bool sparse, int32_t k0c) {
-  const int32_t hi = q - k0c + 1;             // keep c < hi
-  const int32_t lo = q - kLocalWindow - k0c;  // keep c >= lo (sparse rows)
-  const int32_t sk = kSinkTokens - k0c;       // keep c < sk (sink keys)
-  if constexpr (MODE == kMaskCausal) {
-#pragma unroll
-    for (int c = 0; c < W; ++c) s[c] = c < hi ? s[c] : -INFINITY;
-  } else if constexpr (MODE == kMaskWindow) {
-#pragma unroll
-    for (int c = 0; c < W; ++c) s[c] = c >= lo ? s[c] : -INFINITY;
-  } else if constexpr (MODE == kMaskBand) {
-#pragma unroll
-    for (int c = 0; c < W; ++c) s[c] = (c >= lo && c < hi) ? s[c] : -INFINITY;
-  } else if constexpr (MODE == kMaskSink) {
-#pragma unroll
-    for (int c = 0; c < W; ++c) s[c] = c < sk ? s[c] : -INFINITY;
-  } else if constexpr (MODE == kMaskGeneral) {
-    const int32_t lo_g = sparse ? lo : -(1 << 30);
-#pragma unroll
-    for (int c = 0; c < W; ++c) {
-      const bool v = (c < hi) && (c >= lo_g || c < sk);
-      s[c] = v ? s[c] : -INFINITY;
-    }
-  }
+// Bits c of the result: key kc + c (c < 32) is in the key set of query row
+// q.  Dense rows see keys <= q; sparse rows additionally drop keys in
+// [8, q - 512).
+__device__ __forceinline__ uint32_t bits_below(int32_t x) {
+  return x <= 0 ? 0u : (x >= 32 ? ~0u : (1u << x) - 1u);
+}
+__device__ __forceinline__ uint32_t chunk_mask(int32_t q, bool sparse, int32_t kc) {
+  uint32_t m = bits_below(q - kc + 1);
+  if (sparse) m &= ~bits_below(q - kLocalWindow - kc) | bits_below(kSinkTokens - kc);
+  return m;
 }
 
-// Per-thread softmax state.  Both warpgroups of a row hold the same m_run;
-// each holds the partial row sum of its own columns.
+// Online-softmax state of one row over one warpgroup's tiles of an item.
 struct RowState {
   float m_run;
   float l_run;
 };
 
-// Exchanges one float per row between the two softmax warpgroups (the value
-// of warpgroup wg is published, the other one returned).  `xc` counts
-// exchanges; both warpgroups run the same sequence.
-__device__ __forceinline__ bool exchange(const Shared& sh, uint32_t& xc, int wg, int row,
-                                         int lane, float mine, float* other) {
-  volatile float* buf = reinterpret_cast<volatile float*>(sh.base + kOffXchg) + (xc & 1) * 256;
-  buf[wg * 128 + row] = mine;
+// Publishes this warpgroup's (m, l) of the row and returns the other
+// warpgroup's.  `xc` counts exchanges; both warpgroups run the same sequence.
+__device__ __forceinline__ bool exchange_ml(const Shared& sh, uint32_t& xc, int wg, int row,
+                                            int lane, float m, float l, float* m_other,
+                                            float* l_other) {
+  volatile float* buf = reinterpret_cast<volatile float*>(sh.base + kOffXchg) + (xc & 1) * 512;
+  buf[wg * 256 + row] = m;
+  buf[wg * 256 + 128 + row] = l;
   __syncwarp();
   if (lane == 0) ptx::mbar_arrive(sh.bar(kBarWgX));
   const bool ok = wait_bar(sh, sh.bar(kBarWgX), xc & 1);
   ++xc;
   if (!__all_sync(0xffffffffu, ok)) return false;
-  *other = buf[(1 - wg) * 128 + row];
+  *m_other = buf[(1 - wg) * 256 + row];
+  *l_other = buf[(1 - wg) * 256 + 128 + row];
   return true;
 }
 
 struct SoftmaxCtx {
   const tpsa_plan* p;
-  const Shared* sh;
-  uint32_t s_addr;  // this warpgroup's first S column of the tile's buffer
-  uint32_t p_addr;  // this warpgroup's first P column (bf16 pairs)
-  uint32_t o_addr;  // this warpgroup's first O column
-  int wg, row, lane;
+  uint32_t s_addr;  // this warpgroup's S buffer (P overwrites its first half)
+  uint32_t o_addr;  // this warpgroup's O buffer
   int32_t q;
   bool sparse;
 };
 
-// One key tile, this warpgroup's W columns (W = w / 2): mask, joint row
-// max, online-softmax update, P -> TMEM.  `pv_needed`: PV completions to
-// observe before O may be rescaled (every PV issued before this tile).
-template <int W, int MODE>
-__device__ __forceinline__ bool softmax_tile(const SoftmaxCtx& cx, int32_t k0c, bool first,
-                                             uint32_t pv_needed, uint32_t& pv_seen,
-                                             uint32_t& xc, RowState& st, uint32_t* visit_row,
+// Converts one 32-column chunk of S to floats, masking the keys outside the
+// row's key set when kMasked.
+template <bool kMasked>
+__device__ __forceinline__ void chunk_values(const uint32_t (&r)[32], uint32_t m, float (&v)[32]) {
+#pragma unroll
+  for (int c = 0; c < 32; ++c) {
+    const float x = __uint_as_float(r[c]);
+    v[c] = (!kMasked || ((m >> c) & 1u)) ? x : -INFINITY;
+  }
+}
+
+// One key tile of w keys (64 or 128) starting at k0, the whole row: mask,
+// row max, online-softmax update, P -> tensor memory.  `first`: the
+// warpgroup's first tile of the item, whose PV overwrites O (so O is not
+// rescaled).  Two passes over the S columns in tensor memory, 64 columns at
+// a time, keep at most 64 of them in registers: pass 1 takes the row max
+// (and the visited bits), pass 2 reloads, exponentiates and writes P (bf16
+// pairs) over the first half of the S buffer, which it has already read.
+// The loops over 64-column halves are not unrolled: one body serves both
+// tile widths, which keeps the kernel's code small.
+template <bool kMasked>
+__device__ __forceinline__ void softmax_tile(const SoftmaxCtx& cx, int32_t k0, int32_t w,
+                                             bool first, RowState& st, uint32_t* visit_row,
                                              int32_t words_per_row, uint32_t trole,
                                              uint32_t& trn) {
   const tpsa_plan& p = *cx.p;
-  float s[W];
-  load_s<W>(cx.s_addr, s);
-  apply_mask<W, MODE>(s, cx.q, cx.sparse, k0c);
-  TPSA_SM_TR(2);
-  if (visit_row != nullptr) {
+  const int32_t halves = w / 64;
+  float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+#pragma unroll 1
+  for (int32_t h = 0; h < halves; ++h) {
+    uint32_t ra[32], rb[32];
+    ptx::tmem_ld32(cx.s_addr + 64 * h, ra);
+    ptx::tmem_ld32(cx.s_addr + 64 * h + 32, rb);
+    ptx::tmem_wait_ld_regs(ra);
+    ptx::tmem_fence_regs(rb);
+    const int32_t kc = k0 + 64 * h;
+    const uint32_t ma = kMasked ? chunk_mask(cx.q, cx.sparse, kc) : ~0u;
+    const uint32_t mb = kMasked ? chunk_mask(cx.q, cx.sparse, kc + 32) : ~0u;
+    if (visit_row != nullptr) {
+      const int32_t word = kc / 32;
+      if (ma != 0 && word < words_per_row) atomicOr(visit_row + word, ma);
+      if (mb != 0 && word + 1 < words_per_row) atomicOr(visit_row + word + 1, mb);
+    }
+    float v[32];
+    chunk_values<kMasked>(ra, ma, v);
 #pragma unroll
-    for (int j = 0; j < W / 32; ++j) {
-      uint32_t bits = 0;
+    for (int c = 0; c < 32; c += 8) {
+      mx0 = max3(mx0, v[c], v[c + 1]);
+      mx1 = max3(mx1, v[c + 2], v[c + 3]);
+      mx2 = max3(mx2, v[c + 4], v[c + 5]);
+      mx3 = max3(mx3, v[c + 6], v[c + 7]);
+    }
+    chunk_values<kMasked>(rb, mb, v);
 #pragma unroll
-      for (int c = 0; c < 32; ++c) bits |= (s[32 * j + c] != -INFINITY ? 1u : 0u) << c;
-      const int32_t word = k0c / 32 + j;
-      if (bits != 0 && word < words_per_row) atomicOr(visit_row + word, bits);
+    for (int c = 0; c < 32; c += 8) {
+      mx0 = max3(mx0, v[c], v[c + 1]);
+      mx1 = max3(mx1, v[c + 2], v[c + 3]);
+      mx2 = max3(mx2, v[c + 4], v[c + 5]);
+      mx3 = max3(mx3, v[c + 6], v[c + 7]);
     }
   }
-  // Partial row max over this warpgroup's columns, then the joint max.
-  float mx0 = s[0], mx1 = s[2], mx2 = s[4], mx3 = s[6];
-#pragma unroll
-  for (int c = 0; c < W; c += 8) {
-    mx0 = max3(mx0, s[c], s[c + 1]);
-    mx1 = max3(mx1, s[c + 2], s[c + 3]);
-    mx2 = max3(mx2, s[c + 4], s[c + 5]);
-    mx3 = max3(mx3, s[c + 6], s[c + 7]);
-  }
-  float mx = fmaxf(max3(mx0, mx1, mx2), mx3);
-  // S of both halves is in registers before either warpgroup writes P over
-  // the other's S columns (the exchange orders the two).
-  ptx::tc_fence_before();
-  float mx_other;
-  if (!exchange(*cx.sh, xc, cx.wg, cx.row, cx.lane, mx, &mx_other)) return false;
-  ptx::tc_fence_after();
-  mx = fmaxf(mx, mx_other);
+  TPSA_SM_TR(2);
+  const float mx = fmaxf(max3(mx0, mx1, mx2), mx3);
   const float m_new = fmaxf(st.m_run, mx);
   const bool need = (m_new - st.m_run) * p.scale_log2 > kRescaleLog2;
-  if (__any_sync(0xffffffffu, need)) {
-    const float factor = need ? mufu_exp2((st.m_run - m_new) * p.scale_log2) : 1.0f;
-    if (!first) {
-      // O holds PVs of earlier tiles: they must have completed.
-      while (pv_seen < pv_needed) {
-        const bool ok = wait_bar(*cx.sh, cx.sh->bar(kBarPvDone), pv_seen & 1);
-        if (!__all_sync(0xffffffffu, ok)) return false;
-        ++pv_seen;
-      }
-      ptx::tc_fence_after();
-      rescale_o_half(cx.o_addr, factor);
-    }
+  const bool any_need = __any_sync(0xffffffffu, need);
+  float factor = 1.0f;
+  if (any_need) {
+    factor = need ? mufu_exp2((st.m_run - m_new) * p.scale_log2) : 1.0f;
     st.l_run *= factor;
     if (need) st.m_run = m_new;
   }
   const float neg_mb = st.m_run == -INFINITY ? 0.0f : -st.m_run * p.scale_log2;
   TPSA_SM_TR(6);
   float sum0 = 0.0f, sum1 = 0.0f;
+#pragma unroll 1
+  for (int32_t h = 0; h < halves; ++h) {
+    uint32_t ra[32], rb[32];
+    ptx::tmem_ld32(cx.s_addr + 64 * h, ra);
+    ptx::tmem_ld32(cx.s_addr + 64 * h + 32, rb);
+    ptx::tmem_wait_ld_regs(ra);
+    ptx::tmem_fence_regs(rb);
+    const int32_t kc = k0 + 64 * h;
 #pragma unroll
-  for (int j = 0; j < W / 32; ++j) {
-    uint32_t pk[16];
-#pragma unroll
-    for (int c = 0; c < 16; ++c) {
-      float x0, x1;
-      fma2(s[32 * j + 2 * c], s[32 * j + 2 * c + 1], p.scale_log2, neg_mb, x0, x1);
-      float e0, e1;
-      if ((c & 3) == 3) {
-        e0 = poly_exp2(x0);
-        e1 = poly_exp2(x1);
+    for (int half = 0; half < 2; ++half) {
+      float v[32];
+      if (half == 0) {
+        chunk_values<kMasked>(ra, kMasked ? chunk_mask(cx.q, cx.sparse, kc) : ~0u, v);
       } else {
-        e0 = mufu_exp2(x0);
-        e1 = mufu_exp2(x1);
+        chunk_values<kMasked>(rb, kMasked ? chunk_mask(cx.q, cx.sparse, kc + 32) : ~0u, v);
       }
-      add2(sum0, sum1, e0, e1);
-      pk[c] = pack_bf16x2(e0, e1);
+      uint32_t pk[16];
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        float x0, x1;
+        fma2(v[2 * c], v[2 * c + 1], p.scale_log2, neg_mb, x0, x1);
+        float e0, e1;
+        if ((c & 3) == 3) {
+          e0 = poly_exp2(x0);
+          e1 = poly_exp2(x1);
+        } else {
+          e0 = mufu_exp2(x0);
+          e1 = mufu_exp2(x1);
+        }
+        add2(sum0, sum1, e0, e1);
+        pk[c] = pack_bf16x2(e0, e1);
+      }
+      ptx::tmem_st16(cx.s_addr + 32 * h + 16 * half, pk);
     }
-    ptx::tmem_st16(cx.p_addr + 16 * j, pk);
   }
   st.l_run += sum0 + sum1;
+  // O is rescaled after the exponentials; it only has to be done before P is
+  // published (the PV of this tile accumulates into O).  The PVs of earlier
+  // tiles into O have completed (the caller waited).
+  if (any_need && !first) rescale_o(cx.o_addr, factor);
   ptx::tmem_wait_st();
   TPSA_SM_TR(7);
-  return true;
-}
-
-// Normalises 64 O values and stores them as bf16 (128 bytes).
-__device__ __forceinline__ void store_half_bf16(__nv_bfloat16* dst, const uint32_t* v,
-                                                float scale) {
-  uint4* d = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    uint4 u;
-    u.x = pack_bf16x2(__uint_as_float(v[8 * j + 0]) * scale, __uint_as_float(v[8 * j + 1]) * scale);
-    u.y = pack_bf16x2(__uint_as_float(v[8 * j + 2]) * scale, __uint_as_float(v[8 * j + 3]) * scale);
-    u.z = pack_bf16x2(__uint_as_float(v[8 * j + 4]) * scale, __uint_as_float(v[8 * j + 5]) * scale);
-    u.w = pack_bf16x2(__uint_as_float(v[8 * j + 6]) * scale, __uint_as_float(v[8 * j + 7]) * scale);
-    d[j] = u;
-  }
 }
 
 // One arrival per softmax warp on a CTA-0 barrier.
@@ -744,28 +756,34 @@ __device__ __forceinline__ void warp_arrive0(const Shared& sh, uint32_t id, int 
   if (lane == 0) ptx::mbar_arrive_cluster(sh.bar0(id));
 }
 
+// Softmax warpgroup `wg` (warps 4-7: wg 0, warps 8-11: wg 1; warp % 4 is
+// the tensor-memory lane quadrant, so each warpgroup covers all 128 rows).  Tile
+// gt of the pair's global tile sequence belongs to warpgroup gt % 2, which
+// keeps its own S buffer, O accumulator and (m, l) per row; the two partial
+// results of an item are merged once at its end, each warpgroup producing 64
+// of the 128 output columns.
 __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tmem) {
   const tpsa_plan& p = a.plan;
   const uint32_t r = sh.rank;
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
-  const int wg = (warp - 4) / 4;     // which half of the columns
+  const int wg = (warp - kFirstSoftmaxWarp) / 4;
   const int quad = warp % 4;
   const int row = quad * 32 + lane;  // TMEM lane == row of this CTA's M half
   const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
   const int32_t hq = p.kv_heads * kGroupSize;
   const bool visit = a.visited != nullptr;
-  uint32_t g = 0, pv_seen = 0, split_iter = 0, xc = 0;
+  // own: tiles of this warpgroup so far (tile gt = 2 * own + wg); pv_seen:
+  // completed PV phases of this warpgroup observed.
+  uint32_t g = 0, own = 0, pv_seen = 0, split_iter = 0, xc = 0;
   volatile int* split_last = reinterpret_cast<volatile int*>(sh.base + kOffSplitLast);
   uint32_t tr_sm = 0;  // trace counter (used only with TPSA_TRACE)
 #define tr_n_ tr_sm
+  const uint32_t o_base = tmem + lane_base + 256;  // O0; O1 at +128
   SoftmaxCtx cx;
   cx.p = &p;
-  cx.sh = &sh;
-  cx.wg = wg;
-  cx.row = row;
-  cx.lane = lane;
-  cx.o_addr = tmem + lane_base + 256 + wg * 64;
+  cx.s_addr = tmem + lane_base + wg * 128;
+  cx.o_addr = o_base + wg * 128;
 
   for (uint32_t n_item = 0;; ++n_item) {
     int32_t idx = 0;
@@ -787,105 +805,106 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
             ? a.visited + (static_cast<size_t>(qrow) * hq + head) * a.words_per_row
             : nullptr;
     RowState st{-INFINITY, 0.0f};
-    bool ok = true;
+    bool ok = true, first = true;
     const int32_t ntiles = it.tile_end - it.tile_begin;
-    for (int32_t n = 0; n < ntiles; ++n) {
-      const uint32_t gt = g + static_cast<uint32_t>(n);
+    // Which warpgroups own at least one tile of this item.
+    const bool has_wg0 = ntiles >= 2 || (g & 1) == 0;
+    const bool has_wg1 = ntiles >= 2 || (g & 1) == 1;
+    for (int32_t n = (g + wg) & 1; n < ntiles; n += 2) {
       int32_t k0, w;
       tile_keys(bt, it.tile_begin + n, &k0, &w);
-      const int32_t mode = tile_mask_mode(p, bt, k0, w);
-      const bool w_ok = wait_bar(sh, sh.bar(kBarSFull + gt % 2), (gt / 2) & 1);
+      const bool masked = tile_needs_mask(p, bt, k0, w);
+      const bool w_ok = wait_bar(sh, sh.bar(kBarSFull + wg), own & 1);
       if (!__all_sync(0xffffffffu, w_ok)) { ok = false; break; }
-      if (row == 0 && wg == 0) TPSA_TR(2 + r, 1, n);
-      ptx::tc_fence_after();
-      const uint32_t sbuf = tmem + lane_base + (gt % 2) * 128;
-      const int32_t half = w / 2;
-      cx.s_addr = sbuf + wg * half;
-      cx.p_addr = sbuf + wg * (half / 2);
-      const int32_t k0c = k0 + wg * half;
-      const bool first = n == 0;
-      bool t_ok = true;
-#define TPSA_TILE(WW, MM)                                                                   \
-  t_ok = softmax_tile<WW, MM>(cx, k0c, first, gt, pv_seen, xc, st, visit_row, a.words_per_row, \
-                              2 + r, tr_sm)
-      if (w == 128) {
-        switch (mode) {
-          case kMaskNone: TPSA_TILE(64, kMaskNone); break;
-          case kMaskCausal: TPSA_TILE(64, kMaskCausal); break;
-          case kMaskWindow: TPSA_TILE(64, kMaskWindow); break;
-          case kMaskBand: TPSA_TILE(64, kMaskBand); break;
-          default: TPSA_TILE(64, kMaskGeneral); break;
-        }
-      } else {
-        switch (mode) {
-          case kMaskNone: TPSA_TILE(32, kMaskNone); break;
-          case kMaskCausal: TPSA_TILE(32, kMaskCausal); break;
-          case kMaskWindow: TPSA_TILE(32, kMaskWindow); break;
-          case kMaskBand: TPSA_TILE(32, kMaskBand); break;
-          case kMaskSink: TPSA_TILE(32, kMaskSink); break;
-          default: TPSA_TILE(32, kMaskGeneral); break;
-        }
-      }
-#undef TPSA_TILE
-      if (!t_ok) { ok = false; break; }
-      // Keep the pv_done barrier at most one phase ahead: observe PV(gt - 1),
-      // issued one tile earlier and normally complete by now.
-      while (pv_seen < gt) {
-        const bool pv_ok = wait_bar(sh, sh.bar(kBarPvDone), pv_seen & 1);
+      // PV of this warpgroup's previous tile (issued before this tile's QK,
+      // so already complete): observed before O is touched or P rewritten.
+      if (pv_seen < own) {
+        const bool pv_ok = wait_bar(sh, sh.bar(kBarPvDone + wg), pv_seen & 1);
         if (!__all_sync(0xffffffffu, pv_ok)) { ok = false; break; }
         ++pv_seen;
       }
-      if (!ok) break;
+      if (row == 0 && r == 0) TPSA_TR(2 + wg, 1, n);
+      ptx::tc_fence_after();
+      if (masked) {
+        softmax_tile<true>(cx, k0, w, first, st, visit_row, a.words_per_row, 2 + wg, tr_sm);
+      } else {
+        softmax_tile<false>(cx, k0, w, first, st, visit_row, a.words_per_row, 2 + wg, tr_sm);
+      }
       ptx::tc_fence_before();
-      if (row == 0 && wg == 0) TPSA_TR(2 + r, 3, n);
-      warp_arrive0(sh, kBarPFull, lane);
+      if (row == 0 && r == 0) TPSA_TR(2 + wg, 3, n);
+      warp_arrive0(sh, kBarPFull + wg, lane);
+      first = false;
+      ++own;
     }
     if (!ok) break;
     g += static_cast<uint32_t>(ntiles);
-    // O is final once the item's last PV completed.
-    while (pv_seen < g) {
-      const bool pv_ok = wait_bar(sh, sh.bar(kBarPvDone), pv_seen & 1);
-      if (!__all_sync(0xffffffffu, pv_ok)) { ok = false; break; }
+    // This warpgroup's O is final once its last PV of the item completed.
+    if (pv_seen < own) {
+      const bool pv_ok = wait_bar(sh, sh.bar(kBarPvDone + wg), pv_seen & 1);
+      if (!__all_sync(0xffffffffu, pv_ok)) break;
       ++pv_seen;
     }
-    if (!ok) break;
-    ptx::tc_fence_after();
-    // O leaves tensor memory first, so the next item's PV can start while
-    // this row is normalised and stored.
-    uint32_t o[64];
-#pragma unroll
-    for (int c = 0; c < 2; ++c) {
-      ptx::tmem_ld32(cx.o_addr + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&o[32 * c]));
-    }
-    ptx::tmem_wait_ld();
+    // The exchange also orders the other warpgroup's final-PV observation
+    // before this warpgroup reads the other O buffer.
     ptx::tc_fence_before();
-    warp_arrive0(sh, kBarOEmpty, lane);
-    float l_other;
-    if (!exchange(sh, xc, wg, row, lane, st.l_run, &l_other)) break;
-    const float l_total = st.l_run + l_other;
-    if (row == 0 && wg == 0) TPSA_TR(2 + r, 5, 0);
-
+    float m_o, l_o;
+    if (!exchange_ml(sh, xc, wg, row, lane, st.m_run, st.l_run, &m_o, &l_o)) break;
+    ptx::tc_fence_after();
+    const float m0 = wg == 0 ? st.m_run : m_o, m1 = wg == 0 ? m_o : st.m_run;
+    const float l0 = wg == 0 ? st.l_run : l_o, l1 = wg == 0 ? l_o : st.l_run;
+    const float m_all = fmaxf(m0, m1);
+    const float a0 = m0 == -INFINITY ? 0.0f : mufu_exp2((m0 - m_all) * p.scale_log2);
+    const float a1 = m1 == -INFINITY ? 0.0f : mufu_exp2((m1 - m_all) * p.scale_log2);
+    const float l_total = l0 * a0 + l1 * a1;
+    // Columns [64 wg, 64 wg + 64) of the merged output row, 32 at a time:
+    // bf16 into `out`, or for a split item the unnormalised fp32 partial
+    // (O, m, l) into the item's workspace slot.
     __nv_bfloat16* dst_row = a.out + (static_cast<size_t>(qrow) * hq + head) * kHeadDim;
-    if (it.num_splits == 1) {
-      if (real_row) store_half_bf16(dst_row + wg * 64, o, 1.0f / l_total);
-      continue;
-    }
-
-    // Split item: publish (O, m, l) of this row, then the last split of the
-    // block (per CTA of the pair) merges all partials and writes bf16.
+    const bool split = it.num_splits > 1;
     float* slot = a.scratch + static_cast<size_t>(idx) * kSlotFloats;
     const int32_t srow = static_cast<int32_t>(r) * kRowsPerTile + row;
-    {
-      float4* d =
-          reinterpret_cast<float4*>(slot + static_cast<size_t>(srow) * kHeadDim + wg * 64);
+    const float inv = 1.0f / l_total;
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        d[j] = make_float4(__uint_as_float(o[4 * j]), __uint_as_float(o[4 * j + 1]),
-                           __uint_as_float(o[4 * j + 2]), __uint_as_float(o[4 * j + 3]));
+    for (int c = 0; c < 2; ++c) {
+      const uint32_t col = static_cast<uint32_t>(wg * 64 + 32 * c);
+      uint32_t x0[32], x1[32];
+      if (has_wg0) ptx::tmem_ld32(o_base + col, x0);
+      if (has_wg1) ptx::tmem_ld32(o_base + 128 + col, x1);
+      ptx::tmem_wait_ld();
+      float o[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float v0 = has_wg0 ? a0 * __uint_as_float(x0[j]) : 0.0f;
+        o[j] = has_wg1 ? fmaf(a1, __uint_as_float(x1[j]), v0) : v0;
+      }
+      if (!split) {
+        if (real_row) {
+          uint4* d = reinterpret_cast<uint4*>(dst_row + col);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            d[j] = make_uint4(pack_bf16x2(o[8 * j] * inv, o[8 * j + 1] * inv),
+                              pack_bf16x2(o[8 * j + 2] * inv, o[8 * j + 3] * inv),
+                              pack_bf16x2(o[8 * j + 4] * inv, o[8 * j + 5] * inv),
+                              pack_bf16x2(o[8 * j + 6] * inv, o[8 * j + 7] * inv));
+          }
+        }
+      } else {
+        float4* d = reinterpret_cast<float4*>(slot + static_cast<size_t>(srow) * kHeadDim + col);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          d[j] = make_float4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
+        }
       }
     }
+    ptx::tc_fence_before();
+    warp_arrive0(sh, kBarOEmpty, lane);
+    if (row == 0 && r == 0) TPSA_TR(2 + wg, 5, 0);
+    if (!split) continue;
+
+    // Split item: the last split of the block (per CTA of the pair) merges
+    // all partials and writes bf16.
     if (wg == 0) {
-      slot[2 * kRowsPerTile * kHeadDim + srow] = st.m_run;
+      slot[2 * kRowsPerTile * kHeadDim + srow] = m_all;
       slot[2 * kRowsPerTile * (kHeadDim + 1) + srow] = l_total;
     }
     __threadfence();
@@ -918,7 +937,7 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
       const float ms = __ldcg(sl + m_off);
       if (ms != -INFINITY) lsum += mufu_exp2((ms - mmax) * p.scale_log2) * __ldcg(sl + l_off);
     }
-    const float inv = 1.0f / lsum;
+    const float inv_sum = 1.0f / lsum;
 #pragma unroll 1
     for (int c = 0; c < 2; ++c) {
       const int col = wg * 64 + 32 * c;
@@ -943,10 +962,10 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
       uint4* d = reinterpret_cast<uint4*>(dst_row + col);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        d[j] = make_uint4(pack_bf16x2(acc[8 * j] * inv, acc[8 * j + 1] * inv),
-                          pack_bf16x2(acc[8 * j + 2] * inv, acc[8 * j + 3] * inv),
-                          pack_bf16x2(acc[8 * j + 4] * inv, acc[8 * j + 5] * inv),
-                          pack_bf16x2(acc[8 * j + 6] * inv, acc[8 * j + 7] * inv));
+        d[j] = make_uint4(pack_bf16x2(acc[8 * j] * inv_sum, acc[8 * j + 1] * inv_sum),
+                          pack_bf16x2(acc[8 * j + 2] * inv_sum, acc[8 * j + 3] * inv_sum),
+                          pack_bf16x2(acc[8 * j + 4] * inv_sum, acc[8 * j + 5] * inv_sum),
+                          pack_bf16x2(acc[8 * j + 6] * inv_sum, acc[8 * j + 7] * inv_sum));
       }
     }
   }
@@ -984,8 +1003,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kNumThreads, 1)
       ptx::mbar_init(sh.bar(kBarKVFull + s), 2);
       ptx::mbar_init(sh.bar(kBarKVEmpty + s), 1);
     }
-    ptx::mbar_init(sh.bar(kBarPFull), kPairWarpArrivals);
-    ptx::mbar_init(sh.bar(kBarPvDone), 1);
+    for (int i = 0; i < 2; ++i) {
+      ptx::mbar_init(sh.bar(kBarPFull + i), kPairWgArrivals);
+      ptx::mbar_init(sh.bar(kBarPvDone + i), 1);
+    }
     ptx::mbar_init(sh.bar(kBarOEmpty), kPairWarpArrivals);
     ptx::mbar_init(sh.bar(kBarSplitWritten), kSoftmaxWarps);
     ptx::mbar_init(sh.bar(kBarSplitDecided), 1);
@@ -1004,12 +1025,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kNumThreads, 1)
   ptx::tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sh.base + kOffTmemSlot);
 
-  if (warp == 0) {
-    if (lane == 0) producer_role(args, sh, &tmap_q, &tmap_k64, &tmap_k32, &tmap_v);
-    __syncwarp();
-  } else if (warp == 1) {
-    if (sh.rank == 0) mma_role(args, sh, tmem, lane);
-  } else if (warp >= 4) {
+  if (warp < kFirstSoftmaxWarp) {
+    ptx::setmaxnreg_dec<kControlRegs>();
+    if (warp == 0) {
+      if (lane == 0) producer_role(args, sh, &tmap_q, &tmap_k64, &tmap_k32, &tmap_v);
+      __syncwarp();
+    } else if (warp == 1) {
+      if (sh.rank == 0) mma_role(args, sh, tmem, lane);
+    }
+  } else {
+    ptx::setmaxnreg_inc<kSoftmaxRegs>();
     softmax_role(args, sh, tmem);
   }
 

@@ -67,16 +67,6 @@ struct BlockTiles {
   int32_t all_sparse; // every row of the block is a sparse row
 };
 
-// Per-tile mask kinds (uniform over the tile's rows; chosen per tile).
-enum MaskMode : int32_t {
-  kMaskNone = 0,     // every row sees every key of the tile
-  kMaskCausal = 1,   // keep k <= q
-  kMaskWindow = 2,   // keep k >= q - 512 (sparse rows, tile holds no sink key)
-  kMaskBand = 3,     // keep q - 512 <= k <= q (sparse rows, no sink key)
-  kMaskSink = 4,     // the separate sink tile [0, 64): keep k < 8
-  kMaskGeneral = 5,  // per-row rule of key_visible
-};
-
 // Row q is sparse iff sparse_begin <= q < sparse_end (reference
 // operator/tests/triangle_v2_reference.py:212-215).
 TPSA_HD bool row_is_sparse(const tpsa_plan& p, int32_t q) {
@@ -135,20 +125,6 @@ TPSA_HD bool tile_needs_mask(const tpsa_plan& p, const BlockTiles& t,
   return k0 < last_sparse - kLocalWindow;  // window lower edge or sink gap
 }
 
-// Mask kind of tile [k0, k0 + w) for the rows of block t.
-TPSA_HD int32_t tile_mask_mode(const tpsa_plan& p, const BlockTiles& t, int32_t k0,
-                               int32_t w) {
-  if (!tile_needs_mask(p, t, k0, w)) return kMaskNone;
-  if (t.all_dense) return kMaskCausal;
-  if (!t.all_sparse) return kMaskGeneral;
-  if (k0 < kSinkTokens) {
-    return (t.sink && k0 == 0 && w == kKeyGrain) ? kMaskSink : kMaskGeneral;
-  }
-  const bool causal = k0 + w - 1 > t.q_begin;
-  const bool window = k0 < (t.q_end - 1) - kLocalWindow;
-  if (causal && window) return kMaskBand;
-  return causal ? kMaskCausal : kMaskWindow;
-}
 
 // Key k enters row q's softmax (reference triangle_v2_reference.py:193-232:
 // dense rows read [0, q], sparse rows read [0, 8) U [q - 512, q]).
