@@ -118,9 +118,10 @@ constexpr uint16_t kPairMask = 0x3;
 // Shared memory per CTA (offsets from a 1024-byte aligned base).
 constexpr uint32_t kQHalfBytes = 128 * 128;        // 128 rows x 64 bf16
 constexpr uint32_t kQBytes = 2 * kQHalfBytes;      // one Q buffer (2 d-halves)
-constexpr uint32_t kRingSlotBytes = 16384;         // one K or V half-tile
+constexpr uint32_t kRingSlotBytes = 32768;         // one key tile: K half + V half
 constexpr uint32_t kKHalfBytes = 8192;             // d-half of a K half-tile
-constexpr int kRing = 9;                           // K/V half-tile slots
+constexpr uint32_t kVOffset = 16384;               // V half within a slot
+constexpr int kRing = 4;                           // key-tile slots (power of two)
 constexpr uint32_t kOffQ = 0;                      // 2 Q buffers
 constexpr uint32_t kOffKV = kOffQ + 2 * kQBytes;
 constexpr uint32_t kOffBar = kOffKV + kRing * kRingSlotBytes;
@@ -128,8 +129,8 @@ constexpr uint32_t kOffBar = kOffKV + kRing * kRingSlotBytes;
 enum BarId : uint32_t {
   kBarQFull = 0,                          // [2] CTA 0: both Q halves landed
   kBarQEmpty = kBarQFull + 2,             // [2] both CTAs: Q buffer free
-  kBarKVFull = kBarQEmpty + 2,            // [kRing] CTA 0: both halves landed
-  kBarKVEmpty = kBarKVFull + kRing,       // [kRing] both: slot free
+  kBarKVFull = kBarQEmpty + 2,            // [kRing] CTA 0: K and V of both CTAs landed
+  kBarKVEmpty = kBarKVFull + kRing,       // [kRing] both: slot free (its PV done)
   kBarSFull = kBarKVEmpty + kRing,        // [2] both: S buffer computed
   kBarPFull = kBarSFull + 2,              // [2] CTA 0: P of a warpgroup's tile in TMEM
   kBarPvDone = kBarPFull + 2,             // [2] both: PV of a warpgroup's tile completed
@@ -374,52 +375,49 @@ __device__ void producer_role(const KernelArgs& a, const Shared& sh,
         atomicAdd(a.tiles + 1, static_cast<unsigned long long>(w));
       }
       const int32_t half = w / 2;
-      // K half-tile: keys [k0 + r*half, +half), all 128 d (two d-halves).
-      {
-        const uint32_t s = ring_slot(ring);
-        if (!wait_bar(sh, sh.bar(kBarKVEmpty + s), ring_parity(ring) ^ 1)) { ok = false; break; }
-        ptx::mbar_arrive_expect_tx_cluster(sh.bar0(kBarKVFull + s),
-                                           static_cast<uint32_t>(half) * kHeadDim * 2);
-        const CUtensorMap* km = w == kTileKeys ? tk64 : tk32;
+      // One slot per key tile: K keys [k0 + r*half, +half) (all 128 d, two
+      // d-halves) at +0 and V keys [k0, k0 + w) (d-half r) at +kVOffset,
+      // both completing on the slot's full barrier.
+      const uint32_t s = ring_slot(ring);
+      if (!wait_bar(sh, sh.bar(kBarKVEmpty + s), ring_parity(ring) ^ 1)) { ok = false; break; }
+      ++ring;
+      const uint32_t kdst = sh.base_u32 + kOffKV + s * kRingSlotBytes;
+      const uint32_t vdst = kdst + kVOffset;
+      const uint32_t kbytes = static_cast<uint32_t>(half) * kHeadDim * 2;
+      const uint32_t vbytes = static_cast<uint32_t>(w) * 64 * 2;
+      const CUtensorMap* km = w == kTileKeys ? tk64 : tk32;
+      if (k0 + w <= p.seq_len) {
+        ptx::mbar_arrive_expect_tx_cluster(sh.bar0(kBarKVFull + s), kbytes + vbytes);
         for (int dh = 0; dh < 2; ++dh) {
-          ptx::tma_load_3d_pair(sh.base_u32 + kOffKV + s * kRingSlotBytes + dh * kKHalfBytes, km,
-                                dh * 64, it.kv_head, tok + static_cast<int32_t>(r) * half,
-                                sh.bar0(kBarKVFull + s));
+          ptx::tma_load_3d_pair(kdst + dh * kKHalfBytes, km, dh * 64, it.kv_head,
+                                tok + static_cast<int32_t>(r) * half, sh.bar0(kBarKVFull + s));
         }
-        ++ring;
-      }
-      // V half-tile: keys [k0, k0 + w), d-half r.
-      {
-        const uint32_t s = ring_slot(ring);
-        if (!wait_bar(sh, sh.bar(kBarKVEmpty + s), ring_parity(ring) ^ 1)) { ok = false; break; }
-        const uint32_t vdst = sh.base_u32 + kOffKV + s * kRingSlotBytes;
-        const uint32_t bytes = static_cast<uint32_t>(w) * 64 * 2;
-        if (k0 + w <= p.seq_len) {
-          ptx::mbar_arrive_expect_tx_cluster(sh.bar0(kBarKVFull + s), bytes);
-          for (int sub = 0; sub < w / 64; ++sub) {
-            ptx::tma_load_3d_pair(vdst + sub * 8192, tv, static_cast<int32_t>(r) * 64,
-                                  it.kv_head, tok + sub * 64, sh.bar0(kBarKVFull + s));
-          }
-        } else {
-          // Keys at or beyond seq_len may be unwritten cache slots: load the
-          // tile here, zero those V rows so P = 0 never meets a NaN, then
-          // release it to the MMA issuer with a plain arrival.
-          ptx::mbar_arrive_expect_tx(sh.bar(kBarTail), bytes);
-          for (int sub = 0; sub < w / 64; ++sub) {
-            ptx::tma_load_3d(vdst + sub * 8192, tv, static_cast<int32_t>(r) * 64, it.kv_head,
-                             tok + sub * 64, sh.bar(kBarTail));
-          }
-          if (!wait_bar(sh, sh.bar(kBarTail), tail_iter & 1)) { ok = false; break; }
-          ++tail_iter;
-          for (int32_t row = p.seq_len - k0; row < w; ++row) {
-            uint4* dst = reinterpret_cast<uint4*>(sh.base + (vdst - sh.base_u32) + row * 128);
+        for (int sub = 0; sub < w / 64; ++sub) {
+          ptx::tma_load_3d_pair(vdst + sub * 8192, tv, static_cast<int32_t>(r) * 64, it.kv_head,
+                                tok + sub * 64, sh.bar0(kBarKVFull + s));
+        }
+      } else {
+        // Keys at or beyond seq_len may be unwritten cache slots: load the
+        // tile into this CTA's slot here, zero those V rows so P = 0 never
+        // meets a NaN, then release the slot with a plain arrival.
+        ptx::mbar_arrive_expect_tx(sh.bar(kBarTail), kbytes + vbytes);
+        for (int dh = 0; dh < 2; ++dh) {
+          ptx::tma_load_3d(kdst + dh * kKHalfBytes, km, dh * 64, it.kv_head,
+                           tok + static_cast<int32_t>(r) * half, sh.bar(kBarTail));
+        }
+        for (int sub = 0; sub < w / 64; ++sub) {
+          ptx::tma_load_3d(vdst + sub * 8192, tv, static_cast<int32_t>(r) * 64, it.kv_head,
+                           tok + sub * 64, sh.bar(kBarTail));
+        }
+        if (!wait_bar(sh, sh.bar(kBarTail), tail_iter & 1)) { ok = false; break; }
+        ++tail_iter;
+        for (int32_t row = p.seq_len - k0; row < w; ++row) {
+          uint4* dst = reinterpret_cast<uint4*>(sh.base + (vdst - sh.base_u32) + row * 128);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) dst[j] = make_uint4(0, 0, 0, 0);
-          }
-          ptx::fence_proxy_async_smem();
-          ptx::mbar_arrive_cluster(sh.bar0(kBarKVFull + s));
+          for (int j = 0; j < 8; ++j) dst[j] = make_uint4(0, 0, 0, 0);
         }
-        ++ring;
+        ptx::fence_proxy_async_smem();
+        ptx::mbar_arrive_cluster(sh.bar0(kBarKVFull + s));
       }
       if (r == 0) TPSA_TR(0, 22, t);
     }
@@ -466,8 +464,8 @@ __device__ void mma_role(const KernelArgs& a, const Shared& sh, uint32_t tmem, i
     const uint32_t d = tmem + 256 + (gt % 2) * 128;
     const uint32_t pa = tmem + (gt % 2) * 128;
     constexpr uint32_t idesc = ptx::idesc_bf16_f32(256, 128, 1);
-    const uint64_t vd = ptx::smem_desc_sw128(sh.base_u32 + kOffKV + vslot * kRingSlotBytes,
-                                             kKHalfBytes, 1024);
+    const uint64_t vd = ptx::smem_desc_sw128(
+        sh.base_u32 + kOffKV + vslot * kRingSlotBytes + kVOffset, kKHalfBytes, 1024);
     if (w == kTileKeys) {
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
@@ -498,28 +496,26 @@ __device__ void mma_role(const KernelArgs& a, const Shared& sh, uint32_t tmem, i
     if (!warp_wait(sh.bar(kBarQFull + qb), (q_iter / 2) & 1)) break;
     ++q_iter;
     ptx::tc_fence_after();
-    // Ring positions of this item's tiles: K(t) at base + 2t, V(t) at base + 2t + 1.
+    // Ring position of tile t: base + t (K and V of a tile share a slot,
+    // which PV(t) releases).
     const uint32_t rbase = ring;
-    ring += 2 * static_cast<uint32_t>(ntiles);
+    ring += static_cast<uint32_t>(ntiles);
 
     // QK for the first two tiles.
     for (int32_t t = 0; t < 2 && t < ntiles && ok; ++t) {
       int32_t k0, w;
       tile_keys(bt, it.tile_begin + t, &k0, &w);
-      const uint32_t kr = rbase + 2 * t;
+      const uint32_t kr = rbase + t;
       if (!warp_wait(sh.bar(kBarKVFull + ring_slot(kr)), ring_parity(kr))) { ok = false; break; }
       ptx::tc_fence_after();
       issue_qk(qb, ring_slot(kr), g + t, w);
       ptx::umma_commit_pair_mc_elect(sh.bar(kBarSFull + (g + t) % 2), kPairMask);
-      ptx::umma_commit_pair_mc_elect(sh.bar(kBarKVEmpty + ring_slot(kr)), kPairMask);
       if (t == ntiles - 1) ptx::umma_commit_pair_mc_elect(sh.bar(kBarQEmpty + qb), kPairMask);
     }
     for (int32_t n = 0; n < ntiles && ok; ++n) {
       int32_t k0, w;
       tile_keys(bt, it.tile_begin + n, &k0, &w);
-      const uint32_t vr = rbase + 2 * n + 1;
-      if (lane == 0) TPSA_TR(1, 12, n);
-      if (!warp_wait(sh.bar(kBarKVFull + ring_slot(vr)), ring_parity(vr))) { ok = false; break; }
+      const uint32_t vr = rbase + n;
       if (lane == 0) TPSA_TR(1, 13, n);
       if (n == 0 && item_iter > 0 && !warp_wait(sh.bar(kBarOEmpty), (item_iter - 1) & 1)) {
         ok = false;
@@ -533,19 +529,21 @@ __device__ void mma_role(const KernelArgs& a, const Shared& sh, uint32_t tmem, i
       issue_pv(ring_slot(vr), gt, w, n < 2);
       if (lane == 0) TPSA_TR(1, 15, n);
       ptx::umma_commit_pair_mc_elect(sh.bar(kBarKVEmpty + ring_slot(vr)), kPairMask);
-      ptx::umma_commit_pair_mc_elect(sh.bar(kBarPvDone + gt % 2), kPairMask);
+      // A warpgroup learns that its earlier PVs completed from the S of its
+      // next tile (whose QK is issued after them); only its last tile of the
+      // item needs an explicit completion signal.
+      if (n + 2 >= ntiles) ptx::umma_commit_pair_mc_elect(sh.bar(kBarPvDone + gt % 2), kPairMask);
       if (lane == 0) TPSA_TR(1, 16, n);
       if (n + 2 < ntiles) {
         int32_t k2, w2;
         tile_keys(bt, it.tile_begin + n + 2, &k2, &w2);
-        const uint32_t kr = rbase + 2 * (n + 2);
+        const uint32_t kr = rbase + n + 2;
         if (!warp_wait(sh.bar(kBarKVFull + ring_slot(kr)), ring_parity(kr))) { ok = false; break; }
         if (lane == 0) TPSA_TR(1, 17, n + 2);
         ptx::tc_fence_after();
         issue_qk(qb, ring_slot(kr), g + n + 2, w2);
         if (lane == 0) TPSA_TR(1, 18, n + 2);
         ptx::umma_commit_pair_mc_elect(sh.bar(kBarSFull + (g + n + 2) % 2), kPairMask);
-        ptx::umma_commit_pair_mc_elect(sh.bar(kBarKVEmpty + ring_slot(kr)), kPairMask);
         if (n + 2 == ntiles - 1) {
           ptx::umma_commit_pair_mc_elect(sh.bar(kBarQEmpty + qb), kPairMask);
         }
@@ -773,9 +771,9 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
   const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
   const int32_t hq = p.kv_heads * kGroupSize;
   const bool visit = a.visited != nullptr;
-  // own: tiles of this warpgroup so far (tile gt = 2 * own + wg); pv_seen:
-  // completed PV phases of this warpgroup observed.
-  uint32_t g = 0, own = 0, pv_seen = 0, split_iter = 0, xc = 0;
+  // own: tiles of this warpgroup so far (tile gt = 2 * own + wg); pv_items:
+  // items in which this warpgroup had tiles (one PV-done phase each).
+  uint32_t g = 0, own = 0, pv_items = 0, split_iter = 0, xc = 0;
   volatile int* split_last = reinterpret_cast<volatile int*>(sh.base + kOffSplitLast);
   uint32_t tr_sm = 0;  // trace counter (used only with TPSA_TRACE)
 #define tr_n_ tr_sm
@@ -816,13 +814,8 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
       const bool masked = tile_needs_mask(p, bt, k0, w);
       const bool w_ok = wait_bar(sh, sh.bar(kBarSFull + wg), own & 1);
       if (!__all_sync(0xffffffffu, w_ok)) { ok = false; break; }
-      // PV of this warpgroup's previous tile (issued before this tile's QK,
-      // so already complete): observed before O is touched or P rewritten.
-      if (pv_seen < own) {
-        const bool pv_ok = wait_bar(sh, sh.bar(kBarPvDone + wg), pv_seen & 1);
-        if (!__all_sync(0xffffffffu, pv_ok)) { ok = false; break; }
-        ++pv_seen;
-      }
+      // S of this tile being full also means this warpgroup's earlier PVs
+      // into O completed (their MMAs were issued before this tile's QK).
       if (row == 0 && r == 0) TPSA_TR(2 + wg, 1, n);
       ptx::tc_fence_after();
       if (masked) {
@@ -838,11 +831,12 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
     }
     if (!ok) break;
     g += static_cast<uint32_t>(ntiles);
-    // This warpgroup's O is final once its last PV of the item completed.
-    if (pv_seen < own) {
-      const bool pv_ok = wait_bar(sh, sh.bar(kBarPvDone + wg), pv_seen & 1);
+    // This warpgroup's O is final once its last PV of the item completed
+    // (signalled once per item in which the warpgroup had tiles).
+    if (!first) {
+      const bool pv_ok = wait_bar(sh, sh.bar(kBarPvDone + wg), pv_items & 1);
       if (!__all_sync(0xffffffffu, pv_ok)) break;
-      ++pv_seen;
+      ++pv_items;
     }
     // The exchange also orders the other warpgroup's final-PV observation
     // before this warpgroup reads the other O buffer.
