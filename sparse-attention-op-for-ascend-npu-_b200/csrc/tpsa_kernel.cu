@@ -158,7 +158,11 @@ constexpr uint32_t kOffSplitLast = kOffAbort + 4;
 // (row max, row sum) exchange between the two softmax warpgroups at the
 // end of an item: float [2 buffers][2 warpgroups][2 values][128 rows].
 constexpr uint32_t kOffXchg = (kOffSplitLast + 4 + 15) & ~15u;
-constexpr uint32_t kSmemUsed = kOffXchg + 2 * 2 * 2 * 128 * 4;
+// Output staging: 2 KB per softmax warp (32 rows x 64 bytes), used to turn
+// row-per-thread results into coalesced global stores.
+constexpr uint32_t kStageBytesPerWarp = 32 * 64;
+constexpr uint32_t kOffStage = (kOffXchg + 2 * 2 * 2 * 128 * 4 + 127) & ~127u;
+constexpr uint32_t kSmemUsed = kOffStage + 8 * kStageBytesPerWarp;
 constexpr uint32_t kSmemBytes = kSmemUsed + 1024;  // alignment slack
 static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 
@@ -748,6 +752,42 @@ __device__ __forceinline__ void softmax_tile(const SoftmaxCtx& cx, int32_t k0, i
   TPSA_SM_TR(7);
 }
 
+// Writes columns [col, col + 32) of the 32 output rows of a softmax warp as
+// bf16 (values times `scale`).  Each thread holds one row, and its 64 bytes
+// are one half of a 128-byte line of `out`; storing them directly would make
+// every store instruction touch 32 lines.  The warp instead passes the rows
+// through its 2 KB staging buffer (16-byte chunks XOR-swizzled so both the
+// writes and the reads are bank-conflict free) and each store instruction
+// then writes 64 contiguous bytes of 8 rows.  Warp row R is query token
+// base_q + R / 2, head base_h + R % 2; rows at or past query_tokens are not
+// written.  All 32 lanes must call this.
+__device__ __forceinline__ void store_rows_bf16(const float (&o)[32], float scale, uint8_t* stage,
+                                                int lane, __nv_bfloat16* out, int32_t base_q,
+                                                int32_t base_h, int32_t hq, int32_t query_tokens,
+                                                int32_t col) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint4 v = make_uint4(pack_bf16x2(o[8 * j] * scale, o[8 * j + 1] * scale),
+                               pack_bf16x2(o[8 * j + 2] * scale, o[8 * j + 3] * scale),
+                               pack_bf16x2(o[8 * j + 4] * scale, o[8 * j + 5] * scale),
+                               pack_bf16x2(o[8 * j + 6] * scale, o[8 * j + 7] * scale));
+    *reinterpret_cast<uint4*>(stage + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) = v;
+  }
+  __syncwarp();
+  const int c = lane & 3;
+#pragma unroll
+  for (int jj = 0; jj < 4; ++jj) {
+    const int rr = 8 * jj + (lane >> 2);
+    const uint4 v = *reinterpret_cast<const uint4*>(stage + rr * 64 + ((c ^ ((rr >> 1) & 3)) << 4));
+    const int32_t q = base_q + (rr >> 1);
+    if (q < query_tokens) {
+      *reinterpret_cast<uint4*>(out + (static_cast<size_t>(q) * hq + base_h + (rr & 1)) * kHeadDim +
+                                col + 8 * c) = v;
+    }
+  }
+  __syncwarp();
+}
+
 // One arrival per softmax warp on a CTA-0 barrier.
 __device__ __forceinline__ void warp_arrive0(const Shared& sh, uint32_t id, int lane) {
   __syncwarp();
@@ -838,12 +878,14 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
       if (!__all_sync(0xffffffffu, pv_ok)) break;
       ++pv_items;
     }
+    if (row == 0 && r == 0) TPSA_TR(2 + wg, 8, 0);
     // The exchange also orders the other warpgroup's final-PV observation
     // before this warpgroup reads the other O buffer.
     ptx::tc_fence_before();
     float m_o, l_o;
     if (!exchange_ml(sh, xc, wg, row, lane, st.m_run, st.l_run, &m_o, &l_o)) break;
     ptx::tc_fence_after();
+    if (row == 0 && r == 0) TPSA_TR(2 + wg, 9, 0);
     const float m0 = wg == 0 ? st.m_run : m_o, m1 = wg == 0 ? m_o : st.m_run;
     const float l0 = wg == 0 ? st.l_run : l_o, l1 = wg == 0 ? l_o : st.l_run;
     const float m_all = fmaxf(m0, m1);
@@ -852,11 +894,16 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
     const float l_total = l0 * a0 + l1 * a1;
     // Columns [64 wg, 64 wg + 64) of the merged output row, 32 at a time:
     // bf16 into `out`, or for a split item the unnormalised fp32 partial
-    // (O, m, l) into the item's workspace slot.
-    __nv_bfloat16* dst_row = a.out + (static_cast<size_t>(qrow) * hq + head) * kHeadDim;
+    // (O, m, l) into the item's workspace slot.  A slot is column-major
+    // ([128 columns][256 rows], then m[256] and l[256]), so a warp's row-per-
+    // thread writes and reads of one column are 128 contiguous bytes.
     const bool split = it.num_splits > 1;
     float* slot = a.scratch + static_cast<size_t>(idx) * kSlotFloats;
+    constexpr int32_t kSlotRows = 2 * kRowsPerTile;
     const int32_t srow = static_cast<int32_t>(r) * kRowsPerTile + row;
+    const int32_t base_q = it.block * kBlockQ + quad * 16;
+    const int32_t base_h = it.kv_head * kGroupSize + 2 * static_cast<int32_t>(r);
+    uint8_t* stage = sh.base + kOffStage + (warp - kFirstSoftmaxWarp) * kStageBytesPerWarp;
     const float inv = 1.0f / l_total;
 #pragma unroll
     for (int c = 0; c < 2; ++c) {
@@ -872,22 +919,11 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
         o[j] = has_wg1 ? fmaf(a1, __uint_as_float(x1[j]), v0) : v0;
       }
       if (!split) {
-        if (real_row) {
-          uint4* d = reinterpret_cast<uint4*>(dst_row + col);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            d[j] = make_uint4(pack_bf16x2(o[8 * j] * inv, o[8 * j + 1] * inv),
-                              pack_bf16x2(o[8 * j + 2] * inv, o[8 * j + 3] * inv),
-                              pack_bf16x2(o[8 * j + 4] * inv, o[8 * j + 5] * inv),
-                              pack_bf16x2(o[8 * j + 6] * inv, o[8 * j + 7] * inv));
-          }
-        }
+        store_rows_bf16(o, inv, stage, lane, a.out, base_q, base_h, hq, p.query_tokens,
+                        static_cast<int32_t>(col));
       } else {
-        float4* d = reinterpret_cast<float4*>(slot + static_cast<size_t>(srow) * kHeadDim + col);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          d[j] = make_float4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
-        }
+        for (int j = 0; j < 32; ++j) slot[(col + j) * kSlotRows + srow] = o[j];
       }
     }
     ptx::tc_fence_before();
@@ -898,8 +934,8 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
     // Split item: the last split of the block (per CTA of the pair) merges
     // all partials and writes bf16.
     if (wg == 0) {
-      slot[2 * kRowsPerTile * kHeadDim + srow] = m_all;
-      slot[2 * kRowsPerTile * (kHeadDim + 1) + srow] = l_total;
+      slot[kHeadDim * kSlotRows + srow] = m_all;
+      slot[(kHeadDim + 1) * kSlotRows + srow] = l_total;
     }
     __threadfence();
     __syncwarp();
@@ -916,11 +952,11 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
     w_ok = wait_bar(sh, sh.bar(kBarSplitDecided), split_iter & 1);
     ++split_iter;
     if (!__all_sync(0xffffffffu, w_ok)) break;
-    if (!*split_last || !real_row) continue;
+    if (!*split_last) continue;
     __threadfence();
     const float* first_slot = a.scratch + static_cast<size_t>(idx - it.split) * kSlotFloats;
-    const size_t m_off = 2 * kRowsPerTile * kHeadDim + srow;
-    const size_t l_off = 2 * kRowsPerTile * (kHeadDim + 1) + srow;
+    const size_t m_off = static_cast<size_t>(kHeadDim) * kSlotRows + srow;
+    const size_t l_off = static_cast<size_t>(kHeadDim + 1) * kSlotRows + srow;
     float mmax = -INFINITY;
     for (int32_t sp = 0; sp < it.num_splits; ++sp) {
       mmax = fmaxf(mmax, __ldcg(first_slot + sp * kSlotFloats + m_off));
@@ -942,25 +978,12 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
         const float* sl = first_slot + sp * kSlotFloats;
         const float ms = __ldcg(sl + m_off);
         const float wgt = ms == -INFINITY ? 0.0f : mufu_exp2((ms - mmax) * p.scale_log2);
-        const float4* src =
-            reinterpret_cast<const float4*>(sl + static_cast<size_t>(srow) * kHeadDim + col);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float4 v = __ldcg(src + j);
-          acc[4 * j] += wgt * v.x;
-          acc[4 * j + 1] += wgt * v.y;
-          acc[4 * j + 2] += wgt * v.z;
-          acc[4 * j + 3] += wgt * v.w;
+        for (int j = 0; j < 32; ++j) {
+          acc[j] += wgt * __ldcg(sl + static_cast<size_t>(col + j) * kSlotRows + srow);
         }
       }
-      uint4* d = reinterpret_cast<uint4*>(dst_row + col);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        d[j] = make_uint4(pack_bf16x2(acc[8 * j] * inv_sum, acc[8 * j + 1] * inv_sum),
-                          pack_bf16x2(acc[8 * j + 2] * inv_sum, acc[8 * j + 3] * inv_sum),
-                          pack_bf16x2(acc[8 * j + 4] * inv_sum, acc[8 * j + 5] * inv_sum),
-                          pack_bf16x2(acc[8 * j + 6] * inv_sum, acc[8 * j + 7] * inv_sum));
-      }
+      store_rows_bf16(acc, inv_sum, stage, lane, a.out, base_q, base_h, hq, p.query_tokens, col);
     }
   }
 }
