@@ -282,6 +282,12 @@ __device__ __forceinline__ void st_cluster_u32(uint32_t cluster_addr, uint32_t v
   asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
 }
 
+__device__ __forceinline__ void st_cluster_v4(uint32_t cluster_addr, uint4 v) {
+  asm volatile("st.shared::cluster.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(cluster_addr),
+               "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
 // TMA tile load for a CTA pair: data lands in this CTA's shared memory, the
 // completion is signalled on `bar`, which may live in the peer CTA.
 __device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap* map,

@@ -151,8 +151,8 @@ constexpr uint32_t kPairWarpArrivals = 2 * kSoftmaxWarps;
 constexpr uint32_t kPairWgArrivals = kSoftmaxWarps;  // 4 warps of one warpgroup x 2 CTAs
 constexpr uint32_t kItemConsumers = 2 * (1 + kSoftmaxWarps);
 
-constexpr uint32_t kOffItemSlots = kOffBar + kNumBars * 8;  // 2 x int32
-constexpr uint32_t kOffTmemSlot = kOffItemSlots + 8;
+constexpr uint32_t kOffItemSlots = (kOffBar + kNumBars * 8 + 15) & ~15u;  // 2 x ItemRec
+constexpr uint32_t kOffTmemSlot = kOffItemSlots + 2 * 64;
 constexpr uint32_t kOffAbort = kOffTmemSlot + 4;
 constexpr uint32_t kOffSplitLast = kOffAbort + 4;
 // (row max, row sum) exchange between the two softmax warpgroups at the
@@ -194,10 +194,10 @@ struct Shared {
   __device__ volatile int* abort_flag() const {
     return reinterpret_cast<volatile int*>(base + kOffAbort);
   }
-  __device__ volatile int32_t* item_slot(uint32_t i) const {
-    return reinterpret_cast<volatile int32_t*>(base + kOffItemSlots) + i;
+  __device__ uint4* item_slot(uint32_t i) const {
+    return reinterpret_cast<uint4*>(base + kOffItemSlots + 64 * i);
   }
-  __device__ uint32_t item_slot_addr(uint32_t i) const { return base_u32 + kOffItemSlots + 4 * i; }
+  __device__ uint32_t item_slot_addr(uint32_t i) const { return base_u32 + kOffItemSlots + 64 * i; }
 };
 
 __device__ __forceinline__ void raise_status(uint32_t bits) {
@@ -302,13 +302,38 @@ __device__ __forceinline__ void add2(float& s0, float& s1, float a0, float a1) {
 }
 
 // ------------------------------------------------------------ scheduler ring
-// Item indices flow from CTA 0's producer to every consumer through a
-// 2-slot ring in each CTA's shared memory.  Consumers in CTA 0 release on
-// their own item_empty, consumers in CTA 1 on CTA 0's (remote arrive).
-__device__ __forceinline__ bool take_item(const Shared& sh, uint32_t n, int32_t* idx) {
+// Work items flow from CTA 0's producer to every consumer through a 2-slot
+// ring in each CTA's shared memory.  A slot holds an item record: the item
+// index (total_items or above ends the kernel), the decoded item and its
+// block's tile geometry, decoded once by the scheduler so that no consumer
+// repeats that integer arithmetic.  Consumers in CTA 0 release on their own
+// item_empty, consumers in CTA 1 on CTA 0's (remote arrive).
+struct alignas(16) ItemRec {
+  int32_t idx;
+  tpsa_item it;
+  BlockTiles bt;
+  int32_t pad;
+};
+static_assert(sizeof(ItemRec) == 64, "an item record is four 16-byte words");
+
+__device__ __forceinline__ ItemRec make_item_rec(const tpsa_plan& p, int32_t idx) {
+  ItemRec rec;
+  memset(&rec, 0, sizeof(rec));
+  rec.idx = idx;
+  if (idx < p.total_items) {
+    rec.it = decode_item(p, idx);
+    rec.bt = block_tiles(p, rec.it.block);
+  }
+  return rec;
+}
+
+__device__ __forceinline__ bool take_item(const Shared& sh, uint32_t n, ItemRec* rec) {
   const uint32_t slot = n % 2;
   if (!wait_bar<true>(sh, sh.bar(kBarItemFull + slot), (n / 2) & 1)) return false;
-  *idx = *sh.item_slot(slot);
+  const uint4* src = sh.item_slot(slot);
+  uint4* dst = reinterpret_cast<uint4*>(rec);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) dst[j] = src[j];
   return true;
 }
 
@@ -331,25 +356,30 @@ __device__ void producer_role(const KernelArgs& a, const Shared& sh,
   TPSA_TRACE_STATE;
   int32_t next = r == 0 ? atomicAdd(a.ctl + kCtlNextItem, 1) : 0;
   for (uint32_t n = 0; ok; ++n) {
-    int32_t idx;
+    ItemRec rec;
     const uint32_t slot = n % 2;
     if (r == 0) {
-      idx = next;
+      rec = make_item_rec(p, next);
       if (!wait_bar(sh, sh.bar(kBarItemEmpty + slot), ((n / 2) & 1) ^ 1)) break;
-      *sh.item_slot(slot) = idx;
-      ptx::st_cluster_u32(ptx::mapa(sh.item_slot_addr(slot), 1), static_cast<uint32_t>(idx));
+      const uint4* words = reinterpret_cast<const uint4*>(&rec);
+      const uint32_t peer = ptx::mapa(sh.item_slot_addr(slot), 1);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        sh.item_slot(slot)[j] = words[j];
+        ptx::st_cluster_v4(peer + 16 * j, words[j]);
+      }
       ptx::mbar_arrive(sh.bar(kBarItemFull + slot));
       ptx::mbar_arrive_cluster_release(ptx::mapa(sh.bar(kBarItemFull + slot), 1));
-      if (idx >= p.total_items) break;
+      if (rec.idx >= p.total_items) break;
       next = atomicAdd(a.ctl + kCtlNextItem, 1);  // latency hidden by the loads below
     } else {
-      if (!take_item(sh, n, &idx)) break;
+      if (!take_item(sh, n, &rec)) break;
       release_item(sh, n);
-      if (idx >= p.total_items) break;
+      if (rec.idx >= p.total_items) break;
     }
-    if (r == 0) TPSA_TR(0, 20, idx);
-    const tpsa_item it = decode_item(p, idx);
-    const BlockTiles bt = block_tiles(p, it.block);
+    if (r == 0) TPSA_TR(0, 20, rec.idx);
+    const tpsa_item& it = rec.it;
+    const BlockTiles& bt = rec.bt;
 
     // Q: this CTA's 128 rows (64 tokens x query heads 4h + 2r, 4h + 2r + 1).
     const uint32_t qb = q_iter % 2;
@@ -361,7 +391,7 @@ __device__ void producer_role(const KernelArgs& a, const Shared& sh,
                             sh.bar0(kBarQFull + qb));
     }
     ++q_iter;
-    if (r == 0) TPSA_TR(0, 21, idx);
+    if (r == 0) TPSA_TR(0, 21, rec.idx);
 
     for (int32_t t = it.tile_begin; t < it.tile_end && ok; ++t) {
       int32_t k0, w;
@@ -486,15 +516,15 @@ __device__ void mma_role(const KernelArgs& a, const Shared& sh, uint32_t tmem, i
   };
 
   for (uint32_t n_item = 0; ok; ++n_item) {
-    int32_t idx = 0;
-    const bool got = take_item(sh, n_item, &idx);
+    ItemRec rec;
+    const bool got = take_item(sh, n_item, &rec);
     if (!__all_sync(0xffffffffu, got)) break;
     __syncwarp();
     if (lane == 0) release_item(sh, n_item);
-    if (idx >= p.total_items) break;
-    if (lane == 0) TPSA_TR(1, 10, idx);
-    const tpsa_item it = decode_item(p, idx);
-    const BlockTiles bt = block_tiles(p, it.block);
+    if (rec.idx >= p.total_items) break;
+    if (lane == 0) TPSA_TR(1, 10, rec.idx);
+    const tpsa_item& it = rec.it;
+    const BlockTiles& bt = rec.bt;
     const int32_t ntiles = it.tile_end - it.tile_begin;
     const uint32_t qb = q_iter % 2;
     if (!warp_wait(sh.bar(kBarQFull + qb), (q_iter / 2) & 1)) break;
@@ -811,9 +841,10 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
   const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
   const int32_t hq = p.kv_heads * kGroupSize;
   const bool visit = a.visited != nullptr;
-  // own: tiles of this warpgroup so far (tile gt = 2 * own + wg); pv_items:
-  // items in which this warpgroup had tiles (one PV-done phase each).
-  uint32_t g = 0, own = 0, pv_items = 0, split_iter = 0, xc = 0;
+  // own: tiles of this warpgroup so far (tile gt = 2 * own + wg);
+  // pv_items0/1: items in which warpgroup 0/1 had tiles (one PV-done phase
+  // each on that warpgroup's barrier).
+  uint32_t g = 0, own = 0, pv_items0 = 0, pv_items1 = 0, split_iter = 0, xc = 0;
   volatile int* split_last = reinterpret_cast<volatile int*>(sh.base + kOffSplitLast);
   uint32_t tr_sm = 0;  // trace counter (used only with TPSA_TRACE)
 #define tr_n_ tr_sm
@@ -824,14 +855,15 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
   cx.o_addr = o_base + wg * 128;
 
   for (uint32_t n_item = 0;; ++n_item) {
-    int32_t idx = 0;
-    const bool got = take_item(sh, n_item, &idx);
+    ItemRec rec;
+    const bool got = take_item(sh, n_item, &rec);
     if (!__all_sync(0xffffffffu, got)) break;
     __syncwarp();
     if (lane == 0) release_item(sh, n_item);
-    if (idx >= p.total_items) break;
-    const tpsa_item it = decode_item(p, idx);
-    const BlockTiles bt = block_tiles(p, it.block);
+    if (rec.idx >= p.total_items) break;
+    const int32_t idx = rec.idx;
+    const tpsa_item& it = rec.it;
+    const BlockTiles& bt = rec.bt;
     const int32_t tok = bt.q_begin + row / 2;
     cx.q = tok < p.seq_len ? tok : p.seq_len - 1;
     cx.sparse = row_is_sparse(p, tok);
@@ -871,17 +903,20 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
     }
     if (!ok) break;
     g += static_cast<uint32_t>(ntiles);
-    // This warpgroup's O is final once its last PV of the item completed
-    // (signalled once per item in which the warpgroup had tiles).
-    if (!first) {
-      const bool pv_ok = wait_bar(sh, sh.bar(kBarPvDone + wg), pv_items & 1);
+    // O0 and O1 are final once each warpgroup's last PV of the item
+    // completed (signalled once per item in which that warpgroup had tiles;
+    // both warpgroups observe both signals).
+    if (has_wg0) {
+      const bool pv_ok = wait_bar(sh, sh.bar(kBarPvDone + 0), pv_items0 & 1);
       if (!__all_sync(0xffffffffu, pv_ok)) break;
-      ++pv_items;
+      ++pv_items0;
+    }
+    if (has_wg1) {
+      const bool pv_ok = wait_bar(sh, sh.bar(kBarPvDone + 1), pv_items1 & 1);
+      if (!__all_sync(0xffffffffu, pv_ok)) break;
+      ++pv_items1;
     }
     if (row == 0 && r == 0) TPSA_TR(2 + wg, 8, 0);
-    // The exchange also orders the other warpgroup's final-PV observation
-    // before this warpgroup reads the other O buffer.
-    ptx::tc_fence_before();
     float m_o, l_o;
     if (!exchange_ml(sh, xc, wg, row, lane, st.m_run, st.l_run, &m_o, &l_o)) break;
     ptx::tc_fence_after();
@@ -905,6 +940,10 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
     const int32_t base_h = it.kv_head * kGroupSize + 2 * static_cast<int32_t>(r);
     uint8_t* stage = sh.base + kOffStage + (warp - kFirstSoftmaxWarp) * kStageBytesPerWarp;
     const float inv = 1.0f / l_total;
+    // Both 32-column chunks are merged into registers first and the O
+    // buffers released, so the next item's PVs need not wait for the
+    // stores.
+    float om[2][32];
 #pragma unroll
     for (int c = 0; c < 2; ++c) {
       const uint32_t col = static_cast<uint32_t>(wg * 64 + 32 * c);
@@ -912,12 +951,18 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
       if (has_wg0) ptx::tmem_ld32(o_base + col, x0);
       if (has_wg1) ptx::tmem_ld32(o_base + 128 + col, x1);
       ptx::tmem_wait_ld();
-      float o[32];
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
         const float v0 = has_wg0 ? a0 * __uint_as_float(x0[j]) : 0.0f;
-        o[j] = has_wg1 ? fmaf(a1, __uint_as_float(x1[j]), v0) : v0;
+        om[c][j] = has_wg1 ? fmaf(a1, __uint_as_float(x1[j]), v0) : v0;
       }
+    }
+    ptx::tc_fence_before();
+    warp_arrive0(sh, kBarOEmpty, lane);
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      const uint32_t col = static_cast<uint32_t>(wg * 64 + 32 * c);
+      const float (&o)[32] = om[c];
       if (!split) {
         store_rows_bf16(o, inv, stage, lane, a.out, base_q, base_h, hq, p.query_tokens,
                         static_cast<int32_t>(col));
@@ -926,8 +971,6 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
         for (int j = 0; j < 32; ++j) slot[(col + j) * kSlotRows + srow] = o[j];
       }
     }
-    ptx::tc_fence_before();
-    warp_arrive0(sh, kBarOEmpty, lane);
     if (row == 0 && r == 0) TPSA_TR(2 + wg, 5, 0);
     if (!split) continue;
 
