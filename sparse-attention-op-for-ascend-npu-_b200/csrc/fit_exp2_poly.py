@@ -1,5 +1,5 @@
 #!/usr/bin/env python3
-"""Fit the polynomial used by the kernel's FMA-pipe exp2 (poly_exp2 in
+"""Fit the polynomial used by the kernel's FMA-pipe exp2 (poly_exp2_x2 in
 tpsa_kernel.cu).
 
 Method: Cody-Waite style range reduction x = n + f with n = round(x),

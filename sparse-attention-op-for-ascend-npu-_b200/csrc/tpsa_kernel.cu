@@ -38,7 +38,7 @@
 //
 // Softmax arithmetic: scores are scaled into the log2 domain with one fused
 // multiply-add, exponentiated with ex2.approx (MUFU) for 3 of every 4 column
-// pairs and with poly_exp2 (FMA pipe) for the fourth, summed in fp32, and
+// pairs and with poly_exp2_x2 (FMA pipe) for the fourth, summed in fp32, and
 // rounded to bf16 (round-to-nearest-even) for the PV product, as the
 // reference does (vendor block_epilogue_online_softmax.hpp:886-906).
 #include <cuda.h>
@@ -112,7 +112,12 @@ static_assert(128 * kControlRegs + 256 * kSoftmaxRegs <= 384 * 168, "register sp
 constexpr uint32_t kTmemCols = 512;
 constexpr uint64_t kWaitTimeoutNs = 1000000000ull;  // 1 s per wait
 constexpr uint64_t kAbortSettleNs = 200000ull;      // let in-flight TMA land
-constexpr float kRescaleLog2 = 8.0f;  // lazy O rescale threshold (log2 units)
+constexpr float kRescaleLog2 = 8.0f;
+// Column pairs c (of 16 per 32-column chunk) whose exponentials use the FMA
+// pipe polynomial rather than MUFU ex2: bit c set.
+#ifndef TPSA_POLY_MASK
+#define TPSA_POLY_MASK 0x8888u
+#endif  // lazy O rescale threshold (log2 units)
 constexpr uint16_t kPairMask = 0x3;
 
 // Shared memory per CTA (offsets from a 1024-byte aligned base).
@@ -254,22 +259,6 @@ __device__ __forceinline__ float mufu_exp2(float x) {
   return y;
 }
 
-// 2^x on the FMA/ALU pipes: x = n + f with n = round(x), f in [-1/2, 1/2];
-// 2^f by a degree-3 minimax polynomial (Remez fit, max relative error
-// 7.5e-5, coefficients from csrc/fit_exp2_poly.py); 2^n added to the
-// exponent field.  x is clamped at -127.5 so that 2^n underflows the
-// exponent for any x <= -127.5 (and -inf) and the integer max returns +0.
-__device__ __forceinline__ float poly_exp2(float x) {
-  x = fmaxf(x, -127.5f);
-  const float t = x + 12582912.0f;  // 1.5 * 2^23: round(x) in the low bits
-  const float f = x - (t - 12582912.0f);
-  float p = fmaf(0.0551716685f, f, 0.2426111251f);
-  p = fmaf(p, f, 0.6932609677f);
-  p = fmaf(p, f, 0.9999280572f);
-  const int32_t bits = __float_as_int(p) + (__float_as_int(t) << 23);
-  return __int_as_float(max(bits, 0));
-}
-
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
@@ -299,6 +288,53 @@ __device__ __forceinline__ void add2(float& s0, float& s1, float a0, float a1) {
   asm("mov.b64 %0, {%1, %2};" : "=l"(av) : "f"(a0), "f"(a1));
   asm("add.rn.f32x2 %0, %0, %1;" : "+l"(sv) : "l"(av));
   asm("mov.b64 {%0, %1}, %2;" : "=f"(s0), "=f"(s1) : "l"(sv));
+}
+
+// Packed f32x2 helpers on 64-bit register pairs.
+__device__ __forceinline__ uint64_t pk2(float a, float b) {
+  uint64_t v;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "f"(a), "f"(b));
+  return v;
+}
+__device__ __forceinline__ void unpk2(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t add2v(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t sub2v(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t fma2v(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+
+// (2^x0, 2^x1) on the FMA and ALU pipes, the floating-point steps two lanes
+// per packed f32x2 instruction: x = n + f with n = round(x) (magic-number
+// rounding) and f in [-1/2, 1/2]; 2^f by a degree-3 minimax polynomial (Remez
+// fit, max relative error 7.5e-5, coefficients from csrc/fit_exp2_poly.py);
+// 2^n added to the exponent field.  x is clamped at -127.5 so that 2^n
+// underflows the exponent for any x <= -127.5 (and -inf), and the integer
+// max returns +0 there.
+__device__ __forceinline__ void poly_exp2_x2(float x0, float x1, float& e0, float& e1) {
+  const uint64_t xv = pk2(fmaxf(x0, -127.5f), fmaxf(x1, -127.5f));
+  const uint64_t magic = pk2(12582912.0f, 12582912.0f);  // 1.5 * 2^23
+  const uint64_t t = add2v(xv, magic);
+  const uint64_t f = sub2v(xv, sub2v(t, magic));
+  uint64_t q = fma2v(pk2(0.0551716685f, 0.0551716685f), f, pk2(0.2426111251f, 0.2426111251f));
+  q = fma2v(q, f, pk2(0.6932609677f, 0.6932609677f));
+  q = fma2v(q, f, pk2(0.9999280572f, 0.9999280572f));
+  float q0, q1, t0, t1;
+  unpk2(q, q0, q1);
+  unpk2(t, t0, t1);
+  e0 = __int_as_float(max(__float_as_int(q0) + (__float_as_int(t0) << 23), 0));
+  e1 = __int_as_float(max(__float_as_int(q1) + (__float_as_int(t1) << 23), 0));
 }
 
 // ------------------------------------------------------------ scheduler ring
@@ -760,9 +796,8 @@ __device__ __forceinline__ void softmax_tile(const SoftmaxCtx& cx, int32_t k0, i
         float x0, x1;
         fma2(v[2 * c], v[2 * c + 1], p.scale_log2, neg_mb, x0, x1);
         float e0, e1;
-        if ((c & 3) == 3) {
-          e0 = poly_exp2(x0);
-          e1 = poly_exp2(x1);
+        if ((TPSA_POLY_MASK >> c) & 1u) {
+          poly_exp2_x2(x0, x1, e0, e1);
         } else {
           e0 = mufu_exp2(x0);
           e1 = mufu_exp2(x1);
