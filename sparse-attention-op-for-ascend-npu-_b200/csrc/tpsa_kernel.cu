@@ -103,10 +103,10 @@ namespace {
 constexpr int kNumThreads = 384;
 constexpr int kSoftmaxWarps = 8;  // two warpgroups, alternate key tiles
 constexpr int kFirstSoftmaxWarp = 4;
-// Register split (setmaxnreg): the control warpgroup (warps 0-3) keeps 48
+// Register split (setmaxnreg): the control warpgroup (warps 0-3) keeps 56
 // registers a thread, the two softmax warpgroups 224, within the launch's
-// 384 x 168: 128 x 48 + 256 x 224 = 63488.
-constexpr uint32_t kControlRegs = 48;
+// 384 x 168: 128 x 56 + 256 x 224 = 64512.
+constexpr uint32_t kControlRegs = 56;
 constexpr uint32_t kSoftmaxRegs = 224;
 static_assert(128 * kControlRegs + 256 * kSoftmaxRegs <= 384 * 168, "register split");
 constexpr uint32_t kTmemCols = 512;
@@ -348,7 +348,10 @@ struct alignas(16) ItemRec {
   int32_t idx;
   tpsa_item it;
   BlockTiles bt;
-  int32_t pad;
+  // Item tiles only 64 keys wide (all others are 128): bit 0 the item's
+  // tile 0, bit 1 its tile 1, bit 2 its last tile (the sink tile and a band
+  // or key range that starts or ends half-way through a page).
+  uint32_t narrow;
 };
 static_assert(sizeof(ItemRec) == 64, "an item record is four 16-byte words");
 
@@ -359,6 +362,16 @@ __device__ __forceinline__ ItemRec make_item_rec(const tpsa_plan& p, int32_t idx
   if (idx < p.total_items) {
     rec.it = decode_item(p, idx);
     rec.bt = block_tiles(p, rec.it.block);
+    const int32_t last = rec.it.tile_end - rec.it.tile_begin - 1;
+    int32_t k0, w;
+    tile_keys(rec.bt, rec.it.tile_begin, &k0, &w);
+    rec.narrow |= w < kTileKeys ? 1u : 0u;
+    if (last >= 1) {
+      tile_keys(rec.bt, rec.it.tile_begin + 1, &k0, &w);
+      rec.narrow |= w < kTileKeys ? 2u : 0u;
+    }
+    tile_keys(rec.bt, rec.it.tile_begin + last, &k0, &w);
+    rec.narrow |= w < kTileKeys ? 4u : 0u;
   }
   return rec;
 }
@@ -505,50 +518,70 @@ __device__ void producer_role(const KernelArgs& a, const Shared& sh,
 // are warp-uniform) and one elected lane issues each tcgen05 instruction.
 __device__ void mma_role(const KernelArgs& a, const Shared& sh, uint32_t tmem, int lane) {
   const tpsa_plan& p = a.plan;
-  uint32_t ring = 0, q_iter = 0, g = 0, item_iter = 0;
-  bool ok = true;
   TPSA_TRACE_STATE;
+  // tcgen05.mma issue blocks once about three MMAs are queued, so this warp's
+  // own instructions between MMA batches leave the tensor pipe idle.  The
+  // loop below therefore keeps its per-tile work to barrier waits, commits
+  // and additions to operands prepared once: descriptor bases, barrier
+  // addresses, instruction descriptors and incremental ring positions.
+  const uint32_t bar_kv_full = sh.bar(kBarKVFull), bar_kv_empty = sh.bar(kBarKVEmpty);
+  const uint32_t bar_s_full = sh.bar(kBarSFull), bar_p_full = sh.bar(kBarPFull);
+  const uint32_t bar_pv_done = sh.bar(kBarPvDone), bar_q_full = sh.bar(kBarQFull);
+  const uint32_t bar_q_empty = sh.bar(kBarQEmpty), bar_o_empty = sh.bar(kBarOEmpty);
+  // Descriptor start addresses are in 16-byte units.
+  const uint64_t q_desc0 = ptx::smem_desc_sw128(sh.base_u32 + kOffQ, 16, 1024);
+  const uint64_t k_desc0 = ptx::smem_desc_sw128(sh.base_u32 + kOffKV, 16, 1024);
+  const uint64_t v_desc0 =
+      ptx::smem_desc_sw128(sh.base_u32 + kOffKV + kVOffset, kKHalfBytes, 1024);
+  constexpr uint32_t kSlotUnits = kRingSlotBytes >> 4;
+  constexpr uint32_t kQUnits = kQBytes >> 4;
+  constexpr uint32_t kIdQk128 = ptx::idesc_bf16_f32(256, 128, 0);
+  constexpr uint32_t kIdQk64 = ptx::idesc_bf16_f32(256, 64, 0);
+  constexpr uint32_t kIdPv = ptx::idesc_bf16_f32(256, 128, 1);
 
   auto warp_wait = [&](uint32_t bar, uint32_t parity) -> bool {
     return __all_sync(0xffffffffu, wait_bar(sh, bar, parity));
   };
-  // S(gt) = Q K(gt)^T into S buffer gt % 2 (M = 256 over the pair, N = w).
-  auto issue_qk = [&](uint32_t qb, uint32_t kslot, uint32_t gt, int32_t w) {
-    const uint32_t d = tmem + (gt % 2) * 128;
-    const uint32_t idesc = ptx::idesc_bf16_f32(256, static_cast<uint32_t>(w), 0);
-    const uint64_t qd = ptx::smem_desc_sw128(sh.base_u32 + kOffQ + qb * kQBytes, 16, 1024);
-    const uint64_t kd =
-        ptx::smem_desc_sw128(sh.base_u32 + kOffKV + kslot * kRingSlotBytes, 16, 1024);
+  // S(buf) = Q K^T for the key tile in ring slot `slot` (M = 256 over the
+  // pair, N = 128 or 64).
+  auto issue_qk = [&](uint64_t qd, uint32_t slot, uint32_t buf, bool narrow) {
+    const uint32_t d = tmem + (buf << 7);
+    const uint32_t idesc = narrow ? kIdQk64 : kIdQk128;
+    const uint64_t kd = k_desc0 + slot * kSlotUnits;
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-      // Descriptor start addresses are in 16-byte units.
       const uint64_t qo = (k / 4) * (kQHalfBytes >> 4) + (k % 4) * 2;
       const uint64_t ko = (k / 4) * (kKHalfBytes >> 4) + (k % 4) * 2;
       ptx::umma_ss_pair_elect(d, qd + qo, kd + ko, idesc, k > 0 ? 1u : 0u);
     }
   };
-  // O(gt % 2) += P(gt) V(gt): P from S buffer gt % 2 (bf16 pairs), V d-half
-  // per CTA.  Tile gt belongs to softmax warpgroup gt % 2, which owns S and O
-  // buffer gt % 2.
-  auto issue_pv = [&](uint32_t vslot, uint32_t gt, int32_t w, bool first) {
-    const uint32_t d = tmem + 256 + (gt % 2) * 128;
-    const uint32_t pa = tmem + (gt % 2) * 128;
-    constexpr uint32_t idesc = ptx::idesc_bf16_f32(256, 128, 1);
-    const uint64_t vd = ptx::smem_desc_sw128(
-        sh.base_u32 + kOffKV + vslot * kRingSlotBytes + kVOffset, kKHalfBytes, 1024);
-    if (w == kTileKeys) {
+  // O(buf) += P(buf) V: P (bf16 pairs) over the first half of S buffer buf,
+  // V the d-half of this CTA in ring slot `slot`.  Tile gt belongs to
+  // softmax warpgroup buf = gt % 2, which owns S and O buffer buf.
+  auto issue_pv = [&](uint32_t slot, uint32_t buf, bool narrow, bool first) {
+    const uint32_t d = tmem + 256 + (buf << 7);
+    const uint32_t pa = tmem + (buf << 7);
+    const uint64_t vd = v_desc0 + slot * kSlotUnits;
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        ptx::umma_ts_pair_elect(d, pa + k * 8, vd + k * (2048 >> 4), idesc,
-                                (first && k == 0) ? 0u : 1u);
-      }
-    } else {
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        ptx::umma_ts_pair_elect(d, pa + k * 8, vd + k * (2048 >> 4), idesc,
+    for (int k = 0; k < 8; ++k) {
+      if (k < 4 || !narrow) {
+        ptx::umma_ts_pair_elect(d, pa + k * 8, vd + k * (2048 >> 4), kIdPv,
                                 (first && k == 0) ? 0u : 1u);
       }
     }
+  };
+
+  // Ring cursors: the slot and phase of the next tile whose K/V is awaited
+  // (QK), and the slot of the next tile whose PV is issued (two tiles
+  // behind within an item).
+  uint32_t slot_q = 0, phase_q = 0, slot_v = 0, q_iter = 0, gt = 0, item_iter = 0;
+  bool ok = true;
+  auto next_q = [&]() {
+    slot_q = (slot_q + 1) & (kRing - 1);
+    phase_q ^= slot_q == 0 ? 1u : 0u;
+  };
+  auto wait_kv = [&]() -> bool {
+    return warp_wait(bar_kv_full + 8 * slot_q, phase_q);
   };
 
   for (uint32_t n_item = 0; ok; ++n_item) {
@@ -559,67 +592,58 @@ __device__ void mma_role(const KernelArgs& a, const Shared& sh, uint32_t tmem, i
     if (lane == 0) release_item(sh, n_item);
     if (rec.idx >= p.total_items) break;
     if (lane == 0) TPSA_TR(1, 10, rec.idx);
-    const tpsa_item& it = rec.it;
-    const BlockTiles& bt = rec.bt;
-    const int32_t ntiles = it.tile_end - it.tile_begin;
-    const uint32_t qb = q_iter % 2;
-    if (!warp_wait(sh.bar(kBarQFull + qb), (q_iter / 2) & 1)) break;
+    const int32_t ntiles = rec.it.tile_end - rec.it.tile_begin;
+    const int32_t last = ntiles - 1;
+    const uint32_t narrow = rec.narrow;
+    auto is_narrow = [&](int32_t t) -> bool {
+      return (t < 2 && ((narrow >> t) & 1u)) || (t == last && (narrow & 4u));
+    };
+    const uint32_t qb = q_iter & 1;
+    if (!warp_wait(bar_q_full + 8 * qb, (q_iter >> 1) & 1)) break;
     ++q_iter;
     ptx::tc_fence_after();
-    // Ring position of tile t: base + t (K and V of a tile share a slot,
-    // which PV(t) releases).
-    const uint32_t rbase = ring;
-    ring += static_cast<uint32_t>(ntiles);
+    const uint64_t qd = q_desc0 + qb * kQUnits;
 
     // QK for the first two tiles.
-    for (int32_t t = 0; t < 2 && t < ntiles && ok; ++t) {
-      int32_t k0, w;
-      tile_keys(bt, it.tile_begin + t, &k0, &w);
-      const uint32_t kr = rbase + t;
-      if (!warp_wait(sh.bar(kBarKVFull + ring_slot(kr)), ring_parity(kr))) { ok = false; break; }
+    for (int32_t t = 0; t < 2 && t < ntiles; ++t) {
+      if (!wait_kv()) { ok = false; break; }
       ptx::tc_fence_after();
-      issue_qk(qb, ring_slot(kr), g + t, w);
-      ptx::umma_commit_pair_mc_elect(sh.bar(kBarSFull + (g + t) % 2), kPairMask);
-      if (t == ntiles - 1) ptx::umma_commit_pair_mc_elect(sh.bar(kBarQEmpty + qb), kPairMask);
+      issue_qk(qd, slot_q, (gt + t) & 1, is_narrow(t));
+      ptx::umma_commit_pair_mc_elect(bar_s_full + 8 * ((gt + t) & 1), kPairMask);
+      if (t == last) ptx::umma_commit_pair_mc_elect(bar_q_empty + 8 * qb, kPairMask);
+      next_q();
     }
-    for (int32_t n = 0; n < ntiles && ok; ++n) {
-      int32_t k0, w;
-      tile_keys(bt, it.tile_begin + n, &k0, &w);
-      const uint32_t vr = rbase + n;
+    for (int32_t n = 0; n < ntiles && ok; ++n, ++gt) {
+      const uint32_t buf = gt & 1;
       if (lane == 0) TPSA_TR(1, 13, n);
-      if (n == 0 && item_iter > 0 && !warp_wait(sh.bar(kBarOEmpty), (item_iter - 1) & 1)) {
+      if (n == 0 && item_iter > 0 && !warp_wait(bar_o_empty, (item_iter - 1) & 1)) {
         ok = false;
         break;
       }
-      const uint32_t gt = g + static_cast<uint32_t>(n);
-      if (!warp_wait(sh.bar(kBarPFull + gt % 2), (gt / 2) & 1)) { ok = false; break; }
+      if (!warp_wait(bar_p_full + 8 * buf, (gt >> 1) & 1)) { ok = false; break; }
       if (lane == 0) TPSA_TR(1, 14, n);
       ptx::tc_fence_after();
       // Each warpgroup's first tile of the item overwrites its O buffer.
-      issue_pv(ring_slot(vr), gt, w, n < 2);
+      issue_pv(slot_v, buf, is_narrow(n), n < 2);
       if (lane == 0) TPSA_TR(1, 15, n);
-      ptx::umma_commit_pair_mc_elect(sh.bar(kBarKVEmpty + ring_slot(vr)), kPairMask);
+      ptx::umma_commit_pair_mc_elect(bar_kv_empty + 8 * slot_v, kPairMask);
+      slot_v = (slot_v + 1) & (kRing - 1);
       // A warpgroup learns that its earlier PVs completed from the S of its
       // next tile (whose QK is issued after them); only its last tile of the
       // item needs an explicit completion signal.
-      if (n + 2 >= ntiles) ptx::umma_commit_pair_mc_elect(sh.bar(kBarPvDone + gt % 2), kPairMask);
+      if (n + 2 > last) ptx::umma_commit_pair_mc_elect(bar_pv_done + 8 * buf, kPairMask);
       if (lane == 0) TPSA_TR(1, 16, n);
-      if (n + 2 < ntiles) {
-        int32_t k2, w2;
-        tile_keys(bt, it.tile_begin + n + 2, &k2, &w2);
-        const uint32_t kr = rbase + n + 2;
-        if (!warp_wait(sh.bar(kBarKVFull + ring_slot(kr)), ring_parity(kr))) { ok = false; break; }
+      if (n + 2 <= last) {
+        if (!wait_kv()) { ok = false; break; }
         if (lane == 0) TPSA_TR(1, 17, n + 2);
         ptx::tc_fence_after();
-        issue_qk(qb, ring_slot(kr), g + n + 2, w2);
+        issue_qk(qd, slot_q, buf, is_narrow(n + 2));
         if (lane == 0) TPSA_TR(1, 18, n + 2);
-        ptx::umma_commit_pair_mc_elect(sh.bar(kBarSFull + (g + n + 2) % 2), kPairMask);
-        if (n + 2 == ntiles - 1) {
-          ptx::umma_commit_pair_mc_elect(sh.bar(kBarQEmpty + qb), kPairMask);
-        }
+        ptx::umma_commit_pair_mc_elect(bar_s_full + 8 * buf, kPairMask);
+        if (n + 2 == last) ptx::umma_commit_pair_mc_elect(bar_q_empty + 8 * qb, kPairMask);
+        next_q();
       }
     }
-    g += static_cast<uint32_t>(ntiles);
     ++item_iter;
   }
   // All MMAs issued by this warp complete before TMEM is released.
