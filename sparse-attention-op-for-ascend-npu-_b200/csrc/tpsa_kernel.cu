@@ -58,27 +58,22 @@ namespace tpsa {
 
 __device__ uint32_t g_device_status = 0;
 
-// Optional event trace of cluster 0 (build with -DTPSA_TRACE; compiled out of
+// Optional event trace of one CTA pair (build with -DTPSA_TRACE, pair chosen by
+// TPSA_TRACE_CLUSTER; compiled out of
 // the library otherwise).  Each tracing thread owns one buffer and a register
 // counter, so a trace point is two plain stores and a clock read.
 #ifdef TPSA_TRACE
+#ifndef TPSA_TRACE_CLUSTER
+#define TPSA_TRACE_CLUSTER 0  // CTA pair whose events are recorded
+#endif
 constexpr uint32_t kTraceRoles = 4;
 constexpr uint32_t kTraceCap = 1u << 14;
 __device__ unsigned long long g_trace[kTraceRoles][kTraceCap][2];
 __device__ uint32_t g_trace_n[kTraceRoles];
 #define TPSA_TRACE_STATE uint32_t tr_n_ = 0
-#define TPSA_SM_TR(ev)                                                             \
-  do {                                                                             \
-    if (blockIdx.x == 0 && (threadIdx.x == 128 || threadIdx.x == 256) && trn < kTraceCap) {              \
-      g_trace[trole][trn][0] = static_cast<unsigned long long>(ev) << 32;          \
-      g_trace[trole][trn][1] = clock64();                                          \
-      ++trn;                                                                       \
-      g_trace_n[trole] = trn;                                                      \
-    }                                                                              \
-  } while (0)
 #define TPSA_TR(role, ev, arg)                                                    \
   do {                                                                            \
-    if (blockIdx.x < 2 && tr_n_ < kTraceCap) {                                    \
+    if ((blockIdx.x >> 1) == TPSA_TRACE_CLUSTER && tr_n_ < kTraceCap) {           \
       g_trace[role][tr_n_][0] = (static_cast<unsigned long long>(ev) << 32) |     \
                                 static_cast<uint32_t>(arg);                        \
       g_trace[role][tr_n_][1] = clock64();                                        \
@@ -93,9 +88,6 @@ __device__ uint32_t g_trace_n[kTraceRoles];
 #define TPSA_TR(role, ev, arg) \
   do {                         \
   } while (0)
-#define TPSA_SM_TR(ev) \
-  do {                 \
-  } while (0)
 #endif
 
 namespace {
@@ -109,7 +101,12 @@ constexpr int kFirstSoftmaxWarp = 4;
 constexpr uint32_t kControlRegs = 56;
 constexpr uint32_t kSoftmaxRegs = 224;
 static_assert(128 * kControlRegs + 256 * kSoftmaxRegs <= 384 * 168, "register split");
+// Tensor memory (512 columns, lane = row): three S buffers (P, as bf16
+// pairs, over columns 64-127 of each) and the O accumulator shared by both
+// softmax warpgroups.
 constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kNumSBufs = 3;
+constexpr uint32_t kTmemO = 384;
 constexpr uint64_t kWaitTimeoutNs = 1000000000ull;  // 1 s per wait
 constexpr uint64_t kAbortSettleNs = 200000ull;      // let in-flight TMA land
 constexpr float kRescaleLog2 = 8.0f;
@@ -136,37 +133,51 @@ enum BarId : uint32_t {
   kBarQEmpty = kBarQFull + 2,             // [2] both CTAs: Q buffer free
   kBarKVFull = kBarQEmpty + 2,            // [kRing] CTA 0: K and V of both CTAs landed
   kBarKVEmpty = kBarKVFull + kRing,       // [kRing] both: slot free (its PV done)
-  kBarSFull = kBarKVEmpty + kRing,        // [2] both: S buffer computed
-  kBarPFull = kBarSFull + 2,              // [2] CTA 0: P of a warpgroup's tile in TMEM
-  kBarPvDone = kBarPFull + 2,             // [2] both: PV of a warpgroup's tile completed
-  kBarOEmpty = kBarPvDone + 2,            // CTA 0: O0 and O1 read by both epilogues
+  kBarSFull = kBarKVEmpty + kRing,        // [3] both: S buffer computed
+  kBarPFull = kBarSFull + kNumSBufs,      // [3] CTA 0: P of the tile in the S buffer written
+  kBarPvDone = kBarPFull + kNumSBufs,     // [3] both: PV from the S buffer completed
+  kBarOEmpty = kBarPvDone + kNumSBufs,    // CTA 0: O read by the item's epilogue
   kBarItemFull = kBarOEmpty + 1,          // [2] both: item index written
   kBarItemEmpty = kBarItemFull + 2,       // [2] CTA 0: item index consumed
-  kBarSplitWritten = kBarItemEmpty + 2,   // per CTA: split partial written
-  kBarSplitDecided = kBarSplitWritten + 1,
-  kBarTail = kBarSplitDecided + 1,        // per CTA: V tail tile landed
+  kBarTail = kBarItemEmpty + 2,           // per CTA: V tail tile landed
   kBarDrain = kBarTail + 1,               // CTA 0: all MMAs complete
-  kBarWgX = kBarDrain + 1,                // per CTA: softmax warpgroups exchanged
   kNumBars
 };
-// Arrivals: p_full and o_empty take one per softmax warp of both CTAs;
-// item_empty takes the MMA issuer and 4 softmax warps of CTA 0 plus the
-// producer and 4 softmax warps of CTA 1.
+// Arrivals: p_full takes one per warp of the tile's softmax warpgroup in
+// both CTAs, o_empty one per softmax warp of both CTAs;
+// item_empty takes the producer, the MMA issuer and the 8 softmax warps of
+// CTA 0 plus the producer and the 8 softmax warps of CTA 1.
+constexpr uint32_t kPairWgArrivals = kSoftmaxWarps;  // 4 warps x 2 CTAs
 constexpr uint32_t kPairWarpArrivals = 2 * kSoftmaxWarps;
-constexpr uint32_t kPairWgArrivals = kSoftmaxWarps;  // 4 warps of one warpgroup x 2 CTAs
-constexpr uint32_t kItemConsumers = 2 * (1 + kSoftmaxWarps);
+constexpr uint32_t kItemConsumers = 2 * (1 + kSoftmaxWarps) + 1;
+// q_empty: the MMA issuer's commit after the item's last QK, plus one arrival
+// from each softmax warpgroup of this CTA once its output store has read the
+// buffer (the finished item's Q buffer stages its output rows).
+constexpr uint32_t kQEmptyArrivals = 3;
 
 constexpr uint32_t kOffItemSlots = (kOffBar + kNumBars * 8 + 15) & ~15u;  // 2 x ItemRec
 constexpr uint32_t kOffTmemSlot = kOffItemSlots + 2 * 64;
 constexpr uint32_t kOffAbort = kOffTmemSlot + 4;
-constexpr uint32_t kOffSplitLast = kOffAbort + 4;
-// (row max, row sum) exchange between the two softmax warpgroups at the
-// end of an item: float [2 buffers][2 warpgroups][2 values][128 rows].
-constexpr uint32_t kOffXchg = (kOffSplitLast + 4 + 15) & ~15u;
+constexpr uint32_t kOffSplitLast = kOffAbort + 4;  // int32 [2] (by split-item parity)
+// Monotonic uint32 counters in shared memory, one count per warp and event
+// (see softmax_role).
+enum CounterId : uint32_t {
+  kCntPub = 0,                  // [8] row values published by softmax warp (wg * 4 + quad)
+  kCntCon = kCntPub + 8,        // [8] partner values read by softmax warp (wg * 4 + quad)
+  kCntStaged = kCntCon + 8,     // [2] output rows of warpgroup wg staged for its TMA store
+  kCntSplitW = kCntStaged + 2,  // split partial written
+  kCntSplitD,                   // split merge decided (one count per split item)
+  kNumCounters
+};
+constexpr uint32_t kOffCounters = kOffSplitLast + 8;
+// Row values passed between the two warps that hold the same rows in the
+// two softmax warpgroups: float [2 publishers][kChanSlots][128 rows].
+constexpr uint32_t kChanSlots = 4;
+constexpr uint32_t kOffXchg = (kOffCounters + 4 * kNumCounters + 15) & ~15u;
 // Output staging: 2 KB per softmax warp (32 rows x 64 bytes), used to turn
 // row-per-thread results into coalesced global stores.
 constexpr uint32_t kStageBytesPerWarp = 32 * 64;
-constexpr uint32_t kOffStage = (kOffXchg + 2 * 2 * 2 * 128 * 4 + 127) & ~127u;
+constexpr uint32_t kOffStage = (kOffXchg + 2 * kChanSlots * 128 * 4 + 127) & ~127u;
 constexpr uint32_t kSmemUsed = kOffStage + 8 * kStageBytesPerWarp;
 constexpr uint32_t kSmemBytes = kSmemUsed + 1024;  // alignment slack
 static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
@@ -199,6 +210,7 @@ struct Shared {
   __device__ volatile int* abort_flag() const {
     return reinterpret_cast<volatile int*>(base + kOffAbort);
   }
+  __device__ uint32_t counter(uint32_t id) const { return base_u32 + kOffCounters + 4 * id; }
   __device__ uint4* item_slot(uint32_t i) const {
     return reinterpret_cast<uint4*>(base + kOffItemSlots + 64 * i);
   }
@@ -208,6 +220,25 @@ struct Shared {
 __device__ __forceinline__ void raise_status(uint32_t bits) {
   atomicOr(&g_device_status, bits);
 }
+
+#ifdef TPSA_TRACE
+// First wait that gave up: {set, block, thread, shared offset, parity or target}.
+__device__ uint32_t g_timeout_site[5];
+extern __shared__ uint8_t smem_raw[];
+__device__ __forceinline__ void note_timeout(uint32_t addr, uint32_t arg) {
+  if (atomicCAS(&g_timeout_site[0], 0u, 1u) == 0u) {
+    g_timeout_site[1] = blockIdx.x;
+    g_timeout_site[2] = threadIdx.x;
+    g_timeout_site[3] = addr - ((ptx::smem_u32(smem_raw) + 1023u) & ~1023u);
+    g_timeout_site[4] = arg;
+  }
+}
+#define TPSA_NOTE_TIMEOUT(addr, arg) note_timeout(addr, arg)
+#else
+#define TPSA_NOTE_TIMEOUT(addr, arg) \
+  do {                               \
+  } while (0)
+#endif
 
 // Bounded wait: gives up after kWaitTimeoutNs or as soon as another role of
 // this CTA has aborted; on timeout records TPSA_DEVICE_WAIT_TIMEOUT.
@@ -228,6 +259,7 @@ __device__ __forceinline__ bool wait_bar_slow(uint32_t bar, uint32_t parity,
     if (ptx::globaltimer_ns() - t0 > kWaitTimeoutNs) {
       *abort_flag = 1;
       raise_status(TPSA_DEVICE_WAIT_TIMEOUT);
+      TPSA_NOTE_TIMEOUT(bar, parity);
       return false;
     }
   }
@@ -248,6 +280,27 @@ __device__ __forceinline__ void drain_bar(uint32_t bar, uint32_t parity) {
       return;
     }
   }
+}
+
+// Bounded wait until the monotonic shared counter `id` reaches `target`
+// (wrap-safe comparison); gives up like wait_bar.
+__device__ __forceinline__ bool wait_count_at(const Shared& sh, uint32_t addr, uint32_t target) {
+  if (static_cast<int32_t>(ptx::ld_acquire_shared(addr) - target) >= 0) return true;
+  const uint64_t t0 = ptx::globaltimer_ns();
+  volatile int* abort_flag = sh.abort_flag();
+  while (static_cast<int32_t>(ptx::ld_acquire_shared(addr) - target) < 0) {
+    if (*abort_flag) return false;
+    if (ptx::globaltimer_ns() - t0 > kWaitTimeoutNs) {
+      *abort_flag = 1;
+      raise_status(TPSA_DEVICE_WAIT_TIMEOUT);
+      TPSA_NOTE_TIMEOUT(addr, target | 0x80000000u);
+      return false;
+    }
+  }
+  return true;
+}
+__device__ __forceinline__ bool wait_count(const Shared& sh, uint32_t id, uint32_t target) {
+  return wait_count_at(sh, sh.counter(id), target);
 }
 
 __device__ __forceinline__ uint32_t ring_slot(uint32_t r) { return r % kRing; }
@@ -386,8 +439,52 @@ __device__ __forceinline__ bool take_item(const Shared& sh, uint32_t n, ItemRec*
   return true;
 }
 
+// The fields of item record n the MMA issuer uses: its index, tile count
+// and narrow-tile bits.
+struct ItemBrief {
+  int32_t idx, ntiles;
+  uint32_t narrow;
+};
+__device__ __forceinline__ bool take_item_brief(const Shared& sh, uint32_t n, ItemBrief* b) {
+  const uint32_t slot = n % 2;
+  if (!wait_bar<true>(sh, sh.bar(kBarItemFull + slot), (n / 2) & 1)) return false;
+  const int32_t* w = reinterpret_cast<const int32_t*>(sh.item_slot(slot));
+  b->idx = w[offsetof(ItemRec, idx) / 4];
+  b->ntiles = w[(offsetof(ItemRec, it) + offsetof(tpsa_item, tile_end)) / 4] -
+              w[(offsetof(ItemRec, it) + offsetof(tpsa_item, tile_begin)) / 4];
+  b->narrow = static_cast<uint32_t>(w[offsetof(ItemRec, narrow) / 4]);
+  return true;
+}
+
 __device__ __forceinline__ void release_item(const Shared& sh, uint32_t n) {
   ptx::mbar_arrive_cluster(sh.bar0(kBarItemEmpty + n % 2));
+}
+
+// ------------------------------------------------------------ scheduler
+// One thread of CTA 0: takes work items from the grid-wide counter
+// (longest first), decodes each into an item record and publishes it into
+// the pair's two-slot item ring (both CTAs' copies), running up to two items
+// ahead of the slowest consumer.  The index past the last item tells every
+// consumer to stop.
+__device__ void scheduler_role(const KernelArgs& a, const Shared& sh) {
+  const tpsa_plan& p = a.plan;
+  int32_t next = atomicAdd(a.ctl + kCtlNextItem, 1);
+  for (uint32_t n = 0;; ++n) {
+    const uint32_t slot = n % 2;
+    const ItemRec rec = make_item_rec(p, next);
+    if (rec.idx < p.total_items) next = atomicAdd(a.ctl + kCtlNextItem, 1);
+    if (!wait_bar(sh, sh.bar(kBarItemEmpty + slot), ((n / 2) & 1) ^ 1)) break;
+    const uint4* words = reinterpret_cast<const uint4*>(&rec);
+    const uint32_t peer = ptx::mapa(sh.item_slot_addr(slot), 1);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      sh.item_slot(slot)[j] = words[j];
+      ptx::st_cluster_v4(peer + 16 * j, words[j]);
+    }
+    ptx::mbar_arrive(sh.bar(kBarItemFull + slot));
+    ptx::mbar_arrive_cluster_release(ptx::mapa(sh.bar(kBarItemFull + slot), 1));
+    if (rec.idx >= p.total_items) break;
+  }
 }
 
 // ------------------------------------------------------------ producer
@@ -403,29 +500,11 @@ __device__ void producer_role(const KernelArgs& a, const Shared& sh,
   uint32_t ring = 0, q_iter = 0, tail_iter = 0;
   bool ok = true;
   TPSA_TRACE_STATE;
-  int32_t next = r == 0 ? atomicAdd(a.ctl + kCtlNextItem, 1) : 0;
   for (uint32_t n = 0; ok; ++n) {
     ItemRec rec;
-    const uint32_t slot = n % 2;
-    if (r == 0) {
-      rec = make_item_rec(p, next);
-      if (!wait_bar(sh, sh.bar(kBarItemEmpty + slot), ((n / 2) & 1) ^ 1)) break;
-      const uint4* words = reinterpret_cast<const uint4*>(&rec);
-      const uint32_t peer = ptx::mapa(sh.item_slot_addr(slot), 1);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        sh.item_slot(slot)[j] = words[j];
-        ptx::st_cluster_v4(peer + 16 * j, words[j]);
-      }
-      ptx::mbar_arrive(sh.bar(kBarItemFull + slot));
-      ptx::mbar_arrive_cluster_release(ptx::mapa(sh.bar(kBarItemFull + slot), 1));
-      if (rec.idx >= p.total_items) break;
-      next = atomicAdd(a.ctl + kCtlNextItem, 1);  // latency hidden by the loads below
-    } else {
-      if (!take_item(sh, n, &rec)) break;
-      release_item(sh, n);
-      if (rec.idx >= p.total_items) break;
-    }
+    if (!take_item(sh, n, &rec)) break;
+    release_item(sh, n);
+    if (rec.idx >= p.total_items) break;
     if (r == 0) TPSA_TR(0, 20, rec.idx);
     const tpsa_item& it = rec.it;
     const BlockTiles& bt = rec.bt;
@@ -555,12 +634,11 @@ __device__ void mma_role(const KernelArgs& a, const Shared& sh, uint32_t tmem, i
       ptx::umma_ss_pair_elect(d, qd + qo, kd + ko, idesc, k > 0 ? 1u : 0u);
     }
   };
-  // O(buf) += P(buf) V: P (bf16 pairs) over the first half of S buffer buf,
-  // V the d-half of this CTA in ring slot `slot`.  Tile gt belongs to
-  // softmax warpgroup buf = gt % 2, which owns S and O buffer buf.
+  // O += P V: P (bf16 pairs) over columns 64-127 of S buffer buf, V the
+  // d-half of this CTA in ring slot `slot`.
   auto issue_pv = [&](uint32_t slot, uint32_t buf, bool narrow, bool first) {
-    const uint32_t d = tmem + 256 + (buf << 7);
-    const uint32_t pa = tmem + (buf << 7);
+    const uint32_t d = tmem + kTmemO;
+    const uint32_t pa = tmem + (buf << 7) + 64;
     const uint64_t vd = v_desc0 + slot * kSlotUnits;
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
@@ -571,80 +649,128 @@ __device__ void mma_role(const KernelArgs& a, const Shared& sh, uint32_t tmem, i
     }
   };
 
-  // Ring cursors: the slot and phase of the next tile whose K/V is awaited
-  // (QK), and the slot of the next tile whose PV is issued (two tiles
-  // behind within an item).
-  uint32_t slot_q = 0, phase_q = 0, slot_v = 0, q_iter = 0, gt = 0, item_iter = 0;
+  // The key tiles of all items form one stream over three S buffers (tile
+  // gt uses buffer gt % 3): after PV(t) this warp issues QK(t + 3), which may
+  // belong to a later item (S buffer t % 3 is free once PV(t), which reads
+  // its P, is issued).  Only the first PV of an item waits for the previous
+  // item's O to be released.  A QK cursor takes items from the ring; each QK
+  // leaves a control word for its tile's PV up to three tiles later.  The QK
+  // cursor stays within one item of the PV cursor: the Q buffer of item k + 2
+  // is released by the epilogue of item k, which needs item k's PVs.
+  enum : uint32_t {
+    kTNarrow = 1u,     // 64-key tile
+    kTFirst = 2u,      // first tile of its item (PV overwrites O)
+    kTItemStart = 4u,  // first tile of an item that is not the first item
+    kTItemOdd = 8u,    // with kTItemStart: the O-empty phase to wait for
+    kTIssued = 16u,    // a QK was issued (no control word otherwise)
+    kTItemShift = 8,   // bits 8 and up: the tile's item number (1-based)
+  };
+  uint32_t slot_q = 0, phase_q = 0, slot_v = 0, q_iter = 0;
+  uint32_t sb_q = 0, sb_v = 0, pass_v = 0;  // S buffers of the QK / PV cursors
+  uint32_t n_item = 0;                      // items taken from the ring
+  int32_t q_n = 0, q_ntiles = 0;
+  uint32_t q_narrow = 0, q_qb = 0;
+  uint64_t q_qd = q_desc0;
+  bool q_done = false;
   bool ok = true;
-  auto next_q = [&]() {
+  // Issues the next tile's QK and returns its control word (with kTIssued);
+  // 0 when no tile is left or a wait gave up (then ok is cleared).
+  auto next_qk = [&]() -> uint32_t {
+    if (q_n == q_ntiles) {
+      if (q_done) return 0;
+      ItemBrief rec;
+      const bool got = take_item_brief(sh, n_item, &rec);
+      if (!__all_sync(0xffffffffu, got)) {
+        ok = false;
+        return 0;
+      }
+      __syncwarp();
+      if (lane == 0) release_item(sh, n_item);
+      if (rec.idx >= p.total_items) {
+        q_done = true;
+        return 0;
+      }
+      if (lane == 0) TPSA_TR(1, 10, rec.idx);
+      ++n_item;
+      q_n = 0;
+      q_ntiles = rec.ntiles;
+      q_narrow = rec.narrow;
+      q_qb = q_iter & 1;
+      if (!warp_wait(bar_q_full + 8 * q_qb, (q_iter >> 1) & 1)) {
+        ok = false;
+        return 0;
+      }
+      ++q_iter;
+      q_qd = q_desc0 + q_qb * kQUnits;
+    }
+    const int32_t last = q_ntiles - 1;
+    const bool narrow =
+        (q_n < 2 && ((q_narrow >> q_n) & 1u)) || (q_n == last && (q_narrow & 4u));
+    if (!warp_wait(bar_kv_full + 8 * slot_q, phase_q)) {
+      ok = false;
+      return 0;
+    }
+    ptx::tc_fence_after();
+    issue_qk(q_qd, slot_q, sb_q, narrow);
+    ptx::umma_commit_pair_mc_elect(bar_s_full + 8 * sb_q, kPairMask);
+    if (q_n == last) ptx::umma_commit_pair_mc_elect(bar_q_empty + 8 * q_qb, kPairMask);
+    const uint32_t info = kTIssued | (narrow ? kTNarrow : 0u) | (q_n == 0 ? kTFirst : 0u) |
+                          (q_n == 0 && n_item > 1 ? kTItemStart : 0u) |
+                          (((n_item - 1) & 1) ? kTItemOdd : 0u) | (n_item << kTItemShift);
     slot_q = (slot_q + 1) & (kRing - 1);
     phase_q ^= slot_q == 0 ? 1u : 0u;
-  };
-  auto wait_kv = [&]() -> bool {
-    return warp_wait(bar_kv_full + 8 * slot_q, phase_q);
+    sb_q = sb_q == kNumSBufs - 1 ? 0 : sb_q + 1;
+    ++q_n;
+    return info;
   };
 
-  for (uint32_t n_item = 0; ok; ++n_item) {
-    ItemRec rec;
-    const bool got = take_item(sh, n_item, &rec);
-    if (!__all_sync(0xffffffffu, got)) break;
-    __syncwarp();
-    if (lane == 0) release_item(sh, n_item);
-    if (rec.idx >= p.total_items) break;
-    if (lane == 0) TPSA_TR(1, 10, rec.idx);
-    const int32_t ntiles = rec.it.tile_end - rec.it.tile_begin;
-    const int32_t last = ntiles - 1;
-    const uint32_t narrow = rec.narrow;
-    auto is_narrow = [&](int32_t t) -> bool {
-      return (t < 2 && ((narrow >> t) & 1u)) || (t == last && (narrow & 4u));
-    };
-    const uint32_t qb = q_iter & 1;
-    if (!warp_wait(bar_q_full + 8 * qb, (q_iter >> 1) & 1)) break;
-    ++q_iter;
+  // Control words of the (up to three) tiles whose QK is issued and whose
+  // PV is not, oldest first; 0 for none.
+  uint32_t info0 = 0, info1 = 0, info2 = 0;
+  int have = 0;
+  auto refill = [&]() {
+    while (ok && have < 3 && !q_done) {
+      // A QK that starts item n_item + 1 waits until the PV cursor is in
+      // item n_item.
+      if (q_n == q_ntiles && have > 0 && n_item > (info0 >> kTItemShift)) break;
+      const uint32_t info = next_qk();
+      if (info == 0) break;
+      if (have == 0) {
+        info0 = info;
+      } else if (have == 1) {
+        info1 = info;
+      } else {
+        info2 = info;
+      }
+      ++have;
+    }
+  };
+  while (true) {
+    refill();
+    if (!ok || have == 0) break;
+    if (info0 & kTItemStart) {
+      // O of the previous item (item index k - 1) has been read by its
+      // epilogue: phase (k - 2) & 1 of o_empty.
+      if (!warp_wait(bar_o_empty, (info0 & kTItemOdd) ? 0u : 1u)) { ok = false; break; }
+    }
+    if (!warp_wait(bar_p_full + 8 * sb_v, pass_v & 1)) { ok = false; break; }
+    if (lane == 0) TPSA_TR(1, 14, sb_v);
     ptx::tc_fence_after();
-    const uint64_t qd = q_desc0 + qb * kQUnits;
-
-    // QK for the first two tiles.
-    for (int32_t t = 0; t < 2 && t < ntiles; ++t) {
-      if (!wait_kv()) { ok = false; break; }
-      ptx::tc_fence_after();
-      issue_qk(qd, slot_q, (gt + t) & 1, is_narrow(t));
-      ptx::umma_commit_pair_mc_elect(bar_s_full + 8 * ((gt + t) & 1), kPairMask);
-      if (t == last) ptx::umma_commit_pair_mc_elect(bar_q_empty + 8 * qb, kPairMask);
-      next_q();
+    issue_pv(slot_v, sb_v, (info0 & kTNarrow) != 0, (info0 & kTFirst) != 0);
+    if (lane == 0) TPSA_TR(1, 15, sb_v);
+    ptx::umma_commit_pair_mc_elect(bar_kv_empty + 8 * slot_v, kPairMask);
+    ptx::umma_commit_pair_mc_elect(bar_pv_done + 8 * sb_v, kPairMask);
+    slot_v = (slot_v + 1) & (kRing - 1);
+    if (sb_v == kNumSBufs - 1) {
+      sb_v = 0;
+      ++pass_v;
+    } else {
+      ++sb_v;
     }
-    for (int32_t n = 0; n < ntiles && ok; ++n, ++gt) {
-      const uint32_t buf = gt & 1;
-      if (lane == 0) TPSA_TR(1, 13, n);
-      if (n == 0 && item_iter > 0 && !warp_wait(bar_o_empty, (item_iter - 1) & 1)) {
-        ok = false;
-        break;
-      }
-      if (!warp_wait(bar_p_full + 8 * buf, (gt >> 1) & 1)) { ok = false; break; }
-      if (lane == 0) TPSA_TR(1, 14, n);
-      ptx::tc_fence_after();
-      // Each warpgroup's first tile of the item overwrites its O buffer.
-      issue_pv(slot_v, buf, is_narrow(n), n < 2);
-      if (lane == 0) TPSA_TR(1, 15, n);
-      ptx::umma_commit_pair_mc_elect(bar_kv_empty + 8 * slot_v, kPairMask);
-      slot_v = (slot_v + 1) & (kRing - 1);
-      // A warpgroup learns that its earlier PVs completed from the S of its
-      // next tile (whose QK is issued after them); only its last tile of the
-      // item needs an explicit completion signal.
-      if (n + 2 > last) ptx::umma_commit_pair_mc_elect(bar_pv_done + 8 * buf, kPairMask);
-      if (lane == 0) TPSA_TR(1, 16, n);
-      if (n + 2 <= last) {
-        if (!wait_kv()) { ok = false; break; }
-        if (lane == 0) TPSA_TR(1, 17, n + 2);
-        ptx::tc_fence_after();
-        issue_qk(qd, slot_q, buf, is_narrow(n + 2));
-        if (lane == 0) TPSA_TR(1, 18, n + 2);
-        ptx::umma_commit_pair_mc_elect(bar_s_full + 8 * buf, kPairMask);
-        if (n + 2 == last) ptx::umma_commit_pair_mc_elect(bar_q_empty + 8 * qb, kPairMask);
-        next_q();
-      }
-    }
-    ++item_iter;
+    info0 = info1;
+    info1 = info2;
+    info2 = 0;
+    --have;
   }
   // All MMAs issued by this warp complete before TMEM is released.
   ptx::umma_commit_pair_elect(sh.bar(kBarDrain));
@@ -676,7 +802,6 @@ __device__ __forceinline__ void rescale_o(uint32_t o_addr, float factor) {
     for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * factor);
     ptx::tmem_st32(o_addr + 32 * c, r);
   }
-  ptx::tmem_wait_st();
 }
 
 // Bits c of the result: key kc + c (c < 32) is in the key set of query row
@@ -691,154 +816,222 @@ __device__ __forceinline__ uint32_t chunk_mask(int32_t q, bool sparse, int32_t k
   return m;
 }
 
-// Online-softmax state of one row over one warpgroup's tiles of an item.
-struct RowState {
-  float m_run;
-  float l_run;
-};
-
-// Publishes this warpgroup's (m, l) of the row and returns the other
-// warpgroup's.  `xc` counts exchanges; both warpgroups run the same sequence.
-__device__ __forceinline__ bool exchange_ml(const Shared& sh, uint32_t& xc, int wg, int row,
-                                            int lane, float m, float l, float* m_other,
-                                            float* l_other) {
-  volatile float* buf = reinterpret_cast<volatile float*>(sh.base + kOffXchg) + (xc & 1) * 512;
-  buf[wg * 256 + row] = m;
-  buf[wg * 256 + 128 + row] = l;
-  __syncwarp();
-  if (lane == 0) ptx::mbar_arrive(sh.bar(kBarWgX));
-  const bool ok = wait_bar(sh, sh.bar(kBarWgX), xc & 1);
-  ++xc;
-  if (!__all_sync(0xffffffffu, ok)) return false;
-  *m_other = buf[(1 - wg) * 256 + row];
-  *l_other = buf[(1 - wg) * 256 + 128 + row];
-  return true;
+// Lazy online-softmax reference of a row: the reference max moves to the
+// tile's row max m_tile only when that exceeds it by more than 2^kRescaleLog2
+// after scaling (or when the row had no key yet), so O and l are rescaled
+// rarely and exponentials stay below 2^kRescaleLog2.
+__device__ __forceinline__ float next_ref(float m_ref, float m_tile, float scale_log2) {
+  const bool move =
+      m_tile > m_ref && (m_ref == -INFINITY || (m_tile - m_ref) * scale_log2 > kRescaleLog2);
+  return move ? m_tile : m_ref;
 }
 
-struct SoftmaxCtx {
-  const tpsa_plan* p;
-  uint32_t s_addr;  // this warpgroup's S buffer (P overwrites its first half)
-  uint32_t o_addr;  // this warpgroup's O buffer
-  int32_t q;
-  bool sparse;
-};
+// Row values passed from one softmax warp to the warp holding the same 32
+// rows in the other warpgroup (warps quad + 4 and quad + 8), in order,
+// through a kChanSlots-deep ring per direction.  Publishing counts on the
+// publisher's counter; reading counts on the reader's, and a publisher
+// reuses a slot only once the reader has counted the value it held.
+struct RowChannel {
+  uint32_t mine, theirs;   // shared addresses of this row in the two rings
+  uint32_t pub_cnt;        // this warp's publication counter; the partner's is
+                           // peer_pub below, the read counters follow at +32 bytes
+  uint32_t peer_pub;
+  uint32_t n_pub, n_read;
 
-// Converts one 32-column chunk of S to floats, masking the keys outside the
-// row's key set when kMasked.
-template <bool kMasked>
-__device__ __forceinline__ void chunk_values(const uint32_t (&r)[32], uint32_t m, float (&v)[32]) {
-#pragma unroll
-  for (int c = 0; c < 32; ++c) {
-    const float x = __uint_as_float(r[c]);
-    v[c] = (!kMasked || ((m >> c) & 1u)) ? x : -INFINITY;
+  __device__ __forceinline__ bool publish(const Shared& sh, float v) {
+    if (n_pub >= kChanSlots &&
+        !__all_sync(0xffffffffu, wait_count_at(sh, peer_pub + 32, n_pub - kChanSlots + 1))) {
+      return false;
+    }
+    ptx::st_shared_f32(mine + (n_pub % kChanSlots) * 512, v);
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) ptx::red_release_add_shared(pub_cnt, 1);
+    ++n_pub;
+    return true;
   }
+  // The partner's next value; false if the wait gave up.
+  __device__ __forceinline__ bool read(const Shared& sh, float* v) {
+    if (!__all_sync(0xffffffffu, wait_count_at(sh, peer_pub, n_read + 1))) return false;
+    *v = ptx::ld_shared_f32(theirs + (n_read % kChanSlots) * 512);
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) ptx::red_release_add_shared(pub_cnt + 32, 1);
+    ++n_read;
+    return true;
+  }
+};
+
+// Replaces the keys of a 32-key chunk of S (fp32 bits) that are outside the
+// row's key set (bit c of m clear) by -inf.
+__device__ __forceinline__ void mask_chunk(uint32_t (&r)[32], uint32_t m) {
+#pragma unroll
+  for (int c = 0; c < 32; ++c) r[c] = ((m >> c) & 1u) ? r[c] : 0xff800000u;
 }
 
-// One key tile of w keys (64 or 128) starting at k0, the whole row: mask,
-// row max, online-softmax update, P -> tensor memory.  `first`: the
-// warpgroup's first tile of the item, whose PV overwrites O (so O is not
-// rescaled).  Two passes over the S columns in tensor memory, 64 columns at
-// a time, keep at most 64 of them in registers: pass 1 takes the row max
-// (and the visited bits), pass 2 reloads, exponentiates and writes P (bf16
-// pairs) over the first half of the S buffer, which it has already read.
-// The loops over 64-column halves are not unrolled: one body serves both
-// tile widths, which keeps the kernel's code small.
-template <bool kMasked>
-__device__ __forceinline__ void softmax_tile(const SoftmaxCtx& cx, int32_t k0, int32_t w,
-                                             bool first, RowState& st, uint32_t* visit_row,
-                                             int32_t words_per_row, uint32_t trole,
-                                             uint32_t& trn) {
-  const tpsa_plan& p = *cx.p;
-  const int32_t halves = w / 64;
+// Exponentials of one 32-key chunk of S (fp32 bits in r): P as 16 bf16
+// pairs stored to tensor memory at p_addr, their sum added to (sum0, sum1).
+__device__ __forceinline__ void exp_chunk(const uint32_t (&r)[32], float scale_log2, float neg_mb,
+                                          uint32_t p_addr, float& sum0, float& sum1) {
+  uint32_t pk[16];
+#pragma unroll
+  for (int c = 0; c < 16; ++c) {
+    const float v0 = __uint_as_float(r[2 * c]), v1 = __uint_as_float(r[2 * c + 1]);
+    float x0, x1;
+    fma2(v0, v1, scale_log2, neg_mb, x0, x1);
+    float e0, e1;
+    if ((TPSA_POLY_MASK >> c) & 1u) {
+      poly_exp2_x2(x0, x1, e0, e1);
+    } else {
+      e0 = mufu_exp2(x0);
+      e1 = mufu_exp2(x1);
+    }
+    add2(sum0, sum1, e0, e1);
+    pk[c] = pack_bf16x2(e0, e1);
+  }
+  ptx::tmem_st16(p_addr, pk);
+}
+
+__device__ __forceinline__ float chunk_max(const uint32_t (&r)[32]) {
   float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
-#pragma unroll 1
-  for (int32_t h = 0; h < halves; ++h) {
-    uint32_t ra[32], rb[32];
-    ptx::tmem_ld32(cx.s_addr + 64 * h, ra);
-    ptx::tmem_ld32(cx.s_addr + 64 * h + 32, rb);
+#pragma unroll
+  for (int c = 0; c < 32; c += 8) {
+    mx0 = max3(mx0, __uint_as_float(r[c]), __uint_as_float(r[c + 1]));
+    mx1 = max3(mx1, __uint_as_float(r[c + 2]), __uint_as_float(r[c + 3]));
+    mx2 = max3(mx2, __uint_as_float(r[c + 4]), __uint_as_float(r[c + 5]));
+    mx3 = max3(mx3, __uint_as_float(r[c + 6]), __uint_as_float(r[c + 7]));
+  }
+  return fmaxf(max3(mx0, mx1, mx2), mx3);
+}
+
+// Per-row state of the online softmax over one item's tiles, per warpgroup:
+// the reference max as of the last tile this warpgroup knows of, and the
+// warpgroup's partial row sum (over its own tiles) relative to it.
+struct RowState {
+  float m_ref;
+  float l_part;
+};
+
+// Moves this warpgroup's reference to m (from a tile of the other
+// warpgroup), rescaling the partial sum.  References only grow.
+__device__ __forceinline__ void adopt_ref(RowState& st, float m, float scale_log2) {
+  if (m != st.m_ref) {
+    st.l_part *= st.m_ref == -INFINITY ? 0.0f : mufu_exp2((st.m_ref - m) * scale_log2);
+    st.m_ref = m;
+  }
+}
+
+// Where a tile lives and what its owner needs to know.
+struct TileArgs {
+  uint32_t s_addr;      // the tile's S buffer (P goes to its columns 64-127)
+  uint32_t o_addr;      // O (128 columns)
+  int32_t k0;           // first key of the tile
+  bool wide;            // 128 keys (else 64)
+  bool first;           // first tile of the item (its PV overwrites O)
+  uint32_t prev_bar;    // pv_done barrier of the previous tile, and its parity
+  uint32_t prev_parity;
+  uint32_t* trn;        // trace counter of this thread when it records (TPSA_TRACE)
+  uint32_t trole;
+};
+#ifdef TPSA_TRACE
+#define TPSA_TILE_TR(t, ev)                                   \
+  do {                                                        \
+    if ((t).trn != nullptr) {                                 \
+      uint32_t& tr_n_ = *(t).trn;                             \
+      TPSA_TR((t).trole, ev, 0);                              \
+    }                                                         \
+  } while (0)
+#else
+#define TPSA_TILE_TR(t, ev) \
+  do {                      \
+  } while (0)
+#endif
+
+// Keeps the visited bits of a 32-key chunk (debug output) and masks it.
+template <bool kMasked>
+__device__ __forceinline__ void prepare_chunk(uint32_t (&r)[32], int32_t q, bool sparse, int32_t kc,
+                                              uint32_t* visit_row, int32_t words_per_row) {
+  const uint32_t m = kMasked ? chunk_mask(q, sparse, kc) : ~0u;
+  if (visit_row != nullptr && m != 0 && kc / 32 < words_per_row) atomicOr(visit_row + kc / 32, m);
+  if (kMasked) mask_chunk(r, m);
+}
+
+// One key tile of this warpgroup, the whole row of this thread: load S,
+// mask, row max; take the reference the previous tile (the other
+// warpgroup's) left, move it if this tile's maxima require, and pass it on;
+// exponentials and P into tensor memory; rescale O (after the previous
+// tile's PV completed) when the reference moved.  P (bf16 pairs) goes to
+// columns 64-127 of the S buffer.  A 64-key tile stays in registers; of a
+// 128-key tile, keys 64-127 stay in registers while keys 0-63 are loaded
+// twice (for the max, then for the exponentials), which keeps 64 of them
+// live at a time: their P lands over S columns 64-127 only after those
+// were read.  Returns false if a wait gave up.
+template <bool kMasked>
+__device__ __forceinline__ bool softmax_tile(const Shared& sh, const tpsa_plan& p,
+                                             const TileArgs& t, int32_t q, bool sparse,
+                                             RowChannel& ch, RowState& st,
+                                             uint32_t* visit_row, int32_t words_per_row) {
+  uint32_t ra[32], rb[32];
+  ptx::tmem_ld32(t.s_addr, ra);
+  ptx::tmem_ld32(t.s_addr + 32, rb);
+  ptx::tmem_wait_ld_regs(ra);
+  ptx::tmem_fence_regs(rb);
+  prepare_chunk<kMasked>(ra, q, sparse, t.k0, visit_row, words_per_row);
+  prepare_chunk<kMasked>(rb, q, sparse, t.k0 + 32, visit_row, words_per_row);
+  float lm = fmaxf(chunk_max(ra), chunk_max(rb));
+  if (t.wide) {
+    ptx::tmem_ld32(t.s_addr + 64, ra);
+    ptx::tmem_ld32(t.s_addr + 96, rb);
     ptx::tmem_wait_ld_regs(ra);
     ptx::tmem_fence_regs(rb);
-    const int32_t kc = k0 + 64 * h;
-    const uint32_t ma = kMasked ? chunk_mask(cx.q, cx.sparse, kc) : ~0u;
-    const uint32_t mb = kMasked ? chunk_mask(cx.q, cx.sparse, kc + 32) : ~0u;
-    if (visit_row != nullptr) {
-      const int32_t word = kc / 32;
-      if (ma != 0 && word < words_per_row) atomicOr(visit_row + word, ma);
-      if (mb != 0 && word + 1 < words_per_row) atomicOr(visit_row + word + 1, mb);
-    }
-    float v[32];
-    chunk_values<kMasked>(ra, ma, v);
-#pragma unroll
-    for (int c = 0; c < 32; c += 8) {
-      mx0 = max3(mx0, v[c], v[c + 1]);
-      mx1 = max3(mx1, v[c + 2], v[c + 3]);
-      mx2 = max3(mx2, v[c + 4], v[c + 5]);
-      mx3 = max3(mx3, v[c + 6], v[c + 7]);
-    }
-    chunk_values<kMasked>(rb, mb, v);
-#pragma unroll
-    for (int c = 0; c < 32; c += 8) {
-      mx0 = max3(mx0, v[c], v[c + 1]);
-      mx1 = max3(mx1, v[c + 2], v[c + 3]);
-      mx2 = max3(mx2, v[c + 4], v[c + 5]);
-      mx3 = max3(mx3, v[c + 6], v[c + 7]);
-    }
+    prepare_chunk<kMasked>(ra, q, sparse, t.k0 + 64, visit_row, words_per_row);
+    prepare_chunk<kMasked>(rb, q, sparse, t.k0 + 96, visit_row, words_per_row);
+    lm = fmaxf(lm, fmaxf(chunk_max(ra), chunk_max(rb)));
   }
-  TPSA_SM_TR(2);
-  const float mx = fmaxf(max3(mx0, mx1, mx2), mx3);
-  const float m_new = fmaxf(st.m_run, mx);
-  const bool need = (m_new - st.m_run) * p.scale_log2 > kRescaleLog2;
-  const bool any_need = __any_sync(0xffffffffu, need);
-  float factor = 1.0f;
-  if (any_need) {
-    factor = need ? mufu_exp2((st.m_run - m_new) * p.scale_log2) : 1.0f;
-    st.l_run *= factor;
-    if (need) st.m_run = m_new;
+  TPSA_TILE_TR(t, 30);
+  const float sl2 = p.scale_log2;
+  if (!t.first) {
+    float mp;
+    if (!ch.read(sh, &mp)) return false;
+    adopt_ref(st, mp, sl2);
   }
-  const float neg_mb = st.m_run == -INFINITY ? 0.0f : -st.m_run * p.scale_log2;
-  TPSA_SM_TR(6);
+  const float m_new = next_ref(st.m_ref, lm, sl2);
+  if (!ch.publish(sh, m_new)) return false;
+  TPSA_TILE_TR(t, 31);
+  const float neg_mb = m_new == -INFINITY ? 0.0f : -m_new * sl2;
   float sum0 = 0.0f, sum1 = 0.0f;
+  const uint32_t p_addr = t.s_addr + 64;
+  if (t.wide) {
 #pragma unroll 1
-  for (int32_t h = 0; h < halves; ++h) {
-    uint32_t ra[32], rb[32];
-    ptx::tmem_ld32(cx.s_addr + 64 * h, ra);
-    ptx::tmem_ld32(cx.s_addr + 64 * h + 32, rb);
-    ptx::tmem_wait_ld_regs(ra);
-    ptx::tmem_fence_regs(rb);
-    const int32_t kc = k0 + 64 * h;
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      float v[32];
-      if (half == 0) {
-        chunk_values<kMasked>(ra, kMasked ? chunk_mask(cx.q, cx.sparse, kc) : ~0u, v);
-      } else {
-        chunk_values<kMasked>(rb, kMasked ? chunk_mask(cx.q, cx.sparse, kc + 32) : ~0u, v);
-      }
-      uint32_t pk[16];
-#pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        float x0, x1;
-        fma2(v[2 * c], v[2 * c + 1], p.scale_log2, neg_mb, x0, x1);
-        float e0, e1;
-        if ((TPSA_POLY_MASK >> c) & 1u) {
-          poly_exp2_x2(x0, x1, e0, e1);
-        } else {
-          e0 = mufu_exp2(x0);
-          e1 = mufu_exp2(x1);
-        }
-        add2(sum0, sum1, e0, e1);
-        pk[c] = pack_bf16x2(e0, e1);
-      }
-      ptx::tmem_st16(cx.s_addr + 32 * h + 16 * half, pk);
+    for (int c = 0; c < 2; ++c) {
+      uint32_t rc[32];
+      ptx::tmem_ld32(t.s_addr + 32 * c, rc);
+      ptx::tmem_wait_ld_regs(rc);
+      if (kMasked) mask_chunk(rc, chunk_mask(q, sparse, t.k0 + 32 * c));
+      exp_chunk(rc, sl2, neg_mb, p_addr + 16 * c, sum0, sum1);
     }
   }
-  st.l_run += sum0 + sum1;
-  // O is rescaled after the exponentials; it only has to be done before P is
-  // published (the PV of this tile accumulates into O).  The PVs of earlier
-  // tiles into O have completed (the caller waited).
-  if (any_need && !first) rescale_o(cx.o_addr, factor);
+  const uint32_t p_kept = p_addr + (t.wide ? 32 : 0);
+  exp_chunk(ra, sl2, neg_mb, p_kept, sum0, sum1);
+  exp_chunk(rb, sl2, neg_mb, p_kept + 16, sum0, sum1);
+  TPSA_TILE_TR(t, 32);
+  const bool moved = m_new != st.m_ref;
+  if (__any_sync(0xffffffffu, moved)) {
+    float factor = 1.0f;
+    if (moved) factor = st.m_ref == -INFINITY ? 0.0f : mufu_exp2((st.m_ref - m_new) * sl2);
+    st.l_part *= factor;
+    st.m_ref = m_new;
+    if (!t.first) {
+      // O holds the PVs of the earlier tiles, the last of which has
+      // completed before O is rescaled; this tile's PV is issued only after
+      // this warp publishes P.
+      if (!__all_sync(0xffffffffu, wait_bar(sh, t.prev_bar, t.prev_parity))) return false;
+      ptx::tc_fence_after();
+      rescale_o(t.o_addr, factor);
+    }
+  }
+  st.l_part += sum0 + sum1;
   ptx::tmem_wait_st();
-  TPSA_SM_TR(7);
+  TPSA_TILE_TR(t, 34);
+  return true;
 }
 
 // Writes columns [col, col + 32) of the 32 output rows of a softmax warp as
@@ -884,12 +1077,15 @@ __device__ __forceinline__ void warp_arrive0(const Shared& sh, uint32_t id, int 
 }
 
 // Softmax warpgroup `wg` (warps 4-7: wg 0, warps 8-11: wg 1; warp % 4 is
-// the tensor-memory lane quadrant, so each warpgroup covers all 128 rows).  Tile
-// gt of the pair's global tile sequence belongs to warpgroup gt % 2, which
-// keeps its own S buffer, O accumulator and (m, l) per row; the two partial
-// results of an item are merged once at its end, each warpgroup producing 64
-// of the 128 output columns.
-__device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tmem) {
+// the tensor-memory lane quadrant, so each warpgroup covers all 128 rows).
+// Tile gt of the pair's tile stream (in S buffer gt % 3) belongs to
+// warpgroup gt % 2.  The two warpgroups share the O accumulator and hand
+// each row's lazy reference max from tile to tile through RowChannel, so
+// P of every tile is relative to the reference O is kept in; each keeps a
+// partial row sum over its own tiles, combined at the item's end.  At the
+// end of an item each warpgroup writes O columns [64 wg, 64 wg + 64).
+__device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tmem,
+                             const CUtensorMap* tout) {
   const tpsa_plan& p = a.plan;
   const uint32_t r = sh.rank;
   const int warp = threadIdx.x / 32;
@@ -900,18 +1096,39 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
   const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
   const int32_t hq = p.kv_heads * kGroupSize;
   const bool visit = a.visited != nullptr;
-  // own: tiles of this warpgroup so far (tile gt = 2 * own + wg);
-  // pv_items0/1: items in which warpgroup 0/1 had tiles (one PV-done phase
-  // each on that warpgroup's barrier).
-  uint32_t g = 0, own = 0, pv_items0 = 0, pv_items1 = 0, split_iter = 0, xc = 0;
+  // Tiles of the pair's stream before the current item.
+  uint32_t g = 0;
+  // Items whose output this warpgroup staged, and split items so far.
+  uint32_t staged_items = 0, split_items = 0;
+  RowChannel ch;
+  static_assert(kCntCon == kCntPub + 8, "read counters follow the publication counters");
+  ch.mine = sh.base_u32 + kOffXchg + (wg * kChanSlots * 128 + row) * 4;
+  ch.theirs = sh.base_u32 + kOffXchg + ((1 - wg) * kChanSlots * 128 + row) * 4;
+  ch.pub_cnt = sh.counter(kCntPub + wg * 4 + quad);
+  ch.peer_pub = sh.counter(kCntPub + (1 - wg) * 4 + quad);
+  ch.n_pub = 0;
+  ch.n_read = 0;
+  // The first thread of each warpgroup issues that warpgroup's output store
+  // and releases the Q buffer that staged it.
+  const bool store_thread = quad == 0 && lane == 0;
+  bool release_pending = false;
+  uint32_t pending_qb = 0;
+  auto release_q = [&](bool full_completion) {
+    if (store_thread && release_pending) {
+      if (full_completion) {
+        ptx::bulk_wait_group<0>();
+      } else {
+        ptx::bulk_wait_group_read<0>();
+      }
+      ptx::mbar_arrive(sh.bar(kBarQEmpty + pending_qb));
+      release_pending = false;
+    }
+  };
   volatile int* split_last = reinterpret_cast<volatile int*>(sh.base + kOffSplitLast);
   uint32_t tr_sm = 0;  // trace counter (used only with TPSA_TRACE)
 #define tr_n_ tr_sm
-  const uint32_t o_base = tmem + lane_base + 256;  // O0; O1 at +128
-  SoftmaxCtx cx;
-  cx.p = &p;
-  cx.s_addr = tmem + lane_base + wg * 128;
-  cx.o_addr = o_base + wg * 128;
+  const uint32_t o_all = tmem + lane_base + kTmemO;  // O, 128 columns
+  const uint32_t o_addr = o_all + 64 * wg;             // this warpgroup's output columns
 
   for (uint32_t n_item = 0;; ++n_item) {
     ItemRec rec;
@@ -919,13 +1136,16 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
     if (!__all_sync(0xffffffffu, got)) break;
     __syncwarp();
     if (lane == 0) release_item(sh, n_item);
+    // The previous item's output store has long read its staging buffer.
+    release_q(false);
     if (rec.idx >= p.total_items) break;
     const int32_t idx = rec.idx;
+    const uint32_t qb = n_item & 1;  // this item's Q buffer (items alternate)
     const tpsa_item& it = rec.it;
     const BlockTiles& bt = rec.bt;
     const int32_t tok = bt.q_begin + row / 2;
-    cx.q = tok < p.seq_len ? tok : p.seq_len - 1;
-    cx.sparse = row_is_sparse(p, tok);
+    const int32_t q = tok < p.seq_len ? tok : p.seq_len - 1;
+    const bool sparse = row_is_sparse(p, tok);
     const int32_t qrow = it.block * kBlockQ + row / 2;  // row within the chunk
     const int32_t head = it.kv_head * kGroupSize + 2 * static_cast<int32_t>(r) + (row & 1);
     const bool real_row = qrow < p.query_tokens;
@@ -934,127 +1154,147 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
             ? a.visited + (static_cast<size_t>(qrow) * hq + head) * a.words_per_row
             : nullptr;
     RowState st{-INFINITY, 0.0f};
-    bool ok = true, first = true;
+    bool ok = true;
     const int32_t ntiles = it.tile_end - it.tile_begin;
-    // Which warpgroups own at least one tile of this item.
-    const bool has_wg0 = ntiles >= 2 || (g & 1) == 0;
-    const bool has_wg1 = ntiles >= 2 || (g & 1) == 1;
     for (int32_t n = (g + wg) & 1; n < ntiles; n += 2) {
+      const uint32_t gt = g + static_cast<uint32_t>(n);
+      const uint32_t sb = gt % kNumSBufs;
       int32_t k0, w;
       tile_keys(bt, it.tile_begin + n, &k0, &w);
       const bool masked = tile_needs_mask(p, bt, k0, w);
-      const bool w_ok = wait_bar(sh, sh.bar(kBarSFull + wg), own & 1);
+      TileArgs ta;
+      ta.s_addr = tmem + lane_base + (sb << 7);
+      ta.o_addr = o_all;
+      ta.k0 = k0;
+      ta.wide = w > 64;
+      ta.first = n == 0;
+      ta.prev_bar = sh.bar(kBarPvDone + (gt - 1) % kNumSBufs);
+      ta.prev_parity = ((gt - 1) / kNumSBufs) & 1;
+      ta.trn = (row == 0 && r == 0) ? &tr_sm : nullptr;
+      ta.trole = 2 + wg;
+      const bool w_ok = wait_bar(sh, sh.bar(kBarSFull + sb), (gt / kNumSBufs) & 1);
       if (!__all_sync(0xffffffffu, w_ok)) { ok = false; break; }
-      // S of this tile being full also means this warpgroup's earlier PVs
-      // into O completed (their MMAs were issued before this tile's QK).
       if (row == 0 && r == 0) TPSA_TR(2 + wg, 1, n);
       ptx::tc_fence_after();
-      if (masked) {
-        softmax_tile<true>(cx, k0, w, first, st, visit_row, a.words_per_row, 2 + wg, tr_sm);
-      } else {
-        softmax_tile<false>(cx, k0, w, first, st, visit_row, a.words_per_row, 2 + wg, tr_sm);
-      }
+      const bool t_ok =
+          masked ? softmax_tile<true>(sh, p, ta, q, sparse, ch, st, visit_row, a.words_per_row)
+                 : softmax_tile<false>(sh, p, ta, q, sparse, ch, st, visit_row, a.words_per_row);
+      if (!t_ok) { ok = false; break; }
       ptx::tc_fence_before();
       if (row == 0 && r == 0) TPSA_TR(2 + wg, 3, n);
-      warp_arrive0(sh, kBarPFull + wg, lane);
-      first = false;
-      ++own;
+      warp_arrive0(sh, kBarPFull + sb, lane);
     }
     if (!ok) break;
     g += static_cast<uint32_t>(ntiles);
-    // O0 and O1 are final once each warpgroup's last PV of the item
-    // completed (signalled once per item in which that warpgroup had tiles;
-    // both warpgroups observe both signals).
-    if (has_wg0) {
-      const bool pv_ok = wait_bar(sh, sh.bar(kBarPvDone + 0), pv_items0 & 1);
-      if (!__all_sync(0xffffffffu, pv_ok)) break;
-      ++pv_items0;
+
+    // Item end.  The final reference is the last tile's (read from the
+    // other warpgroup if it owned that tile); the row sum is the two
+    // partial sums; O is complete once the item's last PV has.
+    const uint32_t gl = g - 1;
+    if ((gl & 1) != static_cast<uint32_t>(wg)) {
+      float mp;
+      if (!ch.read(sh, &mp)) break;
+      adopt_ref(st, mp, p.scale_log2);
     }
-    if (has_wg1) {
-      const bool pv_ok = wait_bar(sh, sh.bar(kBarPvDone + 1), pv_items1 & 1);
-      if (!__all_sync(0xffffffffu, pv_ok)) break;
-      ++pv_items1;
+    if (!ch.publish(sh, st.l_part)) break;
+    float l_peer;
+    if (!ch.read(sh, &l_peer)) break;
+    const float l_total = st.l_part + l_peer;
+    if (!__all_sync(0xffffffffu, wait_bar(sh, sh.bar(kBarPvDone + gl % kNumSBufs),
+                                          (gl / kNumSBufs) & 1))) {
+      break;
     }
-    if (row == 0 && r == 0) TPSA_TR(2 + wg, 8, 0);
-    float m_o, l_o;
-    if (!exchange_ml(sh, xc, wg, row, lane, st.m_run, st.l_run, &m_o, &l_o)) break;
     ptx::tc_fence_after();
     if (row == 0 && r == 0) TPSA_TR(2 + wg, 9, 0);
-    const float m0 = wg == 0 ? st.m_run : m_o, m1 = wg == 0 ? m_o : st.m_run;
-    const float l0 = wg == 0 ? st.l_run : l_o, l1 = wg == 0 ? l_o : st.l_run;
-    const float m_all = fmaxf(m0, m1);
-    const float a0 = m0 == -INFINITY ? 0.0f : mufu_exp2((m0 - m_all) * p.scale_log2);
-    const float a1 = m1 == -INFINITY ? 0.0f : mufu_exp2((m1 - m_all) * p.scale_log2);
-    const float l_total = l0 * a0 + l1 * a1;
-    // Columns [64 wg, 64 wg + 64) of the merged output row, 32 at a time:
-    // bf16 into `out`, or for a split item the unnormalised fp32 partial
-    // (O, m, l) into the item's workspace slot.  A slot is column-major
-    // ([128 columns][256 rows], then m[256] and l[256]), so a warp's row-per-
-    // thread writes and reads of one column are 128 contiguous bytes.
     const bool split = it.num_splits > 1;
     float* slot = a.scratch + static_cast<size_t>(idx) * kSlotFloats;
     constexpr int32_t kSlotRows = 2 * kRowsPerTile;
     const int32_t srow = static_cast<int32_t>(r) * kRowsPerTile + row;
-    const int32_t base_q = it.block * kBlockQ + quad * 16;
-    const int32_t base_h = it.kv_head * kGroupSize + 2 * static_cast<int32_t>(r);
-    uint8_t* stage = sh.base + kOffStage + (warp - kFirstSoftmaxWarp) * kStageBytesPerWarp;
-    const float inv = 1.0f / l_total;
-    // Both 32-column chunks are merged into registers first and the O
-    // buffers released, so the next item's PVs need not wait for the
-    // stores.
-    float om[2][32];
+    if (!split) {
+      // This warpgroup's 64 output columns, as bf16, into d-half wg of the
+      // item's Q buffer, which is dead (its QKs completed before the last PV)
+      // and has the output tile's shape (per d-half, [64 tokens x 2 heads]
+      // rows of 64 d, 128-byte swizzled as the Q tensor map loads it).
+      const float inv = 1.0f / l_total;
+      uint8_t* dst = sh.base + kOffQ + qb * kQBytes + wg * kQHalfBytes + row * 128;
+#pragma unroll 1
+      for (int c = 0; c < 2; ++c) {
+        uint32_t x[32];
+        ptx::tmem_ld32(o_addr + 32 * c, x);
+        ptx::tmem_wait_ld_regs(x);
 #pragma unroll
-    for (int c = 0; c < 2; ++c) {
-      const uint32_t col = static_cast<uint32_t>(wg * 64 + 32 * c);
-      uint32_t x0[32], x1[32];
-      if (has_wg0) ptx::tmem_ld32(o_base + col, x0);
-      if (has_wg1) ptx::tmem_ld32(o_base + 128 + col, x1);
-      ptx::tmem_wait_ld();
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const float v0 = has_wg0 ? a0 * __uint_as_float(x0[j]) : 0.0f;
-        om[c][j] = has_wg1 ? fmaf(a1, __uint_as_float(x1[j]), v0) : v0;
+        for (int jj = 0; jj < 4; ++jj) {
+          const int j = 4 * c + jj;  // 16-byte chunk within the d-half row
+          const uint32_t* v = &x[8 * jj];
+          *reinterpret_cast<uint4*>(dst + ((j ^ (row & 7)) << 4)) = make_uint4(
+              pack_bf16x2(__uint_as_float(v[0]) * inv, __uint_as_float(v[1]) * inv),
+              pack_bf16x2(__uint_as_float(v[2]) * inv, __uint_as_float(v[3]) * inv),
+              pack_bf16x2(__uint_as_float(v[4]) * inv, __uint_as_float(v[5]) * inv),
+              pack_bf16x2(__uint_as_float(v[6]) * inv, __uint_as_float(v[7]) * inv));
+        }
       }
-    }
-    ptx::tc_fence_before();
-    warp_arrive0(sh, kBarOEmpty, lane);
-#pragma unroll
-    for (int c = 0; c < 2; ++c) {
-      const uint32_t col = static_cast<uint32_t>(wg * 64 + 32 * c);
-      const float (&o)[32] = om[c];
-      if (!split) {
-        store_rows_bf16(o, inv, stage, lane, a.out, base_q, base_h, hq, p.query_tokens,
-                        static_cast<int32_t>(col));
-      } else {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) slot[(col + j) * kSlotRows + srow] = o[j];
+      // Each warp releases O only after its staged count: the next item's
+      // counts need its PVs, which need O, so every count of this item lands
+      // before any count of the next one.
+      ptx::fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) ptx::red_release_add_shared(sh.counter(kCntStaged + wg), 1);
+      ptx::tc_fence_before();
+      warp_arrive0(sh, kBarOEmpty, lane);
+      ++staged_items;
+      if (store_thread && wait_count(sh, kCntStaged + wg, 4 * staged_items)) {
+        // One TMA store of this warpgroup's d-half box (clipped at
+        // query_tokens by the tensor map).
+        const int32_t hbase = it.kv_head * kGroupSize + 2 * static_cast<int32_t>(r);
+        const uint32_t src = sh.base_u32 + kOffQ + qb * kQBytes + wg * kQHalfBytes;
+        ptx::tma_store_3d(tout, 64 * wg, hbase, it.block * kBlockQ, src);
+        ptx::bulk_commit_group();
       }
+      release_pending = true;  // the Q buffer returns to the producer (later)
+      pending_qb = qb;
+      if (row == 0 && r == 0) TPSA_TR(2 + wg, 5, 0);
+      continue;
     }
-    if (row == 0 && r == 0) TPSA_TR(2 + wg, 5, 0);
-    if (!split) continue;
 
-    // Split item: the last split of the block (per CTA of the pair) merges
-    // all partials and writes bf16.
+    // Split item: the fp32 partial of this warpgroup's 64 columns into the
+    // item's column-major slot ([128 columns][256 rows], then m[256] and
+    // l[256]); the last split of the block (per CTA of the pair) merges all
+    // partials and writes bf16.
+#pragma unroll 1
+    for (int c = 0; c < 2; ++c) {
+      uint32_t x[32];
+      ptx::tmem_ld32(o_addr + 32 * c, x);
+      ptx::tmem_wait_ld_regs(x);
+      float* col = slot + static_cast<size_t>(64 * wg + 32 * c) * kSlotRows + srow;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) col[j * kSlotRows] = __uint_as_float(x[j]);
+    }
     if (wg == 0) {
-      slot[kHeadDim * kSlotRows + srow] = m_all;
+      slot[kHeadDim * kSlotRows + srow] = st.m_ref;
       slot[(kHeadDim + 1) * kSlotRows + srow] = l_total;
     }
+    release_pending = true;
+    pending_qb = qb;
     __threadfence();
     __syncwarp();
-    if (lane == 0) ptx::mbar_arrive(sh.bar(kBarSplitWritten));
-    bool w_ok = wait_bar(sh, sh.bar(kBarSplitWritten), split_iter & 1);
-    if (!__all_sync(0xffffffffu, w_ok)) break;
-    if (row == 0 && wg == 0) {
-      int32_t* ctr = a.ctl + kCtlSplitBase +
-                     ((it.block - p.tail_block0) * p.kv_heads + it.kv_head) * 2 + r;
-      const int prev = atomicAdd(ctr, 1);
-      *split_last = prev == it.num_splits - 1;
-      ptx::mbar_arrive(sh.bar(kBarSplitDecided));
+    if (lane == 0) ptx::red_release_add_shared(sh.counter(kCntSplitW), 1);
+    const uint32_t sp_slot = split_items & 1;
+    ++split_items;
+    if (wg == 0 && row == 0) {
+      if (wait_count(sh, kCntSplitW, kSoftmaxWarps * split_items)) {
+        int32_t* ctr = a.ctl + kCtlSplitBase +
+                       ((it.block - p.tail_block0) * p.kv_heads + it.kv_head) * 2 + r;
+        const int prev = atomicAdd(ctr, 1);
+        split_last[sp_slot] = prev == it.num_splits - 1;
+        ptx::red_release_add_shared(sh.counter(kCntSplitD), 1);
+      }
     }
-    w_ok = wait_bar(sh, sh.bar(kBarSplitDecided), split_iter & 1);
-    ++split_iter;
-    if (!__all_sync(0xffffffffu, w_ok)) break;
-    if (!*split_last) continue;
+    const bool decided = __all_sync(0xffffffffu, wait_count(sh, kCntSplitD, split_items));
+    const bool last_split = decided && split_last[sp_slot];
+    ptx::tc_fence_before();
+    warp_arrive0(sh, kBarOEmpty, lane);
+    if (!decided) break;
+    if (!last_split) continue;
     __threadfence();
     const float* first_slot = a.scratch + static_cast<size_t>(idx - it.split) * kSlotFloats;
     const size_t m_off = static_cast<size_t>(kHeadDim) * kSlotRows + srow;
@@ -1070,24 +1310,29 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
       if (ms != -INFINITY) lsum += mufu_exp2((ms - mmax) * p.scale_log2) * __ldcg(sl + l_off);
     }
     const float inv_sum = 1.0f / lsum;
+    const int32_t base_q = it.block * kBlockQ + quad * 16;
+    const int32_t base_h = it.kv_head * kGroupSize + 2 * static_cast<int32_t>(r);
+    uint8_t* stage = sh.base + kOffStage + (warp - kFirstSoftmaxWarp) * kStageBytesPerWarp;
 #pragma unroll 1
     for (int c = 0; c < 2; ++c) {
-      const int col = wg * 64 + 32 * c;
+      const int col = 64 * wg + 32 * c;
       float acc[32];
 #pragma unroll
       for (int j = 0; j < 32; ++j) acc[j] = 0.0f;
+#pragma unroll 1
       for (int32_t sp = 0; sp < it.num_splits; ++sp) {
         const float* sl = first_slot + sp * kSlotFloats;
         const float ms = __ldcg(sl + m_off);
         const float wgt = ms == -INFINITY ? 0.0f : mufu_exp2((ms - mmax) * p.scale_log2);
+        const float* colp = sl + static_cast<size_t>(col) * kSlotRows + srow;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          acc[j] += wgt * __ldcg(sl + static_cast<size_t>(col + j) * kSlotRows + srow);
-        }
+        for (int j = 0; j < 32; ++j) acc[j] += wgt * __ldcg(colp + j * kSlotRows);
       }
       store_rows_bf16(acc, inv_sum, stage, lane, a.out, base_q, base_h, hq, p.query_tokens, col);
     }
   }
+  // Output stores complete before the CTA exits.
+  release_q(true);
 }
 #undef tr_n_
 
@@ -1097,7 +1342,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kNumThreads, 1)
                       const __grid_constant__ CUtensorMap tmap_q,
                       const __grid_constant__ CUtensorMap tmap_k64,
                       const __grid_constant__ CUtensorMap tmap_k32,
-                      const __grid_constant__ CUtensorMap tmap_v) {
+                      const __grid_constant__ CUtensorMap tmap_v,
+                      const __grid_constant__ CUtensorMap tmap_out) {
   extern __shared__ uint8_t smem_raw[];
   Shared sh;
   {
@@ -1113,8 +1359,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kNumThreads, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
       ptx::mbar_init(sh.bar(kBarQFull + i), 2);
-      ptx::mbar_init(sh.bar(kBarQEmpty + i), 1);
-      ptx::mbar_init(sh.bar(kBarSFull + i), 1);
+      ptx::mbar_init(sh.bar(kBarQEmpty + i), kQEmptyArrivals);
       ptx::mbar_init(sh.bar(kBarItemFull + i), 1);
       ptx::mbar_init(sh.bar(kBarItemEmpty + i), kItemConsumers);
     }
@@ -1122,17 +1367,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kNumThreads, 1)
       ptx::mbar_init(sh.bar(kBarKVFull + s), 2);
       ptx::mbar_init(sh.bar(kBarKVEmpty + s), 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (uint32_t i = 0; i < kNumSBufs; ++i) {
+      ptx::mbar_init(sh.bar(kBarSFull + i), 1);
       ptx::mbar_init(sh.bar(kBarPFull + i), kPairWgArrivals);
       ptx::mbar_init(sh.bar(kBarPvDone + i), 1);
     }
     ptx::mbar_init(sh.bar(kBarOEmpty), kPairWarpArrivals);
-    ptx::mbar_init(sh.bar(kBarSplitWritten), kSoftmaxWarps);
-    ptx::mbar_init(sh.bar(kBarSplitDecided), 1);
     ptx::mbar_init(sh.bar(kBarTail), 1);
     ptx::mbar_init(sh.bar(kBarDrain), 1);
-    ptx::mbar_init(sh.bar(kBarWgX), kSoftmaxWarps);
     *sh.abort_flag() = 0;
+    for (uint32_t i = 0; i < kNumCounters; ++i) {
+      *reinterpret_cast<volatile uint32_t*>(sh.base + kOffCounters + 4 * i) = 0;
+    }
     ptx::fence_mbar_init();
   }
   if (warp == 1) {
@@ -1151,10 +1397,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kNumThreads, 1)
       __syncwarp();
     } else if (warp == 1) {
       if (sh.rank == 0) mma_role(args, sh, tmem, lane);
+    } else if (warp == 2 && sh.rank == 0) {
+      // The scheduler has a warp of its own: it spins on the item ring, and
+      // a lane of a busy warp would compete with that warp's work.
+      if (lane == 0) scheduler_role(args, sh);
+      __syncwarp();
     }
   } else {
     ptx::setmaxnreg_inc<kSoftmaxRegs>();
-    softmax_role(args, sh, tmem);
+    softmax_role(args, sh, tmem, &tmap_out);
   }
 
   ptx::tc_fence_before();
@@ -1392,6 +1643,9 @@ tpsa_status launch(const void* query, const void* key_cache, const void* value_c
   if (st != TPSA_OK) return st;
   st = encode_map(&tv, value_cache, kv_heads, cache_tokens, 1, 64);
   if (st != TPSA_OK) return st;
+  CUtensorMap tout;  // output tile stores: the Q tile's shape over `out`
+  st = encode_map(&tout, out, hq, static_cast<uint64_t>(query_tokens), 2, kBlockQ);
+  if (st != TPSA_OK) return st;
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   args.block_table = block_table;
@@ -1407,9 +1661,11 @@ tpsa_status launch(const void* query, const void* key_cache, const void* value_c
   args.words_per_row = (p.seq_len + 31) / 32;
 
   if (visited != nullptr || tile_counter != nullptr) {
-    tpsa_paged_kernel<true><<<p.grid, kNumThreads, kSmemBytes, s>>>(args, tq, tk64, tk32, tv);
+    tpsa_paged_kernel<true><<<p.grid, kNumThreads, kSmemBytes, s>>>(args, tq, tk64, tk32, tv,
+                                                                     tout);
   } else {
-    tpsa_paged_kernel<false><<<p.grid, kNumThreads, kSmemBytes, s>>>(args, tq, tk64, tk32, tv);
+    tpsa_paged_kernel<false><<<p.grid, kNumThreads, kSmemBytes, s>>>(args, tq, tk64, tk32, tv,
+                                                                      tout);
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
@@ -1605,6 +1861,11 @@ tpsa_status tpsa_paged_attention_static_scratch(const void* query, const void* k
 
 #ifdef TPSA_TRACE
 // Copies role `role`'s events of the last launch into out (2 x uint64 each).
+TPSA_API void tpsa_debug_timeout(uint32_t* out5) {
+  cudaDeviceSynchronize();
+  cudaMemcpyFromSymbol(out5, g_timeout_site, sizeof(uint32_t) * 5);
+}
+
 TPSA_API uint32_t tpsa_debug_trace(uint32_t role, unsigned long long* out, uint32_t max_events) {
   uint32_t n[kTraceRoles] = {0, 0, 0, 0};
   cudaDeviceSynchronize();
