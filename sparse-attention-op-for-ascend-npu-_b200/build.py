@@ -49,24 +49,28 @@ def _run(cmd: list[str]) -> None:
         raise RuntimeError(f"build step failed ({' '.join(cmd[:3])} ...):\n{res.stdout}\n{res.stderr}")
 
 
-# A few bytes of spill slots (a rarely used value kept in local memory) are
-# tolerated; more means softmax rows left the registers.
-MAX_SPILL_BYTES = 16
+# Spill limits in bytes of spill stores (see _check_ptxas_report).
+MAX_SPILL_BYTES = 0
+MAX_VISIT_SPILL_BYTES = 64
 
 
 def _check_ptxas_report(text: str) -> None:
-    """The kernel must compile without material local-memory spills (softmax
-    rows live in registers; spilled rows put local-memory traffic on the
-    critical path)."""
+    """The production kernel (tpsa_paged_kernel<false>) must compile without
+    local-memory spills (softmax rows live in registers; spilled rows put
+    local-memory traffic on the critical path).  The instantiation that also
+    records visited keys (<true>) is a test instrument; it may spill a little,
+    up to MAX_VISIT_SPILL_BYTES."""
     import re
 
-    found = re.findall(r"Compiling entry function '\w*tpsa_paged_kernel\w*' for 'sm_100a'\n"
+    found = re.findall(r"Compiling entry function '\w*tpsa_paged_kernelILb([01])E\w*' for 'sm_100a'\n"
                        r"(?:.*\n)*?\s*(\d+) bytes stack frame, (\d+) bytes spill stores", text)
-    if not found:
+    kinds = {visit: int(st) for visit, _, st in found}
+    if set(kinds) != {"0", "1"}:
         raise RuntimeError("could not read the ptxas report of tpsa_paged_kernel")
-    spills = [int(st) for _, st in found]
-    if max(spills) > MAX_SPILL_BYTES:
-        raise RuntimeError(f"tpsa_paged_kernel spills registers ({spills} bytes)")
+    if kinds["0"] > MAX_SPILL_BYTES:
+        raise RuntimeError(f"tpsa_paged_kernel spills registers ({kinds['0']} bytes)")
+    if kinds["1"] > MAX_VISIT_SPILL_BYTES:
+        raise RuntimeError(f"tpsa_paged_kernel<visit> spills registers ({kinds['1']} bytes)")
 
 
 def build_lib(force: bool = False) -> Path:

@@ -66,7 +66,7 @@ __device__ uint32_t g_device_status = 0;
 #ifndef TPSA_TRACE_CLUSTER
 #define TPSA_TRACE_CLUSTER 0  // CTA pair whose events are recorded
 #endif
-constexpr uint32_t kTraceRoles = 4;
+constexpr uint32_t kTraceRoles = 5;
 constexpr uint32_t kTraceCap = 1u << 14;
 __device__ unsigned long long g_trace[kTraceRoles][kTraceCap][2];
 __device__ uint32_t g_trace_n[kTraceRoles];
@@ -109,31 +109,35 @@ constexpr uint32_t kNumSBufs = 3;
 constexpr uint32_t kTmemO = 384;
 constexpr uint64_t kWaitTimeoutNs = 1000000000ull;  // 1 s per wait
 constexpr uint64_t kAbortSettleNs = 200000ull;      // let in-flight TMA land
-constexpr float kRescaleLog2 = 8.0f;
+constexpr float kRescaleLog2 = 8.0f;  // lazy O rescale threshold (log2 units)
 // Column pairs c (of 16 per 32-column chunk) whose exponentials use the FMA
-// pipe polynomial rather than MUFU ex2: bit c set.
+// pipe polynomial rather than MUFU ex2: bit c set.  None by default: with
+// two softmax warps per SM sub-partition the MUFU pipe is not the limit
+// (measured: every nonzero mask tried was slower).
 #ifndef TPSA_POLY_MASK
-#define TPSA_POLY_MASK 0x8888u
-#endif  // lazy O rescale threshold (log2 units)
+#define TPSA_POLY_MASK 0u
+#endif
 constexpr uint16_t kPairMask = 0x3;
 
 // Shared memory per CTA (offsets from a 1024-byte aligned base).
 constexpr uint32_t kQHalfBytes = 128 * 128;        // 128 rows x 64 bf16
 constexpr uint32_t kQBytes = 2 * kQHalfBytes;      // one Q buffer (2 d-halves)
-constexpr uint32_t kRingSlotBytes = 32768;         // one key tile: K half + V half
+constexpr uint32_t kRingSlotBytes = 16384;         // one key tile's K half, or its V half
 constexpr uint32_t kKHalfBytes = 8192;             // d-half of a K half-tile
-constexpr uint32_t kVOffset = 16384;               // V half within a slot
 constexpr int kRing = 4;                           // key-tile slots (power of two)
 constexpr uint32_t kOffQ = 0;                      // 2 Q buffers
-constexpr uint32_t kOffKV = kOffQ + 2 * kQBytes;
-constexpr uint32_t kOffBar = kOffKV + kRing * kRingSlotBytes;
+constexpr uint32_t kOffK = kOffQ + 2 * kQBytes;     // K ring
+constexpr uint32_t kOffV = kOffK + kRing * kRingSlotBytes;  // V ring
+constexpr uint32_t kOffBar = kOffV + kRing * kRingSlotBytes;
 
 enum BarId : uint32_t {
   kBarQFull = 0,                          // [2] CTA 0: both Q halves landed
   kBarQEmpty = kBarQFull + 2,             // [2] both CTAs: Q buffer free
-  kBarKVFull = kBarQEmpty + 2,            // [kRing] CTA 0: K and V of both CTAs landed
-  kBarKVEmpty = kBarKVFull + kRing,       // [kRing] both: slot free (its PV done)
-  kBarSFull = kBarKVEmpty + kRing,        // [3] both: S buffer computed
+  kBarKFull = kBarQEmpty + 2,             // [kRing] CTA 0: K of both CTAs landed
+  kBarKEmpty = kBarKFull + kRing,         // [kRing] both: K slot free (its QK done)
+  kBarVFull = kBarKEmpty + kRing,         // [kRing] CTA 0: V of both CTAs landed
+  kBarVEmpty = kBarVFull + kRing,         // [kRing] both: V slot free (its PV done)
+  kBarSFull = kBarVEmpty + kRing,         // [3] both: S buffer computed
   kBarPFull = kBarSFull + kNumSBufs,      // [3] CTA 0: P of the tile in the S buffer written
   kBarPvDone = kBarPFull + kNumSBufs,     // [3] both: PV from the S buffer completed
   kBarOEmpty = kBarPvDone + kNumSBufs,    // CTA 0: O read by the item's epilogue
@@ -145,11 +149,11 @@ enum BarId : uint32_t {
 };
 // Arrivals: p_full takes one per warp of the tile's softmax warpgroup in
 // both CTAs, o_empty one per softmax warp of both CTAs;
-// item_empty takes the producer, the MMA issuer and the 8 softmax warps of
-// CTA 0 plus the producer and the 8 softmax warps of CTA 1.
+// item_empty takes the two producers, the MMA issuer and the 8 softmax
+// warps of CTA 0 plus the two producers and the 8 softmax warps of CTA 1.
 constexpr uint32_t kPairWgArrivals = kSoftmaxWarps;  // 4 warps x 2 CTAs
 constexpr uint32_t kPairWarpArrivals = 2 * kSoftmaxWarps;
-constexpr uint32_t kItemConsumers = 2 * (1 + kSoftmaxWarps) + 1;
+constexpr uint32_t kItemConsumers = 2 * (2 + kSoftmaxWarps) + 1;
 // q_empty: the MMA issuer's commit after the item's last QK, plus one arrival
 // from each softmax warpgroup of this CTA once its output store has read the
 // buffer (the finished item's Q buffer stages its output rows).
@@ -487,16 +491,29 @@ __device__ void scheduler_role(const KernelArgs& a, const Shared& sh) {
   }
 }
 
-// ------------------------------------------------------------ producer
-__device__ void producer_role(const KernelArgs& a, const Shared& sh,
-                              const CUtensorMap* tq, const CUtensorMap* tk64,
-                              const CUtensorMap* tk32, const CUtensorMap* tv) {
+// ------------------------------------------------------------ producers
+// Two single-thread producers per CTA, each following the item ring: the K
+// producer loads Q and the K half-tiles into the K ring (a slot frees when
+// its QK completes), the V producer the V half-tiles into the V ring (a
+// slot frees when its PV completes), so K can run ahead of V by the QK
+// lookahead.  Both CTAs of the pair load their halves with pair TMA loads
+// that complete on CTA 0's full barrier: of K, keys [r*half, (r+1)*half)
+// of the tile, all 128 d; of V, all keys of the tile, d-half r.
+__device__ void producer_role(const KernelArgs& a, const Shared& sh, const CUtensorMap* tq,
+                              const CUtensorMap* tk64, const CUtensorMap* tk32,
+                              const CUtensorMap* tv, bool v_side) {
   const tpsa_plan& p = a.plan;
   const uint32_t r = sh.rank;
-  ptx::prefetch_tmap(tq);
-  ptx::prefetch_tmap(tk64);
-  ptx::prefetch_tmap(tk32);
-  ptx::prefetch_tmap(tv);
+  if (v_side) {
+    ptx::prefetch_tmap(tv);
+  } else {
+    ptx::prefetch_tmap(tq);
+    ptx::prefetch_tmap(tk64);
+    ptx::prefetch_tmap(tk32);
+  }
+  const uint32_t bar_full = sh.bar0(v_side ? kBarVFull : kBarKFull);
+  const uint32_t bar_empty = sh.bar(v_side ? kBarVEmpty : kBarKEmpty);
+  const uint32_t ring_base = sh.base_u32 + (v_side ? kOffV : kOffK);
   uint32_t ring = 0, q_iter = 0, tail_iter = 0;
   bool ok = true;
   TPSA_TRACE_STATE;
@@ -505,21 +522,23 @@ __device__ void producer_role(const KernelArgs& a, const Shared& sh,
     if (!take_item(sh, n, &rec)) break;
     release_item(sh, n);
     if (rec.idx >= p.total_items) break;
-    if (r == 0) TPSA_TR(0, 20, rec.idx);
+    if (r == 0 && !v_side) TPSA_TR(0, 20, rec.idx);
     const tpsa_item& it = rec.it;
     const BlockTiles& bt = rec.bt;
 
-    // Q: this CTA's 128 rows (64 tokens x query heads 4h + 2r, 4h + 2r + 1).
-    const uint32_t qb = q_iter % 2;
-    if (q_iter >= 2 && !wait_bar(sh, sh.bar(kBarQEmpty + qb), ((q_iter / 2) - 1) & 1)) break;
-    ptx::mbar_arrive_expect_tx_cluster(sh.bar0(kBarQFull + qb), kQBytes);
-    for (int dh = 0; dh < 2; ++dh) {
-      ptx::tma_load_3d_pair(sh.base_u32 + kOffQ + qb * kQBytes + dh * kQHalfBytes, tq, dh * 64,
-                            it.kv_head * kGroupSize + 2 * r, it.block * kBlockQ,
-                            sh.bar0(kBarQFull + qb));
+    if (!v_side) {
+      // Q: this CTA's 128 rows (64 tokens x query heads 4h + 2r, 4h + 2r + 1).
+      const uint32_t qb = q_iter % 2;
+      if (q_iter >= 2 && !wait_bar(sh, sh.bar(kBarQEmpty + qb), ((q_iter / 2) - 1) & 1)) break;
+      ptx::mbar_arrive_expect_tx_cluster(sh.bar0(kBarQFull + qb), kQBytes);
+      for (int dh = 0; dh < 2; ++dh) {
+        ptx::tma_load_3d_pair(sh.base_u32 + kOffQ + qb * kQBytes + dh * kQHalfBytes, tq, dh * 64,
+                              it.kv_head * kGroupSize + 2 * r, it.block * kBlockQ,
+                              sh.bar0(kBarQFull + qb));
+      }
+      ++q_iter;
+      if (r == 0) TPSA_TR(0, 21, rec.idx);
     }
-    ++q_iter;
-    if (r == 0) TPSA_TR(0, 21, rec.idx);
 
     for (int32_t t = it.tile_begin; t < it.tile_end && ok; ++t) {
       int32_t k0, w;
@@ -532,56 +551,51 @@ __device__ void producer_role(const KernelArgs& a, const Shared& sh,
       } else {
         tok = page * kPageSize + (k0 % kPageSize);
       }
-      if (a.tiles != nullptr && r == 0) {
+      if (a.tiles != nullptr && r == 0 && !v_side) {
         atomicAdd(a.tiles, 1ull);
         atomicAdd(a.tiles + 1, static_cast<unsigned long long>(w));
       }
-      const int32_t half = w / 2;
-      // One slot per key tile: K keys [k0 + r*half, +half) (all 128 d, two
-      // d-halves) at +0 and V keys [k0, k0 + w) (d-half r) at +kVOffset,
-      // both completing on the slot's full barrier.
       const uint32_t s = ring_slot(ring);
-      if (!wait_bar(sh, sh.bar(kBarKVEmpty + s), ring_parity(ring) ^ 1)) { ok = false; break; }
+      if (!wait_bar(sh, bar_empty + 8 * s, ring_parity(ring) ^ 1)) { ok = false; break; }
       ++ring;
-      const uint32_t kdst = sh.base_u32 + kOffKV + s * kRingSlotBytes;
-      const uint32_t vdst = kdst + kVOffset;
-      const uint32_t kbytes = static_cast<uint32_t>(half) * kHeadDim * 2;
-      const uint32_t vbytes = static_cast<uint32_t>(w) * 64 * 2;
-      const CUtensorMap* km = w == kTileKeys ? tk64 : tk32;
-      if (k0 + w <= p.seq_len) {
-        ptx::mbar_arrive_expect_tx_cluster(sh.bar0(kBarKVFull + s), kbytes + vbytes);
+      const uint32_t dst = ring_base + s * kRingSlotBytes;
+      if (!v_side) {
+        // Keys at or beyond seq_len (unwritten cache slots of the last page)
+        // only meet masked scores, which select -inf whatever they hold.
+        const int32_t half = w / 2;
+        const CUtensorMap* km = w == kTileKeys ? tk64 : tk32;
+        ptx::mbar_arrive_expect_tx_cluster(bar_full + 8 * s,
+                                           static_cast<uint32_t>(half) * kHeadDim * 2);
         for (int dh = 0; dh < 2; ++dh) {
-          ptx::tma_load_3d_pair(kdst + dh * kKHalfBytes, km, dh * 64, it.kv_head,
-                                tok + static_cast<int32_t>(r) * half, sh.bar0(kBarKVFull + s));
+          ptx::tma_load_3d_pair(dst + dh * kKHalfBytes, km, dh * 64, it.kv_head,
+                                tok + static_cast<int32_t>(r) * half, bar_full + 8 * s);
         }
+      } else if (k0 + w <= p.seq_len) {
+        ptx::mbar_arrive_expect_tx_cluster(bar_full + 8 * s, static_cast<uint32_t>(w) * 64 * 2);
         for (int sub = 0; sub < w / 64; ++sub) {
-          ptx::tma_load_3d_pair(vdst + sub * 8192, tv, static_cast<int32_t>(r) * 64, it.kv_head,
-                                tok + sub * 64, sh.bar0(kBarKVFull + s));
+          ptx::tma_load_3d_pair(dst + sub * 8192, tv, static_cast<int32_t>(r) * 64, it.kv_head,
+                                tok + sub * 64, bar_full + 8 * s);
         }
       } else {
-        // Keys at or beyond seq_len may be unwritten cache slots: load the
-        // tile into this CTA's slot here, zero those V rows so P = 0 never
+        // Values at or beyond seq_len may be unwritten cache slots: load the
+        // tile into this CTA's slot here, zero those rows so P = 0 never
         // meets a NaN, then release the slot with a plain arrival.
-        ptx::mbar_arrive_expect_tx(sh.bar(kBarTail), kbytes + vbytes);
-        for (int dh = 0; dh < 2; ++dh) {
-          ptx::tma_load_3d(kdst + dh * kKHalfBytes, km, dh * 64, it.kv_head,
-                           tok + static_cast<int32_t>(r) * half, sh.bar(kBarTail));
-        }
+        ptx::mbar_arrive_expect_tx(sh.bar(kBarTail), static_cast<uint32_t>(w) * 64 * 2);
         for (int sub = 0; sub < w / 64; ++sub) {
-          ptx::tma_load_3d(vdst + sub * 8192, tv, static_cast<int32_t>(r) * 64, it.kv_head,
+          ptx::tma_load_3d(dst + sub * 8192, tv, static_cast<int32_t>(r) * 64, it.kv_head,
                            tok + sub * 64, sh.bar(kBarTail));
         }
         if (!wait_bar(sh, sh.bar(kBarTail), tail_iter & 1)) { ok = false; break; }
         ++tail_iter;
         for (int32_t row = p.seq_len - k0; row < w; ++row) {
-          uint4* dst = reinterpret_cast<uint4*>(sh.base + (vdst - sh.base_u32) + row * 128);
+          uint4* d4 = reinterpret_cast<uint4*>(sh.base + (dst - sh.base_u32) + row * 128);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) dst[j] = make_uint4(0, 0, 0, 0);
+          for (int j = 0; j < 8; ++j) d4[j] = make_uint4(0, 0, 0, 0);
         }
         ptx::fence_proxy_async_smem();
-        ptx::mbar_arrive_cluster(sh.bar0(kBarKVFull + s));
+        ptx::mbar_arrive_cluster(bar_full + 8 * s);
       }
-      if (r == 0) TPSA_TR(0, 22, t);
+      if (r == 0) TPSA_TR(v_side ? 4 : 0, 22, t);
     }
   }
   if (!ok || *sh.abort_flag()) {
@@ -598,20 +612,27 @@ __device__ void producer_role(const KernelArgs& a, const Shared& sh,
 __device__ void mma_role(const KernelArgs& a, const Shared& sh, uint32_t tmem, int lane) {
   const tpsa_plan& p = a.plan;
   TPSA_TRACE_STATE;
-  // tcgen05.mma issue blocks once about three MMAs are queued, so this warp's
-  // own instructions between MMA batches leave the tensor pipe idle.  The
-  // loop below therefore keeps its per-tile work to barrier waits, commits
-  // and additions to operands prepared once: descriptor bases, barrier
-  // addresses, instruction descriptors and incremental ring positions.
-  const uint32_t bar_kv_full = sh.bar(kBarKVFull), bar_kv_empty = sh.bar(kBarKVEmpty);
+  // tcgen05.mma issue blocks once about three MMAs are queued, so this
+  // warp's own instructions between MMA batches leave the tensor pipe idle.
+  // The loop below therefore keeps its per-tile work to barrier waits,
+  // commits and additions to operands prepared once: descriptor bases
+  // (32-bit additions to their low word, which holds the start address),
+  // barrier addresses, instruction descriptors and incremental ring
+  // positions.  (Measured: the same loop run by one thread of the warp is
+  // slower.)
+  const uint32_t bar_k_full = sh.bar(kBarKFull), bar_k_empty = sh.bar(kBarKEmpty);
+  const uint32_t bar_v_full = sh.bar(kBarVFull), bar_v_empty = sh.bar(kBarVEmpty);
   const uint32_t bar_s_full = sh.bar(kBarSFull), bar_p_full = sh.bar(kBarPFull);
   const uint32_t bar_pv_done = sh.bar(kBarPvDone), bar_q_full = sh.bar(kBarQFull);
   const uint32_t bar_q_empty = sh.bar(kBarQEmpty), bar_o_empty = sh.bar(kBarOEmpty);
-  // Descriptor start addresses are in 16-byte units.
+  // Descriptor start addresses are in 16-byte units, in the low word.
   const uint64_t q_desc0 = ptx::smem_desc_sw128(sh.base_u32 + kOffQ, 16, 1024);
-  const uint64_t k_desc0 = ptx::smem_desc_sw128(sh.base_u32 + kOffKV, 16, 1024);
-  const uint64_t v_desc0 =
-      ptx::smem_desc_sw128(sh.base_u32 + kOffKV + kVOffset, kKHalfBytes, 1024);
+  const uint64_t k_desc0 = ptx::smem_desc_sw128(sh.base_u32 + kOffK, 16, 1024);
+  const uint64_t v_desc0 = ptx::smem_desc_sw128(sh.base_u32 + kOffV, kKHalfBytes, 1024);
+  const uint32_t q_hi = static_cast<uint32_t>(q_desc0 >> 32);
+  const uint32_t k_hi = static_cast<uint32_t>(k_desc0 >> 32);
+  const uint32_t v_hi = static_cast<uint32_t>(v_desc0 >> 32);
+  auto desc = [](uint32_t lo, uint32_t hi) { return (static_cast<uint64_t>(hi) << 32) | lo; };
   constexpr uint32_t kSlotUnits = kRingSlotBytes >> 4;
   constexpr uint32_t kQUnits = kQBytes >> 4;
   constexpr uint32_t kIdQk128 = ptx::idesc_bf16_f32(256, 128, 0);
@@ -623,15 +644,16 @@ __device__ void mma_role(const KernelArgs& a, const Shared& sh, uint32_t tmem, i
   };
   // S(buf) = Q K^T for the key tile in ring slot `slot` (M = 256 over the
   // pair, N = 128 or 64).
-  auto issue_qk = [&](uint64_t qd, uint32_t slot, uint32_t buf, bool narrow) {
+  auto issue_qk = [&](uint32_t q_lo, uint32_t slot, uint32_t buf, bool narrow) {
     const uint32_t d = tmem + (buf << 7);
     const uint32_t idesc = narrow ? kIdQk64 : kIdQk128;
-    const uint64_t kd = k_desc0 + slot * kSlotUnits;
+    const uint32_t k_lo = static_cast<uint32_t>(k_desc0) + slot * kSlotUnits;
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-      const uint64_t qo = (k / 4) * (kQHalfBytes >> 4) + (k % 4) * 2;
-      const uint64_t ko = (k / 4) * (kKHalfBytes >> 4) + (k % 4) * 2;
-      ptx::umma_ss_pair_elect(d, qd + qo, kd + ko, idesc, k > 0 ? 1u : 0u);
+      const uint32_t qo = (k / 4) * (kQHalfBytes >> 4) + (k % 4) * 2;
+      const uint32_t ko = (k / 4) * (kKHalfBytes >> 4) + (k % 4) * 2;
+      ptx::umma_ss_pair_elect(d, desc(q_lo + qo, q_hi), desc(k_lo + ko, k_hi), idesc,
+                              k > 0 ? 1u : 0u);
     }
   };
   // O += P V: P (bf16 pairs) over columns 64-127 of S buffer buf, V the
@@ -639,12 +661,12 @@ __device__ void mma_role(const KernelArgs& a, const Shared& sh, uint32_t tmem, i
   auto issue_pv = [&](uint32_t slot, uint32_t buf, bool narrow, bool first) {
     const uint32_t d = tmem + kTmemO;
     const uint32_t pa = tmem + (buf << 7) + 64;
-    const uint64_t vd = v_desc0 + slot * kSlotUnits;
+    const uint32_t v_lo = static_cast<uint32_t>(v_desc0) + slot * kSlotUnits;
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       if (k < 4 || !narrow) {
-        ptx::umma_ts_pair_elect(d, pa + k * 8, vd + k * (2048 >> 4), kIdPv,
-                                (first && k == 0) ? 0u : 1u);
+        ptx::umma_ts_pair_elect(d, pa + k * 8, desc(v_lo + k * (2048 >> 4), v_hi), kIdPv,
+                          (first && k == 0) ? 0u : 1u);
       }
     }
   };
@@ -665,12 +687,12 @@ __device__ void mma_role(const KernelArgs& a, const Shared& sh, uint32_t tmem, i
     kTIssued = 16u,    // a QK was issued (no control word otherwise)
     kTItemShift = 8,   // bits 8 and up: the tile's item number (1-based)
   };
-  uint32_t slot_q = 0, phase_q = 0, slot_v = 0, q_iter = 0;
+  uint32_t slot_q = 0, phase_q = 0, slot_v = 0, phase_v = 0, q_iter = 0;
   uint32_t sb_q = 0, sb_v = 0, pass_v = 0;  // S buffers of the QK / PV cursors
   uint32_t n_item = 0;                      // items taken from the ring
   int32_t q_n = 0, q_ntiles = 0;
   uint32_t q_narrow = 0, q_qb = 0;
-  uint64_t q_qd = q_desc0;
+  uint32_t q_qd = static_cast<uint32_t>(q_desc0);
   bool q_done = false;
   bool ok = true;
   // Issues the next tile's QK and returns its control word (with kTIssued);
@@ -701,18 +723,22 @@ __device__ void mma_role(const KernelArgs& a, const Shared& sh, uint32_t tmem, i
         return 0;
       }
       ++q_iter;
-      q_qd = q_desc0 + q_qb * kQUnits;
+      q_qd = static_cast<uint32_t>(q_desc0) + q_qb * kQUnits;
     }
     const int32_t last = q_ntiles - 1;
     const bool narrow =
         (q_n < 2 && ((q_narrow >> q_n) & 1u)) || (q_n == last && (q_narrow & 4u));
-    if (!warp_wait(bar_kv_full + 8 * slot_q, phase_q)) {
+    if (lane == 0) TPSA_TR(1, 19, sb_q);
+    if (!warp_wait(bar_k_full + 8 * slot_q, phase_q)) {
       ok = false;
       return 0;
     }
+    if (lane == 0) TPSA_TR(1, 17, sb_q);
     ptx::tc_fence_after();
     issue_qk(q_qd, slot_q, sb_q, narrow);
+    if (lane == 0) TPSA_TR(1, 18, sb_q);
     ptx::umma_commit_pair_mc_elect(bar_s_full + 8 * sb_q, kPairMask);
+    ptx::umma_commit_pair_mc_elect(bar_k_empty + 8 * slot_q, kPairMask);
     if (q_n == last) ptx::umma_commit_pair_mc_elect(bar_q_empty + 8 * q_qb, kPairMask);
     const uint32_t info = kTIssued | (narrow ? kTNarrow : 0u) | (q_n == 0 ? kTFirst : 0u) |
                           (q_n == 0 && n_item > 1 ? kTItemStart : 0u) |
@@ -754,13 +780,16 @@ __device__ void mma_role(const KernelArgs& a, const Shared& sh, uint32_t tmem, i
       if (!warp_wait(bar_o_empty, (info0 & kTItemOdd) ? 0u : 1u)) { ok = false; break; }
     }
     if (!warp_wait(bar_p_full + 8 * sb_v, pass_v & 1)) { ok = false; break; }
+    if (!warp_wait(bar_v_full + 8 * slot_v, phase_v)) { ok = false; break; }
     if (lane == 0) TPSA_TR(1, 14, sb_v);
     ptx::tc_fence_after();
     issue_pv(slot_v, sb_v, (info0 & kTNarrow) != 0, (info0 & kTFirst) != 0);
     if (lane == 0) TPSA_TR(1, 15, sb_v);
-    ptx::umma_commit_pair_mc_elect(bar_kv_empty + 8 * slot_v, kPairMask);
+    ptx::umma_commit_pair_mc_elect(bar_v_empty + 8 * slot_v, kPairMask);
     ptx::umma_commit_pair_mc_elect(bar_pv_done + 8 * sb_v, kPairMask);
+    if (lane == 0) TPSA_TR(1, 16, sb_v);
     slot_v = (slot_v + 1) & (kRing - 1);
+    phase_v ^= slot_v == 0 ? 1u : 0u;
     if (sb_v == kNumSBufs - 1) {
       sb_v = 0;
       ++pass_v;
@@ -946,11 +975,13 @@ struct TileArgs {
 #endif
 
 // Keeps the visited bits of a 32-key chunk (debug output) and masks it.
-template <bool kMasked>
+template <bool kMasked, bool kVisit>
 __device__ __forceinline__ void prepare_chunk(uint32_t (&r)[32], int32_t q, bool sparse, int32_t kc,
                                               uint32_t* visit_row, int32_t words_per_row) {
   const uint32_t m = kMasked ? chunk_mask(q, sparse, kc) : ~0u;
-  if (visit_row != nullptr && m != 0 && kc / 32 < words_per_row) atomicOr(visit_row + kc / 32, m);
+  if (kVisit && visit_row != nullptr && m != 0 && kc / 32 < words_per_row) {
+    atomicOr(visit_row + kc / 32, m);
+  }
   if (kMasked) mask_chunk(r, m);
 }
 
@@ -964,7 +995,7 @@ __device__ __forceinline__ void prepare_chunk(uint32_t (&r)[32], int32_t q, bool
 // twice (for the max, then for the exponentials), which keeps 64 of them
 // live at a time: their P lands over S columns 64-127 only after those
 // were read.  Returns false if a wait gave up.
-template <bool kMasked>
+template <bool kMasked, bool kVisit>
 __device__ __forceinline__ bool softmax_tile(const Shared& sh, const tpsa_plan& p,
                                              const TileArgs& t, int32_t q, bool sparse,
                                              RowChannel& ch, RowState& st,
@@ -974,45 +1005,63 @@ __device__ __forceinline__ bool softmax_tile(const Shared& sh, const tpsa_plan& 
   ptx::tmem_ld32(t.s_addr + 32, rb);
   ptx::tmem_wait_ld_regs(ra);
   ptx::tmem_fence_regs(rb);
-  prepare_chunk<kMasked>(ra, q, sparse, t.k0, visit_row, words_per_row);
-  prepare_chunk<kMasked>(rb, q, sparse, t.k0 + 32, visit_row, words_per_row);
+  prepare_chunk<kMasked, kVisit>(ra, q, sparse, t.k0, visit_row, words_per_row);
+  prepare_chunk<kMasked, kVisit>(rb, q, sparse, t.k0 + 32, visit_row, words_per_row);
   float lm = fmaxf(chunk_max(ra), chunk_max(rb));
   if (t.wide) {
     ptx::tmem_ld32(t.s_addr + 64, ra);
     ptx::tmem_ld32(t.s_addr + 96, rb);
     ptx::tmem_wait_ld_regs(ra);
     ptx::tmem_fence_regs(rb);
-    prepare_chunk<kMasked>(ra, q, sparse, t.k0 + 64, visit_row, words_per_row);
-    prepare_chunk<kMasked>(rb, q, sparse, t.k0 + 96, visit_row, words_per_row);
+    prepare_chunk<kMasked, kVisit>(ra, q, sparse, t.k0 + 64, visit_row, words_per_row);
+    prepare_chunk<kMasked, kVisit>(rb, q, sparse, t.k0 + 96, visit_row, words_per_row);
     lm = fmaxf(lm, fmaxf(chunk_max(ra), chunk_max(rb)));
   }
   TPSA_TILE_TR(t, 30);
   const float sl2 = p.scale_log2;
-  if (!t.first) {
-    float mp;
-    if (!ch.read(sh, &mp)) return false;
-    adopt_ref(st, mp, sl2);
-  }
-  const float m_new = next_ref(st.m_ref, lm, sl2);
-  if (!ch.publish(sh, m_new)) return false;
-  TPSA_TILE_TR(t, 31);
-  const float neg_mb = m_new == -INFINITY ? 0.0f : -m_new * sl2;
+  // Optimistic agreement: the exponentials use this warpgroup's reference
+  // as of its previous tile; the other warpgroup's decision for the tile in
+  // between is read after the reloaded keys 0-63 (it is usually published
+  // by then) and, in the rare case that it changes this tile's reference,
+  // those are redone; keys 64-127, still in registers, follow with the
+  // final reference.
+  float m_new = next_ref(st.m_ref, lm, sl2);
+  bool agreed = t.first;
   float sum0 = 0.0f, sum1 = 0.0f;
   const uint32_t p_addr = t.s_addr + 64;
-  if (t.wide) {
 #pragma unroll 1
-    for (int c = 0; c < 2; ++c) {
-      uint32_t rc[32];
-      ptx::tmem_ld32(t.s_addr + 32 * c, rc);
-      ptx::tmem_wait_ld_regs(rc);
-      if (kMasked) mask_chunk(rc, chunk_mask(q, sparse, t.k0 + 32 * c));
-      exp_chunk(rc, sl2, neg_mb, p_addr + 16 * c, sum0, sum1);
+  while (true) {
+    if (t.wide) {
+      const float neg_mb = m_new == -INFINITY ? 0.0f : -m_new * sl2;
+      sum0 = 0.0f;
+      sum1 = 0.0f;
+#pragma unroll 1
+      for (int c = 0; c < 2; ++c) {
+        uint32_t rc[32];
+        ptx::tmem_ld32(t.s_addr + 32 * c, rc);
+        ptx::tmem_wait_ld_regs(rc);
+        if (kMasked) mask_chunk(rc, chunk_mask(q, sparse, t.k0 + 32 * c));
+        exp_chunk(rc, sl2, neg_mb, p_addr + 16 * c, sum0, sum1);
+      }
     }
+    if (agreed) break;
+    float mp;
+    if (!ch.read(sh, &mp)) return false;
+    agreed = true;
+    adopt_ref(st, mp, sl2);
+    const float m2 = next_ref(st.m_ref, lm, sl2);
+    if (!__any_sync(0xffffffffu, m2 != m_new)) break;
+    m_new = m2;
   }
-  const uint32_t p_kept = p_addr + (t.wide ? 32 : 0);
-  exp_chunk(ra, sl2, neg_mb, p_kept, sum0, sum1);
-  exp_chunk(rb, sl2, neg_mb, p_kept + 16, sum0, sum1);
+  {
+    const float neg_mb = m_new == -INFINITY ? 0.0f : -m_new * sl2;
+    const uint32_t p_kept = p_addr + (t.wide ? 32 : 0);
+    exp_chunk(ra, sl2, neg_mb, p_kept, sum0, sum1);
+    exp_chunk(rb, sl2, neg_mb, p_kept + 16, sum0, sum1);
+  }
   TPSA_TILE_TR(t, 32);
+  if (!ch.publish(sh, m_new)) return false;
+  TPSA_TILE_TR(t, 31);
   const bool moved = m_new != st.m_ref;
   if (__any_sync(0xffffffffu, moved)) {
     float factor = 1.0f;
@@ -1084,6 +1133,7 @@ __device__ __forceinline__ void warp_arrive0(const Shared& sh, uint32_t id, int 
 // P of every tile is relative to the reference O is kept in; each keeps a
 // partial row sum over its own tiles, combined at the item's end.  At the
 // end of an item each warpgroup writes O columns [64 wg, 64 wg + 64).
+template <bool kVisit>
 __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tmem,
                              const CUtensorMap* tout) {
   const tpsa_plan& p = a.plan;
@@ -1095,7 +1145,7 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
   const int row = quad * 32 + lane;  // TMEM lane == row of this CTA's M half
   const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
   const int32_t hq = p.kv_heads * kGroupSize;
-  const bool visit = a.visited != nullptr;
+  const bool visit = kVisit && a.visited != nullptr;
   // Tiles of the pair's stream before the current item.
   uint32_t g = 0;
   // Items whose output this warpgroup staged, and split items so far.
@@ -1177,8 +1227,9 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
       if (row == 0 && r == 0) TPSA_TR(2 + wg, 1, n);
       ptx::tc_fence_after();
       const bool t_ok =
-          masked ? softmax_tile<true>(sh, p, ta, q, sparse, ch, st, visit_row, a.words_per_row)
-                 : softmax_tile<false>(sh, p, ta, q, sparse, ch, st, visit_row, a.words_per_row);
+          masked
+              ? softmax_tile<true, kVisit>(sh, p, ta, q, sparse, ch, st, visit_row, a.words_per_row)
+              : softmax_tile<false, kVisit>(sh, p, ta, q, sparse, ch, st, visit_row, a.words_per_row);
       if (!t_ok) { ok = false; break; }
       ptx::tc_fence_before();
       if (row == 0 && r == 0) TPSA_TR(2 + wg, 3, n);
@@ -1364,8 +1415,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kNumThreads, 1)
       ptx::mbar_init(sh.bar(kBarItemEmpty + i), kItemConsumers);
     }
     for (int s = 0; s < kRing; ++s) {
-      ptx::mbar_init(sh.bar(kBarKVFull + s), 2);
-      ptx::mbar_init(sh.bar(kBarKVEmpty + s), 1);
+      ptx::mbar_init(sh.bar(kBarKFull + s), 2);
+      ptx::mbar_init(sh.bar(kBarKEmpty + s), 1);
+      ptx::mbar_init(sh.bar(kBarVFull + s), 2);
+      ptx::mbar_init(sh.bar(kBarVEmpty + s), 1);
     }
     for (uint32_t i = 0; i < kNumSBufs; ++i) {
       ptx::mbar_init(sh.bar(kBarSFull + i), 1);
@@ -1393,7 +1446,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kNumThreads, 1)
   if (warp < kFirstSoftmaxWarp) {
     ptx::setmaxnreg_dec<kControlRegs>();
     if (warp == 0) {
-      if (lane == 0) producer_role(args, sh, &tmap_q, &tmap_k64, &tmap_k32, &tmap_v);
+      if (lane == 0) producer_role(args, sh, &tmap_q, &tmap_k64, &tmap_k32, &tmap_v, false);
       __syncwarp();
     } else if (warp == 1) {
       if (sh.rank == 0) mma_role(args, sh, tmem, lane);
@@ -1402,10 +1455,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kNumThreads, 1)
       // a lane of a busy warp would compete with that warp's work.
       if (lane == 0) scheduler_role(args, sh);
       __syncwarp();
+    } else if (warp == 3) {
+      if (lane == 0) producer_role(args, sh, &tmap_q, &tmap_k64, &tmap_k32, &tmap_v, true);
+      __syncwarp();
     }
   } else {
     ptx::setmaxnreg_inc<kSoftmaxRegs>();
-    softmax_role(args, sh, tmem, &tmap_out);
+    softmax_role<kVisit>(args, sh, tmem, &tmap_out);
   }
 
   ptx::tc_fence_before();
@@ -1867,7 +1923,7 @@ TPSA_API void tpsa_debug_timeout(uint32_t* out5) {
 }
 
 TPSA_API uint32_t tpsa_debug_trace(uint32_t role, unsigned long long* out, uint32_t max_events) {
-  uint32_t n[kTraceRoles] = {0, 0, 0, 0};
+  uint32_t n[kTraceRoles] = {0, 0, 0, 0, 0};
   cudaDeviceSynchronize();
   if (role >= kTraceRoles) {  // softmax sub-phase buffers of CTA role - 4
     return 0;
