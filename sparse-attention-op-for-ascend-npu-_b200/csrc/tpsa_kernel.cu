@@ -695,22 +695,30 @@ __device__ void mma_role(const KernelArgs& a, const Shared& sh, uint32_t tmem, i
   uint32_t q_qd = static_cast<uint32_t>(q_desc0);
   bool q_done = false;
   bool ok = true;
-  // Issues the next tile's QK and returns its control word (with kTIssued);
-  // 0 when no tile is left or a wait gave up (then ok is cleared).
-  auto next_qk = [&]() -> uint32_t {
+  // The next QK is prepared (its item taken, its Q and K waited for, its
+  // control word computed) by plan_qk and issued by fire_qk, so that in the
+  // steady state the QK that follows PV(t) is prepared while this warp waits
+  // for P(t), and PV(t) and QK(t + 3) go to the tensor pipe back to back.
+  uint32_t plan_info = 0;
+  bool plan_narrow = false;
+  // Prepares the next tile's QK; false when none may be issued now (no tile
+  // left, or it starts an item more than one ahead of item `bound`, 0 for
+  // no bound), or when a wait gave up (then ok is cleared).
+  auto plan_qk = [&](uint32_t bound) -> bool {
+    if (q_done) return false;
     if (q_n == q_ntiles) {
-      if (q_done) return 0;
+      if (bound != 0 && n_item > bound) return false;
       ItemBrief rec;
       const bool got = take_item_brief(sh, n_item, &rec);
       if (!__all_sync(0xffffffffu, got)) {
         ok = false;
-        return 0;
+        return false;
       }
       __syncwarp();
       if (lane == 0) release_item(sh, n_item);
       if (rec.idx >= p.total_items) {
         q_done = true;
-        return 0;
+        return false;
       }
       if (lane == 0) TPSA_TR(1, 10, rec.idx);
       ++n_item;
@@ -720,60 +728,66 @@ __device__ void mma_role(const KernelArgs& a, const Shared& sh, uint32_t tmem, i
       q_qb = q_iter & 1;
       if (!warp_wait(bar_q_full + 8 * q_qb, (q_iter >> 1) & 1)) {
         ok = false;
-        return 0;
+        return false;
       }
       ++q_iter;
       q_qd = static_cast<uint32_t>(q_desc0) + q_qb * kQUnits;
     }
     const int32_t last = q_ntiles - 1;
-    const bool narrow =
-        (q_n < 2 && ((q_narrow >> q_n) & 1u)) || (q_n == last && (q_narrow & 4u));
+    plan_narrow = (q_n < 2 && ((q_narrow >> q_n) & 1u)) || (q_n == last && (q_narrow & 4u));
+    plan_info = kTIssued | (plan_narrow ? kTNarrow : 0u) | (q_n == 0 ? kTFirst : 0u) |
+                (q_n == 0 && n_item > 1 ? kTItemStart : 0u) |
+                (((n_item - 1) & 1) ? kTItemOdd : 0u) | (n_item << kTItemShift);
     if (lane == 0) TPSA_TR(1, 19, sb_q);
     if (!warp_wait(bar_k_full + 8 * slot_q, phase_q)) {
       ok = false;
-      return 0;
+      return false;
     }
     if (lane == 0) TPSA_TR(1, 17, sb_q);
+    return true;
+  };
+  // Issues the planned QK and returns its control word.
+  auto fire_qk = [&]() -> uint32_t {
     ptx::tc_fence_after();
-    issue_qk(q_qd, slot_q, sb_q, narrow);
+    issue_qk(q_qd, slot_q, sb_q, plan_narrow);
     if (lane == 0) TPSA_TR(1, 18, sb_q);
     ptx::umma_commit_pair_mc_elect(bar_s_full + 8 * sb_q, kPairMask);
     ptx::umma_commit_pair_mc_elect(bar_k_empty + 8 * slot_q, kPairMask);
-    if (q_n == last) ptx::umma_commit_pair_mc_elect(bar_q_empty + 8 * q_qb, kPairMask);
-    const uint32_t info = kTIssued | (narrow ? kTNarrow : 0u) | (q_n == 0 ? kTFirst : 0u) |
-                          (q_n == 0 && n_item > 1 ? kTItemStart : 0u) |
-                          (((n_item - 1) & 1) ? kTItemOdd : 0u) | (n_item << kTItemShift);
+    if (q_n == q_ntiles - 1) ptx::umma_commit_pair_mc_elect(bar_q_empty + 8 * q_qb, kPairMask);
     slot_q = (slot_q + 1) & (kRing - 1);
     phase_q ^= slot_q == 0 ? 1u : 0u;
     sb_q = sb_q == kNumSBufs - 1 ? 0 : sb_q + 1;
     ++q_n;
-    return info;
+    return plan_info;
   };
 
   // Control words of the (up to three) tiles whose QK is issued and whose
   // PV is not, oldest first; 0 for none.
   uint32_t info0 = 0, info1 = 0, info2 = 0;
   int have = 0;
-  auto refill = [&]() {
-    while (ok && have < 3 && !q_done) {
-      // A QK that starts item n_item + 1 waits until the PV cursor is in
-      // item n_item.
-      if (q_n == q_ntiles && have > 0 && n_item > (info0 >> kTItemShift)) break;
-      const uint32_t info = next_qk();
-      if (info == 0) break;
-      if (have == 0) {
-        info0 = info;
-      } else if (have == 1) {
-        info1 = info;
-      } else {
-        info2 = info;
-      }
-      ++have;
+  auto push = [&](uint32_t info) {
+    if (have == 0) {
+      info0 = info;
+    } else if (have == 1) {
+      info1 = info;
+    } else {
+      info2 = info;
     }
+    ++have;
   };
-  while (true) {
-    refill();
-    if (!ok || have == 0) break;
+  // Issues QKs up to three ahead.  A QK that starts item n_item + 1 waits
+  // until the oldest pending PV is in item n_item: that item's Q buffer is
+  // released by the epilogue of item n_item - 1.
+  auto refill = [&]() {
+    while (ok && have < 3 && plan_qk(have > 0 ? (info0 >> kTItemShift) : 0u)) push(fire_qk());
+  };
+  refill();
+  while (ok && have > 0) {
+    // The QK to follow PV(t), prepared before P(t) is waited for.  Starting
+    // a new item here needs PV(t) itself to be in item n_item or later (the
+    // Q wait may not depend on PV(t)); otherwise refill takes it after PV(t).
+    const bool planned = plan_qk(info0 >> kTItemShift);
+    if (!ok) break;
     if (info0 & kTItemStart) {
       // O of the previous item (item index k - 1) has been read by its
       // epilogue: phase (k - 2) & 1 of o_empty.
@@ -787,6 +801,7 @@ __device__ void mma_role(const KernelArgs& a, const Shared& sh, uint32_t tmem, i
     if (lane == 0) TPSA_TR(1, 15, sb_v);
     ptx::umma_commit_pair_mc_elect(bar_v_empty + 8 * slot_v, kPairMask);
     ptx::umma_commit_pair_mc_elect(bar_pv_done + 8 * sb_v, kPairMask);
+    const uint32_t fired = planned ? fire_qk() : 0u;
     if (lane == 0) TPSA_TR(1, 16, sb_v);
     slot_v = (slot_v + 1) & (kRing - 1);
     phase_v ^= slot_v == 0 ? 1u : 0u;
@@ -800,6 +815,8 @@ __device__ void mma_role(const KernelArgs& a, const Shared& sh, uint32_t tmem, i
     info1 = info2;
     info2 = 0;
     --have;
+    if (fired != 0) push(fired);
+    refill();
   }
   // All MMAs issued by this warp complete before TMEM is released.
   ptx::umma_commit_pair_elect(sh.bar(kBarDrain));
