@@ -192,6 +192,45 @@ TPSA_API tpsa_status tpsa_paged_attention_heads(
     void* workspace, uint64_t workspace_bytes, void* stream);
 
 /*
+ * Packed ragged batch (varlen): `batch` requests whose query rows are packed
+ * back to back, each computed exactly as one tpsa_paged_attention call on
+ * its own rows.  Same semantics as the reference's packed-batch helper
+ * reference_attention_ragged_python (operator/tests/triangle_v2_reference.py:
+ * 437-487), which the reference computes by calling the batch-one op once
+ * per request; the reference op itself rejects batch > 1 (op_host :151-157,
+ * planning.py:149-150).  Here the whole batch shares one persistent launch
+ * per 16 requests, so short requests fill the GPU together.
+ *
+ *   query         bf16 [cu_seqlens_q[batch], 32, 128], packed
+ *   out           bf16, same shape as query
+ *   key_cache,
+ *   value_cache   bf16 [num_pages, 128, 8, 128], one page pool for all requests
+ *   block_tables  int32 [batch, table_cols] (device): row i maps request i's
+ *                 logical pages to physical pages
+ *   cu_seqlens_q  int64 [batch + 1] (host): request i owns packed rows
+ *                 [cu_seqlens_q[i], cu_seqlens_q[i+1]); cu_seqlens_q[0] == 0
+ *   seq_lens      int64 [batch] (host): request i's query rows are the last
+ *                 rows of its first seq_lens[i] tokens (query_start =
+ *                 seq_lens[i] - rows)
+ *   prompt_lens   int64 [batch] (host): prompt_lens[i] >= seq_lens[i]
+ *   workspace     at least tpsa_varlen_workspace_size() bytes, 256-byte
+ *                 aligned; reused by the launches of one call in stream order
+ *
+ * Every row count must be positive (reference: "each ragged query length must
+ * be positive").  The other gates are tpsa_paged_attention's, per request.
+ */
+TPSA_API tpsa_status tpsa_varlen_workspace_size(int32_t batch, const int64_t* cu_seqlens_q,
+                                       const int64_t* seq_lens,
+                                       const int64_t* prompt_lens, uint64_t* bytes);
+
+TPSA_API tpsa_status tpsa_paged_attention_varlen(
+    const void* query, const void* key_cache, const void* value_cache,
+    const int32_t* block_tables, void* out, int32_t batch,
+    const int64_t* cu_seqlens_q, const int64_t* seq_lens,
+    const int64_t* prompt_lens, int64_t num_pages, int64_t table_cols,
+    float scale, void* workspace, uint64_t workspace_bytes, void* stream);
+
+/*
  * Debug variant that runs the identical kernel and additionally records,
  * for every (query row, query head), the key indices that entered its
  * softmax: bit k of visited[(row * 4*kv_heads + head) * words_per_row +

@@ -55,22 +55,25 @@ MAX_VISIT_SPILL_BYTES = 64
 
 
 def _check_ptxas_report(text: str) -> None:
-    """The production kernel (tpsa_paged_kernel<false>) must compile without
+    """The production kernels (tpsa_paged_kernel<false, false> for batch-one
+    calls, <false, true> for packed ragged batches) must compile without
     local-memory spills (softmax rows live in registers; spilled rows put
     local-memory traffic on the critical path).  The instantiation that also
-    records visited keys (<true>) is a test instrument; it may spill a little,
-    up to MAX_VISIT_SPILL_BYTES."""
+    records visited keys (<true, false>) is a test instrument; it may spill a
+    little, up to MAX_VISIT_SPILL_BYTES."""
     import re
 
-    found = re.findall(r"Compiling entry function '\w*tpsa_paged_kernelILb([01])E\w*' for 'sm_100a'\n"
-                       r"(?:.*\n)*?\s*(\d+) bytes stack frame, (\d+) bytes spill stores", text)
-    kinds = {visit: int(st) for visit, _, st in found}
-    if set(kinds) != {"0", "1"}:
+    found = re.findall(r"Compiling entry function '\w*tpsa_paged_kernelILb([01])ELb([01])E\w*' "
+                       r"for 'sm_100a'\n(?:.*\n)*?\s*(\d+) bytes stack frame, (\d+) bytes spill stores",
+                       text)
+    kinds = {visit + varlen: int(st) for visit, varlen, _, st in found}
+    if set(kinds) != {"00", "01", "10"}:
         raise RuntimeError("could not read the ptxas report of tpsa_paged_kernel")
-    if kinds["0"] > MAX_SPILL_BYTES:
-        raise RuntimeError(f"tpsa_paged_kernel spills registers ({kinds['0']} bytes)")
-    if kinds["1"] > MAX_VISIT_SPILL_BYTES:
-        raise RuntimeError(f"tpsa_paged_kernel<visit> spills registers ({kinds['1']} bytes)")
+    for kind in ("00", "01"):
+        if kinds[kind] > MAX_SPILL_BYTES:
+            raise RuntimeError(f"tpsa_paged_kernel<{kind}> spills registers ({kinds[kind]} bytes)")
+    if kinds["10"] > MAX_VISIT_SPILL_BYTES:
+        raise RuntimeError(f"tpsa_paged_kernel<visit> spills registers ({kinds['10']} bytes)")
 
 
 def build_lib(force: bool = False) -> Path:

@@ -45,9 +45,11 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <memory>
 #include <mutex>
 #include <string>
 
@@ -192,8 +194,24 @@ static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 constexpr int kCtlNextItem = 0;
 constexpr int kCtlSplitBase = 64;
 
+// One request of a launch (a batch-one call is a launch of one request).
+// Its rows are packed at [q_row0, q_row0 + plan.query_tokens) of query and
+// out, and its items at [item_base, item_base + plan.total_items) of the
+// launch's item order.
+struct ReqDesc {
+  tpsa_plan plan;     // the request's own plan: its blocks, items and splits
+  int32_t item_base;  // first launch item of the request
+  int32_t q_row0;     // first packed query / output row
+  int32_t table_off;  // its block-table row (int32 elements from block_table)
+  int32_t slot_base;  // its first split-KV partial slot
+  int32_t ctr_base;   // its first split counter
+};
+constexpr int kMaxReqs = 16;  // requests per launch (varlen batches are cut into launches)
+
 struct KernelArgs {
-  tpsa_plan plan;
+  tpsa_plan plan;  // launch totals: total_items, kv_heads, scale, grid
+  int32_t num_reqs;
+  ReqDesc reqs[kMaxReqs];
   const int32_t* block_table;
   __nv_bfloat16* out;
   float* scratch;      // split partials (tail_items slots)
@@ -407,8 +425,10 @@ struct alignas(16) ItemRec {
   BlockTiles bt;
   // Item tiles only 64 keys wide (all others are 128): bit 0 the item's
   // tile 0, bit 1 its tile 1, bit 2 its last tile (the sink tile and a band
-  // or key range that starts or ends half-way through a page).
+  // or key range that starts or ends half-way through a page).  Bits 8 and
+  // up: the item's request within the launch.
   uint32_t narrow;
+  __device__ __forceinline__ int32_t req() const { return static_cast<int32_t>(narrow >> 8); }
 };
 static_assert(sizeof(ItemRec) == 64, "an item record is four 16-byte words");
 
@@ -470,12 +490,26 @@ __device__ __forceinline__ void release_item(const Shared& sh, uint32_t n) {
 // the pair's two-slot item ring (both CTAs' copies), running up to two items
 // ahead of the slowest consumer.  The index past the last item tells every
 // consumer to stop.
+template <bool kVarlen>
 __device__ void scheduler_role(const KernelArgs& a, const Shared& sh) {
   const tpsa_plan& p = a.plan;
   int32_t next = atomicAdd(a.ctl + kCtlNextItem, 1);
   for (uint32_t n = 0;; ++n) {
     const uint32_t slot = n % 2;
-    const ItemRec rec = make_item_rec(p, next);
+    ItemRec rec;
+    if (kVarlen) {
+      // The request holding launch item `next`, then the item within it.
+      int32_t q = 0;
+      if (next < p.total_items) {
+        while (q + 1 < a.num_reqs && next >= a.reqs[q + 1].item_base) ++q;
+      }
+      rec = make_item_rec(a.reqs[q].plan, next < p.total_items ? next - a.reqs[q].item_base
+                                                               : a.reqs[q].plan.total_items);
+      rec.idx = next;
+      rec.narrow |= static_cast<uint32_t>(q) << 8;
+    } else {
+      rec = make_item_rec(p, next);
+    }
     if (rec.idx < p.total_items) next = atomicAdd(a.ctl + kCtlNextItem, 1);
     if (!wait_bar(sh, sh.bar(kBarItemEmpty + slot), ((n / 2) & 1) ^ 1)) break;
     const uint4* words = reinterpret_cast<const uint4*>(&rec);
@@ -499,6 +533,7 @@ __device__ void scheduler_role(const KernelArgs& a, const Shared& sh) {
 // lookahead.  Both CTAs of the pair load their halves with pair TMA loads
 // that complete on CTA 0's full barrier: of K, keys [r*half, (r+1)*half)
 // of the tile, all 128 d; of V, all keys of the tile, d-half r.
+template <bool kVarlen>
 __device__ void producer_role(const KernelArgs& a, const Shared& sh, const CUtensorMap* tq,
                               const CUtensorMap* tk64, const CUtensorMap* tk32,
                               const CUtensorMap* tv, bool v_side) {
@@ -525,6 +560,11 @@ __device__ void producer_role(const KernelArgs& a, const Shared& sh, const CUten
     if (r == 0 && !v_side) TPSA_TR(0, 20, rec.idx);
     const tpsa_item& it = rec.it;
     const BlockTiles& bt = rec.bt;
+    // The item's request (a batch-one launch has one, at row and table 0).
+    const ReqDesc& rq = a.reqs[kVarlen ? rec.req() : 0];
+    const int32_t* table = kVarlen ? a.block_table + rq.table_off : a.block_table;
+    const int32_t req_seq_len = kVarlen ? rq.plan.seq_len : p.seq_len;
+    const int32_t q_row0 = kVarlen ? rq.q_row0 : 0;
 
     if (!v_side) {
       // Q: this CTA's 128 rows (64 tokens x query heads 4h + 2r, 4h + 2r + 1).
@@ -533,7 +573,7 @@ __device__ void producer_role(const KernelArgs& a, const Shared& sh, const CUten
       ptx::mbar_arrive_expect_tx_cluster(sh.bar0(kBarQFull + qb), kQBytes);
       for (int dh = 0; dh < 2; ++dh) {
         ptx::tma_load_3d_pair(sh.base_u32 + kOffQ + qb * kQBytes + dh * kQHalfBytes, tq, dh * 64,
-                              it.kv_head * kGroupSize + 2 * r, it.block * kBlockQ,
+                              it.kv_head * kGroupSize + 2 * r, q_row0 + it.block * kBlockQ,
                               sh.bar0(kBarQFull + qb));
       }
       ++q_iter;
@@ -543,7 +583,7 @@ __device__ void producer_role(const KernelArgs& a, const Shared& sh, const CUten
     for (int32_t t = it.tile_begin; t < it.tile_end && ok; ++t) {
       int32_t k0, w;
       tile_keys(bt, t, &k0, &w);
-      const int32_t page = __ldg(a.block_table + k0 / kPageSize);
+      const int32_t page = __ldg(table + k0 / kPageSize);
       int32_t tok;
       if (page < 0 || page >= a.num_pages) {
         raise_status(TPSA_DEVICE_BAD_PAGE);
@@ -570,7 +610,7 @@ __device__ void producer_role(const KernelArgs& a, const Shared& sh, const CUten
           ptx::tma_load_3d_pair(dst + dh * kKHalfBytes, km, dh * 64, it.kv_head,
                                 tok + static_cast<int32_t>(r) * half, bar_full + 8 * s);
         }
-      } else if (k0 + w <= p.seq_len) {
+      } else if (k0 + w <= req_seq_len) {
         ptx::mbar_arrive_expect_tx_cluster(bar_full + 8 * s, static_cast<uint32_t>(w) * 64 * 2);
         for (int sub = 0; sub < w / 64; ++sub) {
           ptx::tma_load_3d_pair(dst + sub * 8192, tv, static_cast<int32_t>(r) * 64, it.kv_head,
@@ -587,7 +627,7 @@ __device__ void producer_role(const KernelArgs& a, const Shared& sh, const CUten
         }
         if (!wait_bar(sh, sh.bar(kBarTail), tail_iter & 1)) { ok = false; break; }
         ++tail_iter;
-        for (int32_t row = p.seq_len - k0; row < w; ++row) {
+        for (int32_t row = req_seq_len - k0; row < w; ++row) {
           uint4* d4 = reinterpret_cast<uint4*>(sh.base + (dst - sh.base_u32) + row * 128);
 #pragma unroll
           for (int j = 0; j < 8; ++j) d4[j] = make_uint4(0, 0, 0, 0);
@@ -1150,7 +1190,7 @@ __device__ __forceinline__ void warp_arrive0(const Shared& sh, uint32_t id, int 
 // P of every tile is relative to the reference O is kept in; each keeps a
 // partial row sum over its own tiles, combined at the item's end.  At the
 // end of an item each warpgroup writes O columns [64 wg, 64 wg + 64).
-template <bool kVisit>
+template <bool kVisit, bool kVarlen>
 __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tmem,
                              const CUtensorMap* tout) {
   const tpsa_plan& p = a.plan;
@@ -1206,16 +1246,21 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
     // The previous item's output store has long read its staging buffer.
     release_q(false);
     if (rec.idx >= p.total_items) break;
-    const int32_t idx = rec.idx;
     const uint32_t qb = n_item & 1;  // this item's Q buffer (items alternate)
     const tpsa_item& it = rec.it;
     const BlockTiles& bt = rec.bt;
+    // The item's request (a batch-one launch has one, at row, item, slot and
+    // counter 0).
+    const ReqDesc& rq = a.reqs[kVarlen ? rec.req() : 0];
+    const tpsa_plan& pr = kVarlen ? rq.plan : p;
+    const int32_t q_row0 = kVarlen ? rq.q_row0 : 0;
+    const int32_t ridx = kVarlen ? rec.idx - rq.item_base : rec.idx;  // item within its request
     const int32_t tok = bt.q_begin + row / 2;
-    const int32_t q = tok < p.seq_len ? tok : p.seq_len - 1;
-    const bool sparse = row_is_sparse(p, tok);
-    const int32_t qrow = it.block * kBlockQ + row / 2;  // row within the chunk
+    const int32_t q = tok < pr.seq_len ? tok : pr.seq_len - 1;
+    const bool sparse = row_is_sparse(pr, tok);
+    const int32_t qrow = it.block * kBlockQ + row / 2;  // row within the request's chunk
     const int32_t head = it.kv_head * kGroupSize + 2 * static_cast<int32_t>(r) + (row & 1);
-    const bool real_row = qrow < p.query_tokens;
+    const bool real_row = qrow < pr.query_tokens;
     uint32_t* visit_row =
         (visit && real_row)
             ? a.visited + (static_cast<size_t>(qrow) * hq + head) * a.words_per_row
@@ -1228,7 +1273,7 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
       const uint32_t sb = gt % kNumSBufs;
       int32_t k0, w;
       tile_keys(bt, it.tile_begin + n, &k0, &w);
-      const bool masked = tile_needs_mask(p, bt, k0, w);
+      const bool masked = tile_needs_mask(pr, bt, k0, w);
       TileArgs ta;
       ta.s_addr = tmem + lane_base + (sb << 7);
       ta.o_addr = o_all;
@@ -1275,9 +1320,39 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
     ptx::tc_fence_after();
     if (row == 0 && r == 0) TPSA_TR(2 + wg, 9, 0);
     const bool split = it.num_splits > 1;
-    float* slot = a.scratch + static_cast<size_t>(idx) * kSlotFloats;
+    float* slot =
+        a.scratch + static_cast<size_t>((kVarlen ? rq.slot_base : 0) + ridx) * kSlotFloats;
     constexpr int32_t kSlotRows = 2 * kRowsPerTile;
     const int32_t srow = static_cast<int32_t>(r) * kRowsPerTile + row;
+    // Output rows of this warp: packed token base_q + R / 2, head
+    // base_h + R % 2 for warp row R; rows at or past row_end are not written.
+    const int32_t base_q = q_row0 + it.block * kBlockQ + quad * 16;
+    const int32_t base_h = it.kv_head * kGroupSize + 2 * static_cast<int32_t>(r);
+    const int32_t row_end = q_row0 + pr.query_tokens;
+    uint8_t* stage = sh.base + kOffStage + (warp - kFirstSoftmaxWarp) * kStageBytesPerWarp;
+    if (kVarlen && !split && bt.q_end - bt.q_begin < kBlockQ) {
+      // A block that ends inside its 64-token box (a request's last block):
+      // a TMA store of the box would also write rows of the next packed
+      // request, so these rows are stored one by one.  (In a batch-one
+      // launch the tensor map's end clips the last box.)
+      const float inv = 1.0f / l_total;
+#pragma unroll 1
+      for (int c = 0; c < 2; ++c) {
+        uint32_t x[32];
+        ptx::tmem_ld32(o_addr + 32 * c, x);
+        ptx::tmem_wait_ld_regs(x);
+        float o[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) o[j] = __uint_as_float(x[j]);
+        store_rows_bf16(o, inv, stage, lane, a.out, base_q, base_h, hq, row_end, 64 * wg + 32 * c);
+      }
+      ptx::tc_fence_before();
+      warp_arrive0(sh, kBarOEmpty, lane);
+      release_pending = true;  // the Q buffer returns to the producer (later)
+      pending_qb = qb;
+      if (row == 0 && r == 0) TPSA_TR(2 + wg, 5, 0);
+      continue;
+    }
     if (!split) {
       // This warpgroup's 64 output columns, as bf16, into d-half wg of the
       // item's Q buffer, which is dead (its QKs completed before the last PV)
@@ -1311,11 +1386,10 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
       warp_arrive0(sh, kBarOEmpty, lane);
       ++staged_items;
       if (store_thread && wait_count(sh, kCntStaged + wg, 4 * staged_items)) {
-        // One TMA store of this warpgroup's d-half box (clipped at
-        // query_tokens by the tensor map).
-        const int32_t hbase = it.kv_head * kGroupSize + 2 * static_cast<int32_t>(r);
+        // One TMA store of this warpgroup's d-half box (a full block: all
+        // 64 tokens belong to the item's request).
         const uint32_t src = sh.base_u32 + kOffQ + qb * kQBytes + wg * kQHalfBytes;
-        ptx::tma_store_3d(tout, 64 * wg, hbase, it.block * kBlockQ, src);
+        ptx::tma_store_3d(tout, 64 * wg, base_h, q_row0 + it.block * kBlockQ, src);
         ptx::bulk_commit_group();
       }
       release_pending = true;  // the Q buffer returns to the producer (later)
@@ -1350,8 +1424,8 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
     ++split_items;
     if (wg == 0 && row == 0) {
       if (wait_count(sh, kCntSplitW, kSoftmaxWarps * split_items)) {
-        int32_t* ctr = a.ctl + kCtlSplitBase +
-                       ((it.block - p.tail_block0) * p.kv_heads + it.kv_head) * 2 + r;
+        int32_t* ctr = a.ctl + kCtlSplitBase + (kVarlen ? rq.ctr_base : 0) +
+                       ((it.block - pr.tail_block0) * p.kv_heads + it.kv_head) * 2 + r;
         const int prev = atomicAdd(ctr, 1);
         split_last[sp_slot] = prev == it.num_splits - 1;
         ptx::red_release_add_shared(sh.counter(kCntSplitD), 1);
@@ -1364,7 +1438,7 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
     if (!decided) break;
     if (!last_split) continue;
     __threadfence();
-    const float* first_slot = a.scratch + static_cast<size_t>(idx - it.split) * kSlotFloats;
+    const float* first_slot = slot - static_cast<size_t>(it.split) * kSlotFloats;
     const size_t m_off = static_cast<size_t>(kHeadDim) * kSlotRows + srow;
     const size_t l_off = static_cast<size_t>(kHeadDim + 1) * kSlotRows + srow;
     float mmax = -INFINITY;
@@ -1378,9 +1452,6 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
       if (ms != -INFINITY) lsum += mufu_exp2((ms - mmax) * p.scale_log2) * __ldcg(sl + l_off);
     }
     const float inv_sum = 1.0f / lsum;
-    const int32_t base_q = it.block * kBlockQ + quad * 16;
-    const int32_t base_h = it.kv_head * kGroupSize + 2 * static_cast<int32_t>(r);
-    uint8_t* stage = sh.base + kOffStage + (warp - kFirstSoftmaxWarp) * kStageBytesPerWarp;
 #pragma unroll 1
     for (int c = 0; c < 2; ++c) {
       const int col = 64 * wg + 32 * c;
@@ -1396,7 +1467,7 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
 #pragma unroll
         for (int j = 0; j < 32; ++j) acc[j] += wgt * __ldcg(colp + j * kSlotRows);
       }
-      store_rows_bf16(acc, inv_sum, stage, lane, a.out, base_q, base_h, hq, p.query_tokens, col);
+      store_rows_bf16(acc, inv_sum, stage, lane, a.out, base_q, base_h, hq, row_end, col);
     }
   }
   // Output stores complete before the CTA exits.
@@ -1404,7 +1475,7 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
 }
 #undef tr_n_
 
-template <bool kVisit>
+template <bool kVisit, bool kVarlen>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kNumThreads, 1)
     tpsa_paged_kernel(const __grid_constant__ KernelArgs args,
                       const __grid_constant__ CUtensorMap tmap_q,
@@ -1463,22 +1534,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kNumThreads, 1)
   if (warp < kFirstSoftmaxWarp) {
     ptx::setmaxnreg_dec<kControlRegs>();
     if (warp == 0) {
-      if (lane == 0) producer_role(args, sh, &tmap_q, &tmap_k64, &tmap_k32, &tmap_v, false);
+      if (lane == 0) {
+        producer_role<kVarlen>(args, sh, &tmap_q, &tmap_k64, &tmap_k32, &tmap_v, false);
+      }
       __syncwarp();
     } else if (warp == 1) {
       if (sh.rank == 0) mma_role(args, sh, tmem, lane);
     } else if (warp == 2 && sh.rank == 0) {
       // The scheduler has a warp of its own: it spins on the item ring, and
       // a lane of a busy warp would compete with that warp's work.
-      if (lane == 0) scheduler_role(args, sh);
+      if (lane == 0) scheduler_role<kVarlen>(args, sh);
       __syncwarp();
     } else if (warp == 3) {
-      if (lane == 0) producer_role(args, sh, &tmap_q, &tmap_k64, &tmap_k32, &tmap_v, true);
+      if (lane == 0) {
+        producer_role<kVarlen>(args, sh, &tmap_q, &tmap_k64, &tmap_k32, &tmap_v, true);
+      }
       __syncwarp();
     }
   } else {
     ptx::setmaxnreg_inc<kSoftmaxRegs>();
-    softmax_role<kVisit>(args, sh, tmem, &tmap_out);
+    softmax_role<kVisit, kVarlen>(args, sh, tmem, &tmap_out);
   }
 
   ptx::tc_fence_before();
@@ -1531,10 +1606,13 @@ tpsa_status device_state(DeviceState** out) {
                 "the kernel is built for sm_100a (B200); current device is not");
   }
   if (!st.attr_set) {
-    e = cudaFuncSetAttribute(tpsa_paged_kernel<false>,
+    e = cudaFuncSetAttribute(tpsa_paged_kernel<false, false>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
-    e = cudaFuncSetAttribute(tpsa_paged_kernel<true>,
+    e = cudaFuncSetAttribute(tpsa_paged_kernel<true, false>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+    e = cudaFuncSetAttribute(tpsa_paged_kernel<false, true>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
     cudaLaunchConfig_t cfg = {};
@@ -1542,7 +1620,7 @@ tpsa_status device_state(DeviceState** out) {
     cfg.blockDim = dim3(kNumThreads, 1, 1);
     cfg.dynamicSmemBytes = kSmemBytes;
     int clusters = 0;
-    e = cudaOccupancyMaxActiveClusters(&clusters, tpsa_paged_kernel<false>, &cfg);
+    e = cudaOccupancyMaxActiveClusters(&clusters, tpsa_paged_kernel<false, false>, &cfg);
     if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveClusters");
     if (clusters <= 0) return fail(TPSA_ERR_CUDA, "no CTA pair fits on this device");
     st.max_pairs = clusters;
@@ -1601,9 +1679,11 @@ tpsa_status encode_map(CUtensorMap* map, const void* base, uint64_t d1, uint64_t
 
 // `pairs`: CTA pairs (2-SM clusters) the launch runs; each pair runs one item
 // at a time.
+// `split_override` > 0 replaces the split threshold derived from this
+// request's own work (a varlen launch derives it from the whole launch).
 tpsa_status build_plan(int64_t query_tokens, int64_t query_start, int64_t seq_len,
                        int64_t prompt_len, int32_t kv_heads, int32_t pairs,
-                       float scale, tpsa_plan* p) {
+                       float scale, tpsa_plan* p, int32_t split_override = 0) {
   if (p == nullptr) return fail(TPSA_ERR_INVALID_ARGUMENT, "plan pointer is NULL");
   if (!(kv_heads == 1 || kv_heads == 2 || kv_heads == 4 || kv_heads == 8)) {
     return fail(TPSA_ERR_INVALID_ARGUMENT, "kv_heads must be 1, 2, 4 or 8");
@@ -1642,7 +1722,7 @@ tpsa_status build_plan(int64_t query_tokens, int64_t query_start, int64_t seq_le
   for (int32_t b = 0; b < p->num_blocks; ++b) tiles += block_tiles(*p, b).count;
   tiles *= kv_heads;
   const double target = static_cast<double>(tiles) / pairs;
-  int32_t split = static_cast<int32_t>(0.7 * target);
+  int32_t split = split_override > 0 ? split_override : static_cast<int32_t>(0.7 * target);
   if (split < kMinSplitTiles) split = kMinSplitTiles;
   // The in-kernel merge keeps per-split weights for at most 64 splits.
   for (int32_t b = b0; b < p->num_blocks; ++b) {
@@ -1721,6 +1801,8 @@ tpsa_status launch(const void* query, const void* key_cache, const void* value_c
   if (st != TPSA_OK) return st;
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  args.num_reqs = 1;
+  args.reqs[0].plan = p;  // one request: item, row, table, slot and counter bases 0
   args.block_table = block_table;
   args.out = static_cast<__nv_bfloat16*>(out);
   args.num_pages = static_cast<int32_t>(num_pages);
@@ -1734,14 +1816,192 @@ tpsa_status launch(const void* query, const void* key_cache, const void* value_c
   args.words_per_row = (p.seq_len + 31) / 32;
 
   if (visited != nullptr || tile_counter != nullptr) {
-    tpsa_paged_kernel<true><<<p.grid, kNumThreads, kSmemBytes, s>>>(args, tq, tk64, tk32, tv,
+    tpsa_paged_kernel<true, false><<<p.grid, kNumThreads, kSmemBytes, s>>>(args, tq, tk64, tk32,
+                                                                            tv,
                                                                      tout);
   } else {
-    tpsa_paged_kernel<false><<<p.grid, kNumThreads, kSmemBytes, s>>>(args, tq, tk64, tk32, tv,
+    tpsa_paged_kernel<false, false><<<p.grid, kNumThreads, kSmemBytes, s>>>(args, tq, tk64, tk32,
+                                                                             tv,
                                                                       tout);
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
+  return TPSA_OK;
+}
+
+// ------------------------------------------------ varlen packed batch
+// Requests [first, first + count) of a packed batch as one launch: each
+// request keeps its own plan; the split threshold comes from the launch's
+// whole work; split counters and partial slots are laid out request after
+// request in the workspace.
+struct BatchLaunch {
+  KernelArgs args;
+  int64_t ctl_bytes;        // zeroed control words (scheduler + split counters)
+  int64_t workspace_bytes;  // control words + partial slots
+};
+
+tpsa_status build_batch(int32_t first, int32_t count, const int64_t* cu_seqlens_q,
+                        const int64_t* seq_lens, const int64_t* prompt_lens, int32_t kv_heads,
+                        int32_t pairs, float scale, int64_t table_cols, BatchLaunch* b) {
+  std::memset(&b->args, 0, sizeof(b->args));
+  KernelArgs& a = b->args;
+  int64_t tiles = 0;
+  for (int32_t i = 0; i < count; ++i) {
+    const int32_t r = first + i;
+    const int64_t tq = cu_seqlens_q[r + 1] - cu_seqlens_q[r];
+    tpsa_plan probe;
+    tpsa_status st = build_plan(tq, seq_lens[r] - tq, seq_lens[r], prompt_lens[r], kv_heads,
+                                pairs, scale, &probe, 1 << 30);
+    if (st != TPSA_OK) return st;
+    tiles += probe.total_tiles;
+  }
+  int32_t split = static_cast<int32_t>(0.7 * static_cast<double>(tiles) / pairs);
+  if (split < kMinSplitTiles) split = kMinSplitTiles;
+  int32_t items = 0, slots = 0, counters = 0;
+  for (int32_t i = 0; i < count; ++i) {
+    const int32_t r = first + i;
+    const int64_t tq = cu_seqlens_q[r + 1] - cu_seqlens_q[r];
+    ReqDesc& d = a.reqs[i];
+    tpsa_status st = build_plan(tq, seq_lens[r] - tq, seq_lens[r], prompt_lens[r], kv_heads,
+                                pairs, scale, &d.plan, split);
+    if (st != TPSA_OK) return st;
+    d.item_base = items;
+    d.q_row0 = static_cast<int32_t>(cu_seqlens_q[r]);
+    d.table_off = static_cast<int32_t>(static_cast<int64_t>(r) * table_cols);
+    d.slot_base = slots;
+    d.ctr_base = counters;
+    items += d.plan.total_items;
+    if (d.plan.workspace_bytes > kControlBytes) {  // the request splits some block
+      slots += d.plan.tail_items;
+      counters += (d.plan.num_blocks - d.plan.tail_block0) * kv_heads * 2;
+    }
+  }
+  a.num_reqs = count;
+  a.plan = a.reqs[0].plan;
+  a.plan.query_tokens = static_cast<int32_t>(cu_seqlens_q[first + count] - cu_seqlens_q[first]);
+  a.plan.total_items = items;
+  a.plan.total_tiles = tiles;
+  a.plan.grid = 2 * (items < pairs ? items : pairs);
+  const int64_t ctl = (int64_t{kCtlSplitBase} + counters) * 4;
+  b->ctl_bytes = std::max<int64_t>(kControlBytes, (ctl + 255) / 256 * 256);
+  b->workspace_bytes = b->ctl_bytes + static_cast<int64_t>(slots) * kSlotBytes;
+  a.plan.workspace_bytes = b->workspace_bytes;
+  return TPSA_OK;
+}
+
+tpsa_status check_batch(int32_t batch, const int64_t* cu_seqlens_q, const int64_t* seq_lens,
+                        const int64_t* prompt_lens) {
+  if (batch <= 0) return fail(TPSA_ERR_INVALID_ARGUMENT, "batch must be positive");
+  if (cu_seqlens_q == nullptr || seq_lens == nullptr || prompt_lens == nullptr) {
+    return fail(TPSA_ERR_INVALID_ARGUMENT, "a batch metadata pointer is NULL");
+  }
+  if (cu_seqlens_q[0] != 0) return fail(TPSA_ERR_INVALID_ARGUMENT, "cu_seqlens_q[0] must be 0");
+  for (int32_t r = 0; r < batch; ++r) {
+    const int64_t tq = cu_seqlens_q[r + 1] - cu_seqlens_q[r];
+    if (tq <= 0) {
+      return fail(TPSA_ERR_INVALID_ARGUMENT, "each ragged query length must be positive");
+    }
+    if (seq_lens[r] < tq) {
+      return fail(TPSA_ERR_INVALID_ARGUMENT, "seq_lens[i] must cover the request's query rows");
+    }
+  }
+  if (cu_seqlens_q[batch] > (int64_t{1} << 31) - 1) {
+    return fail(TPSA_ERR_INVALID_ARGUMENT, "packed query rows above 2^31 - 1");
+  }
+  return TPSA_OK;
+}
+
+tpsa_status varlen_workspace(int32_t batch, const int64_t* cu_seqlens_q, const int64_t* seq_lens,
+                             const int64_t* prompt_lens, int32_t pairs, uint64_t* bytes) {
+  tpsa_status st = check_batch(batch, cu_seqlens_q, seq_lens, prompt_lens);
+  if (st != TPSA_OK) return st;
+  std::unique_ptr<BatchLaunch> b(new BatchLaunch);
+  int64_t most = kControlBytes;
+  for (int32_t first = 0; first < batch; first += kMaxReqs) {
+    const int32_t count = std::min(kMaxReqs, batch - first);
+    st = build_batch(first, count, cu_seqlens_q, seq_lens, prompt_lens, TPSA_KV_HEADS, pairs,
+                     1.0f, 1, b.get());
+    if (st != TPSA_OK) return st;
+    most = std::max(most, b->workspace_bytes);
+  }
+  *bytes = static_cast<uint64_t>(most);
+  return TPSA_OK;
+}
+
+tpsa_status launch_varlen(const void* query, const void* key_cache, const void* value_cache,
+                          const int32_t* block_tables, void* out, int32_t batch,
+                          const int64_t* cu_seqlens_q, const int64_t* seq_lens,
+                          const int64_t* prompt_lens, int64_t num_pages, int64_t table_cols,
+                          float scale, void* workspace, uint64_t workspace_bytes, void* stream) {
+  t_last_error.clear();
+  if (query == nullptr || key_cache == nullptr || value_cache == nullptr ||
+      block_tables == nullptr || out == nullptr) {
+    return fail(TPSA_ERR_INVALID_ARGUMENT, "a tensor pointer is NULL");
+  }
+  if (num_pages <= 0 || num_pages > (int64_t{1} << 24)) {
+    return fail(TPSA_ERR_INVALID_ARGUMENT, "num_pages must be in [1, 2^24]");
+  }
+  tpsa_status st = check_batch(batch, cu_seqlens_q, seq_lens, prompt_lens);
+  if (st != TPSA_OK) return st;
+  for (int32_t r = 0; r < batch; ++r) {
+    if (table_cols < (seq_lens[r] + kPageSize - 1) / kPageSize) {
+      return fail(TPSA_ERR_INVALID_ARGUMENT,
+                  "block_tables lack logical pages required by seq_lens");
+    }
+  }
+  if (static_cast<int64_t>(batch) * table_cols > (int64_t{1} << 31) - 1) {
+    return fail(TPSA_ERR_INVALID_ARGUMENT, "block_tables above 2^31 - 1 entries");
+  }
+  if (workspace == nullptr || reinterpret_cast<uintptr_t>(workspace) % 256 != 0) {
+    return fail(TPSA_ERR_WORKSPACE, "workspace must be non-NULL and 256-byte aligned");
+  }
+  for (const void* ptr : {query, key_cache, value_cache, static_cast<const void*>(out)}) {
+    if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0) {
+      return fail(TPSA_ERR_INVALID_ARGUMENT, "tensors must be 16-byte aligned");
+    }
+  }
+  DeviceState* dev = nullptr;
+  st = device_state(&dev);
+  if (st != TPSA_OK) return st;
+  const uint64_t total_rows = static_cast<uint64_t>(cu_seqlens_q[batch]);
+  CUtensorMap tq, tk64, tk32, tv, tout;
+  const uint64_t hq = static_cast<uint64_t>(TPSA_KV_HEADS) * kGroupSize;
+  const uint64_t cache_tokens = static_cast<uint64_t>(num_pages) * kPageSize;
+  st = encode_map(&tq, query, hq, total_rows, 2, kBlockQ);
+  if (st != TPSA_OK) return st;
+  st = encode_map(&tk64, key_cache, TPSA_KV_HEADS, cache_tokens, 1, 64);
+  if (st != TPSA_OK) return st;
+  st = encode_map(&tk32, key_cache, TPSA_KV_HEADS, cache_tokens, 1, 32);
+  if (st != TPSA_OK) return st;
+  st = encode_map(&tv, value_cache, TPSA_KV_HEADS, cache_tokens, 1, 64);
+  if (st != TPSA_OK) return st;
+  st = encode_map(&tout, out, hq, total_rows, 2, kBlockQ);
+  if (st != TPSA_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  std::unique_ptr<BatchLaunch> b(new BatchLaunch);
+  // Launches of at most kMaxReqs requests each, in stream order; each
+  // reuses the workspace after the previous one.
+  for (int32_t first = 0; first < batch; first += kMaxReqs) {
+    const int32_t count = std::min(kMaxReqs, batch - first);
+    st = build_batch(first, count, cu_seqlens_q, seq_lens, prompt_lens, TPSA_KV_HEADS,
+                     dev->max_pairs, scale, table_cols, b.get());
+    if (st != TPSA_OK) return st;
+    if (workspace_bytes < static_cast<uint64_t>(b->workspace_bytes)) {
+      return fail(TPSA_ERR_WORKSPACE, "workspace smaller than tpsa_varlen_workspace_size()");
+    }
+    KernelArgs& args = b->args;
+    args.block_table = block_tables;
+    args.out = static_cast<__nv_bfloat16*>(out);
+    args.num_pages = static_cast<int32_t>(num_pages);
+    args.ctl = static_cast<int32_t*>(workspace);
+    args.scratch = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + b->ctl_bytes);
+    cudaError_t e = cudaMemsetAsync(workspace, 0, static_cast<size_t>(b->ctl_bytes), s);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(workspace)");
+    tpsa_paged_kernel<false, true><<<args.plan.grid, kNumThreads, kSmemBytes, s>>>(
+        args, tq, tk64, tk32, tv, tout);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
+  }
   return TPSA_OK;
 }
 
@@ -1872,6 +2132,29 @@ tpsa_status tpsa_paged_attention(const void* query, const void* key_cache,
   return launch(query, key_cache, value_cache, block_table, out, query_tokens, num_pages,
                 table_cols, query_start, seq_len, prompt_len, scale, TPSA_KV_HEADS,
                 workspace, workspace_bytes, nullptr, nullptr, stream);
+}
+
+tpsa_status tpsa_varlen_workspace_size(int32_t batch, const int64_t* cu_seqlens_q,
+                                       const int64_t* seq_lens, const int64_t* prompt_lens,
+                                       uint64_t* bytes) {
+  t_last_error.clear();
+  if (bytes == nullptr) return fail(TPSA_ERR_INVALID_ARGUMENT, "bytes pointer is NULL");
+  DeviceState* dev = nullptr;
+  tpsa_status st = device_state(&dev);
+  if (st != TPSA_OK) return st;
+  return varlen_workspace(batch, cu_seqlens_q, seq_lens, prompt_lens, dev->max_pairs, bytes);
+}
+
+tpsa_status tpsa_paged_attention_varlen(const void* query, const void* key_cache,
+                                        const void* value_cache, const int32_t* block_tables,
+                                        void* out, int32_t batch, const int64_t* cu_seqlens_q,
+                                        const int64_t* seq_lens, const int64_t* prompt_lens,
+                                        int64_t num_pages, int64_t table_cols, float scale,
+                                        void* workspace, uint64_t workspace_bytes,
+                                        void* stream) {
+  return launch_varlen(query, key_cache, value_cache, block_tables, out, batch, cu_seqlens_q,
+                       seq_lens, prompt_lens, num_pages, table_cols, scale, workspace,
+                       workspace_bytes, stream);
 }
 
 tpsa_status tpsa_paged_attention_heads(const void* query, const void* key_cache,

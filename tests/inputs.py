@@ -67,3 +67,35 @@ def inputs_digest(*tensors: torch.Tensor) -> str:
         h.update(t.contiguous().view(torch.uint8).numpy().tobytes() if t.dtype != torch.int32
                  else t.contiguous().numpy().tobytes())
     return h.hexdigest()
+
+
+def varlen_inputs(specs, seed: int = 0, spare_pages: int = 5):
+    """A packed ragged batch over one shared page pool.
+
+    ``specs`` lists (query_rows, seq_len, prompt_len) per request; request i's
+    query rows are the last ``query_rows`` of its first ``seq_len`` tokens.
+    Pages of all requests are drawn without replacement from one random
+    permutation of the pool, so every request has its own scattered pages.
+    Returns (packed query, key pool, value pool, block_tables [B, max_pages]
+    padded with page 0, per-request [1, pages] tables, cu_seqlens_q).
+    """
+    gen = torch.Generator().manual_seed(seed)
+    logical = [math.ceil(seq / PAGE) for _, seq, _ in specs]
+    physical = sum(logical) + spare_pages
+    perm = torch.randperm(physical, generator=gen, dtype=torch.int64)
+    cols = max(logical)
+    tables = torch.zeros(len(specs), cols, dtype=torch.int32)
+    per_request, used = [], 0
+    for i, n in enumerate(logical):
+        row = perm[used:used + n].to(torch.int32)
+        used += n
+        tables[i, :n] = row
+        per_request.append(row.view(1, -1).contiguous())
+    cu = [0]
+    for rows, _, _ in specs:
+        cu.append(cu[-1] + rows)
+    q = torch.randn(cu[-1], QUERY_HEADS, HEAD_DIM, generator=gen).to(torch.bfloat16)
+    shape = (physical, PAGE, KV_HEADS, HEAD_DIM)
+    k = torch.randn(shape, generator=gen).to(torch.bfloat16)
+    v = torch.randn(shape, generator=gen).to(torch.bfloat16)
+    return q, k, v, tables.contiguous(), per_request, cu

@@ -1,0 +1,96 @@
+"""Packed ragged batches (varlen) through the C ABI.
+
+Semantics: the reference's packed-batch helper reference_attention_ragged_python
+(operator/tests/triangle_v2_reference.py:437-487) computes a packed batch as
+the batch-one operator applied to each request's slice of rows.  Every case
+here checks each request's rows against the CPU oracle on that request alone
+(same key sets, its own pages of the shared pool), within the parity
+tolerance.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from gpu_helpers import assert_close, run_cabi
+from inputs import SCALE, varlen_inputs
+from oracle.triangle_oracle import oracle_attention
+
+pytestmark = pytest.mark.gpu
+
+
+def _run_varlen(tm, dev, q, k, v, tables, cu, seq_lens, prompt_lens):
+    out = torch.full_like(q, float("nan"), device=dev)
+    tm._native.paged_attention_varlen(q.to(dev), k.to(dev), v.to(dev), tables.to(dev), out, cu,
+                                      seq_lens, prompt_lens, SCALE)
+    torch.cuda.synchronize(dev)
+    assert tm._native.device_status(dev.index or 0) == 0
+    return out.cpu()
+
+
+def _check_against_oracle(out, q, k, v, per_request, cu, specs, what):
+    for i, (rows, seq, prompt) in enumerate(specs):
+        got = out[cu[i]:cu[i + 1]]
+        ref = oracle_attention(q[cu[i]:cu[i + 1]], k, v, per_request[i], seq - rows, seq, prompt,
+                               SCALE)
+        assert_close(got, ref.to(torch.bfloat16), f"{what} request {i} ({rows}/{seq}/{prompt})")
+
+
+# (query rows, seq_len, prompt_len): ragged last blocks (37, 65, 200),
+# chunked requests (rows < seq_len), prompt_len > seq_len (sparse tail
+# moved past the chunk), requests that cross 521 and the dense tail, one
+# exactly block-aligned request.
+MIXED = [
+    (37, 37, 37),
+    (200, 900, 900),
+    (64, 1024, 4096),
+    (530, 530, 530),
+    (65, 2113, 2113),
+    (1000, 1700, 2500),
+    (128, 128, 128),
+]
+
+
+def test_varlen_mixed_batch_matches_oracle_per_request(tm, cuda_device):
+    q, k, v, tables, per_request, cu = varlen_inputs(MIXED, seed=21)
+    out = _run_varlen(tm, cuda_device, q, k, v, tables, cu, [s for _, s, _ in MIXED],
+                      [p for _, _, p in MIXED])
+    _check_against_oracle(out, q, k, v, per_request, cu, MIXED, "mixed")
+
+
+def test_varlen_more_than_one_launch(tm, cuda_device):
+    """19 requests: launches of 16 and 3 requests reuse one workspace."""
+    gen = torch.Generator().manual_seed(5)
+    specs = []
+    for _ in range(19):
+        seq = int(torch.randint(40, 1400, (1,), generator=gen))
+        rows = int(torch.randint(1, seq + 1, (1,), generator=gen))
+        specs.append((rows, seq, seq + int(torch.randint(0, 300, (1,), generator=gen))))
+    q, k, v, tables, per_request, cu = varlen_inputs(specs, seed=22)
+    out = _run_varlen(tm, cuda_device, q, k, v, tables, cu, [s for _, s, _ in specs],
+                      [p for _, _, p in specs])
+    _check_against_oracle(out, q, k, v, per_request, cu, specs, "19 requests")
+
+
+def test_varlen_split_kv_requests(tm, cuda_device):
+    """Long dense tails split across items inside a varlen launch."""
+    specs = [(1024, 12288, 12288), (256, 9000, 9000), (64, 3000, 3000)]
+    q, k, v, tables, per_request, cu = varlen_inputs(specs, seed=23)
+    seq_lens, prompt_lens = [s for _, s, _ in specs], [p for _, _, p in specs]
+    assert tm._native.varlen_workspace_size(cu, seq_lens, prompt_lens) > 2048, \
+        "the batch must use split-KV partial slots"
+    out = _run_varlen(tm, cuda_device, q, k, v, tables, cu, seq_lens, prompt_lens)
+    _check_against_oracle(out, q, k, v, per_request, cu, specs, "split")
+
+
+def test_varlen_equals_batch_one_calls(tm, cuda_device):
+    """Each request's rows equal a batch-one call on the same inputs."""
+    specs = [(300, 300, 300), (96, 777, 777), (513, 1500, 1600)]
+    q, k, v, tables, per_request, cu = varlen_inputs(specs, seed=24)
+    out = _run_varlen(tm, cuda_device, q, k, v, tables, cu, [s for _, s, _ in specs],
+                      [p for _, _, p in specs])
+    for i, (rows, seq, prompt) in enumerate(specs):
+        one = run_cabi(tm, q[cu[i]:cu[i + 1]], k, v, per_request[i], seq - rows, seq, prompt,
+                       cuda_device)
+        assert_close(out[cu[i]:cu[i + 1]], one, f"request {i} vs batch-one")

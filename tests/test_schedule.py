@@ -157,3 +157,23 @@ def test_workspace_is_control_words_without_splits(tm):
     # scheduler's control words are needed.
     plan = tm._native.make_plan(2048, 2048, 4096, 8320, 8, SM)
     assert plan.workspace_bytes == 2048 and plan.tail_items == 0
+
+
+@pytest.mark.parametrize("cu, seq_lens, prompt_lens, message", [
+    ([0, 10, 10], [10, 20], [10, 20], "each ragged query length must be positive"),
+    ([1, 10], [10], [10], "cu_seqlens_q[0] must be 0"),
+    ([0, 30], [20], [20], "seq_lens[i] must cover the request's query rows"),
+])
+def test_varlen_metadata_gates_on_host(tm, cu, seq_lens, prompt_lens, message):
+    """The packed-batch gates run before any device call (reference
+    triangle_v2_reference.py:466-475 rejects the same metadata)."""
+    import ctypes
+
+    nat = tm._native
+    fake = ctypes.c_void_p(0x1000)  # never dereferenced: the metadata gate fails first
+    st = nat.lib().tpsa_paged_attention_varlen(fake, fake, fake, fake, fake, len(seq_lens),
+                                               nat._int64_array(cu), nat._int64_array(seq_lens),
+                                               nat._int64_array(prompt_lens), 8, 1, 0.088, fake,
+                                               1 << 20, None)
+    assert st == 1  # TPSA_ERR_INVALID_ARGUMENT
+    assert message in nat.lib().tpsa_last_error().decode()
