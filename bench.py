@@ -233,6 +233,103 @@ def run_reference_arm(args, rank: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+def make_batch_inputs(batch: int, seed: int = 0):
+    """B one-chunk prompts, lengths U[2048, 16384] (seeded),
+    per-request block tables drawn from one shared random page pool."""
+    gen = torch.Generator().manual_seed(seed)
+    lens = torch.randint(2048, 16385, (batch,), generator=gen).tolist()
+    logical = [math.ceil(n / PAGE) for n in lens]
+    physical = sum(logical) + batch
+    perm = torch.randperm(physical, generator=gen).to(torch.int32)
+    tables = torch.zeros(batch, max(logical), dtype=torch.int32)
+    used = 0
+    for i, n in enumerate(logical):
+        tables[i, :n] = perm[used:used + n]
+        used += n
+    cu = [0]
+    for n in lens:
+        cu.append(cu[-1] + n)
+    q = torch.randn(cu[-1], QUERY_HEADS, HEAD_DIM, generator=gen).to(torch.bfloat16)
+    k = torch.randn(physical, PAGE, KV_HEADS, HEAD_DIM, generator=gen).to(torch.bfloat16)
+    v = torch.randn(physical, PAGE, KV_HEADS, HEAD_DIM, generator=gen).to(torch.bfloat16)
+    return lens, cu, q, k, v, tables
+
+
+def run_batch(args) -> None:
+    """Config 4 on one GPU: the whole packed batch per step through
+    tpsa_paged_attention_varlen, beside the same requests as batch-one calls."""
+    from __graft_entry__ import load_package
+
+    tm = load_package()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    lens, cu, q, k, v, tables = make_batch_inputs(args.batch)
+    qd, kd, vd, td = q.to(dev), k.to(dev), v.to(dev), tables.to(dev)
+    out = torch.empty_like(qd)
+    ws = torch.empty(tm._native.varlen_workspace_size(cu, lens, lens), dtype=torch.uint8,
+                     device=dev)
+    one = [torch.empty(tm._native.make_plan(n, 0, n, n).workspace_bytes, dtype=torch.uint8,
+                       device=dev) for n in lens]
+    stream = torch.cuda.current_stream(dev)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+
+    def varlen_step():
+        tm._native.paged_attention_varlen(qd, kd, vd, td, out, cu, lens, lens, SCALE,
+                                          workspace=ws, stream=stream.cuda_stream)
+
+    def batch_one_step():
+        for i, n in enumerate(lens):
+            tm._native.paged_attention(qd[cu[i]:cu[i + 1]], kd, vd, td[i:i + 1],
+                                       out[cu[i]:cu[i + 1]], 0, n, n, SCALE, workspace=one[i],
+                                       stream=stream.cuda_stream)
+
+    def timed(fn) -> float:
+        for _ in range(args.warmup):
+            flush.fill_(1.0)
+            fn()
+        torch.cuda.synchronize(dev)
+        ms = []
+        for i in range(args.steps):
+            flush.fill_(float(i))
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+            ms.append(e0.elapsed_time(e1))
+        return sum(ms) / len(ms)
+
+    sampler = ClockSampler(0)
+    sampler.start()
+    ms_varlen = timed(varlen_step)
+    clocks = sampler.stop()
+    ms_seq = timed(batch_one_step)
+    status = tm._native.device_status(0)
+    if status:
+        raise RuntimeError(f"device status {status:#x}")
+    pairs = sum(effective_pairs(0, n, n, n) for n in lens)
+    flops = 4.0 * HEAD_DIM * QUERY_HEADS * pairs
+    peaks, peak_kind = load_peaks()
+    value = flops / (ms_varlen * 1e-3) / 1e12
+    line = {"metric": METRIC, "value": value, "unit": "TFLOP/s (effective)", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_varlen,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) bf16, lengths U[2048,16384])",
+            "config": {"workload": f"varlen_batch{args.batch}", "batch": args.batch,
+                       "lengths": lens, "tokens": cu[-1],
+                       "geometry": "Qwen3-8B attention (Hq=32, Hkv=8, D=128, page 128)",
+                       "l2": "flushed between timed steps (256 MiB write)"},
+            "gpu_launches": args.steps * ((args.batch + 15) // 16), "clocks": clocks,
+            "roofline": {"bound": "tensor", "achieved": value, "peak": peaks["bf16_tflops"],
+                         "unit": "TFLOP/s", "frac": value / peaks["bf16_tflops"],
+                         "traffic": None, "peak_source": f"{peak_kind} bf16_tflops (burst)",
+                         "kernel": "tpsa_paged_kernel<false, true>"},
+            "batch_one_calls": {"ms_per_step": ms_seq,
+                                "value": flops / (ms_seq * 1e-3) / 1e12,
+                                "launches_per_step": args.batch}}
+    print(json.dumps(line), flush=True)
+
+
 def workload_config(args) -> dict:
     name = "prefill_8k" if args.seq_len == 8192 else f"prefill_{args.seq_len // 1024}k_q{args.query_tokens}"
     return {"workload": name, "seq_len": args.seq_len, "query_tokens": args.query_tokens,
@@ -253,6 +350,8 @@ def main() -> None:
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="BASELINE config 4: a packed batch of this many prompts (one GPU)")
     ap.add_argument("--validate", action="store_true",
                     help="N > 1: all-gather the head slices of layer 0 over NCCL and compare "
                          "them with a full-layer run on rank 0 (outside the timing)")
@@ -269,6 +368,11 @@ def main() -> None:
         ap.error(f"--gpus {args.gpus} but WORLD_SIZE={world}")
     if args.impl == "reference":
         run_reference_arm(args, rank)
+        return
+    if args.batch:
+        if world != 1:
+            ap.error("--batch runs on one GPU")
+        run_batch(args)
         return
 
     from __graft_entry__ import load_package
