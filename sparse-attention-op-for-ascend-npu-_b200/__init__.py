@@ -11,9 +11,12 @@ Layers, bottom up:
   _native.py            ctypes binding of the C ABI
   kernel.py             reference-compatible direct-path API
   sharding.py           KV-head partition across 1/2/4/8 GPUs
+  config.py, planning.py, stats.py, plugin.py
+                        serving integration: configuration, per-step plans,
+                        counters, and the router / vLLM FlashAttention hook
 """
 
-from . import _native, sharding
+from . import _native, config, planning, plugin, sharding, stats
 from ._native import TpsaError, load_adapter
 from .kernel import (
     TriangleMixConfig,
@@ -50,5 +53,9 @@ __all__ = [
     "triangle_sparse_span",
     "triangle_streaming_start",
     "_native",
+    "config",
+    "planning",
+    "plugin",
     "sharding",
+    "stats",
 ]

@@ -1,0 +1,111 @@
+"""Typed TriangleMix plugin configuration (vLLM ``additional_config`` or environment).
+
+Same keys, environment variable names, defaults and validation errors as the
+reference plugin's configuration (package/src/vllm_ascend_trianglemix/
+config.py:11-197 in the reference project), so a deployment switches over
+without touching its configuration.  The section is
+``additional_config["trianglemix"]`` (or the top-level ``additional_config``
+mapping); a key present there wins over its environment variable.
+"""
+
+from __future__ import annotations
+
+import os
+from dataclasses import dataclass
+from typing import Any, Mapping
+
+from .kernel import TriangleMixConfig, parse_layer_indices
+
+_TRUE = frozenset({"1", "true", "yes", "on"})
+_FALSE = frozenset({"0", "false", "no", "off"})
+
+
+def coerce_bool(value: object, *, name: str) -> bool:
+    """bool, 0/1, or one of the usual true/false words (config.py:16-29)."""
+    if isinstance(value, bool):
+        return value
+    if isinstance(value, int) and value in (0, 1):
+        return bool(value)
+    if isinstance(value, str):
+        word = value.strip().lower()
+        if word in _TRUE:
+            return True
+        if word in _FALSE:
+            return False
+    raise ValueError(f"TriangleMix {name} must be a boolean, got {value!r}")
+
+
+# key -> (environment variable, default)
+_KEYS: dict[str, tuple[str, Any]] = {
+    "enabled": ("VLLM_ASCEND_ENABLE_TRIANGLE_MIX", False),
+    "layers": ("VLLM_ASCEND_TRIANGLE_MIX_LAYERS", ""),
+    "sink_tokens": ("VLLM_ASCEND_TRIANGLE_MIX_SINK_TOKENS", 8),
+    "local_window": ("VLLM_ASCEND_TRIANGLE_MIX_LOCAL_WINDOW", 512),
+    "last_rows": ("VLLM_ASCEND_TRIANGLE_MIX_LAST_ROWS", 128),
+    "min_seq_len": ("VLLM_ASCEND_TRIANGLE_MIX_DIRECT_MIN_SEQ_LEN", 0),
+    "min_sparse_rows": ("VLLM_ASCEND_TRIANGLE_MIX_DIRECT_MIN_SPARSE_ROWS", 128),
+    "min_saved_qk": ("VLLM_ASCEND_TRIANGLE_MIX_DIRECT_MIN_SAVED_QK", 913_152),
+    "split_min_sparse_rows": ("VLLM_ASCEND_TRIANGLE_MIX_DIRECT_SPLIT_MIN_SPARSE_ROWS", 192),
+    "split_min_saved_qk": ("VLLM_ASCEND_TRIANGLE_MIX_DIRECT_SPLIT_MIN_SAVED_QK", 1_299_264),
+    "strict": ("VLLM_ASCEND_TRIANGLE_MIX_STRICT", False),
+    "stats_recent_capacity": ("VLLM_ASCEND_TRIANGLE_MIX_STATS_RECENT_CAPACITY", 256),
+    "stats_log_interval": ("VLLM_ASCEND_TRIANGLE_MIX_STATS_LOG_INTERVAL", 0),
+}
+
+
+def _lookup(section: Mapping[str, Any], key: str) -> Any:
+    env, default = _KEYS[key]
+    if key in section:
+        return section[key]
+    raw = os.getenv(env)
+    if raw is None:
+        return default
+    if isinstance(default, bool):
+        return coerce_bool(raw, name=env)
+    if isinstance(default, int):
+        return int(raw)
+    return raw
+
+
+@dataclass(frozen=True)
+class PluginConfig:
+    """Process configuration shared by the planner and the attention hook."""
+
+    kernel: TriangleMixConfig
+    strict: bool = False
+    stats_recent_capacity: int = 256
+    stats_log_interval: int = 0
+
+    @property
+    def enabled(self) -> bool:
+        return self.kernel.enabled and bool(self.kernel.layer_indices)
+
+
+def resolve_plugin_config(vllm_config: object | None) -> PluginConfig:
+    """Resolve the typed configuration, preferring ``additional_config.trianglemix``."""
+    additional = getattr(vllm_config, "additional_config", None)
+    additional = additional if isinstance(additional, Mapping) else {}
+    section = additional.get("trianglemix", additional)
+    section = section if isinstance(section, Mapping) else {}
+    layers = _lookup(section, "layers")
+    if isinstance(layers, (list, tuple, set, frozenset)):
+        layers = ",".join(str(x) for x in layers)
+    kernel = TriangleMixConfig(
+        enabled=coerce_bool(_lookup(section, "enabled"), name="enabled"),
+        layer_indices=parse_layer_indices(str(layers)),
+        sink_tokens=int(_lookup(section, "sink_tokens")),
+        local_window=int(_lookup(section, "local_window")),
+        last_rows=int(_lookup(section, "last_rows")),
+        direct_min_seq_len=int(_lookup(section, "min_seq_len")),
+        direct_min_sparse_rows=int(_lookup(section, "min_sparse_rows")),
+        direct_min_saved_qk=int(_lookup(section, "min_saved_qk")),
+        direct_split_min_sparse_rows=int(_lookup(section, "split_min_sparse_rows")),
+        direct_split_min_saved_qk=int(_lookup(section, "split_min_saved_qk")),
+    )
+    recent = int(_lookup(section, "stats_recent_capacity"))
+    interval = int(_lookup(section, "stats_log_interval"))
+    if recent < 0 or interval < 0:
+        raise ValueError("TriangleMix stats capacities must be non-negative")
+    return PluginConfig(kernel=kernel,
+                        strict=coerce_bool(_lookup(section, "strict"), name="strict"),
+                        stats_recent_capacity=recent, stats_log_interval=interval)
