@@ -156,10 +156,10 @@ enum BarId : uint32_t {
 constexpr uint32_t kPairWgArrivals = kSoftmaxWarps;  // 4 warps x 2 CTAs
 constexpr uint32_t kPairWarpArrivals = 2 * kSoftmaxWarps;
 constexpr uint32_t kItemConsumers = 2 * (2 + kSoftmaxWarps) + 1;
-// q_empty: the MMA issuer's commit after the item's last QK, plus one arrival
-// from each softmax warpgroup of this CTA once its output store has read the
-// buffer (the finished item's Q buffer stages its output rows).
-constexpr uint32_t kQEmptyArrivals = 3;
+// q_empty: the MMA issuer's commit after the item's last QK.  (The finished
+// item's Q buffer then stages its output rows; the K producer stores them
+// and waits for the store to read the buffer before it loads the next Q.)
+constexpr uint32_t kQEmptyArrivals = 1;
 
 constexpr uint32_t kOffItemSlots = (kOffBar + kNumBars * 8 + 15) & ~15u;  // 2 x ItemRec
 constexpr uint32_t kOffTmemSlot = kOffItemSlots + 2 * 64;
@@ -533,10 +533,32 @@ __device__ void scheduler_role(const KernelArgs& a, const Shared& sh) {
 // lookahead.  Both CTAs of the pair load their halves with pair TMA loads
 // that complete on CTA 0's full barrier: of K, keys [r*half, (r+1)*half)
 // of the tile, all 128 d; of V, all keys of the tile, d-half r.
+// An item's output box staged in its Q buffer, to be stored by the K producer.
+struct PendingStore {
+  bool stages;          // a full, unsplit block: its epilogue stages the box
+  uint32_t staged;      // staged items up to and including this one
+  int32_t head, token;  // box coordinates in `out` (d is 0 and 64)
+};
+
+// Waits until both softmax warpgroups staged item `ps`, TMA-stores its two
+// d-half boxes from Q buffer qb, and waits until the stores have read it.
+__device__ __forceinline__ void flush_store(const Shared& sh, const CUtensorMap* tout,
+                                            PendingStore& ps, uint32_t qb) {
+  if (!ps.stages) return;
+  ps.stages = false;
+  if (!wait_count(sh, kCntStaged + 0, 4 * ps.staged)) return;
+  if (!wait_count(sh, kCntStaged + 1, 4 * ps.staged)) return;
+  const uint32_t src = sh.base_u32 + kOffQ + qb * kQBytes;
+  ptx::tma_store_3d(tout, 0, ps.head, ps.token, src);
+  ptx::tma_store_3d(tout, 64, ps.head, ps.token, src + kQHalfBytes);
+  ptx::bulk_commit_group();
+  ptx::bulk_wait_group_read<0>();
+}
+
 template <bool kVarlen>
 __device__ void producer_role(const KernelArgs& a, const Shared& sh, const CUtensorMap* tq,
                               const CUtensorMap* tk64, const CUtensorMap* tk32,
-                              const CUtensorMap* tv, bool v_side) {
+                              const CUtensorMap* tv, const CUtensorMap* tout, bool v_side) {
   const tpsa_plan& p = a.plan;
   const uint32_t r = sh.rank;
   if (v_side) {
@@ -550,6 +572,9 @@ __device__ void producer_role(const KernelArgs& a, const Shared& sh, const CUten
   const uint32_t bar_empty = sh.bar(v_side ? kBarVEmpty : kBarKEmpty);
   const uint32_t ring_base = sh.base_u32 + (v_side ? kOffV : kOffK);
   uint32_t ring = 0, q_iter = 0, tail_iter = 0;
+  // K side: the output boxes staged in the two Q buffers, and staged items so far.
+  PendingStore pend0{false, 0, 0, 0}, pend1{false, 0, 0, 0};  // Q buffers 0 and 1
+  uint32_t staged = 0;
   bool ok = true;
   TPSA_TRACE_STATE;
   for (uint32_t n = 0; ok; ++n) {
@@ -568,8 +593,29 @@ __device__ void producer_role(const KernelArgs& a, const Shared& sh, const CUten
 
     if (!v_side) {
       // Q: this CTA's 128 rows (64 tokens x query heads 4h + 2r, 4h + 2r + 1).
+      // The buffer last held item n - 2: its QKs completed (q_empty) and its
+      // output, if staged there, is stored first.
       const uint32_t qb = q_iter % 2;
-      if (q_iter >= 2 && !wait_bar(sh, sh.bar(kBarQEmpty + qb), ((q_iter / 2) - 1) & 1)) break;
+      if (q_iter >= 2) {
+        if (qb == 0) {
+          flush_store(sh, tout, pend0, 0);
+        } else {
+          flush_store(sh, tout, pend1, 1);
+        }
+        if (!wait_bar(sh, sh.bar(kBarQEmpty + qb), ((q_iter / 2) - 1) & 1)) break;
+      }
+      const bool full_block = !kVarlen || bt.q_end - bt.q_begin == kBlockQ;
+      PendingStore cur;
+      cur.stages = it.num_splits == 1 && full_block;
+      staged += cur.stages ? 1u : 0u;
+      cur.staged = staged;
+      cur.head = it.kv_head * kGroupSize + 2 * static_cast<int32_t>(r);
+      cur.token = q_row0 + it.block * kBlockQ;
+      if (qb == 0) {
+        pend0 = cur;
+      } else {
+        pend1 = cur;
+      }
       ptx::mbar_arrive_expect_tx_cluster(sh.bar0(kBarQFull + qb), kQBytes);
       for (int dh = 0; dh < 2; ++dh) {
         ptx::tma_load_3d_pair(sh.base_u32 + kOffQ + qb * kQBytes + dh * kQHalfBytes, tq, dh * 64,
@@ -637,6 +683,20 @@ __device__ void producer_role(const KernelArgs& a, const Shared& sh, const CUten
       }
       if (r == 0) TPSA_TR(v_side ? 4 : 0, 22, t);
     }
+  }
+  if (!v_side) {
+    // The last two items' outputs, oldest first, complete before the CTA
+    // exits (flush_store gives up if the softmax aborted).
+    if (ok && !*sh.abort_flag()) {
+      if (q_iter % 2 == 0) {
+        flush_store(sh, tout, pend0, 0);
+        flush_store(sh, tout, pend1, 1);
+      } else {
+        flush_store(sh, tout, pend1, 1);
+        flush_store(sh, tout, pend0, 0);
+      }
+    }
+    ptx::bulk_wait_group<0>();
   }
   if (!ok || *sh.abort_flag()) {
     // Aborted: give in-flight TMA loads time to land before the CTA exits.
@@ -1191,8 +1251,7 @@ __device__ __forceinline__ void warp_arrive0(const Shared& sh, uint32_t id, int 
 // partial row sum over its own tiles, combined at the item's end.  At the
 // end of an item each warpgroup writes O columns [64 wg, 64 wg + 64).
 template <bool kVisit, bool kVarlen>
-__device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tmem,
-                             const CUtensorMap* tout) {
+__device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tmem) {
   const tpsa_plan& p = a.plan;
   const uint32_t r = sh.rank;
   const int warp = threadIdx.x / 32;
@@ -1205,8 +1264,8 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
   const bool visit = kVisit && a.visited != nullptr;
   // Tiles of the pair's stream before the current item.
   uint32_t g = 0;
-  // Items whose output this warpgroup staged, and split items so far.
-  uint32_t staged_items = 0, split_items = 0;
+  // Split items so far.
+  uint32_t split_items = 0;
   RowChannel ch;
   static_assert(kCntCon == kCntPub + 8, "read counters follow the publication counters");
   ch.mine = sh.base_u32 + kOffXchg + (wg * kChanSlots * 128 + row) * 4;
@@ -1215,22 +1274,6 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
   ch.peer_pub = sh.counter(kCntPub + (1 - wg) * 4 + quad);
   ch.n_pub = 0;
   ch.n_read = 0;
-  // The first thread of each warpgroup issues that warpgroup's output store
-  // and releases the Q buffer that staged it.
-  const bool store_thread = quad == 0 && lane == 0;
-  bool release_pending = false;
-  uint32_t pending_qb = 0;
-  auto release_q = [&](bool full_completion) {
-    if (store_thread && release_pending) {
-      if (full_completion) {
-        ptx::bulk_wait_group<0>();
-      } else {
-        ptx::bulk_wait_group_read<0>();
-      }
-      ptx::mbar_arrive(sh.bar(kBarQEmpty + pending_qb));
-      release_pending = false;
-    }
-  };
   volatile int* split_last = reinterpret_cast<volatile int*>(sh.base + kOffSplitLast);
   uint32_t tr_sm = 0;  // trace counter (used only with TPSA_TRACE)
 #define tr_n_ tr_sm
@@ -1243,8 +1286,6 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
     if (!__all_sync(0xffffffffu, got)) break;
     __syncwarp();
     if (lane == 0) release_item(sh, n_item);
-    // The previous item's output store has long read its staging buffer.
-    release_q(false);
     if (rec.idx >= p.total_items) break;
     const uint32_t qb = n_item & 1;  // this item's Q buffer (items alternate)
     const tpsa_item& it = rec.it;
@@ -1348,8 +1389,6 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
       }
       ptx::tc_fence_before();
       warp_arrive0(sh, kBarOEmpty, lane);
-      release_pending = true;  // the Q buffer returns to the producer (later)
-      pending_qb = qb;
       if (row == 0 && r == 0) TPSA_TR(2 + wg, 5, 0);
       continue;
     }
@@ -1376,24 +1415,15 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
               pack_bf16x2(__uint_as_float(v[6]) * inv, __uint_as_float(v[7]) * inv));
         }
       }
-      // Each warp releases O only after its staged count: the next item's
-      // counts need its PVs, which need O, so every count of this item lands
-      // before any count of the next one.
+      // The K producer stores the staged box (TMA) before it reuses this Q
+      // buffer.  Each warp releases O only after its staged count: the next
+      // item's counts need its PVs, which need O, so every count of this
+      // item lands before any count of the next one.
       ptx::fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) ptx::red_release_add_shared(sh.counter(kCntStaged + wg), 1);
       ptx::tc_fence_before();
       warp_arrive0(sh, kBarOEmpty, lane);
-      ++staged_items;
-      if (store_thread && wait_count(sh, kCntStaged + wg, 4 * staged_items)) {
-        // One TMA store of this warpgroup's d-half box (a full block: all
-        // 64 tokens belong to the item's request).
-        const uint32_t src = sh.base_u32 + kOffQ + qb * kQBytes + wg * kQHalfBytes;
-        ptx::tma_store_3d(tout, 64 * wg, base_h, q_row0 + it.block * kBlockQ, src);
-        ptx::bulk_commit_group();
-      }
-      release_pending = true;  // the Q buffer returns to the producer (later)
-      pending_qb = qb;
       if (row == 0 && r == 0) TPSA_TR(2 + wg, 5, 0);
       continue;
     }
@@ -1415,8 +1445,6 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
       slot[kHeadDim * kSlotRows + srow] = st.m_ref;
       slot[(kHeadDim + 1) * kSlotRows + srow] = l_total;
     }
-    release_pending = true;
-    pending_qb = qb;
     __threadfence();
     __syncwarp();
     if (lane == 0) ptx::red_release_add_shared(sh.counter(kCntSplitW), 1);
@@ -1470,8 +1498,6 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
       store_rows_bf16(acc, inv_sum, stage, lane, a.out, base_q, base_h, hq, row_end, col);
     }
   }
-  // Output stores complete before the CTA exits.
-  release_q(true);
 }
 #undef tr_n_
 
@@ -1535,7 +1561,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kNumThreads, 1)
     ptx::setmaxnreg_dec<kControlRegs>();
     if (warp == 0) {
       if (lane == 0) {
-        producer_role<kVarlen>(args, sh, &tmap_q, &tmap_k64, &tmap_k32, &tmap_v, false);
+        producer_role<kVarlen>(args, sh, &tmap_q, &tmap_k64, &tmap_k32, &tmap_v, &tmap_out,
+                               false);
       }
       __syncwarp();
     } else if (warp == 1) {
@@ -1547,13 +1574,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kNumThreads, 1)
       __syncwarp();
     } else if (warp == 3) {
       if (lane == 0) {
-        producer_role<kVarlen>(args, sh, &tmap_q, &tmap_k64, &tmap_k32, &tmap_v, true);
+        producer_role<kVarlen>(args, sh, &tmap_q, &tmap_k64, &tmap_k32, &tmap_v, &tmap_out,
+                               true);
       }
       __syncwarp();
     }
   } else {
     ptx::setmaxnreg_inc<kSoftmaxRegs>();
-    softmax_role<kVisit, kVarlen>(args, sh, tmem, &tmap_out);
+    softmax_role<kVisit, kVarlen>(args, sh, tmem);
   }
 
   ptx::tc_fence_before();
