@@ -1170,6 +1170,11 @@ __device__ __forceinline__ bool softmax_tile(const Shared& sh, const tpsa_plan& 
     if (!__any_sync(0xffffffffu, m2 != m_new)) break;
     m_new = m2;
   }
+  // The decision is final here: pass it on before the remaining
+  // exponentials, so that the other warpgroup's next tile, which reads it
+  // half-way through, does not wait for them.
+  if (!ch.publish(sh, m_new)) return false;
+  TPSA_TILE_TR(t, 31);
   {
     const float neg_mb = m_new == -INFINITY ? 0.0f : -m_new * sl2;
     const uint32_t p_kept = p_addr + (t.wide ? 32 : 0);
@@ -1177,8 +1182,6 @@ __device__ __forceinline__ bool softmax_tile(const Shared& sh, const tpsa_plan& 
     exp_chunk(rb, sl2, neg_mb, p_kept + 16, sum0, sum1);
   }
   TPSA_TILE_TR(t, 32);
-  if (!ch.publish(sh, m_new)) return false;
-  TPSA_TILE_TR(t, 31);
   const bool moved = m_new != st.m_ref;
   if (__any_sync(0xffffffffu, moved)) {
     float factor = 1.0f;
