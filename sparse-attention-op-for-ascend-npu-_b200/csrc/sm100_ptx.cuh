@@ -451,6 +451,53 @@ __device__ __forceinline__ void umma_commit_pair_elect(uint32_t bar) {
       : "memory");
 }
 
+// Forms issued by the lanes whose `leader` is nonzero (one lane of the warp,
+// elected once): a predicate instead of an elect.sync per instruction.
+__device__ __forceinline__ uint32_t elect_one() {
+  uint32_t pred;
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "selp.b32 %0, 1, 0, e;\n\t}"
+      : "=r"(pred));
+  return pred;
+}
+
+__device__ __forceinline__ void umma_ss_pair_if(uint32_t leader, uint32_t d_tmem, uint64_t a_desc,
+                                                uint64_t b_desc, uint32_t idesc,
+                                                uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t"
+      "setp.ne.b32 e, %5, 0;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(leader)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_ts_pair_if(uint32_t leader, uint32_t d_tmem, uint32_t a_tmem,
+                                                uint64_t b_desc, uint32_t idesc,
+                                                uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t"
+      "setp.ne.b32 e, %5, 0;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(leader)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit_pair_mc_if(uint32_t leader, uint32_t bar,
+                                                       uint16_t cta_mask) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "setp.ne.b32 e, %2, 0;\n\t"
+      "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 "
+      "[%0], %1;\n\t}" ::"r"(bar),
+      "h"(cta_mask), "r"(leader)
+      : "memory");
+}
+
 // ------------------------------------------------------------ descriptors
 // Shared-memory matrix descriptor, SWIZZLE_128B, 1024-byte aligned atoms.
 //   bits  0-13 start address >> 4     bits 16-29 leading byte offset >> 4

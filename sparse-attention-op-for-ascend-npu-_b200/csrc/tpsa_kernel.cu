@@ -68,7 +68,9 @@ __device__ uint32_t g_device_status = 0;
 #ifndef TPSA_TRACE_CLUSTER
 #define TPSA_TRACE_CLUSTER 0  // CTA pair whose events are recorded
 #endif
-constexpr uint32_t kTraceRoles = 5;
+// Roles: 0 K producer, 1 MMA issuer, 2-3 softmax warpgroups of CTA 0,
+// 4 V producer, 5-6 softmax warpgroups of CTA 1.
+constexpr uint32_t kTraceRoles = 7;
 constexpr uint32_t kTraceCap = 1u << 14;
 __device__ unsigned long long g_trace[kTraceRoles][kTraceCap][2];
 __device__ uint32_t g_trace_n[kTraceRoles];
@@ -306,10 +308,9 @@ __device__ __forceinline__ void drain_bar(uint32_t bar, uint32_t parity) {
 
 // Bounded wait until the monotonic shared counter `id` reaches `target`
 // (wrap-safe comparison); gives up like wait_bar.
-__device__ __forceinline__ bool wait_count_at(const Shared& sh, uint32_t addr, uint32_t target) {
-  if (static_cast<int32_t>(ptx::ld_acquire_shared(addr) - target) >= 0) return true;
+__device__ __forceinline__ bool wait_count_slow(volatile int* abort_flag, uint32_t addr,
+                                            uint32_t target) {
   const uint64_t t0 = ptx::globaltimer_ns();
-  volatile int* abort_flag = sh.abort_flag();
   while (static_cast<int32_t>(ptx::ld_acquire_shared(addr) - target) < 0) {
     if (*abort_flag) return false;
     if (ptx::globaltimer_ns() - t0 > kWaitTimeoutNs) {
@@ -320,6 +321,10 @@ __device__ __forceinline__ bool wait_count_at(const Shared& sh, uint32_t addr, u
     }
   }
   return true;
+}
+__device__ __forceinline__ bool wait_count_at(const Shared& sh, uint32_t addr, uint32_t target) {
+  if (static_cast<int32_t>(ptx::ld_acquire_shared(addr) - target) >= 0) return true;
+  return wait_count_slow(sh.abort_flag(), addr, target);
 }
 __device__ __forceinline__ bool wait_count(const Shared& sh, uint32_t id, uint32_t target) {
   return wait_count_at(sh, sh.counter(id), target);
@@ -739,9 +744,13 @@ __device__ void mma_role(const KernelArgs& a, const Shared& sh, uint32_t tmem, i
   constexpr uint32_t kIdQk64 = ptx::idesc_bf16_f32(256, 64, 0);
   constexpr uint32_t kIdPv = ptx::idesc_bf16_f32(256, 128, 1);
 
+  // One lane, elected once, issues every tcgen05 instruction of this role
+  // under a predicate (an elect.sync per instruction costs more).
+  const uint32_t leader = ptx::elect_one();
   auto warp_wait = [&](uint32_t bar, uint32_t parity) -> bool {
     return __all_sync(0xffffffffu, wait_bar(sh, bar, parity));
   };
+
   // S(buf) = Q K^T for the key tile in ring slot `slot` (M = 256 over the
   // pair, N = 128 or 64).
   auto issue_qk = [&](uint32_t q_lo, uint32_t slot, uint32_t buf, bool narrow) {
@@ -752,8 +761,7 @@ __device__ void mma_role(const KernelArgs& a, const Shared& sh, uint32_t tmem, i
     for (int k = 0; k < 8; ++k) {
       const uint32_t qo = (k / 4) * (kQHalfBytes >> 4) + (k % 4) * 2;
       const uint32_t ko = (k / 4) * (kKHalfBytes >> 4) + (k % 4) * 2;
-      ptx::umma_ss_pair_elect(d, desc(q_lo + qo, q_hi), desc(k_lo + ko, k_hi), idesc,
-                              k > 0 ? 1u : 0u);
+      ptx::umma_ss_pair_if(leader, d, desc(q_lo + qo, q_hi), desc(k_lo + ko, k_hi), idesc, k > 0 ? 1u : 0u);
     }
   };
   // O += P V: P (bf16 pairs) over columns 64-127 of S buffer buf, V the
@@ -765,8 +773,8 @@ __device__ void mma_role(const KernelArgs& a, const Shared& sh, uint32_t tmem, i
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       if (k < 4 || !narrow) {
-        ptx::umma_ts_pair_elect(d, pa + k * 8, desc(v_lo + k * (2048 >> 4), v_hi), kIdPv,
-                          (first && k == 0) ? 0u : 1u);
+        ptx::umma_ts_pair_if(leader, d, pa + k * 8, desc(v_lo + k * (2048 >> 4), v_hi), kIdPv,
+                             (first && k == 0) ? 0u : 1u);
       }
     }
   };
@@ -851,9 +859,9 @@ __device__ void mma_role(const KernelArgs& a, const Shared& sh, uint32_t tmem, i
     ptx::tc_fence_after();
     issue_qk(q_qd, slot_q, sb_q, plan_narrow);
     if (lane == 0) TPSA_TR(1, 18, sb_q);
-    ptx::umma_commit_pair_mc_elect(bar_s_full + 8 * sb_q, kPairMask);
-    ptx::umma_commit_pair_mc_elect(bar_k_empty + 8 * slot_q, kPairMask);
-    if (q_n == q_ntiles - 1) ptx::umma_commit_pair_mc_elect(bar_q_empty + 8 * q_qb, kPairMask);
+    ptx::umma_commit_pair_mc_if(leader, bar_s_full + 8 * sb_q, kPairMask);
+    ptx::umma_commit_pair_mc_if(leader, bar_k_empty + 8 * slot_q, kPairMask);
+    if (q_n == q_ntiles - 1) ptx::umma_commit_pair_mc_if(leader, bar_q_empty + 8 * q_qb, kPairMask);
     slot_q = (slot_q + 1) & (kRing - 1);
     phase_q ^= slot_q == 0 ? 1u : 0u;
     sb_q = sb_q == kNumSBufs - 1 ? 0 : sb_q + 1;
@@ -888,19 +896,22 @@ __device__ void mma_role(const KernelArgs& a, const Shared& sh, uint32_t tmem, i
     // Q wait may not depend on PV(t)); otherwise refill takes it after PV(t).
     const bool planned = plan_qk(info0 >> kTItemShift);
     if (!ok) break;
+    if (lane == 0) TPSA_TR(1, 12, sb_v);
     if (info0 & kTItemStart) {
       // O of the previous item (item index k - 1) has been read by its
       // epilogue: phase (k - 2) & 1 of o_empty.
       if (!warp_wait(bar_o_empty, (info0 & kTItemOdd) ? 0u : 1u)) { ok = false; break; }
+      if (lane == 0) TPSA_TR(1, 11, sb_v);
     }
     if (!warp_wait(bar_p_full + 8 * sb_v, pass_v & 1)) { ok = false; break; }
+    if (lane == 0) TPSA_TR(1, 13, sb_v);
     if (!warp_wait(bar_v_full + 8 * slot_v, phase_v)) { ok = false; break; }
     if (lane == 0) TPSA_TR(1, 14, sb_v);
     ptx::tc_fence_after();
     issue_pv(slot_v, sb_v, (info0 & kTNarrow) != 0, (info0 & kTFirst) != 0);
     if (lane == 0) TPSA_TR(1, 15, sb_v);
-    ptx::umma_commit_pair_mc_elect(bar_v_empty + 8 * slot_v, kPairMask);
-    ptx::umma_commit_pair_mc_elect(bar_pv_done + 8 * sb_v, kPairMask);
+    ptx::umma_commit_pair_mc_if(leader, bar_v_empty + 8 * slot_v, kPairMask);
+    ptx::umma_commit_pair_mc_if(leader, bar_pv_done + 8 * sb_v, kPairMask);
     const uint32_t fired = planned ? fire_qk() : 0u;
     if (lane == 0) TPSA_TR(1, 16, sb_v);
     slot_v = (slot_v + 1) & (kRing - 1);
@@ -917,6 +928,7 @@ __device__ void mma_role(const KernelArgs& a, const Shared& sh, uint32_t tmem, i
     --have;
     if (fired != 0) push(fired);
     refill();
+    if (lane == 0) TPSA_TR(1, 23, have);
   }
   // All MMAs issued by this warp complete before TMEM is released.
   ptx::umma_commit_pair_elect(sh.bar(kBarDrain));
@@ -1071,6 +1083,7 @@ struct TileArgs {
   uint32_t o_addr;      // O (128 columns)
   int32_t k0;           // first key of the tile
   bool wide;            // 128 keys (else 64)
+  bool masked;          // some key of the tile is outside some row's key set
   bool first;           // first tile of the item (its PV overwrites O)
   uint32_t prev_bar;    // pv_done barrier of the previous tile, and its parity
   uint32_t prev_parity;
@@ -1092,14 +1105,15 @@ struct TileArgs {
 #endif
 
 // Keeps the visited bits of a 32-key chunk (debug output) and masks it.
-template <bool kMasked, bool kVisit>
-__device__ __forceinline__ void prepare_chunk(uint32_t (&r)[32], int32_t q, bool sparse, int32_t kc,
-                                              uint32_t* visit_row, int32_t words_per_row) {
-  const uint32_t m = kMasked ? chunk_mask(q, sparse, kc) : ~0u;
+template <bool kVisit>
+__device__ __forceinline__ void prepare_chunk(uint32_t (&r)[32], bool mk, int32_t q, bool sparse,
+                                              int32_t kc, uint32_t* visit_row,
+                                              int32_t words_per_row) {
+  const uint32_t m = mk ? chunk_mask(q, sparse, kc) : ~0u;
   if (kVisit && visit_row != nullptr && m != 0 && kc / 32 < words_per_row) {
     atomicOr(visit_row + kc / 32, m);
   }
-  if (kMasked) mask_chunk(r, m);
+  if (mk) mask_chunk(r, m);
 }
 
 // One key tile of this warpgroup, the whole row of this thread: load S,
@@ -1112,7 +1126,7 @@ __device__ __forceinline__ void prepare_chunk(uint32_t (&r)[32], int32_t q, bool
 // twice (for the max, then for the exponentials), which keeps 64 of them
 // live at a time: their P lands over S columns 64-127 only after those
 // were read.  Returns false if a wait gave up.
-template <bool kMasked, bool kVisit>
+template <bool kVisit>
 __device__ __forceinline__ bool softmax_tile(const Shared& sh, const tpsa_plan& p,
                                              const TileArgs& t, int32_t q, bool sparse,
                                              RowChannel& ch, RowState& st,
@@ -1122,16 +1136,16 @@ __device__ __forceinline__ bool softmax_tile(const Shared& sh, const tpsa_plan& 
   ptx::tmem_ld32(t.s_addr + 32, rb);
   ptx::tmem_wait_ld_regs(ra);
   ptx::tmem_fence_regs(rb);
-  prepare_chunk<kMasked, kVisit>(ra, q, sparse, t.k0, visit_row, words_per_row);
-  prepare_chunk<kMasked, kVisit>(rb, q, sparse, t.k0 + 32, visit_row, words_per_row);
+  prepare_chunk<kVisit>(ra, t.masked, q, sparse, t.k0, visit_row, words_per_row);
+  prepare_chunk<kVisit>(rb, t.masked, q, sparse, t.k0 + 32, visit_row, words_per_row);
   float lm = fmaxf(chunk_max(ra), chunk_max(rb));
   if (t.wide) {
     ptx::tmem_ld32(t.s_addr + 64, ra);
     ptx::tmem_ld32(t.s_addr + 96, rb);
     ptx::tmem_wait_ld_regs(ra);
     ptx::tmem_fence_regs(rb);
-    prepare_chunk<kMasked, kVisit>(ra, q, sparse, t.k0 + 64, visit_row, words_per_row);
-    prepare_chunk<kMasked, kVisit>(rb, q, sparse, t.k0 + 96, visit_row, words_per_row);
+    prepare_chunk<kVisit>(ra, t.masked, q, sparse, t.k0 + 64, visit_row, words_per_row);
+    prepare_chunk<kVisit>(rb, t.masked, q, sparse, t.k0 + 96, visit_row, words_per_row);
     lm = fmaxf(lm, fmaxf(chunk_max(ra), chunk_max(rb)));
   }
   TPSA_TILE_TR(t, 30);
@@ -1157,7 +1171,7 @@ __device__ __forceinline__ bool softmax_tile(const Shared& sh, const tpsa_plan& 
         uint32_t rc[32];
         ptx::tmem_ld32(t.s_addr + 32 * c, rc);
         ptx::tmem_wait_ld_regs(rc);
-        if (kMasked) mask_chunk(rc, chunk_mask(q, sparse, t.k0 + 32 * c));
+        if (t.masked) mask_chunk(rc, chunk_mask(q, sparse, t.k0 + 32 * c));
         exp_chunk(rc, sl2, neg_mb, p_addr + 16 * c, sum0, sum1);
       }
     }
@@ -1326,19 +1340,21 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
       ta.first = n == 0;
       ta.prev_bar = sh.bar(kBarPvDone + (gt - 1) % kNumSBufs);
       ta.prev_parity = ((gt - 1) / kNumSBufs) & 1;
-      ta.trn = (row == 0 && r == 0) ? &tr_sm : nullptr;
-      ta.trole = 2 + wg;
+      ta.trn = row == 0 ? &tr_sm : nullptr;
+      ta.trole = 2 + wg + 3 * r;
       const bool w_ok = wait_bar(sh, sh.bar(kBarSFull + sb), (gt / kNumSBufs) & 1);
       if (!__all_sync(0xffffffffu, w_ok)) { ok = false; break; }
-      if (row == 0 && r == 0) TPSA_TR(2 + wg, 1, n);
+      if (row == 0) TPSA_TR(2 + wg + 3 * r, 1, n);
       ptx::tc_fence_after();
+      // One instantiation for masked and unmasked tiles (a uniform branch
+      // around the masking): a second copy of this code would compete with
+      // the MMA issuer's loop for the instruction cache.
+      ta.masked = masked;
       const bool t_ok =
-          masked
-              ? softmax_tile<true, kVisit>(sh, p, ta, q, sparse, ch, st, visit_row, a.words_per_row)
-              : softmax_tile<false, kVisit>(sh, p, ta, q, sparse, ch, st, visit_row, a.words_per_row);
+          softmax_tile<kVisit>(sh, p, ta, q, sparse, ch, st, visit_row, a.words_per_row);
       if (!t_ok) { ok = false; break; }
       ptx::tc_fence_before();
-      if (row == 0 && r == 0) TPSA_TR(2 + wg, 3, n);
+      if (row == 0) TPSA_TR(2 + wg + 3 * r, 3, n);
       warp_arrive0(sh, kBarPFull + sb, lane);
     }
     if (!ok) break;
@@ -1362,7 +1378,7 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
       break;
     }
     ptx::tc_fence_after();
-    if (row == 0 && r == 0) TPSA_TR(2 + wg, 9, 0);
+    if (row == 0) TPSA_TR(2 + wg + 3 * r, 9, 0);
     const bool split = it.num_splits > 1;
     float* slot =
         a.scratch + static_cast<size_t>((kVarlen ? rq.slot_base : 0) + ridx) * kSlotFloats;
@@ -1392,7 +1408,7 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
       }
       ptx::tc_fence_before();
       warp_arrive0(sh, kBarOEmpty, lane);
-      if (row == 0 && r == 0) TPSA_TR(2 + wg, 5, 0);
+      if (row == 0) TPSA_TR(2 + wg + 3 * r, 5, 0);
       continue;
     }
     if (!split) {
@@ -1427,7 +1443,7 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
       if (lane == 0) ptx::red_release_add_shared(sh.counter(kCntStaged + wg), 1);
       ptx::tc_fence_before();
       warp_arrive0(sh, kBarOEmpty, lane);
-      if (row == 0 && r == 0) TPSA_TR(2 + wg, 5, 0);
+      if (row == 0) TPSA_TR(2 + wg + 3 * r, 5, 0);
       continue;
     }
 
@@ -2254,7 +2270,7 @@ TPSA_API void tpsa_debug_timeout(uint32_t* out5) {
 }
 
 TPSA_API uint32_t tpsa_debug_trace(uint32_t role, unsigned long long* out, uint32_t max_events) {
-  uint32_t n[kTraceRoles] = {0, 0, 0, 0, 0};
+  uint32_t n[kTraceRoles] = {};
   cudaDeviceSynchronize();
   if (role >= kTraceRoles) {  // softmax sub-phase buffers of CTA role - 4
     return 0;
