@@ -17,28 +17,24 @@
 //     (for S = Q K^T) and d-half r of V (for O = P V), so every K/V byte is
 //     loaded once per pair and serves 4 query heads.
 // Roles (384 threads per CTA):
-//   warp 0      TMA producer; in CTA 0 also the work scheduler (a global
-//               counter, longest items first), which hands items to CTA 1
-//               through its shared memory
+//   warp 0      K producer (Q of each item, K half-tiles; stores finished
+//               output boxes)
 //   warp 1      CTA 0: tcgen05 MMA issuer; both: TMEM owner
-//   warps 2-3   idle (they complete the control warpgroup for setmaxnreg)
-//   warps 4-11  two softmax warpgroups.  Key tile gt of the pair's global
-//               tile sequence belongs to warpgroup gt % 2, which keeps its
-//               own S buffer, O accumulator and row (max, sum) over whole
-//               128-column rows; the two partial results of an item are
-//               merged once at its end.  While one warpgroup exponentiates,
-//               the tensor pipe runs the other's QK and PV.
-// Tensor memory per CTA (fp32 columns): S0 [0,128), S1 [128,256),
-// O0 [256,384), O1 [384,512).  P (bf16 pairs) overwrites the first half of
-// its S buffer and PV(n) reads it from there.  MMA issue order per item:
-//   QK(0), QK(1), PV(0), QK(2), PV(1), QK(3), ...
-// so QK(n+1) (the other warpgroup's S) runs while tile n's softmax is
-// computed.  The O rescale for a grown row max is lazy (only when the max
-// grows by more than 2^8) and done by the softmax warps in tensor memory.
+//   warp 2      CTA 0: work scheduler (global counter, longest items first;
+//               item records into both CTAs' item rings)
+//   warp 3      V producer (V half-tiles)
+//   warps 4-11  two softmax warpgroups.  Key tile gt of the pair's tile
+//               stream belongs to warpgroup gt % 2; both work on the same
+//               rows and pass each row's lazy reference max from tile to
+//               tile, so P of every tile is relative to the reference O is
+//               kept in.  The owner of an item's last tile finishes the item.
+// Tensor memory per CTA (fp32 columns): three S buffers [0,384) and the O
+// accumulator [384,512).  Tile gt uses S buffer gt % 3; its P (bf16 pairs)
+// overwrites columns 64-127 of that buffer and PV(gt) reads it there.  The
+// issuer runs QK up to three tiles ahead of PV across item boundaries.
 //
 // Softmax arithmetic: scores are scaled into the log2 domain with one fused
-// multiply-add, exponentiated with ex2.approx (MUFU) for 3 of every 4 column
-// pairs and with poly_exp2_x2 (FMA pipe) for the fourth, summed in fp32, and
+// multiply-add, exponentiated with ex2.approx (MUFU), summed in fp32, and
 // rounded to bf16 (round-to-nearest-even) for the PV product, as the
 // reference does (vendor block_epilogue_online_softmax.hpp:886-906).
 #include <cuda.h>
@@ -75,9 +71,13 @@ constexpr uint32_t kTraceCap = 1u << 14;
 __device__ unsigned long long g_trace[kTraceRoles][kTraceCap][2];
 __device__ uint32_t g_trace_n[kTraceRoles];
 #define TPSA_TRACE_STATE uint32_t tr_n_ = 0
+#ifndef TPSA_TRACE_EVMASK
+#define TPSA_TRACE_EVMASK ~0ull  // events recorded (bit ev)
+#endif
 #define TPSA_TR(role, ev, arg)                                                    \
   do {                                                                            \
-    if ((blockIdx.x >> 1) == TPSA_TRACE_CLUSTER && tr_n_ < kTraceCap) {           \
+    if (((TPSA_TRACE_EVMASK >> (ev)) & 1ull) &&                                   \
+        (blockIdx.x >> 1) == TPSA_TRACE_CLUSTER && tr_n_ < kTraceCap) {           \
       g_trace[role][tr_n_][0] = (static_cast<unsigned long long>(ev) << 32) |     \
                                 static_cast<uint32_t>(arg);                        \
       g_trace[role][tr_n_][1] = clock64();                                        \
@@ -156,7 +156,6 @@ enum BarId : uint32_t {
 // item_empty takes the two producers, the MMA issuer and the 8 softmax
 // warps of CTA 0 plus the two producers and the 8 softmax warps of CTA 1.
 constexpr uint32_t kPairWgArrivals = kSoftmaxWarps;  // 4 warps x 2 CTAs
-constexpr uint32_t kPairWarpArrivals = 2 * kSoftmaxWarps;
 constexpr uint32_t kItemConsumers = 2 * (2 + kSoftmaxWarps) + 1;
 // q_empty: the MMA issuer's commit after the item's last QK.  (The finished
 // item's Q buffer then stages its output rows; the K producer stores them
@@ -1085,6 +1084,7 @@ struct TileArgs {
   bool wide;            // 128 keys (else 64)
   bool masked;          // some key of the tile is outside some row's key set
   bool first;           // first tile of the item (its PV overwrites O)
+  bool last;            // last tile of the item (its decision is not passed on)
   uint32_t prev_bar;    // pv_done barrier of the previous tile, and its parity
   uint32_t prev_parity;
   uint32_t* trn;        // trace counter of this thread when it records (TPSA_TRACE)
@@ -1187,7 +1187,7 @@ __device__ __forceinline__ bool softmax_tile(const Shared& sh, const tpsa_plan& 
   // The decision is final here: pass it on before the remaining
   // exponentials, so that the other warpgroup's next tile, which reads it
   // half-way through, does not wait for them.
-  if (!ch.publish(sh, m_new)) return false;
+  if (!t.last && !ch.publish(sh, m_new)) return false;
   TPSA_TILE_TR(t, 31);
   {
     const float neg_mb = m_new == -INFINITY ? 0.0f : -m_new * sl2;
@@ -1295,7 +1295,6 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
   uint32_t tr_sm = 0;  // trace counter (used only with TPSA_TRACE)
 #define tr_n_ tr_sm
   const uint32_t o_all = tmem + lane_base + kTmemO;  // O, 128 columns
-  const uint32_t o_addr = o_all + 64 * wg;             // this warpgroup's output columns
 
   for (uint32_t n_item = 0;; ++n_item) {
     ItemRec rec;
@@ -1338,6 +1337,7 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
       ta.k0 = k0;
       ta.wide = w > 64;
       ta.first = n == 0;
+      ta.last = n == ntiles - 1;
       ta.prev_bar = sh.bar(kBarPvDone + (gt - 1) % kNumSBufs);
       ta.prev_parity = ((gt - 1) / kNumSBufs) & 1;
       ta.trn = row == 0 ? &tr_sm : nullptr;
@@ -1360,26 +1360,35 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
     if (!ok) break;
     g += static_cast<uint32_t>(ntiles);
 
-    // Item end.  The final reference is the last tile's (read from the
-    // other warpgroup if it owned that tile); the row sum is the two
-    // partial sums; O is complete once the item's last PV has.
+    // Item end.  The warpgroup that owned the item's last tile (the owner)
+    // finishes the item alone: its reference is final, and the other
+    // warpgroup, if it owned any tile of the item, hands over its reference
+    // and partial row sum and goes on to the next item at once (whose first
+    // tile is its own), so the next item's first P does not wait for this
+    // epilogue.  O is complete once the item's last PV has.
     const uint32_t gl = g - 1;
-    if ((gl & 1) != static_cast<uint32_t>(wg)) {
-      float mp;
-      if (!ch.read(sh, &mp)) break;
-      adopt_ref(st, mp, p.scale_log2);
+    const bool owner = (gl & 1) == static_cast<uint32_t>(wg);
+    const bool shared_item = ntiles >= 2;
+    const bool split = it.num_splits > 1;
+    const uint32_t sp_slot = split_items & 1;
+    split_items += split ? 1u : 0u;
+    if (!owner) {
+      if (shared_item && !(ch.publish(sh, st.m_ref) && ch.publish(sh, st.l_part))) break;
+      continue;
     }
-    if (!ch.publish(sh, st.l_part)) break;
-    float l_peer;
-    if (!ch.read(sh, &l_peer)) break;
-    const float l_total = st.l_part + l_peer;
+    float l_total = st.l_part;
+    if (shared_item) {
+      float m_peer, l_peer;
+      if (!ch.read(sh, &m_peer) || !ch.read(sh, &l_peer)) break;
+      // The peer's reference is at most the final one (references only grow).
+      if (m_peer != -INFINITY) l_total += l_peer * mufu_exp2((m_peer - st.m_ref) * p.scale_log2);
+    }
     if (!__all_sync(0xffffffffu, wait_bar(sh, sh.bar(kBarPvDone + gl % kNumSBufs),
                                           (gl / kNumSBufs) & 1))) {
       break;
     }
     ptx::tc_fence_after();
     if (row == 0) TPSA_TR(2 + wg + 3 * r, 9, 0);
-    const bool split = it.num_splits > 1;
     float* slot =
         a.scratch + static_cast<size_t>((kVarlen ? rq.slot_base : 0) + ridx) * kSlotFloats;
     constexpr int32_t kSlotRows = 2 * kRowsPerTile;
@@ -1397,14 +1406,14 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
       // launch the tensor map's end clips the last box.)
       const float inv = 1.0f / l_total;
 #pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
+      for (int c = 0; c < 4; ++c) {
         uint32_t x[32];
-        ptx::tmem_ld32(o_addr + 32 * c, x);
+        ptx::tmem_ld32(o_all + 32 * c, x);
         ptx::tmem_wait_ld_regs(x);
         float o[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) o[j] = __uint_as_float(x[j]);
-        store_rows_bf16(o, inv, stage, lane, a.out, base_q, base_h, hq, row_end, 64 * wg + 32 * c);
+        store_rows_bf16(o, inv, stage, lane, a.out, base_q, base_h, hq, row_end, 32 * c);
       }
       ptx::tc_fence_before();
       warp_arrive0(sh, kBarOEmpty, lane);
@@ -1412,20 +1421,20 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
       continue;
     }
     if (!split) {
-      // This warpgroup's 64 output columns, as bf16, into d-half wg of the
-      // item's Q buffer, which is dead (its QKs completed before the last PV)
-      // and has the output tile's shape (per d-half, [64 tokens x 2 heads]
-      // rows of 64 d, 128-byte swizzled as the Q tensor map loads it).
+      // The 128 output columns, as bf16, into the item's Q buffer, which is
+      // dead (its QKs completed before the last PV) and has the output tile's
+      // shape (per d-half, [64 tokens x 2 heads] rows of 64 d, 128-byte
+      // swizzled as the Q tensor map loads it).
       const float inv = 1.0f / l_total;
-      uint8_t* dst = sh.base + kOffQ + qb * kQBytes + wg * kQHalfBytes + row * 128;
 #pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
+      for (int c = 0; c < 4; ++c) {
+        uint8_t* dst = sh.base + kOffQ + qb * kQBytes + (c >> 1) * kQHalfBytes + row * 128;
         uint32_t x[32];
-        ptx::tmem_ld32(o_addr + 32 * c, x);
+        ptx::tmem_ld32(o_all + 32 * c, x);
         ptx::tmem_wait_ld_regs(x);
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj) {
-          const int j = 4 * c + jj;  // 16-byte chunk within the d-half row
+          const int j = 4 * (c & 1) + jj;  // 16-byte chunk within the d-half row
           const uint32_t* v = &x[8 * jj];
           *reinterpret_cast<uint4*>(dst + ((j ^ (row & 7)) << 4)) = make_uint4(
               pack_bf16x2(__uint_as_float(v[0]) * inv, __uint_as_float(v[1]) * inv),
@@ -1435,42 +1444,41 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
         }
       }
       // The K producer stores the staged box (TMA) before it reuses this Q
-      // buffer.  Each warp releases O only after its staged count: the next
-      // item's counts need its PVs, which need O, so every count of this
-      // item lands before any count of the next one.
+      // buffer; it counts four warps per d-half.  Each warp releases O only
+      // after its staged counts: the next item's counts need its PVs, which
+      // need O, so every count of this item lands before any of the next.
       ptx::fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) ptx::red_release_add_shared(sh.counter(kCntStaged + wg), 1);
+      if (lane == 0) {
+        ptx::red_release_add_shared(sh.counter(kCntStaged + 0), 1);
+        ptx::red_release_add_shared(sh.counter(kCntStaged + 1), 1);
+      }
       ptx::tc_fence_before();
       warp_arrive0(sh, kBarOEmpty, lane);
       if (row == 0) TPSA_TR(2 + wg + 3 * r, 5, 0);
       continue;
     }
 
-    // Split item: the fp32 partial of this warpgroup's 64 columns into the
-    // item's column-major slot ([128 columns][256 rows], then m[256] and
-    // l[256]); the last split of the block (per CTA of the pair) merges all
-    // partials and writes bf16.
+    // Split item: the fp32 partial (128 columns) into the item's
+    // column-major slot ([128 columns][256 rows], then m[256] and l[256]);
+    // the last split of the block (per CTA of the pair) merges all partials
+    // and writes bf16.  Each split item counts four warps (its owner's).
 #pragma unroll 1
-    for (int c = 0; c < 2; ++c) {
+    for (int c = 0; c < 4; ++c) {
       uint32_t x[32];
-      ptx::tmem_ld32(o_addr + 32 * c, x);
+      ptx::tmem_ld32(o_all + 32 * c, x);
       ptx::tmem_wait_ld_regs(x);
-      float* col = slot + static_cast<size_t>(64 * wg + 32 * c) * kSlotRows + srow;
+      float* col = slot + static_cast<size_t>(32 * c) * kSlotRows + srow;
 #pragma unroll
       for (int j = 0; j < 32; ++j) col[j * kSlotRows] = __uint_as_float(x[j]);
     }
-    if (wg == 0) {
-      slot[kHeadDim * kSlotRows + srow] = st.m_ref;
-      slot[(kHeadDim + 1) * kSlotRows + srow] = l_total;
-    }
+    slot[kHeadDim * kSlotRows + srow] = st.m_ref;
+    slot[(kHeadDim + 1) * kSlotRows + srow] = l_total;
     __threadfence();
     __syncwarp();
     if (lane == 0) ptx::red_release_add_shared(sh.counter(kCntSplitW), 1);
-    const uint32_t sp_slot = split_items & 1;
-    ++split_items;
-    if (wg == 0 && row == 0) {
-      if (wait_count(sh, kCntSplitW, kSoftmaxWarps * split_items)) {
+    if (row == 0) {
+      if (wait_count(sh, kCntSplitW, 4 * split_items)) {
         int32_t* ctr = a.ctl + kCtlSplitBase + (kVarlen ? rq.ctr_base : 0) +
                        ((it.block - pr.tail_block0) * p.kv_heads + it.kv_head) * 2 + r;
         const int prev = atomicAdd(ctr, 1);
@@ -1500,8 +1508,8 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
     }
     const float inv_sum = 1.0f / lsum;
 #pragma unroll 1
-    for (int c = 0; c < 2; ++c) {
-      const int col = 64 * wg + 32 * c;
+    for (int c = 0; c < 4; ++c) {
+      const int col = 32 * c;
       float acc[32];
 #pragma unroll
       for (int j = 0; j < 32; ++j) acc[j] = 0.0f;
@@ -1558,7 +1566,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kNumThreads, 1)
       ptx::mbar_init(sh.bar(kBarPFull + i), kPairWgArrivals);
       ptx::mbar_init(sh.bar(kBarPvDone + i), 1);
     }
-    ptx::mbar_init(sh.bar(kBarOEmpty), kPairWarpArrivals);
+    ptx::mbar_init(sh.bar(kBarOEmpty), kPairWgArrivals);
     ptx::mbar_init(sh.bar(kBarTail), 1);
     ptx::mbar_init(sh.bar(kBarDrain), 1);
     *sh.abort_flag() = 0;
