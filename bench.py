@@ -330,6 +330,174 @@ def run_batch(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+# (prompt length, scheduler chunk).
+CROSSOVER_PROMPTS = ((2869, 512), (4096, 512), (6144, 512), (8192, 512), (8320, 2048))
+
+
+def dense_paged_attention(kind: str, tq: int, seq: int, dev):
+    """The stock dense path a non-selected layer takes: causal GQA attention
+    of one chunk over its whole cached context (bottom-right aligned: row i
+    of the chunk sees keys <= seq - tq + i).  Neither library reads 128-token
+    pages (FlashAttention-2's paged mode needs 256-token pages), so the
+    context is first gathered from the pages; the gather is part of the
+    timed call.  kind "fa2": flash_attn varlen; "sdpa": torch
+    scaled_dot_product_attention (backend chosen by torch).
+    Returns fn(q, k_cache, v_cache, table) -> out."""
+    npages = math.ceil(seq / PAGE)
+
+    def gather(k_cache, v_cache, table):
+        pages = table[0, :npages].long()
+        kc = k_cache.index_select(0, pages).reshape(-1, KV_HEADS, HEAD_DIM)[:seq]
+        vc = v_cache.index_select(0, pages).reshape(-1, KV_HEADS, HEAD_DIM)[:seq]
+        return kc, vc
+
+    if kind == "fa2":
+        from flash_attn import flash_attn_varlen_func
+
+        cu_q = torch.tensor([0, tq], dtype=torch.int32, device=dev)
+        cu_k = torch.tensor([0, seq], dtype=torch.int32, device=dev)
+
+        def run(q, k_cache, v_cache, table):
+            kc, vc = gather(k_cache, v_cache, table)
+            return flash_attn_varlen_func(q, kc, vc, cu_q, cu_k, tq, seq, softmax_scale=SCALE,
+                                          causal=True)
+        return run
+
+    from torch.nn.attention.bias import causal_lower_right
+    import torch.nn.functional as F
+
+    mask = causal_lower_right(tq, seq)
+
+    def run(q, k_cache, v_cache, table):
+        kc, vc = gather(k_cache, v_cache, table)
+        o = F.scaled_dot_product_attention(q.transpose(0, 1).unsqueeze(0),
+                                           kc.transpose(0, 1).unsqueeze(0),
+                                           vc.transpose(0, 1).unsqueeze(0),
+                                           attn_mask=mask, scale=SCALE, enable_gqa=True)
+        return o[0].transpose(0, 1)
+    return run
+
+
+def run_crossover(args) -> None:
+    """BASELINE config 1 on one GPU: every chunk of each chunked prefill timed
+    through this library (C ABI, batch-one) and through the dense baseline on
+    the same inputs; the planner's quantities per chunk (sparse rows, saved
+    QK pairs per head, reference kernel.py:185-269) beside the two times, so
+    that the direct-route thresholds can be calibrated for B200."""
+    from __graft_entry__ import load_package
+
+    tm = load_package()
+    kernel = tm.kernel
+    cfg = kernel.TriangleMixConfig(enabled=True, layer_indices=frozenset())
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    errors: list[str] = []
+
+    def timed(fn) -> float | None:
+        """Median device time of one call, replayed from a CUDA graph so that
+        host launch overhead stays out of it; None if the call cannot be
+        captured (its error is recorded)."""
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            for _ in range(args.warmup):
+                fn()
+        stream.wait_stream(side)
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        try:
+            with torch.cuda.graph(graph):
+                fn()
+        except RuntimeError as exc:
+            errors.append(str(exc).splitlines()[0])
+            torch.cuda.synchronize(dev)
+            return None
+        for _ in range(3):
+            flush.fill_(1.0)
+            graph.replay()
+        torch.cuda.synchronize(dev)
+        ms = []
+        for i in range(args.steps):
+            flush.fill_(float(i))
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            graph.replay()
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+            ms.append(e0.elapsed_time(e1))
+        ms.sort()
+        del graph
+        return ms[len(ms) // 2]
+
+    rows = []
+    sampler = ClockSampler(0)
+    sampler.start()
+    for prompt, chunk in CROSSOVER_PROMPTS:
+        q, k, v, table = make_inputs(prompt, prompt, seed=0)
+        qd, kd, vd, td = q.to(dev), k.to(dev), v.to(dev), table.to(dev)
+        out = torch.empty_like(qd)
+        per_prompt = {"prompt_len": prompt, "chunk": chunk, "chunks": []}
+        for q0 in range(0, prompt, chunk):
+            tq = min(chunk, prompt - q0)
+            seq = q0 + tq
+            span = kernel.triangle_sparse_span(query_len=tq, seq_len=seq, prompt_len=prompt,
+                                               config=cfg)
+            ws = torch.empty(tm._native.make_plan(tq, q0, seq, prompt).workspace_bytes,
+                             dtype=torch.uint8, device=dev)
+            qc, oc = qd[q0:seq], out[q0:seq]
+
+            def sparse_call():
+                tm._native.paged_attention(qc, kd, vd, td, oc, q0, seq, prompt, SCALE,
+                                           workspace=ws)
+
+            ms_sparse = timed(sparse_call)
+            fa2 = dense_paged_attention("fa2", tq, seq, dev)
+            sdpa = dense_paged_attention("sdpa", tq, seq, dev)
+            ms_fa2 = timed(lambda: fa2(qc, kd, vd, td))
+            ms_sdpa = timed(lambda: sdpa(qc, kd, vd, td))
+            dense_ms = [m for m in (ms_fa2, ms_sdpa) if m is not None]
+            ms_dense = min(dense_ms) if dense_ms else float("inf")
+            per_prompt["chunks"].append({
+                "query_start": q0, "query_len": tq, "seq_len": seq,
+                "sparse_rows": span.sparse_rows, "saved_qk": span.saved_qk,
+                "split": span.is_split, "ms_sparse": ms_sparse, "ms_dense": ms_dense,
+                "ms_dense_fa2": ms_fa2, "ms_dense_sdpa": ms_sdpa,
+                "eligible_reference_thresholds": kernel.triangle_direct_eligible(
+                    query_len=tq, seq_len=seq, prompt_len=prompt, config=cfg)})
+        c = per_prompt["chunks"]
+        per_prompt["ms_sparse_all"] = sum(x["ms_sparse"] for x in c)
+        per_prompt["ms_dense_all"] = sum(x["ms_dense"] for x in c)
+        per_prompt["ms_routed"] = sum(min(x["ms_sparse"], x["ms_dense"]) if x["sparse_rows"]
+                                      else x["ms_dense"] for x in c)
+        rows.append(per_prompt)
+    clocks = sampler.stop()
+    status = tm._native.device_status(0)
+    if status:
+        raise RuntimeError(f"device status {status:#x}")
+    chunks = [x for r in rows for x in r["chunks"] if x["sparse_rows"] > 0]
+    wins = [x for x in chunks if x["ms_sparse"] < x["ms_dense"]]
+    losses = [x for x in chunks if x["ms_sparse"] >= x["ms_dense"]]
+    # Smallest saved-QK threshold above which every measured chunk is faster
+    # through this library.
+    threshold = (max(x["saved_qk"] for x in losses) + 1) if losses else 0
+    line = {"metric": "TriangleMix chunked-prefill crossover (BASELINE config 1)",
+            "unit": "ms per prompt (sum over chunks)", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "data": "synthetic (seeded N(0,1) bf16)",
+            "dense_baseline": "faster of flash_attn 2 varlen and torch SDPA (causal bottom-right, "
+                              "GQA) over the context gathered from 128-token pages, gather timed",
+            "timing": "CUDA graph replay per call, L2 flushed between calls (256 MiB write), "
+                      "median of steps",
+            "errors": errors,
+            "clocks": clocks, "prompts": rows,
+            "calibration": {"chunks_with_sparse_rows": len(chunks), "sparse_faster": len(wins),
+                            "min_saved_qk_all_faster": threshold,
+                            "losing_chunks": [(x["query_start"], x["seq_len"], x["saved_qk"])
+                                              for x in losses]}}
+    print(json.dumps(line), flush=True)
+
+
 def workload_config(args) -> dict:
     name = "prefill_8k" if args.seq_len == 8192 else f"prefill_{args.seq_len // 1024}k_q{args.query_tokens}"
     return {"workload": name, "seq_len": args.seq_len, "query_tokens": args.query_tokens,
@@ -352,6 +520,9 @@ def main() -> None:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--batch", type=int, default=0,
                     help="BASELINE config 4: a packed batch of this many prompts (one GPU)")
+    ap.add_argument("--crossover", action="store_true",
+                    help="BASELINE config 1: chunked-prefill sweep against the dense baseline "
+                         "(one GPU)")
     ap.add_argument("--validate", action="store_true",
                     help="N > 1: all-gather the head slices of layer 0 over NCCL and compare "
                          "them with a full-layer run on rank 0 (outside the timing)")
@@ -368,6 +539,11 @@ def main() -> None:
         ap.error(f"--gpus {args.gpus} but WORLD_SIZE={world}")
     if args.impl == "reference":
         run_reference_arm(args, rank)
+        return
+    if args.crossover:
+        if world != 1:
+            ap.error("--crossover runs on one GPU")
+        run_crossover(args)
         return
     if args.batch:
         if world != 1:

@@ -35,8 +35,28 @@ def coerce_bool(value: object, *, name: str) -> bool:
     raise ValueError(f"TriangleMix {name} must be a boolean, got {value!r}")
 
 
-# key -> (environment variable, default)
+# Direct-route thresholds (planner gates, reference kernel.py:240-269) per
+# device.  "910b" holds the reference's values, calibrated on Ascend 910B3.
+# "b200" comes from the BASELINE config 1 sweep on one B200 (bench.py
+# --crossover): every chunk with sparse rows (181 to 2048 of them, 127 K to
+# 13.6 M skipped QK pairs per head) ran 2.0x to 14.5x faster through this
+# library than the faster of FlashAttention-2 and torch SDPA over the same
+# paged context, so no saved-pairs minimum is kept; chunks below 128 sparse
+# rows were not measured and keep the reference's floor.
+THRESHOLD_PROFILES: dict[str, dict[str, int]] = {
+    "910b": {"min_seq_len": 0, "min_sparse_rows": 128, "min_saved_qk": 913_152,
+             "split_min_sparse_rows": 192, "split_min_saved_qk": 1_299_264},
+    "b200": {"min_seq_len": 0, "min_sparse_rows": 128, "min_saved_qk": 0,
+             "split_min_sparse_rows": 128, "split_min_saved_qk": 0},
+}
+_THRESHOLD_KEYS = tuple(THRESHOLD_PROFILES["910b"])
+
+# key -> (environment variable, default).  The threshold keys' defaults come
+# from the selected profile (threshold_profile, not a key of the reference
+# plugin); a threshold key set in the section or its environment variable
+# still wins over the profile.
 _KEYS: dict[str, tuple[str, Any]] = {
+    "threshold_profile": ("VLLM_ASCEND_TRIANGLE_MIX_THRESHOLD_PROFILE", "b200"),
     "enabled": ("VLLM_ASCEND_ENABLE_TRIANGLE_MIX", False),
     "layers": ("VLLM_ASCEND_TRIANGLE_MIX_LAYERS", ""),
     "sink_tokens": ("VLLM_ASCEND_TRIANGLE_MIX_SINK_TOKENS", 8),
@@ -87,6 +107,18 @@ def resolve_plugin_config(vllm_config: object | None) -> PluginConfig:
     additional = additional if isinstance(additional, Mapping) else {}
     section = additional.get("trianglemix", additional)
     section = section if isinstance(section, Mapping) else {}
+    profile_name = str(_lookup(section, "threshold_profile")).strip().lower()
+    if profile_name not in THRESHOLD_PROFILES:
+        raise ValueError(f"TriangleMix threshold_profile must be one of "
+                         f"{sorted(THRESHOLD_PROFILES)}, got {profile_name!r}")
+    profile = THRESHOLD_PROFILES[profile_name]
+
+    def threshold(key: str) -> int:
+        env, _ = _KEYS[key]
+        if key in section or os.getenv(env) is not None:
+            return int(_lookup(section, key))
+        return profile[key]
+
     layers = _lookup(section, "layers")
     if isinstance(layers, (list, tuple, set, frozenset)):
         layers = ",".join(str(x) for x in layers)
@@ -96,11 +128,11 @@ def resolve_plugin_config(vllm_config: object | None) -> PluginConfig:
         sink_tokens=int(_lookup(section, "sink_tokens")),
         local_window=int(_lookup(section, "local_window")),
         last_rows=int(_lookup(section, "last_rows")),
-        direct_min_seq_len=int(_lookup(section, "min_seq_len")),
-        direct_min_sparse_rows=int(_lookup(section, "min_sparse_rows")),
-        direct_min_saved_qk=int(_lookup(section, "min_saved_qk")),
-        direct_split_min_sparse_rows=int(_lookup(section, "split_min_sparse_rows")),
-        direct_split_min_saved_qk=int(_lookup(section, "split_min_saved_qk")),
+        direct_min_seq_len=threshold("min_seq_len"),
+        direct_min_sparse_rows=threshold("min_sparse_rows"),
+        direct_min_saved_qk=threshold("min_saved_qk"),
+        direct_split_min_sparse_rows=threshold("split_min_sparse_rows"),
+        direct_split_min_saved_qk=threshold("split_min_saved_qk"),
     )
     recent = int(_lookup(section, "stats_recent_capacity"))
     interval = int(_lookup(section, "stats_log_interval"))

@@ -65,6 +65,42 @@ def test_environment_is_the_fallback_and_section_wins():
         assert tm.config.resolve_plugin_config(holder).kernel.layer_indices == frozenset({7})
 
 
+def test_threshold_profiles():
+    # Default: the thresholds measured on B200 (no saved-pairs minimum).
+    with patch.dict(os.environ, {}, clear=True):
+        b200 = tm.config.resolve_plugin_config(None).kernel
+        assert (b200.direct_min_saved_qk, b200.direct_split_min_saved_qk) == (0, 0)
+        assert b200.direct_min_sparse_rows == 128 and b200.direct_split_min_sparse_rows == 128
+        # "910b" restores the reference's values.
+        ref = tm.config.resolve_plugin_config(types.SimpleNamespace(
+            additional_config={"trianglemix": {"threshold_profile": "910B"}})).kernel
+        assert (ref.direct_min_saved_qk, ref.direct_split_min_saved_qk) == (913_152, 1_299_264)
+        assert ref.direct_split_min_sparse_rows == 192
+        # An explicit threshold key wins over the profile.
+        mixed = tm.config.resolve_plugin_config(types.SimpleNamespace(
+            additional_config={"trianglemix": {"min_saved_qk": 7}})).kernel
+        assert mixed.direct_min_saved_qk == 7 and mixed.direct_split_min_saved_qk == 0
+    with patch.dict(os.environ, {"VLLM_ASCEND_TRIANGLE_MIX_THRESHOLD_PROFILE": "910b"},
+                    clear=True):
+        assert tm.config.resolve_plugin_config(None).kernel.direct_min_saved_qk == 913_152
+    with pytest.raises(ValueError, match="threshold_profile"):
+        tm.config.resolve_plugin_config(types.SimpleNamespace(
+            additional_config={"threshold_profile": "h100"}))
+
+
+def test_b200_thresholds_route_early_chunks_direct():
+    # The second 512-token chunk of a long prompt (503 sparse rows, 126,756
+    # saved pairs) falls back under the reference's 910B gates but measured
+    # 2.4x faster through this library on B200 than the dense baseline.
+    with patch.dict(os.environ, {"VLLM_ASCEND_ENABLE_TRIANGLE_MIX": "1",
+                                 "VLLM_ASCEND_TRIANGLE_MIX_LAYERS": "1"}, clear=True):
+        b200 = tm.config.resolve_plugin_config(None).kernel
+    args = dict(ends=[512], seqs=[1024], prompts=[8192], state="ChunkedPrefill")
+    assert plan(**args, config=b200).direct
+    reference = plan(**args)
+    assert not reference.direct
+
+
 def test_negative_stats_capacity_is_rejected():
     holder = types.SimpleNamespace(additional_config={"stats_recent_capacity": -1})
     with pytest.raises(ValueError, match="non-negative"):
