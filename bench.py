@@ -498,6 +498,175 @@ def run_crossover(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+# Qwen3-8B geometry, one 8320-token prompt, chunk 2048,
+# TriangleMix on layers 5, 7, 10, 15-35.
+QWEN3_8B = {"layers": 36, "hidden": 4096, "intermediate": 12288, "vocab": 151936,
+            "rope_theta": 1.0e6, "eps": 1e-6}
+TTFT_PROMPT, TTFT_CHUNK, TTFT_LAYERS = 8320, 2048, "5,7,10,15-35"
+
+
+class Qwen3Prefill:
+    """Random-init Qwen3-8B (bf16) prefill over a paged KV cache (page 128,
+    random block table).  Layers whose index is selected and whose chunk the
+    planner's gate admits (reference kernel.py:240-269, this package's B200
+    thresholds) run triangle_direct_paged_attention; every other layer runs
+    the dense baseline of run_crossover.  Synthetic weights: N(0, 0.02)."""
+
+    def __init__(self, tm, dev, seed: int = 0):
+        c = QWEN3_8B
+        self.tm, self.dev, self.c = tm, dev, c
+        g = torch.Generator(device=dev).manual_seed(seed)
+        h, inter, nl = c["hidden"], c["intermediate"], c["layers"]
+        qkv = (QUERY_HEADS + 2 * KV_HEADS) * HEAD_DIM
+
+        def w(*shape):
+            return (torch.randn(*shape, generator=g, device=dev, dtype=torch.float32) * 0.02).to(
+                torch.bfloat16)
+
+        self.embed = w(c["vocab"], h)
+        self.lm_head = w(h, c["vocab"])
+        self.layers = [dict(wqkv=w(h, qkv), wo=w(QUERY_HEADS * HEAD_DIM, h), wgu=w(h, 2 * inter),
+                            wd=w(inter, h)) for _ in range(nl)]
+        ones = lambda n: torch.ones(n, dtype=torch.bfloat16, device=dev)  # noqa: E731
+        self.norm_in = [ones(h) for _ in range(nl)]
+        self.norm_post = [ones(h) for _ in range(nl)]
+        self.q_norm = [ones(HEAD_DIM) for _ in range(nl)]
+        self.k_norm = [ones(HEAD_DIM) for _ in range(nl)]
+        self.norm_final = ones(h)
+        pages = math.ceil(TTFT_PROMPT / PAGE)
+        perm = torch.randperm(2 * pages, generator=torch.Generator().manual_seed(seed))[:pages]
+        self.table = perm.to(torch.int32).view(1, -1).to(dev)
+        self.kcache = [torch.zeros(2 * pages, PAGE, KV_HEADS, HEAD_DIM, dtype=torch.bfloat16,
+                                   device=dev) for _ in range(nl)]
+        self.vcache = [torch.zeros_like(k) for k in self.kcache]
+        inv = 1.0 / (c["rope_theta"] ** (torch.arange(0, HEAD_DIM, 2, device=dev,
+                                                         dtype=torch.float32) / HEAD_DIM))
+        ang = torch.arange(TTFT_PROMPT, device=dev, dtype=torch.float32)[:, None] * inv[None]
+        self.cos, self.sin = ang.cos(), ang.sin()
+
+    def rmsnorm(self, x, weight):
+        xf = x.float()
+        return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.c["eps"])).to(
+            x.dtype) * weight
+
+    def rope(self, x, p0: int):
+        tq = x.shape[0]
+        cos = self.cos[p0:p0 + tq, None, :]
+        sin = self.sin[p0:p0 + tq, None, :]
+        x1, x2 = x.float().chunk(2, dim=-1)
+        return torch.cat((x1 * cos - x2 * sin, x2 * cos + x1 * sin), dim=-1).to(x.dtype)
+
+    def prefill(self, ids_host, triangle_layers: frozenset, cfg, counts: dict) -> torch.Tensor:
+        """One prompt, chunk by chunk; returns the first generated token id (host)."""
+        tm, dev, c = self.tm, self.dev, self.c
+        kernel = tm.kernel
+        ids = ids_host.to(dev, non_blocking=True)
+        prompt = ids.shape[0]
+        x = None
+        for p0 in range(0, prompt, TTFT_CHUNK):
+            tq = min(TTFT_CHUNK, prompt - p0)
+            seq = p0 + tq
+            pos = torch.arange(p0, seq, device=dev)
+            slots = (self.table[0, pos // PAGE].long() * PAGE + pos % PAGE)
+            x = self.embed[ids[p0:seq]]
+            direct = kernel.triangle_direct_eligible(query_len=tq, seq_len=seq, prompt_len=prompt,
+                                                     config=cfg)
+            dense = dense_paged_attention("fa2", tq, seq, dev)
+            for li in range(c["layers"]):
+                lw = self.layers[li]
+                hdn = self.rmsnorm(x, self.norm_in[li])
+                qkv = hdn @ lw["wqkv"]
+                q = qkv[:, :QUERY_HEADS * HEAD_DIM].view(tq, QUERY_HEADS, HEAD_DIM)
+                k = qkv[:, QUERY_HEADS * HEAD_DIM:(QUERY_HEADS + KV_HEADS) * HEAD_DIM].view(
+                    tq, KV_HEADS, HEAD_DIM)
+                v = qkv[:, (QUERY_HEADS + KV_HEADS) * HEAD_DIM:].view(tq, KV_HEADS, HEAD_DIM)
+                q = self.rope(self.rmsnorm(q, self.q_norm[li]), p0).contiguous()
+                k = self.rope(self.rmsnorm(k, self.k_norm[li]), p0)
+                self.kcache[li].view(-1, KV_HEADS, HEAD_DIM)[slots] = k
+                self.vcache[li].view(-1, KV_HEADS, HEAD_DIM)[slots] = v
+                if li in triangle_layers and direct:
+                    attn = torch.empty_like(q)
+                    kernel.triangle_direct_paged_attention(
+                        query=q, key_cache=self.kcache[li], value_cache=self.vcache[li],
+                        block_table=self.table, seq_len=seq, prompt_len=prompt, output=attn,
+                        softmax_scale=SCALE, config=cfg)
+                    counts["direct"] += 1
+                else:
+                    attn = dense(q, self.kcache[li], self.vcache[li], self.table)
+                    counts["dense"] += 1
+                x = x + attn.reshape(tq, -1) @ lw["wo"]
+                gu = self.rmsnorm(x, self.norm_post[li]) @ lw["wgu"]
+                gate, up = gu.chunk(2, dim=-1)
+                x = x + (torch.nn.functional.silu(gate) * up) @ lw["wd"]
+        logits = self.rmsnorm(x[-1:], self.norm_final) @ self.lm_head
+        return logits.argmax(-1).to("cpu")
+
+
+def run_ttft(args) -> None:
+    """BASELINE config 2 on one GPU: TTFT of one 8320-token prompt (chunk
+    2048) with TriangleMix on layers 5, 7, 10, 15-35 against all-dense,
+    alternating D-S-S-D (reference ttft_abba.py:73-197).  The timed region
+    of a run starts before the token ids' H2D copy and ends after the first
+    generated token is on the host (CUDA events on the launching stream)."""
+    from __graft_entry__ import load_package
+
+    tm = load_package()
+    tm.load_adapter()
+    kernel = tm.kernel
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev)
+    model = Qwen3Prefill(tm, dev)
+    cfg = tm.config.resolve_plugin_config(None).kernel
+    layers = kernel.parse_layer_indices(TTFT_LAYERS)
+    ids = torch.randint(0, QWEN3_8B["vocab"], (TTFT_PROMPT,),
+                        generator=torch.Generator().manual_seed(0)).pin_memory()
+
+    def one(mode: str) -> tuple[float, dict]:
+        counts = {"direct": 0, "dense": 0}
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(dev)
+        e0.record(stream)
+        model.prefill(ids, layers if mode == "triangle" else frozenset(), cfg, counts)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1), counts
+
+    for _ in range(args.warmup):
+        one("dense")
+        one("triangle")
+    times = {"dense": [], "triangle": []}
+    counts = {}
+    sampler = ClockSampler(0)
+    sampler.start()
+    for r in range(args.steps):
+        order = ("dense", "triangle", "triangle", "dense") if r % 2 == 0 else \
+            ("triangle", "dense", "dense", "triangle")
+        for mode in order:
+            ms, counts[mode] = one(mode)
+            times[mode].append(ms)
+    clocks = sampler.stop()
+    status = tm._native.device_status(0)
+    if status:
+        raise RuntimeError(f"device status {status:#x}")
+    med = {m: sorted(v)[len(v) // 2] for m, v in times.items()}
+    line = {"metric": METRIC, "workload": "ttft_qwen3_8b_8320_c2048",
+            "value": med["triangle"], "unit": "ms TTFT", "higher_is_better": False,
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "data": "synthetic (random-init Qwen3-8B weights N(0,0.02), uniform random token ids)",
+            "dtype": "bf16",
+            "config": {"model": "Qwen3-8B geometry (36 layers, hidden 4096, Hq 32, Hkv 8, D 128, "
+                                "MLP 12288, vocab 151936, QK-norm, RoPE 1e6)",
+                       "prompt": TTFT_PROMPT, "chunk": TTFT_CHUNK, "triangle_layers": TTFT_LAYERS,
+                       "thresholds": "b200 profile", "kv_cache": "paged, page 128, random table",
+                       "dense_attention": "flash_attn 2 varlen over the gathered paged context"},
+            "ttft_ms": {"triangle": med["triangle"], "dense": med["dense"],
+                        "speedup": med["dense"] / med["triangle"]},
+            "runs_ms": times, "attention_calls_per_prefill": counts, "clocks": clocks,
+            "order": "D-S-S-D / S-D-D-S alternating rounds, median per mode"}
+    print(json.dumps(line), flush=True)
+
+
 def workload_config(args) -> dict:
     name = "prefill_8k" if args.seq_len == 8192 else f"prefill_{args.seq_len // 1024}k_q{args.query_tokens}"
     return {"workload": name, "seq_len": args.seq_len, "query_tokens": args.query_tokens,
@@ -523,6 +692,9 @@ def main() -> None:
     ap.add_argument("--crossover", action="store_true",
                     help="BASELINE config 1: chunked-prefill sweep against the dense baseline "
                          "(one GPU)")
+    ap.add_argument("--ttft", action="store_true",
+                    help="BASELINE config 2: Qwen3-8B prefill TTFT, TriangleMix layers against "
+                         "all-dense (one GPU)")
     ap.add_argument("--validate", action="store_true",
                     help="N > 1: all-gather the head slices of layer 0 over NCCL and compare "
                          "them with a full-layer run on rank 0 (outside the timing)")
@@ -544,6 +716,11 @@ def main() -> None:
         if world != 1:
             ap.error("--crossover runs on one GPU")
         run_crossover(args)
+        return
+    if args.ttft:
+        if world != 1:
+            ap.error("--ttft runs on one GPU")
+        run_ttft(args)
         return
     if args.batch:
         if world != 1:
