@@ -748,18 +748,43 @@ def main() -> None:
     for layer in range(layers):
         q, k, v, table = make_inputs(tq, seq, layer, rank, world)
         rank_inputs.append((q, k, v, table))
+    cu = [tq * j for j in range(layers + 1)]
+    seq_lens = [seq] * layers
+    if world > 1:
+        # The rank's head slices of its N layers live in one page pool (layer
+        # j's pages after layer j - 1's, its block table offset to them) and
+        # run as the N requests of one launch, which is as large as a full
+        # 8-head layer on one GPU.
+        pages = rank_inputs[0][1].shape[0]
+        rank_inputs = [(torch.cat([x[0] for x in rank_inputs]),
+                        torch.cat([x[1] for x in rank_inputs]),
+                        torch.cat([x[2] for x in rank_inputs]),
+                        torch.cat([x[3] + j * pages for j, x in enumerate(rank_inputs)]))]
     dev_inputs = [tuple(t.to(dev) for t in x) for x in rank_inputs]
     outs = [torch.empty_like(x[0]) for x in dev_inputs]
     plan = tm._native.make_plan(tq, q0, seq, seq, heads_per_rank, 0, SCALE)
-    ws = (torch.empty(plan.workspace_bytes, dtype=torch.uint8, device=dev)
-          if plan.workspace_bytes else None)
+    if world > 1:
+        ws = torch.empty(tm._native.varlen_workspace_size(cu, seq_lens, seq_lens,
+                                                          kv_heads=heads_per_rank),
+                         dtype=torch.uint8, device=dev)
+    else:
+        ws = (torch.empty(plan.workspace_bytes, dtype=torch.uint8, device=dev)
+              if plan.workspace_bytes else None)
     stream = torch.cuda.current_stream(dev)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
 
+    def launch(q, k, v, table, out):
+        if world > 1:
+            tm._native.paged_attention_varlen(q, k, v, table, out, cu, seq_lens, seq_lens, SCALE,
+                                              kv_heads=heads_per_rank, workspace=ws,
+                                              stream=stream.cuda_stream)
+        else:
+            tm._native.paged_attention(q, k, v, table, out, q0, seq, seq, SCALE,
+                                       workspace=ws, stream=stream.cuda_stream)
+
     def step():
         for (q, k, v, table), out in zip(dev_inputs, outs):
-            tm._native.paged_attention(q, k, v, table, out, q0, seq, seq, SCALE, kv_heads=heads_per_rank,
-                                       workspace=ws, stream=stream.cuda_stream)
+            launch(q, k, v, table, out)
 
     def barrier():
         if world > 1:
@@ -789,7 +814,7 @@ def main() -> None:
     clocks = sampler.stop()
     times = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     ms_rank = sum(times) / len(times)
-    kernel_ms = ms_rank / layers
+    kernel_ms = ms_rank  # one launch per step on every rank
     if world > 1:
         t = torch.tensor([ms_rank], device=dev)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
@@ -840,9 +865,7 @@ def main() -> None:
                         dq, dk, dv, dt, q0, seq, seq, SCALE)
                 else:
                     o = torch.empty_like(dq)
-                    tm._native.paged_attention(dq, dk, dv, dt, o, q0, seq, seq, SCALE,
-                                               kv_heads=heads_per_rank, workspace=ws,
-                                               stream=stream.cuda_stream)
+                    launch(dq, dk, dv, dt, o)
                 hout.copy_(o, non_blocking=True)
             free[b].record(stream)
 
@@ -866,25 +889,28 @@ def main() -> None:
                "unit": "TFLOP/s (effective)", "ms_per_step": e2e_ms,
                "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
                "path": ("torch.ops.trianglemix_reference.triangle_paged_sparse_attention"
-                        if world == 1 else "C ABI tpsa_paged_attention_heads per rank"),
+                        if world == 1 else
+                        "C ABI tpsa_paged_attention_varlen_heads, one launch per rank"),
                "pipelining": "step i+1's H2D (copy stream, second device buffer) overlaps "
                              "step i's kernel and D2H"}
     check = None
     if args.validate and world > 1:
-        check = validate_shards(tm, rank, world, dev, outs[0], q0, seq, tq)
+        check = validate_shards(tm, rank, world, dev, outs[0][:tq], q0, seq, tq)
     status = tm._native.device_status(local)
     if status:
         raise RuntimeError(f"device status {status:#x} after timing")
 
     peaks, peak_kind = load_peaks()
-    achieved = flops_layer * heads_per_rank / KV_HEADS / (kernel_ms * 1e-3) / 1e12
+    achieved = flops_layer * layers * heads_per_rank / KV_HEADS / (kernel_ms * 1e-3) / 1e12
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
                 "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
                 "traffic": None,
                 "peak_source": f"{peak_kind} bf16_tflops (burst)",
-                "kernel": "tpsa_paged_kernel<false>", "kernel_ms": kernel_ms,
+                "kernel": "tpsa_paged_kernel<false, false>" if world == 1 else
+                          "tpsa_paged_kernel<false, true> (layers x head slice per launch)",
+                "kernel_ms": kernel_ms,
                 "algorithmic": "4*128*heads*pairs effective FLOPs per launch"}
-    traffic = profiled_traffic(workload_config(args)["workload"], heads_per_rank)
+    traffic = profiled_traffic(workload_config(args)["workload"], heads_per_rank * layers)
     if traffic is not None:
         roofline["traffic"] = traffic["bytes"]
         roofline["traffic_unit"] = "bytes/launch (ncu dram read+write)"
@@ -893,7 +919,7 @@ def main() -> None:
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
             "ms_per_layer": ms_step / layers, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) bf16)",
-            "config": workload_config(args), "gpu_launches": args.steps * layers,
+            "config": workload_config(args), "gpu_launches": args.steps,
             "clocks": clocks, "roofline": roofline, "e2e": e2e,
             "plan": {"grid": plan.grid, "items": plan.total_items, "split_tiles": plan.split_tiles,
                      "tiles": plan.total_tiles}}

@@ -231,6 +231,29 @@ TPSA_API tpsa_status tpsa_paged_attention_varlen(
     float scale, void* workspace, uint64_t workspace_bytes, void* stream);
 
 /*
+ * Head-slice forms of the two entries above, for one rank of a KV-head
+ * partition (the multi-GPU layout of tpsa_paged_attention_heads): query and
+ * out are [rows, 4*kv_heads, 128], the caches [num_pages, 128, kv_heads,
+ * 128], kv_heads in {1, 2, 4, 8}.  A rank that holds its head slice of
+ * several layers in one page pool (each layer's block table pointing at its
+ * own pages) runs them all as the requests of one launch, which keeps the
+ * launch as large as a full 8-head layer.  No counterpart in the reference,
+ * which has no multi-device path (it falls back for tensor-parallel shards,
+ * package/src/vllm_ascend_trianglemix/planning.py:14-39).
+ */
+TPSA_API tpsa_status tpsa_varlen_workspace_size_heads(int32_t batch, const int64_t* cu_seqlens_q,
+                                                      const int64_t* seq_lens,
+                                                      const int64_t* prompt_lens,
+                                                      int32_t kv_heads, uint64_t* bytes);
+
+TPSA_API tpsa_status tpsa_paged_attention_varlen_heads(
+    const void* query, const void* key_cache, const void* value_cache,
+    const int32_t* block_tables, void* out, int32_t batch,
+    const int64_t* cu_seqlens_q, const int64_t* seq_lens,
+    const int64_t* prompt_lens, int64_t num_pages, int64_t table_cols,
+    float scale, int32_t kv_heads, void* workspace, uint64_t workspace_bytes, void* stream);
+
+/*
  * Debug variant that runs the identical kernel and additionally records,
  * for every (query row, query head), the key indices that entered its
  * softmax: bit k of visited[(row * 4*kv_heads + head) * words_per_row +

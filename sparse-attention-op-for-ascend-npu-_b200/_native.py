@@ -42,6 +42,8 @@ EXPORTED_SYMBOLS = (
     "tpsa_paged_attention_static_scratch",
     "tpsa_varlen_workspace_size",
     "tpsa_paged_attention_varlen",
+    "tpsa_varlen_workspace_size_heads",
+    "tpsa_paged_attention_varlen_heads",
 )
 
 
@@ -117,11 +119,17 @@ def lib() -> ctypes.CDLL:
         h.tpsa_varlen_workspace_size.argtypes = [_i32, _p64, _p64, _p64, ctypes.POINTER(_u64)]
         h.tpsa_paged_attention_varlen.argtypes = [_vp, _vp, _vp, _vp, _vp, _i32, _p64, _p64, _p64,
                                                   _i64, _i64, _f32, _vp, _u64, _vp]
+        h.tpsa_varlen_workspace_size_heads.argtypes = [_i32, _p64, _p64, _p64, _i32,
+                                                       ctypes.POINTER(_u64)]
+        h.tpsa_paged_attention_varlen_heads.argtypes = [_vp, _vp, _vp, _vp, _vp, _i32, _p64, _p64,
+                                                        _p64, _i64, _i64, _f32, _i32, _vp, _u64,
+                                                        _vp]
         for name in ("tpsa_make_plan", "tpsa_plan_item", "tpsa_plan_tile", "tpsa_workspace_size",
                      "tpsa_paged_attention", "tpsa_paged_attention_heads",
                      "tpsa_paged_attention_visit", "tpsa_device_status",
                      "tpsa_paged_attention_static_scratch", "tpsa_varlen_workspace_size",
-                     "tpsa_paged_attention_varlen"):
+                     "tpsa_paged_attention_varlen", "tpsa_varlen_workspace_size_heads",
+                     "tpsa_paged_attention_varlen_heads"):
             getattr(h, name).restype = ctypes.c_int
         _LIB = h
         return h
@@ -165,24 +173,30 @@ def _int64_array(values) -> ctypes.Array:
     return (_i64 * len(vals))(*vals)
 
 
-def varlen_workspace_size(cu_seqlens_q, seq_lens, prompt_lens) -> int:
-    """Scratch bytes of tpsa_paged_attention_varlen on the current device (host metadata)."""
+def varlen_workspace_size(cu_seqlens_q, seq_lens, prompt_lens, *, kv_heads=None) -> int:
+    """Scratch bytes of tpsa_paged_attention_varlen (or, with ``kv_heads``, of its
+    head-slice form) on the current device (host metadata)."""
     batch = len(seq_lens)
     out = _u64()
-    check(lib().tpsa_varlen_workspace_size(batch, _int64_array(cu_seqlens_q), _int64_array(seq_lens),
-                                           _int64_array(prompt_lens), ctypes.byref(out)))
+    args = (batch, _int64_array(cu_seqlens_q), _int64_array(seq_lens), _int64_array(prompt_lens))
+    if kv_heads is None:
+        check(lib().tpsa_varlen_workspace_size(*args, ctypes.byref(out)))
+    else:
+        check(lib().tpsa_varlen_workspace_size_heads(*args, kv_heads, ctypes.byref(out)))
     return out.value
 
 
 def paged_attention_varlen(query, key_cache, value_cache, block_tables, out, cu_seqlens_q,
-                           seq_lens, prompt_lens, scale: float, *, workspace=None,
-                           stream=None) -> None:
+                           seq_lens, prompt_lens, scale: float, *, kv_heads=None,
+                           workspace=None, stream=None) -> None:
     """Packed ragged batch through the C ABI.
 
     ``query``/``out`` are packed ``[cu_seqlens_q[-1], 32, 128]`` CUDA tensors and
     ``block_tables`` a ``[batch, table_cols]`` int32 CUDA tensor; the per-request
     metadata (``cu_seqlens_q``, ``seq_lens``, ``prompt_lens``) are host integer
-    sequences.  A workspace is allocated from torch when none is given.
+    sequences.  With ``kv_heads`` the head-slice form runs (``[rows, 4*kv_heads,
+    128]`` queries, ``kv_heads``-head caches).  A workspace is allocated from
+    torch when none is given.
     """
     import torch
 
@@ -190,13 +204,17 @@ def paged_attention_varlen(query, key_cache, value_cache, block_tables, out, cu_
     if stream is None:
         stream = torch.cuda.current_stream(query.device).cuda_stream
     if workspace is None:
-        nbytes = varlen_workspace_size(cu_seqlens_q, seq_lens, prompt_lens)
+        nbytes = varlen_workspace_size(cu_seqlens_q, seq_lens, prompt_lens, kv_heads=kv_heads)
         workspace = torch.empty(nbytes, dtype=torch.uint8, device=query.device)
-    check(lib().tpsa_paged_attention_varlen(
-        query.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(), block_tables.data_ptr(),
-        out.data_ptr(), batch, _int64_array(cu_seqlens_q), _int64_array(seq_lens),
-        _int64_array(prompt_lens), key_cache.shape[0], block_tables.shape[-1], scale,
-        workspace.data_ptr(), workspace.numel() * workspace.element_size(), stream))
+    common = (query.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(),
+              block_tables.data_ptr(), out.data_ptr(), batch, _int64_array(cu_seqlens_q),
+              _int64_array(seq_lens), _int64_array(prompt_lens), key_cache.shape[0],
+              block_tables.shape[-1], scale)
+    ws = (workspace.data_ptr(), workspace.numel() * workspace.element_size(), stream)
+    if kv_heads is None:
+        check(lib().tpsa_paged_attention_varlen(*common, *ws))
+    else:
+        check(lib().tpsa_paged_attention_varlen_heads(*common, kv_heads, *ws))
 
 
 def device_status(device: int = 0) -> int:

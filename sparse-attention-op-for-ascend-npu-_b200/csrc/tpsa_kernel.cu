@@ -1967,14 +1967,15 @@ tpsa_status check_batch(int32_t batch, const int64_t* cu_seqlens_q, const int64_
 }
 
 tpsa_status varlen_workspace(int32_t batch, const int64_t* cu_seqlens_q, const int64_t* seq_lens,
-                             const int64_t* prompt_lens, int32_t pairs, uint64_t* bytes) {
+                             const int64_t* prompt_lens, int32_t kv_heads, int32_t pairs,
+                             uint64_t* bytes) {
   tpsa_status st = check_batch(batch, cu_seqlens_q, seq_lens, prompt_lens);
   if (st != TPSA_OK) return st;
   std::unique_ptr<BatchLaunch> b(new BatchLaunch);
   int64_t most = kControlBytes;
   for (int32_t first = 0; first < batch; first += kMaxReqs) {
     const int32_t count = std::min(kMaxReqs, batch - first);
-    st = build_batch(first, count, cu_seqlens_q, seq_lens, prompt_lens, TPSA_KV_HEADS, pairs,
+    st = build_batch(first, count, cu_seqlens_q, seq_lens, prompt_lens, kv_heads, pairs,
                      1.0f, 1, b.get());
     if (st != TPSA_OK) return st;
     most = std::max(most, b->workspace_bytes);
@@ -1987,7 +1988,8 @@ tpsa_status launch_varlen(const void* query, const void* key_cache, const void* 
                           const int32_t* block_tables, void* out, int32_t batch,
                           const int64_t* cu_seqlens_q, const int64_t* seq_lens,
                           const int64_t* prompt_lens, int64_t num_pages, int64_t table_cols,
-                          float scale, void* workspace, uint64_t workspace_bytes, void* stream) {
+                          float scale, int32_t kv_heads, void* workspace,
+                          uint64_t workspace_bytes, void* stream) {
   t_last_error.clear();
   if (query == nullptr || key_cache == nullptr || value_cache == nullptr ||
       block_tables == nullptr || out == nullptr) {
@@ -2018,17 +2020,20 @@ tpsa_status launch_varlen(const void* query, const void* key_cache, const void* 
   DeviceState* dev = nullptr;
   st = device_state(&dev);
   if (st != TPSA_OK) return st;
+  if (!(kv_heads == 1 || kv_heads == 2 || kv_heads == 4 || kv_heads == 8)) {
+    return fail(TPSA_ERR_INVALID_ARGUMENT, "kv_heads must be 1, 2, 4 or 8");
+  }
   const uint64_t total_rows = static_cast<uint64_t>(cu_seqlens_q[batch]);
   CUtensorMap tq, tk64, tk32, tv, tout;
-  const uint64_t hq = static_cast<uint64_t>(TPSA_KV_HEADS) * kGroupSize;
+  const uint64_t hq = static_cast<uint64_t>(kv_heads) * kGroupSize;
   const uint64_t cache_tokens = static_cast<uint64_t>(num_pages) * kPageSize;
   st = encode_map(&tq, query, hq, total_rows, 2, kBlockQ);
   if (st != TPSA_OK) return st;
-  st = encode_map(&tk64, key_cache, TPSA_KV_HEADS, cache_tokens, 1, 64);
+  st = encode_map(&tk64, key_cache, kv_heads, cache_tokens, 1, 64);
   if (st != TPSA_OK) return st;
-  st = encode_map(&tk32, key_cache, TPSA_KV_HEADS, cache_tokens, 1, 32);
+  st = encode_map(&tk32, key_cache, kv_heads, cache_tokens, 1, 32);
   if (st != TPSA_OK) return st;
-  st = encode_map(&tv, value_cache, TPSA_KV_HEADS, cache_tokens, 1, 64);
+  st = encode_map(&tv, value_cache, kv_heads, cache_tokens, 1, 64);
   if (st != TPSA_OK) return st;
   st = encode_map(&tout, out, hq, total_rows, 2, kBlockQ);
   if (st != TPSA_OK) return st;
@@ -2038,7 +2043,7 @@ tpsa_status launch_varlen(const void* query, const void* key_cache, const void* 
   // reuses the workspace after the previous one.
   for (int32_t first = 0; first < batch; first += kMaxReqs) {
     const int32_t count = std::min(kMaxReqs, batch - first);
-    st = build_batch(first, count, cu_seqlens_q, seq_lens, prompt_lens, TPSA_KV_HEADS,
+    st = build_batch(first, count, cu_seqlens_q, seq_lens, prompt_lens, kv_heads,
                      dev->max_pairs, scale, table_cols, b.get());
     if (st != TPSA_OK) return st;
     if (workspace_bytes < static_cast<uint64_t>(b->workspace_bytes)) {
@@ -2197,7 +2202,23 @@ tpsa_status tpsa_varlen_workspace_size(int32_t batch, const int64_t* cu_seqlens_
   DeviceState* dev = nullptr;
   tpsa_status st = device_state(&dev);
   if (st != TPSA_OK) return st;
-  return varlen_workspace(batch, cu_seqlens_q, seq_lens, prompt_lens, dev->max_pairs, bytes);
+  return varlen_workspace(batch, cu_seqlens_q, seq_lens, prompt_lens, TPSA_KV_HEADS,
+                          dev->max_pairs, bytes);
+}
+
+tpsa_status tpsa_varlen_workspace_size_heads(int32_t batch, const int64_t* cu_seqlens_q,
+                                             const int64_t* seq_lens, const int64_t* prompt_lens,
+                                             int32_t kv_heads, uint64_t* bytes) {
+  t_last_error.clear();
+  if (bytes == nullptr) return fail(TPSA_ERR_INVALID_ARGUMENT, "bytes pointer is NULL");
+  if (!(kv_heads == 1 || kv_heads == 2 || kv_heads == 4 || kv_heads == 8)) {
+    return fail(TPSA_ERR_INVALID_ARGUMENT, "kv_heads must be 1, 2, 4 or 8");
+  }
+  DeviceState* dev = nullptr;
+  tpsa_status st = device_state(&dev);
+  if (st != TPSA_OK) return st;
+  return varlen_workspace(batch, cu_seqlens_q, seq_lens, prompt_lens, kv_heads,
+                          dev->max_pairs, bytes);
 }
 
 tpsa_status tpsa_paged_attention_varlen(const void* query, const void* key_cache,
@@ -2208,8 +2229,18 @@ tpsa_status tpsa_paged_attention_varlen(const void* query, const void* key_cache
                                         void* workspace, uint64_t workspace_bytes,
                                         void* stream) {
   return launch_varlen(query, key_cache, value_cache, block_tables, out, batch, cu_seqlens_q,
-                       seq_lens, prompt_lens, num_pages, table_cols, scale, workspace,
-                       workspace_bytes, stream);
+                       seq_lens, prompt_lens, num_pages, table_cols, scale, TPSA_KV_HEADS,
+                       workspace, workspace_bytes, stream);
+}
+
+tpsa_status tpsa_paged_attention_varlen_heads(
+    const void* query, const void* key_cache, const void* value_cache,
+    const int32_t* block_tables, void* out, int32_t batch, const int64_t* cu_seqlens_q,
+    const int64_t* seq_lens, const int64_t* prompt_lens, int64_t num_pages, int64_t table_cols,
+    float scale, int32_t kv_heads, void* workspace, uint64_t workspace_bytes, void* stream) {
+  return launch_varlen(query, key_cache, value_cache, block_tables, out, batch, cu_seqlens_q,
+                       seq_lens, prompt_lens, num_pages, table_cols, scale, kv_heads,
+                       workspace, workspace_bytes, stream);
 }
 
 tpsa_status tpsa_paged_attention_heads(const void* query, const void* key_cache,

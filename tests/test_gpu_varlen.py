@@ -94,3 +94,36 @@ def test_varlen_equals_batch_one_calls(tm, cuda_device):
         one = run_cabi(tm, q[cu[i]:cu[i + 1]], k, v, per_request[i], seq - rows, seq, prompt,
                        cuda_device)
         assert_close(out[cu[i]:cu[i + 1]], one, f"request {i} vs batch-one")
+
+
+@pytest.mark.parametrize("kv_heads", [1, 2, 4])
+def test_varlen_heads_packs_layer_slices(tm, cuda_device, kv_heads):
+    """tpsa_paged_attention_varlen_heads: one rank's kv-head slice of several
+    layers, their caches in one page pool and each layer's block table offset
+    to its own pages, in one launch; every layer's rows checked against the
+    oracle on that layer alone."""
+    layers, rows, seq = 8 // kv_heads, 700, 1800
+    gen = torch.Generator().manual_seed(40 + kv_heads)
+    logical = (seq + 127) // 128
+    qs, ks, vs, tables = [], [], [], []
+    for _ in range(layers):
+        qs.append(torch.randn(rows, 4 * kv_heads, 128, generator=gen).to(torch.bfloat16))
+        ks.append(torch.randn(2 * logical, 128, kv_heads, 128, generator=gen).to(torch.bfloat16))
+        vs.append(torch.randn(2 * logical, 128, kv_heads, 128, generator=gen).to(torch.bfloat16))
+        tables.append(torch.randperm(2 * logical, generator=gen)[:logical].to(torch.int32))
+    pool_k, pool_v = torch.cat(ks), torch.cat(vs)
+    packed_tables = torch.stack([t + j * 2 * logical for j, t in enumerate(tables)])
+    cu = [rows * j for j in range(layers + 1)]
+    seq_lens = [seq] * layers
+    q = torch.cat(qs).to(cuda_device)
+    out = torch.full_like(q, float("nan"))
+    tm._native.paged_attention_varlen(q, pool_k.to(cuda_device), pool_v.to(cuda_device),
+                                      packed_tables.to(cuda_device), out, cu, seq_lens, seq_lens,
+                                      SCALE, kv_heads=kv_heads)
+    torch.cuda.synchronize(cuda_device)
+    assert tm._native.device_status(cuda_device.index or 0) == 0
+    out = out.cpu()
+    for j in range(layers):
+        ref = oracle_attention(qs[j], ks[j], vs[j], tables[j].view(1, -1), seq - rows, seq, seq,
+                               SCALE)
+        assert_close(out[cu[j]:cu[j + 1]], ref.to(torch.bfloat16), f"layer {j} of {layers}")
