@@ -206,12 +206,15 @@ struct ReqDesc {
   int32_t table_off;  // its block-table row (int32 elements from block_table)
   int32_t slot_base;  // its first split-KV partial slot
   int32_t ctr_base;   // its first split counter
+  int32_t tail_base;  // dispatch position of its first dense-tail item
+  int32_t rest_base;  // dispatch position of its first other item, after all tail items
 };
 constexpr int kMaxReqs = 16;  // requests per launch (varlen batches are cut into launches)
 
 struct KernelArgs {
   tpsa_plan plan;  // launch totals: total_items, kv_heads, scale, grid
   int32_t num_reqs;
+  int32_t tail_total;  // dense-tail items of all requests (dispatched first)
   ReqDesc reqs[kMaxReqs];
   const int32_t* block_table;
   __nv_bfloat16* out;
@@ -502,14 +505,27 @@ __device__ void scheduler_role(const KernelArgs& a, const Shared& sh) {
     const uint32_t slot = n % 2;
     ItemRec rec;
     if (kVarlen) {
-      // The request holding launch item `next`, then the item within it.
-      int32_t q = 0;
+      // Dispatch order across the launch's requests: first every request's
+      // dense-tail items (the longest), then every request's other items,
+      // so that a later request's long items do not start last.  The record
+      // carries the request-major index (item_base + item within request),
+      // which the consumers use; the terminator carries total_items.
+      int32_t q = 0, ridx = 0;
       if (next < p.total_items) {
-        while (q + 1 < a.num_reqs && next >= a.reqs[q + 1].item_base) ++q;
+        if (next < a.tail_total) {
+          while (q + 1 < a.num_reqs && next >= a.reqs[q + 1].tail_base) ++q;
+          ridx = next - a.reqs[q].tail_base;
+        } else {
+          const int32_t j = next - a.tail_total;
+          while (q + 1 < a.num_reqs && j >= a.reqs[q + 1].rest_base) ++q;
+          ridx = a.reqs[q].plan.tail_items + (j - a.reqs[q].rest_base);
+        }
+        rec = make_item_rec(a.reqs[q].plan, ridx);
+        rec.idx = a.reqs[q].item_base + ridx;
+      } else {
+        rec = make_item_rec(a.reqs[0].plan, a.reqs[0].plan.total_items);
+        rec.idx = p.total_items;
       }
-      rec = make_item_rec(a.reqs[q].plan, next < p.total_items ? next - a.reqs[q].item_base
-                                                               : a.reqs[q].plan.total_items);
-      rec.idx = next;
       rec.narrow |= static_cast<uint32_t>(q) << 8;
     } else {
       rec = make_item_rec(p, next);
@@ -1912,7 +1928,7 @@ tpsa_status build_batch(int32_t first, int32_t count, const int64_t* cu_seqlens_
   }
   int32_t split = static_cast<int32_t>(0.7 * static_cast<double>(tiles) / pairs);
   if (split < kMinSplitTiles) split = kMinSplitTiles;
-  int32_t items = 0, slots = 0, counters = 0;
+  int32_t items = 0, slots = 0, counters = 0, tail = 0, rest = 0;
   for (int32_t i = 0; i < count; ++i) {
     const int32_t r = first + i;
     const int64_t tq = cu_seqlens_q[r + 1] - cu_seqlens_q[r];
@@ -1921,6 +1937,10 @@ tpsa_status build_batch(int32_t first, int32_t count, const int64_t* cu_seqlens_
                                 pairs, scale, &d.plan, split);
     if (st != TPSA_OK) return st;
     d.item_base = items;
+    d.tail_base = tail;
+    d.rest_base = rest;
+    tail += d.plan.tail_items;
+    rest += d.plan.total_items - d.plan.tail_items;
     d.q_row0 = static_cast<int32_t>(cu_seqlens_q[r]);
     d.table_off = static_cast<int32_t>(static_cast<int64_t>(r) * table_cols);
     d.slot_base = slots;
@@ -1932,6 +1952,7 @@ tpsa_status build_batch(int32_t first, int32_t count, const int64_t* cu_seqlens_
     }
   }
   a.num_reqs = count;
+  a.tail_total = tail;
   a.plan = a.reqs[0].plan;
   a.plan.query_tokens = static_cast<int32_t>(cu_seqlens_q[first + count] - cu_seqlens_q[first]);
   a.plan.total_items = items;
