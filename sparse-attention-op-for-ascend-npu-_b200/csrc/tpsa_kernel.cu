@@ -1643,6 +1643,49 @@ tpsa_status fail(tpsa_status s, const std::string& msg) {
   return s;
 }
 
+// Dense-tail blocks longer than this fraction of the average work per CTA
+// pair are split into several items (merged in-kernel).
+#ifndef TPSA_SPLIT_FACTOR
+#define TPSA_SPLIT_FACTOR 0.7
+#endif
+constexpr double kSplitFactor = TPSA_SPLIT_FACTOR;
+
+// Split threshold (tiles per item) for the dense-tail blocks of a plan.  The
+// B = tail blocks x kv heads longest items, each cut into ns pieces of
+// ceil(T / ns) tiles, go first to the CTA pairs (longest first), so the
+// busiest pair carries ceil(B ns / P) pieces; the short items fill the other
+// pairs.  The estimated makespan, in tiles, is
+//   max(ceil(B ns / P) (ceil(T / ns) + c), (total + B ns c) / P)
+// with c the per-piece cost of a partial write and its share of the merge
+// (kSplitPieceTiles); the smallest ns with the least estimate wins.  ns is
+// at most what a threshold of kSplitFactor times the average work per pair
+// gives, so no plan needs more split slots than that rule (the static-scratch
+// entry point's limit rests on it).  (That rule alone cut the 128K-context
+// tail into 5 pieces: 80 pieces for 74 pairs, six pairs with two.)
+constexpr double kSplitPieceTiles = 2.0;
+int32_t choose_split(const tpsa_plan& p, int32_t b0, int64_t tiles, int32_t pairs) {
+  int32_t longest = 0;
+  for (int32_t b = b0; b < p.num_blocks; ++b) longest = max_i(longest, block_tiles(p, b).count);
+  const int64_t tail = static_cast<int64_t>(p.num_blocks - b0) * p.kv_heads;
+  if (tail == 0 || longest == 0) return 1 << 30;
+  const int32_t by_fraction = max_i(kMinSplitTiles, static_cast<int32_t>(
+      kSplitFactor * static_cast<double>(tiles) / pairs));
+  const int32_t ns_max = min_i(64, ceil_div(longest, by_fraction));
+  double best = 0.0;
+  int32_t best_ns = 1;
+  for (int32_t ns = 1; ns <= ns_max; ++ns) {
+    const double piece = static_cast<double>(ceil_div(longest, ns)) + kSplitPieceTiles;
+    const double rounds = static_cast<double>((tail * ns + pairs - 1) / pairs);
+    const double avg = (static_cast<double>(tiles) + kSplitPieceTiles * tail * ns) / pairs;
+    const double est = std::max(rounds * piece, avg);
+    if (ns == 1 || est < best - 1e-9) {
+      best = est;
+      best_ns = ns;
+    }
+  }
+  return best_ns == 1 ? (1 << 30) : ceil_div(longest, best_ns);
+}
+
 tpsa_status cuda_fail(cudaError_t e, const char* what) {
   return fail(TPSA_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
 }
@@ -1792,8 +1835,7 @@ tpsa_status build_plan(int64_t query_tokens, int64_t query_start, int64_t seq_le
   int64_t tiles = 0;
   for (int32_t b = 0; b < p->num_blocks; ++b) tiles += block_tiles(*p, b).count;
   tiles *= kv_heads;
-  const double target = static_cast<double>(tiles) / pairs;
-  int32_t split = split_override > 0 ? split_override : static_cast<int32_t>(0.7 * target);
+  int32_t split = split_override > 0 ? split_override : choose_split(*p, b0, tiles, pairs);
   if (split < kMinSplitTiles) split = kMinSplitTiles;
   // The in-kernel merge keeps per-split weights for at most 64 splits.
   for (int32_t b = b0; b < p->num_blocks; ++b) {
@@ -1926,7 +1968,7 @@ tpsa_status build_batch(int32_t first, int32_t count, const int64_t* cu_seqlens_
     if (st != TPSA_OK) return st;
     tiles += probe.total_tiles;
   }
-  int32_t split = static_cast<int32_t>(0.7 * static_cast<double>(tiles) / pairs);
+  int32_t split = static_cast<int32_t>(kSplitFactor * static_cast<double>(tiles) / pairs);
   if (split < kMinSplitTiles) split = kMinSplitTiles;
   int32_t items = 0, slots = 0, counters = 0, tail = 0, rest = 0;
   for (int32_t i = 0; i < count; ++i) {
@@ -2091,7 +2133,7 @@ tpsa_status launch_varlen(const void* query, const void* key_cache, const void* 
 // split-KV partial slots that tpsa_paged_attention keeps in a caller-provided
 // workspace, in one module-global array per device instead.  Its maximum
 // size, 16 MiB, covers 8192-token query chunks over contexts up to 128K
-// tokens (10.2 MiB there).
+// tokens (8.1 MiB there) and 64- to 1024-token chunks up to 1M (9.1 MiB).
 constexpr uint64_t kStaticScratchBytes = uint64_t{16} << 20;
 constexpr int kMaxScratchDevices = 64;
 std::mutex g_scratch_mutex;

@@ -18,10 +18,11 @@ from inputs import SCALE, baseline_inputs
 
 pytestmark = pytest.mark.gpu
 
-# (query_tokens, seq_len): BASELINE config 0 (one 4096-token chunk) and the
-# last 2048-token chunk of an 8320-token prompt; both split their dense-tail
-# blocks, so the scratch holds partial slots as well as control words.
-CASES = ((4096, 4096, 11), (2048, 8320, 12))
+# (query_tokens, seq_len): the last 4096-token chunk of an 8192-token prompt
+# and the last 2048-token chunk of an 8320-token prompt; both split their
+# dense-tail blocks, so the scratch holds partial slots as well as control
+# words.
+CASES = ((4096, 8192, 11), (2048, 8320, 12))
 
 
 def _run(tm, dev, q, k, v, table, q0, seq, *, static):
