@@ -1663,10 +1663,9 @@ constexpr double kSplitFactor = TPSA_SPLIT_FACTOR;
 // entry point's limit rests on it).  (That rule alone cut the 128K-context
 // tail into 5 pieces: 80 pieces for 74 pairs, six pairs with two.)
 constexpr double kSplitPieceTiles = 2.0;
-int32_t choose_split(const tpsa_plan& p, int32_t b0, int64_t tiles, int32_t pairs) {
-  int32_t longest = 0;
-  for (int32_t b = b0; b < p.num_blocks; ++b) longest = max_i(longest, block_tiles(p, b).count);
-  const int64_t tail = static_cast<int64_t>(p.num_blocks - b0) * p.kv_heads;
+// `longest`: tiles of the longest dense-tail block; `tail`: dense-tail
+// (block, head) items before splitting; `tiles`: all tiles of the launch.
+int32_t choose_split_counts(int32_t longest, int64_t tail, int64_t tiles, int32_t pairs) {
   if (tail == 0 || longest == 0) return 1 << 30;
   const int32_t by_fraction = max_i(kMinSplitTiles, static_cast<int32_t>(
       kSplitFactor * static_cast<double>(tiles) / pairs));
@@ -1684,6 +1683,13 @@ int32_t choose_split(const tpsa_plan& p, int32_t b0, int64_t tiles, int32_t pair
     }
   }
   return best_ns == 1 ? (1 << 30) : ceil_div(longest, best_ns);
+}
+
+int32_t choose_split(const tpsa_plan& p, int32_t b0, int64_t tiles, int32_t pairs) {
+  int32_t longest = 0;
+  for (int32_t b = b0; b < p.num_blocks; ++b) longest = max_i(longest, block_tiles(p, b).count);
+  return choose_split_counts(longest, static_cast<int64_t>(p.num_blocks - b0) * p.kv_heads, tiles,
+                             pairs);
 }
 
 tpsa_status cuda_fail(cudaError_t e, const char* what) {
@@ -1958,7 +1964,8 @@ tpsa_status build_batch(int32_t first, int32_t count, const int64_t* cu_seqlens_
                         int32_t pairs, float scale, int64_t table_cols, BatchLaunch* b) {
   std::memset(&b->args, 0, sizeof(b->args));
   KernelArgs& a = b->args;
-  int64_t tiles = 0;
+  int64_t tiles = 0, tail_items = 0;
+  int32_t longest = 0;
   for (int32_t i = 0; i < count; ++i) {
     const int32_t r = first + i;
     const int64_t tq = cu_seqlens_q[r + 1] - cu_seqlens_q[r];
@@ -1967,8 +1974,14 @@ tpsa_status build_batch(int32_t first, int32_t count, const int64_t* cu_seqlens_
                                 pairs, scale, &probe, 1 << 30);
     if (st != TPSA_OK) return st;
     tiles += probe.total_tiles;
+    tail_items += static_cast<int64_t>(probe.num_blocks - probe.tail_block0) * kv_heads;
+    for (int32_t b = probe.tail_block0; b < probe.num_blocks; ++b) {
+      longest = max_i(longest, block_tiles(probe, b).count);
+    }
   }
-  int32_t split = static_cast<int32_t>(kSplitFactor * static_cast<double>(tiles) / pairs);
+  // One split threshold for the launch, from the makespan estimate over all
+  // requests' dense-tail items (which are dispatched first).
+  int32_t split = choose_split_counts(longest, tail_items, tiles, pairs);
   if (split < kMinSplitTiles) split = kMinSplitTiles;
   int32_t items = 0, slots = 0, counters = 0, tail = 0, rest = 0;
   for (int32_t i = 0; i < count; ++i) {
