@@ -152,6 +152,28 @@ def test_long_tail_blocks_are_split_and_run_first(tm):
     assert plan.total_tiles / (SM // 2) >= longest
 
 
+@pytest.mark.parametrize("seq, pieces", [(8192, 1), (32768, 2), (65536, 3), (131072, 4)])
+def test_tail_split_count_fits_the_pairs(tm, seq, pieces):
+    """BASELINE config 3 (8192-row chunk ending an N-token prompt): the 16
+    dense-tail (block, head) items are cut into as many pieces as the
+    makespan estimate picks; at 128K that is 4 (64 pieces for 74 CTA pairs,
+    one each), not 5 (80 pieces: six pairs would carry two)."""
+    plan = tm._native.make_plan(8192, seq - 8192, seq, seq, 8, SM)
+    tail_blocks = (plan.num_blocks - plan.tail_block0) * 8
+    assert plan.tail_items == tail_blocks * pieces
+    assert pieces == 1 or plan.tail_items <= SM // 2
+
+
+def test_static_scratch_range_fits_its_array(tm):
+    """Every plan the static-scratch entry point documents (query chunks of
+    64-1024 rows at the end of prompts of 4K-1M tokens) fits in 16 MiB."""
+    worst = 0
+    for seq in (4096, 16384, 65536, 262144, 1 << 20):
+        for tq in (64, 256, 1024):
+            worst = max(worst, tm._native.make_plan(tq, seq - tq, seq, seq, 8, SM).workspace_bytes)
+    assert worst <= 16 << 20
+
+
 def test_workspace_is_control_words_without_splits(tm):
     # Intermediate chunk with no dense tail: nothing is split, only the
     # scheduler's control words are needed.
