@@ -152,9 +152,10 @@ enum BarId : uint32_t {
   kNumBars
 };
 // Arrivals: p_full takes one per warp of the tile's softmax warpgroup in
-// both CTAs, o_empty one per softmax warp of both CTAs;
-// item_empty takes the two producers, the MMA issuer and the 8 softmax
-// warps of CTA 0 plus the two producers and the 8 softmax warps of CTA 1.
+// both CTAs, o_empty one per warp of the item's finishing warpgroup in both
+// CTAs; item_empty takes the two producers, the MMA issuer and the 8
+// softmax warps of CTA 0 plus the two producers and the 8 softmax warps of
+// CTA 1.
 constexpr uint32_t kPairWgArrivals = kSoftmaxWarps;  // 4 warps x 2 CTAs
 constexpr uint32_t kItemConsumers = 2 * (2 + kSoftmaxWarps) + 1;
 // q_empty: the MMA issuer's commit after the item's last QK.  (The finished
@@ -560,8 +561,9 @@ struct PendingStore {
   int32_t head, token;  // box coordinates in `out` (d is 0 and 64)
 };
 
-// Waits until both softmax warpgroups staged item `ps`, TMA-stores its two
-// d-half boxes from Q buffer qb, and waits until the stores have read it.
+// Waits until item `ps` is staged (the finishing warpgroup counts four warps
+// on each d-half counter), TMA-stores its two d-half boxes from Q buffer qb,
+// and waits until the stores have read it.
 __device__ __forceinline__ void flush_store(const Shared& sh, const CUtensorMap* tout,
                                             PendingStore& ps, uint32_t qb) {
   if (!ps.stages) return;
@@ -1281,8 +1283,10 @@ __device__ __forceinline__ void warp_arrive0(const Shared& sh, uint32_t id, int 
 // warpgroup gt % 2.  The two warpgroups share the O accumulator and hand
 // each row's lazy reference max from tile to tile through RowChannel, so
 // P of every tile is relative to the reference O is kept in; each keeps a
-// partial row sum over its own tiles, combined at the item's end.  At the
-// end of an item each warpgroup writes O columns [64 wg, 64 wg + 64).
+// partial row sum over its own tiles.  The warpgroup that owns an item's
+// last tile finishes the item: the other hands over its (reference, partial
+// sum) and goes on to the next item, and the owner normalises and writes
+// all 128 O columns.
 template <bool kVisit, bool kVarlen>
 __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tmem) {
   const tpsa_plan& p = a.plan;
