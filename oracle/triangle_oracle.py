@@ -290,9 +290,12 @@ def oracle_attention_rowwise(query, key_cache, value_cache, block_table, query_s
     out = torch.zeros_like(qf)
     for r in (range(qf.shape[0]) if rows is None else rows):
         ivs = selected_intervals(query_start + r, seq_len, prompt_len, g)
-        idx = torch.cat([torch.arange(b, e, dtype=torch.int64) for b, e in ivs])
-        k = lk.index_select(0, idx)
-        v = lv.index_select(0, idx)
+        if len(ivs) == 1:  # a dense row: one contiguous range, read in place
+            k, v = lk[ivs[0][0]:ivs[0][1]], lv[ivs[0][0]:ivs[0][1]]
+        else:
+            idx = torch.cat([torch.arange(b, e, dtype=torch.int64) for b, e in ivs])
+            k = lk.index_select(0, idx)
+            v = lv.index_select(0, idx)
         gq = qf[r].reshape(hkv, g.group_size, g.head_dim)
         p = torch.softmax(torch.einsum("hgd,thd->hgt", gq, k) * float(scale), dim=-1)
         out[r] = torch.einsum("hgt,thd->hgd", p, v).reshape(-1, g.head_dim)
