@@ -280,8 +280,9 @@ TPSA_API tpsa_status tpsa_paged_attention_visit(
  * up front, where an allocation in the middle of a step could fail or
  * fragment the pool.  This variant keeps its scratch (the control words and
  * the split-KV partials) in one module-global device array of at most
- * 16 MiB per device.  That covers 8192-token query chunks over contexts up to
- * 128K tokens.  A call whose plan needs more scratch returns
+ * 24 MiB per device.  That covers every plan on a 148-SM B200 (at most
+ * 18.3 MiB, for query chunks of 64 to 16384 rows over contexts up to 4M
+ * tokens).  A call whose plan needs more scratch returns
  * TPSA_ERR_WORKSPACE with the required size in tpsa_last_error(); use
  * tpsa_paged_attention with a caller workspace for those shapes.  The call
  * makes no cudaMalloc or cudaFree and uses no allocating library routine.
@@ -290,6 +291,9 @@ TPSA_API tpsa_status tpsa_paged_attention_visit(
  * the array's device address with cudaGetSymbolAddress and caches it.  That
  * lookup also makes the CUDA runtime load this library's device globals on
  * the device.  Make the first call on each device before any stream capture.
+ * The cached address belongs to the device's primary context: after
+ * cudaDeviceReset on that device it is stale, so do not call this entry
+ * point on a device that has been reset in this process.
  *
  * Sharing: every call on a device uses the same array, and the array keeps
  * the previous call's contents.  Each call clears the control words that

@@ -77,8 +77,8 @@ def _check_ptxas_report(text: str) -> None:
 
 
 def build_lib(force: bool = False) -> Path:
-    sources = [CSRC / "tpsa_kernel.cu", CSRC / "tpsa_schedule.h", CSRC / "sm100_ptx.cuh",
-               INCLUDE / "tpsa.h"]
+    sources = [CSRC / "tpsa_kernel.cu", CSRC / "tpsa_solo_kernel.cuh", CSRC / "tpsa_schedule.h",
+               CSRC / "sm100_ptx.cuh", INCLUDE / "tpsa.h"]
     if not force and _newer(LIB, sources):
         return LIB
     tmp = LIB.with_suffix(".so.tmp")

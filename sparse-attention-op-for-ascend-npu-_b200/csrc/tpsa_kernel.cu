@@ -44,6 +44,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <mutex>
@@ -1044,6 +1045,9 @@ __device__ __forceinline__ void mask_chunk(uint32_t (&r)[32], uint32_t m) {
 
 // Exponentials of one 32-key chunk of S (fp32 bits in r): P as 16 bf16
 // pairs stored to tensor memory at p_addr, their sum added to (sum0, sum1).
+// Pair c of the chunk uses the FMA-pipe polynomial when bit c of kPoly is
+// set, MUFU ex2 otherwise.
+template <uint32_t kPoly = TPSA_POLY_MASK>
 __device__ __forceinline__ void exp_chunk(const uint32_t (&r)[32], float scale_log2, float neg_mb,
                                           uint32_t p_addr, float& sum0, float& sum1) {
   uint32_t pk[16];
@@ -1053,7 +1057,7 @@ __device__ __forceinline__ void exp_chunk(const uint32_t (&r)[32], float scale_l
     float x0, x1;
     fma2(v0, v1, scale_log2, neg_mb, x0, x1);
     float e0, e1;
-    if ((TPSA_POLY_MASK >> c) & 1u) {
+    if ((kPoly >> c) & 1u) {
       poly_exp2_x2(x0, x1, e0, e1);
     } else {
       e0 = mufu_exp2(x0);
@@ -1639,6 +1643,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kNumThreads, 1)
   }
 }
 
+#include "tpsa_solo_kernel.cuh"
+
 // ================================================================ host side
 thread_local std::string t_last_error;
 
@@ -1700,13 +1706,33 @@ tpsa_status cuda_fail(cudaError_t e, const char* what) {
   return fail(TPSA_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
 }
 
+// Kernel form: one CTA per item (tpsa_solo_kernel, the default) or CTA pairs
+// (tpsa_paged_kernel, selected by TPSA_KERNEL=pair in the environment; kept
+// as the measured comparison).  Read once per process.
+enum class Form { kPair, kSolo };
+
+Form kernel_form() {
+  static const Form form = [] {
+    const char* e = std::getenv("TPSA_KERNEL");
+    if (e != nullptr && std::strcmp(e, "pair") == 0) return Form::kPair;
+    return Form::kSolo;
+  }();
+  return form;
+}
+
 struct DeviceState {
   bool ready = false;
   int sm_count = 0;
   int major = 0;
   bool attr_set = false;
   int max_pairs = 0;  // co-resident CTA pairs (clusters of 2)
+  int max_solo = 0;   // co-resident solo CTAs
+  // Parallel workers of the current kernel form (CTA pairs or solo CTAs)
+  // and CTAs per worker.
+  int workers() const { return kernel_form() == Form::kSolo ? max_solo : max_pairs; }
 };
+
+int ctas_per_worker() { return kernel_form() == Form::kSolo ? 1 : 2; }
 
 std::mutex g_mutex;
 DeviceState g_devices[64];
@@ -1748,6 +1774,21 @@ tpsa_status device_state(DeviceState** out) {
     if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveClusters");
     if (clusters <= 0) return fail(TPSA_ERR_CUDA, "no CTA pair fits on this device");
     st.max_pairs = clusters;
+    e = cudaFuncSetAttribute(tpsa_solo_kernel<false, false>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, solo::kSmemBytes);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+    e = cudaFuncSetAttribute(tpsa_solo_kernel<true, false>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, solo::kSmemBytes);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+    e = cudaFuncSetAttribute(tpsa_solo_kernel<false, true>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, solo::kSmemBytes);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tpsa_solo_kernel<false, false>,
+                                                      solo::kNumThreads, solo::kSmemBytes);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+    if (per_sm <= 0) return fail(TPSA_ERR_CUDA, "the solo kernel does not fit on an SM");
+    st.max_solo = per_sm * st.sm_count;
     st.attr_set = true;
   }
   *out = &st;
@@ -1801,8 +1842,9 @@ tpsa_status encode_map(CUtensorMap* map, const void* base, uint64_t d1, uint64_t
   return TPSA_OK;
 }
 
-// `pairs`: CTA pairs (2-SM clusters) the launch runs; each pair runs one item
-// at a time.
+// `pairs`: parallel workers the launch runs (CTA pairs, or single CTAs for the
+// solo kernel, ctas_per_worker() CTAs each); each worker runs one item at a
+// time.
 // `split_override` > 0 replaces the split threshold derived from this
 // request's own work (a varlen launch derives it from the whole launch).
 tpsa_status build_plan(int64_t query_tokens, int64_t query_start, int64_t seq_len,
@@ -1863,7 +1905,7 @@ tpsa_status build_plan(int64_t query_tokens, int64_t query_start, int64_t seq_le
   }
   p->tail_items = static_cast<int32_t>(tail_items);
   p->total_items = static_cast<int32_t>(tail_items + static_cast<int64_t>(b0) * kv_heads);
-  p->grid = 2 * (p->total_items < pairs ? p->total_items : pairs);
+  p->grid = ctas_per_worker() * (p->total_items < pairs ? p->total_items : pairs);
   p->total_tiles = tiles;
   p->workspace_bytes = kControlBytes + (any_split ? tail_items * kSlotBytes : 0);
   return TPSA_OK;
@@ -1893,7 +1935,7 @@ tpsa_status launch(const void* query, const void* key_cache, const void* value_c
   if (st != TPSA_OK) return st;
   KernelArgs args;
   std::memset(&args, 0, sizeof(args));
-  st = build_plan(query_tokens, query_start, seq_len, prompt_len, kv_heads, dev->max_pairs,
+  st = build_plan(query_tokens, query_start, seq_len, prompt_len, kv_heads, dev->workers(),
                   scale, &args.plan);
   if (st != TPSA_OK) return st;
   const tpsa_plan& p = args.plan;
@@ -1938,14 +1980,26 @@ tpsa_status launch(const void* query, const void* key_cache, const void* value_c
   args.tiles = reinterpret_cast<unsigned long long*>(tile_counter);
   args.words_per_row = (p.seq_len + 31) / 32;
 
-  if (visited != nullptr || tile_counter != nullptr) {
+  const bool visit = visited != nullptr || tile_counter != nullptr;
+  if (kernel_form() == Form::kSolo) {
+    CUtensorMap tk128, tout16;  // whole 128-key K tiles; one softmax warp's output box
+    st = encode_map(&tk128, key_cache, kv_heads, cache_tokens, 1, 128);
+    if (st != TPSA_OK) return st;
+    st = encode_map(&tout16, out, hq, static_cast<uint64_t>(query_tokens), 2, 16);
+    if (st != TPSA_OK) return st;
+    if (visit) {
+      tpsa_solo_kernel<true, false><<<p.grid, solo::kNumThreads, solo::kSmemBytes, s>>>(
+          args, tq, tk128, tk64, tv, tout16);
+    } else {
+      tpsa_solo_kernel<false, false><<<p.grid, solo::kNumThreads, solo::kSmemBytes, s>>>(
+          args, tq, tk128, tk64, tv, tout16);
+    }
+  } else if (visit) {
     tpsa_paged_kernel<true, false><<<p.grid, kNumThreads, kSmemBytes, s>>>(args, tq, tk64, tk32,
-                                                                            tv,
-                                                                     tout);
+                                                                            tv, tout);
   } else {
     tpsa_paged_kernel<false, false><<<p.grid, kNumThreads, kSmemBytes, s>>>(args, tq, tk64, tk32,
-                                                                             tv,
-                                                                      tout);
+                                                                             tv, tout);
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
@@ -2016,7 +2070,7 @@ tpsa_status build_batch(int32_t first, int32_t count, const int64_t* cu_seqlens_
   a.plan.query_tokens = static_cast<int32_t>(cu_seqlens_q[first + count] - cu_seqlens_q[first]);
   a.plan.total_items = items;
   a.plan.total_tiles = tiles;
-  a.plan.grid = 2 * (items < pairs ? items : pairs);
+  a.plan.grid = ctas_per_worker() * (items < pairs ? items : pairs);
   const int64_t ctl = (int64_t{kCtlSplitBase} + counters) * 4;
   b->ctl_bytes = std::max<int64_t>(kControlBytes, (ctl + 255) / 256 * 256);
   b->workspace_bytes = b->ctl_bytes + static_cast<int64_t>(slots) * kSlotBytes;
@@ -2117,6 +2171,11 @@ tpsa_status launch_varlen(const void* query, const void* key_cache, const void* 
   if (st != TPSA_OK) return st;
   st = encode_map(&tout, out, hq, total_rows, 2, kBlockQ);
   if (st != TPSA_OK) return st;
+  CUtensorMap tk128, tout16;  // solo kernel: whole 128-key K tiles, one warp's output box
+  st = encode_map(&tk128, key_cache, kv_heads, cache_tokens, 1, 128);
+  if (st != TPSA_OK) return st;
+  st = encode_map(&tout16, out, hq, total_rows, 2, 16);
+  if (st != TPSA_OK) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   std::unique_ptr<BatchLaunch> b(new BatchLaunch);
   // Launches of at most kMaxReqs requests each, in stream order; each
@@ -2124,7 +2183,7 @@ tpsa_status launch_varlen(const void* query, const void* key_cache, const void* 
   for (int32_t first = 0; first < batch; first += kMaxReqs) {
     const int32_t count = std::min(kMaxReqs, batch - first);
     st = build_batch(first, count, cu_seqlens_q, seq_lens, prompt_lens, kv_heads,
-                     dev->max_pairs, scale, table_cols, b.get());
+                     dev->workers(), scale, table_cols, b.get());
     if (st != TPSA_OK) return st;
     if (workspace_bytes < static_cast<uint64_t>(b->workspace_bytes)) {
       return fail(TPSA_ERR_WORKSPACE, "workspace smaller than tpsa_varlen_workspace_size()");
@@ -2137,8 +2196,13 @@ tpsa_status launch_varlen(const void* query, const void* key_cache, const void* 
     args.scratch = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + b->ctl_bytes);
     cudaError_t e = cudaMemsetAsync(workspace, 0, static_cast<size_t>(b->ctl_bytes), s);
     if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(workspace)");
-    tpsa_paged_kernel<false, true><<<args.plan.grid, kNumThreads, kSmemBytes, s>>>(
-        args, tq, tk64, tk32, tv, tout);
+    if (kernel_form() == Form::kSolo) {
+      tpsa_solo_kernel<false, true><<<args.plan.grid, solo::kNumThreads, solo::kSmemBytes, s>>>(
+          args, tq, tk128, tk64, tv, tout16);
+    } else {
+      tpsa_paged_kernel<false, true><<<args.plan.grid, kNumThreads, kSmemBytes, s>>>(
+          args, tq, tk64, tk32, tv, tout);
+    }
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
   }
@@ -2149,9 +2213,10 @@ tpsa_status launch_varlen(const void* query, const void* key_cache, const void* 
 // Scratch for tpsa_paged_attention_static_scratch: the same control words and
 // split-KV partial slots that tpsa_paged_attention keeps in a caller-provided
 // workspace, in one module-global array per device instead.  Its maximum
-// size, 16 MiB, covers 8192-token query chunks over contexts up to 128K
-// tokens (8.1 MiB there) and 64- to 1024-token chunks up to 1M (9.1 MiB).
-constexpr uint64_t kStaticScratchBytes = uint64_t{16} << 20;
+// size, 24 MiB, covers every batch-one plan on a 148-SM B200: the split
+// count stays near one piece per CTA, so no plan needs more than 144 partial
+// slots (18.3 MiB; query chunks of 64 to 16384 rows over contexts to 4M).
+constexpr uint64_t kStaticScratchBytes = uint64_t{24} << 20;
 constexpr int kMaxScratchDevices = 64;
 std::mutex g_scratch_mutex;
 void* g_scratch_ptr[kMaxScratchDevices] = {};
@@ -2214,12 +2279,12 @@ tpsa_status tpsa_make_plan(int64_t query_tokens, int64_t query_start, int64_t se
                            int64_t prompt_len, int32_t kv_heads, int32_t sm_count,
                            float scale, tpsa_plan* plan) {
   t_last_error.clear();
-  int32_t pairs = sm_count / 2;
+  int32_t pairs = sm_count / ctas_per_worker();  // workers of the kernel form
   if (sm_count <= 0) {
     DeviceState* dev = nullptr;
     tpsa_status st = device_state(&dev);
     if (st != TPSA_OK) return st;
-    pairs = dev->max_pairs;
+    pairs = dev->workers();
   }
   return build_plan(query_tokens, query_start, seq_len, prompt_len, kv_heads, pairs, scale,
                     plan);
@@ -2283,7 +2348,7 @@ tpsa_status tpsa_varlen_workspace_size(int32_t batch, const int64_t* cu_seqlens_
   tpsa_status st = device_state(&dev);
   if (st != TPSA_OK) return st;
   return varlen_workspace(batch, cu_seqlens_q, seq_lens, prompt_lens, TPSA_KV_HEADS,
-                          dev->max_pairs, bytes);
+                          dev->workers(), bytes);
 }
 
 tpsa_status tpsa_varlen_workspace_size_heads(int32_t batch, const int64_t* cu_seqlens_q,
@@ -2298,7 +2363,7 @@ tpsa_status tpsa_varlen_workspace_size_heads(int32_t batch, const int64_t* cu_se
   tpsa_status st = device_state(&dev);
   if (st != TPSA_OK) return st;
   return varlen_workspace(batch, cu_seqlens_q, seq_lens, prompt_lens, kv_heads,
-                          dev->max_pairs, bytes);
+                          dev->workers(), bytes);
 }
 
 tpsa_status tpsa_paged_attention_varlen(const void* query, const void* key_cache,
@@ -2363,7 +2428,7 @@ tpsa_status tpsa_paged_attention_static_scratch(const void* query, const void* k
   tpsa_status st = device_state(&dev);
   if (st != TPSA_OK) return st;
   tpsa_plan p;
-  st = build_plan(query_tokens, query_start, seq_len, prompt_len, TPSA_KV_HEADS, dev->max_pairs,
+  st = build_plan(query_tokens, query_start, seq_len, prompt_len, TPSA_KV_HEADS, dev->workers(),
                   scale, &p);
   if (st != TPSA_OK) return st;
   if (static_cast<uint64_t>(p.workspace_bytes) > kStaticScratchBytes) {
@@ -2371,7 +2436,7 @@ tpsa_status tpsa_paged_attention_static_scratch(const void* query, const void* k
                 "this call needs " + std::to_string(p.workspace_bytes) +
                     " bytes of scratch; the static scratch holds " +
                     std::to_string(kStaticScratchBytes) +
-                    " bytes (16 MiB): use tpsa_paged_attention with a caller workspace");
+                    " bytes (24 MiB): use tpsa_paged_attention with a caller workspace");
   }
   void* scratch = nullptr;
   st = static_scratch_address(&scratch);

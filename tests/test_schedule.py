@@ -136,7 +136,7 @@ def test_items_partition_blocks_heads_and_tiles(tm, q0, tq, seq, prompt):
                     break
             assert parts[-1][2] == ntiles
         assert sum(costs) == plan.total_tiles
-        assert plan.grid == 2 * min(plan.total_items, SM // 2)  # CTA pairs
+        assert plan.grid == min(plan.total_items, SM)  # one CTA per item at a time
         split = any(tm._native.plan_item(plan, i).num_splits > 1 for i in range(plan.tail_items))
         assert plan.workspace_bytes == 2048 + (plan.tail_items * 256 * 130 * 4 if split else 0)
         assert (plan.num_blocks - plan.tail_block0) * kvh * 2 <= 448 or not split
@@ -149,29 +149,32 @@ def test_long_tail_blocks_are_split_and_run_first(tm):
     longest = max(tm._native.plan_item(plan, i).tile_end - tm._native.plan_item(plan, i).tile_begin
                   for i in range(plan.total_items))
     assert longest <= plan.split_tiles
-    assert plan.total_tiles / (SM // 2) >= longest
+    assert plan.total_tiles / SM >= longest
 
 
-@pytest.mark.parametrize("seq, pieces", [(8192, 1), (32768, 2), (65536, 3), (131072, 4)])
-def test_tail_split_count_fits_the_pairs(tm, seq, pieces):
+@pytest.mark.parametrize("seq, pieces", [(8192, 2), (32768, 4), (65536, 6), (131072, 7)])
+def test_tail_split_count_fits_the_ctas(tm, seq, pieces):
     """BASELINE config 3 (8192-row chunk ending an N-token prompt): the 16
     dense-tail (block, head) items are cut into as many pieces as the
-    makespan estimate picks; at 128K that is 4 (64 pieces for 74 CTA pairs,
-    one each), not 5 (80 pieces: six pairs would carry two)."""
+    makespan estimate picks for 148 single-CTA workers: at 128K 7 pieces
+    (112 pieces of 147 tiles, one per CTA, beside an average of 152 tiles
+    per CTA), never more pieces than CTAs."""
     plan = tm._native.make_plan(8192, seq - 8192, seq, seq, 8, SM)
     tail_blocks = (plan.num_blocks - plan.tail_block0) * 8
     assert plan.tail_items == tail_blocks * pieces
-    assert pieces == 1 or plan.tail_items <= SM // 2
+    assert plan.tail_items <= SM
 
 
 def test_static_scratch_range_fits_its_array(tm):
     """Every plan the static-scratch entry point documents (query chunks of
-    64-1024 rows at the end of prompts of 4K-1M tokens) fits in 16 MiB."""
+    64-16384 rows at the end of prompts of 4K-4M tokens) fits in 24 MiB."""
     worst = 0
-    for seq in (4096, 16384, 65536, 262144, 1 << 20):
-        for tq in (64, 256, 1024):
-            worst = max(worst, tm._native.make_plan(tq, seq - tq, seq, seq, 8, SM).workspace_bytes)
-    assert worst <= 16 << 20
+    for seq in (4096, 16384, 65536, 262144, 1 << 20, 1 << 22):
+        for tq in (64, 128, 256, 1024, 4096, 8192, 16384):
+            if tq <= seq:
+                worst = max(worst,
+                            tm._native.make_plan(tq, seq - tq, seq, seq, 8, SM).workspace_bytes)
+    assert worst <= 24 << 20
 
 
 def test_workspace_is_control_words_without_splits(tm):

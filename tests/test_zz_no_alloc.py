@@ -29,7 +29,12 @@ def _run(tm, dev, q, k, v, table, q0, seq, *, static):
     qd, kd, vd, td = (t.to(dev) for t in (q, k, v, table))
     out = torch.full_like(qd, float("nan"))
     if static:
+        # Nothing is allocated through torch's allocator by the call.
+        torch.cuda.synchronize(dev)
+        before = torch.cuda.memory_allocated(dev), torch.cuda.memory_reserved(dev)
         tm._native.paged_attention_static_scratch(qd, kd, vd, td, out, q0, seq, seq, SCALE)
+        torch.cuda.synchronize(dev)
+        assert (torch.cuda.memory_allocated(dev), torch.cuda.memory_reserved(dev)) == before
     else:
         ws = workspace_for(tm, q.shape[0], q0, seq, seq, 8, dev)
         tm._native.paged_attention(qd, kd, vd, td, out, q0, seq, seq, SCALE, workspace=ws)
