@@ -52,10 +52,14 @@ def _run(cmd: list[str]) -> None:
 # Spill limits in bytes of spill stores (see _check_ptxas_report).
 MAX_SPILL_BYTES = 0
 MAX_VISIT_SPILL_BYTES = 64
+# The single-CTA kernel keeps a whole 128-key row of scores in registers; its
+# allocation stores 8 bytes to local memory (measured faster than loading
+# half of the row twice without any spill).
+MAX_SOLO_SPILL_BYTES = 16
 
 
 def _check_ptxas_report(text: str) -> None:
-    """The production kernels (tpsa_paged_kernel<false, false> for batch-one
+    """The pair kernels (tpsa_paged_kernel<false, false> for batch-one
     calls, <false, true> for packed ragged batches) must compile without
     local-memory spills (softmax rows live in registers; spilled rows put
     local-memory traffic on the critical path).  The instantiation that also
@@ -74,6 +78,14 @@ def _check_ptxas_report(text: str) -> None:
             raise RuntimeError(f"tpsa_paged_kernel<{kind}> spills registers ({kinds[kind]} bytes)")
     if kinds["10"] > MAX_VISIT_SPILL_BYTES:
         raise RuntimeError(f"tpsa_paged_kernel<visit> spills registers ({kinds['10']} bytes)")
+    solo = re.findall(r"Compiling entry function '\w*tpsa_solo_kernelILb([01])ELb([01])E\w*' "
+                      r"for 'sm_100a'\n(?:.*\n)*?\s*(\d+) bytes stack frame, (\d+) bytes spill stores",
+                      text)
+    if len(solo) != 3:
+        raise RuntimeError("could not read the ptxas report of tpsa_solo_kernel")
+    for visit, varlen, _, st in solo:
+        if int(st) > MAX_SOLO_SPILL_BYTES:
+            raise RuntimeError(f"tpsa_solo_kernel<{visit}{varlen}> spills registers ({st} bytes)")
 
 
 def build_lib(force: bool = False) -> Path:

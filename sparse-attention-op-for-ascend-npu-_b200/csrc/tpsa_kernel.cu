@@ -250,6 +250,8 @@ __device__ __forceinline__ void raise_status(uint32_t bits) {
 }
 
 #ifdef TPSA_TRACE
+// Start and end (globaltimer ns) and items run of every CTA of the last launch.
+__device__ unsigned long long g_cta_span[1024][3];
 // First wait that gave up: {set, block, thread, shared offset, parity or target}.
 __device__ uint32_t g_timeout_site[5];
 extern __shared__ uint8_t smem_raw[];
@@ -2448,6 +2450,11 @@ tpsa_status tpsa_paged_attention_static_scratch(const void* query, const void* k
 
 #ifdef TPSA_TRACE
 // Copies role `role`'s events of the last launch into out (2 x uint64 each).
+TPSA_API void tpsa_debug_spans(unsigned long long* out, uint32_t ctas) {
+  cudaDeviceSynchronize();
+  cudaMemcpyFromSymbol(out, g_cta_span, sizeof(unsigned long long) * 3 * (ctas < 1024 ? ctas : 1024));
+}
+
 TPSA_API void tpsa_debug_timeout(uint32_t* out5) {
   cudaDeviceSynchronize();
   cudaMemcpyFromSymbol(out5, g_timeout_site, sizeof(uint32_t) * 5);

@@ -160,6 +160,9 @@ __device__ void scheduler_role(const KernelArgs& a, const Smem& sh) {
     const uint32_t slot = n % 2;
     if (!wait(sh, sh.bar(kBarItemEmpty + slot), ((n / 2) & 1) ^ 1)) break;
     const int32_t next = atomicAdd(a.ctl + kCtlNextItem, 1);
+#ifdef TPSA_TRACE
+    if (blockIdx.x < 1024 && next < p.total_items) g_cta_span[blockIdx.x][2] = n + 1;
+#endif
     ItemRec rec;
     if (kVarlen) {
       int32_t q = 0, ridx = 0;
@@ -483,51 +486,49 @@ __device__ void mma_role(const KernelArgs& a, const Smem& sh, uint32_t tmem) {
 }
 
 // ------------------------------------------------------------ softmax
-// One key tile of query tile x, the whole row of this thread: load S, mask,
-// row max, move the lazy reference if this tile's maxima require it,
-// exponentials and P into tensor memory, and O and the row sum rescaled when
-// the reference moved.  P (bf16 pairs) goes to columns 64-127 of the S
-// buffer.  A 64-key tile stays in registers; of a 128-key tile, keys 64-127
-// stay in registers while keys 0-63 are loaded twice (for the max, then for
-// the exponentials): their P lands over S columns 64-127 only after those
-// were read.  O holds the PVs of the earlier tiles of the item, all complete:
-// S of this tile was signalled by a commit issued after the previous PV.
 // Pairs of each 32-key chunk whose exponentials use the FMA-pipe polynomial
-// (bit c: pair c; see exp_chunk).  The two softmax warpgroups of a CTA
-// exponentiate at the same time and share the MUFU pipe; measured at 8K
-// (ms per launch): no pair 0.1350, 0x0101 0.1316, 0x1111 0.1305, 0x5555 0.1371.
+// (bit c: pair c; see exp_chunk).  None by default: measured at 8K with the
+// whole row in registers (ms per launch), no pair 0.1140, 0x0001 0.1146,
+// 0x0401 0.1153, 0x1111 0.1179.  (MUFU ex2 runs at 16 per clock per SM, as
+// many exponentials per clock as the tensor pipe needs for this tile shape.)
 #ifndef TPSA_SOLO_POLY_MASK
-#define TPSA_SOLO_POLY_MASK 0x1111u
+#define TPSA_SOLO_POLY_MASK 0u
 #endif
 constexpr uint32_t kSoloPoly = TPSA_SOLO_POLY_MASK;
 
-// t.prev_bar is the P-half barrier of the tile (arrived once keys 0-63 of P
-// are in tensor memory).
+// One key tile of query tile x, the whole row of this thread: load S (all of
+// it into registers), mask, row max, move the lazy reference if this tile's
+// maxima require it (O and the row sum rescaled first), exponentials and P
+// into tensor memory over columns 64-127 of the S buffer.  P of keys 0-63 is
+// published on t.prev_bar (the P-half barrier) before the exponentials of
+// keys 64-127, so their PV can start.  O holds the PVs of the earlier tiles
+// of the item, all complete: S of this tile was signalled by a commit issued
+// after the previous PV.  (Keeping keys 64-127 in registers and loading keys
+// 0-63 twice measured 10 % slower at 8K.)
 template <bool kVisit>
 __device__ __forceinline__ void softmax_tile(const TileArgs& t, float sl2, int32_t q, bool sparse,
                                              RowState& st, uint32_t* visit_row,
                                              int32_t words_per_row) {
-  uint32_t ra[32], rb[32];
-  ptx::tmem_ld32(t.s_addr, ra);
-  ptx::tmem_ld32(t.s_addr + 32, rb);
-  ptx::tmem_wait_ld_regs(ra);
-  ptx::tmem_fence_regs(rb);
-  prepare_chunk<kVisit>(ra, t.masked, q, sparse, t.k0, visit_row, words_per_row);
-  prepare_chunk<kVisit>(rb, t.masked, q, sparse, t.k0 + 32, visit_row, words_per_row);
-  float lm = fmaxf(chunk_max(ra), chunk_max(rb));
+  uint32_t r0[32], r1[32], r2[32], r3[32];
+  ptx::tmem_ld32(t.s_addr, r0);
+  ptx::tmem_ld32(t.s_addr + 32, r1);
   if (t.wide) {
-    ptx::tmem_ld32(t.s_addr + 64, ra);
-    ptx::tmem_ld32(t.s_addr + 96, rb);
-    ptx::tmem_wait_ld_regs(ra);
-    ptx::tmem_fence_regs(rb);
-    prepare_chunk<kVisit>(ra, t.masked, q, sparse, t.k0 + 64, visit_row, words_per_row);
-    prepare_chunk<kVisit>(rb, t.masked, q, sparse, t.k0 + 96, visit_row, words_per_row);
-    lm = fmaxf(lm, fmaxf(chunk_max(ra), chunk_max(rb)));
+    ptx::tmem_ld32(t.s_addr + 64, r2);
+    ptx::tmem_ld32(t.s_addr + 96, r3);
   }
-  TPSA_TILE_TR(t, 30);
+  ptx::tmem_wait_ld_regs(r0);
+  ptx::tmem_fence_regs(r1);
+  ptx::tmem_fence_regs(r2);
+  ptx::tmem_fence_regs(r3);
+  prepare_chunk<kVisit>(r0, t.masked, q, sparse, t.k0, visit_row, words_per_row);
+  prepare_chunk<kVisit>(r1, t.masked, q, sparse, t.k0 + 32, visit_row, words_per_row);
+  float lm = fmaxf(chunk_max(r0), chunk_max(r1));
+  if (t.wide) {
+    prepare_chunk<kVisit>(r2, t.masked, q, sparse, t.k0 + 64, visit_row, words_per_row);
+    prepare_chunk<kVisit>(r3, t.masked, q, sparse, t.k0 + 96, visit_row, words_per_row);
+    lm = fmaxf(lm, fmaxf(chunk_max(r2), chunk_max(r3)));
+  }
   const float m_new = next_ref(st.m_ref, lm, sl2);
-  // A moved reference rescales O and the row sum before any P of this tile
-  // is published (the PV of keys 0-63 may start right after).
   const bool moved = m_new != st.m_ref;
   if (__any_sync(0xffffffffu, moved)) {
     float factor = 1.0f;
@@ -539,29 +540,16 @@ __device__ __forceinline__ void softmax_tile(const TileArgs& t, float sl2, int32
   const float neg_mb = m_new == -INFINITY ? 0.0f : -m_new * sl2;
   float sum0 = 0.0f, sum1 = 0.0f;
   const uint32_t p_addr = t.s_addr + 64;
-  if (t.wide) {
-#pragma unroll 1
-    for (int c = 0; c < 2; ++c) {
-      uint32_t rc[32];
-      ptx::tmem_ld32(t.s_addr + 32 * c, rc);
-      ptx::tmem_wait_ld_regs(rc);
-      if (t.masked) mask_chunk(rc, chunk_mask(q, sparse, t.k0 + 32 * c));
-      exp_chunk<kSoloPoly>(rc, sl2, neg_mb, p_addr + 16 * c, sum0, sum1);
-    }
-  } else {
-    exp_chunk<kSoloPoly>(ra, sl2, neg_mb, p_addr, sum0, sum1);
-    exp_chunk<kSoloPoly>(rb, sl2, neg_mb, p_addr + 16, sum0, sum1);
-  }
-  // P of keys 0-63 is in tensor memory: its PV may start.
+  exp_chunk<kSoloPoly>(r0, sl2, neg_mb, p_addr, sum0, sum1);
+  exp_chunk<kSoloPoly>(r1, sl2, neg_mb, p_addr + 16, sum0, sum1);
   ptx::tmem_wait_st();
   ptx::tc_fence_before();
   __syncwarp();
   if ((threadIdx.x & 31) == 0) ptx::mbar_arrive(t.prev_bar);
   if (t.wide) {
-    exp_chunk<kSoloPoly>(ra, sl2, neg_mb, p_addr + 32, sum0, sum1);
-    exp_chunk<kSoloPoly>(rb, sl2, neg_mb, p_addr + 48, sum0, sum1);
+    exp_chunk<kSoloPoly>(r2, sl2, neg_mb, p_addr + 32, sum0, sum1);
+    exp_chunk<kSoloPoly>(r3, sl2, neg_mb, p_addr + 48, sum0, sum1);
   }
-  TPSA_TILE_TR(t, 32);
   st.l_part += sum0 + sum1;
   ptx::tmem_wait_st();
 }
@@ -843,6 +831,9 @@ __global__ void __launch_bounds__(solo::kNumThreads, 1)
   const int lane = threadIdx.x % 32;
 
   if (threadIdx.x == 0) {
+#ifdef TPSA_TRACE
+    if (blockIdx.x < 1024) g_cta_span[blockIdx.x][0] = ptx::globaltimer_ns();
+#endif
     for (uint32_t x = 0; x < 2; ++x) {
       ptx::mbar_init(sh.bar(solo::kBarQFull + x), 1);
       ptx::mbar_init(sh.bar(solo::kBarQEmpty + x), 1);
@@ -899,6 +890,9 @@ __global__ void __launch_bounds__(solo::kNumThreads, 1)
 
   ptx::tc_fence_before();
   __syncthreads();  // MMAs drained, every role done
+#ifdef TPSA_TRACE
+  if (threadIdx.x == 0 && blockIdx.x < 1024) g_cta_span[blockIdx.x][1] = ptx::globaltimer_ns();
+#endif
   if (warp == 1) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem, kTmemCols);
