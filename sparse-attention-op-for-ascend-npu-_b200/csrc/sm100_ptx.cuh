@@ -68,22 +68,6 @@ __device__ __forceinline__ void red_release_add_shared(uint32_t addr, uint32_t v
   asm volatile("red.release.cta.shared::cta.add.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
 }
 
-// Plain shared-memory accesses by address (ordered by the counters above and
-// warp barriers; "memory" keeps the compiler from moving them across those).
-__device__ __forceinline__ void st_shared_f32(uint32_t addr, float v) {
-  asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
-}
-
-__device__ __forceinline__ float ld_shared_f32(uint32_t addr) {
-  float v;
-  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t count) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
-
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -151,41 +135,6 @@ __device__ __forceinline__ void tc_fence_before() {
 
 __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-
-// D[tmem] (+)= A[smem desc] * B[smem desc]^T, bf16 inputs, fp32 accumulate.
-__device__ __forceinline__ void umma_ss(uint32_t d_tmem, uint64_t a_desc,
-                                        uint64_t b_desc, uint32_t idesc,
-                                        uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(
-          d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// D[tmem] (+)= A[tmem] * B[smem desc], A read from tensor memory.
-__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem,
-                                        uint64_t b_desc, uint32_t idesc,
-                                        uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(
-          d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// Arrive once on `bar` when every tcgen05 op issued so far by this thread
-// has completed.
-__device__ __forceinline__ void umma_commit(uint32_t bar) {
-  asm volatile(
-      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
-      "[%0];" ::"r"(bar)
-      : "memory");
 }
 
 __device__ __forceinline__ void tmem_wait_ld() {
@@ -257,69 +206,6 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr,
 }
 
 
-// ---------------------------------------------------------------- cluster
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-
-// Address of the same shared-memory offset in CTA `rank` of the cluster.
-__device__ __forceinline__ uint32_t mapa(uint32_t addr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
-  return r;
-}
-
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
-                   : "memory");
-}
-
-// Arrive on an mbarrier given by a shared::cluster address (own or peer
-// CTA).  Default (release, CTA scope) semantics: used for signals whose data
-// is ordered by TMA completion or by tcgen05 fences.
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
-  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
-}
-
-// Arrive with cluster-scope release: orders this thread's earlier stores to
-// the peer's shared memory (st.shared::cluster) before the arrival.
-__device__ __forceinline__ void mbar_arrive_cluster_release(uint32_t cluster_bar) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar)
-               : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive_expect_tx_cluster(uint32_t cluster_bar,
-                                                              uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cluster.b64 _, [%0], %1;" ::"r"(cluster_bar),
-               "r"(bytes)
-               : "memory");
-}
-
-// try_wait with cluster-scope acquire (pairs with arrivals from the peer CTA).
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
-  uint32_t done;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.b32 %0, 1, 0, p;\n\t}"
-      : "=r"(done)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return done != 0;
-}
-
-__device__ __forceinline__ void st_cluster_u32(uint32_t cluster_addr, uint32_t v) {
-  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ void st_cluster_v4(uint32_t cluster_addr, uint4 v) {
-  asm volatile("st.shared::cluster.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(cluster_addr),
-               "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
-               : "memory");
-}
-
 // TMA tile store from this CTA's shared memory (bulk async-group completion).
 __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, int32_t c0, int32_t c1,
                                              int32_t c2, uint32_t src) {
@@ -347,121 +233,9 @@ __device__ __forceinline__ void bulk_wait_group() {
   asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// TMA tile load for a CTA pair: data lands in this CTA's shared memory, the
-// completion is signalled on `bar`, which may live in the peer CTA.
-__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap* map,
-                                                 int32_t c0, int32_t c1, int32_t c2,
-                                                 uint32_t cluster_bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::"
-      "bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(cluster_bar)
-      : "memory");
-}
-
-// ------------------------------------------------------- tcgen05, CTA pair
-__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
-  asm volatile(
-      "tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
-      "r"(ncols)
-      : "memory");
-}
-
-__device__ __forceinline__ void tmem_relinquish_pair() {
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
-               : "memory");
-}
-
-// M=256 MMA over the CTA pair: A rows 0-127 from this CTA, 128-255 from the
-// peer (same shared-memory offsets); B split in N across the pair.
-__device__ __forceinline__ void umma_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                             uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-__device__ __forceinline__ void umma_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
-                                             uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// Arrive on the barrier at offset `bar` in every CTA of `cta_mask` once all
-// prior tcgen05 ops of this thread (pair MMAs) have completed.
-__device__ __forceinline__ void umma_commit_pair_mc(uint32_t bar, uint16_t cta_mask) {
-  asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 "
-      "[%0], %1;" ::"r"(bar),
-      "h"(cta_mask)
-      : "memory");
-}
-
-__device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
-  asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
-      : "memory");
-}
-
-
-// Warp-collective forms: every lane computes the (warp-uniform) operands and
-// exactly one elected lane issues the instruction.
-__device__ __forceinline__ void umma_ss_pair_elect(uint32_t d_tmem, uint64_t a_desc,
-                                                   uint64_t b_desc, uint32_t idesc,
-                                                   uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p, e;\n\t"
-      "elect.sync _|e, 0xffffffff;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-__device__ __forceinline__ void umma_ts_pair_elect(uint32_t d_tmem, uint32_t a_tmem,
-                                                   uint64_t b_desc, uint32_t idesc,
-                                                   uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p, e;\n\t"
-      "elect.sync _|e, 0xffffffff;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-__device__ __forceinline__ void umma_commit_pair_mc_elect(uint32_t bar, uint16_t cta_mask) {
-  asm volatile(
-      "{\n\t.reg .pred e;\n\t"
-      "elect.sync _|e, 0xffffffff;\n\t"
-      "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 "
-      "[%0], %1;\n\t}" ::"r"(bar),
-      "h"(cta_mask)
-      : "memory");
-}
-
-__device__ __forceinline__ void umma_commit_pair_elect(uint32_t bar) {
-  asm volatile(
-      "{\n\t.reg .pred e;\n\t"
-      "elect.sync _|e, 0xffffffff;\n\t"
-      "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(
-          bar)
-      : "memory");
-}
-
-// Forms issued by the lanes whose `leader` is nonzero (one lane of the warp,
-// elected once): a predicate instead of an elect.sync per instruction.
+// One lane of the warp, elected once: the tcgen05 forms below are issued by
+// the lanes whose `leader` is nonzero, a predicate instead of an elect.sync
+// per instruction.
 __device__ __forceinline__ uint32_t elect_one() {
   uint32_t pred;
   asm volatile(
@@ -472,43 +246,11 @@ __device__ __forceinline__ uint32_t elect_one() {
   return pred;
 }
 
-__device__ __forceinline__ void umma_ss_pair_if(uint32_t leader, uint32_t d_tmem, uint64_t a_desc,
-                                                uint64_t b_desc, uint32_t idesc,
-                                                uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p, e;\n\t"
-      "setp.ne.b32 e, %5, 0;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(leader)
-      : "memory");
-}
-
-__device__ __forceinline__ void umma_ts_pair_if(uint32_t leader, uint32_t d_tmem, uint32_t a_tmem,
-                                                uint64_t b_desc, uint32_t idesc,
-                                                uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p, e;\n\t"
-      "setp.ne.b32 e, %5, 0;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(leader)
-      : "memory");
-}
-
-__device__ __forceinline__ void umma_commit_pair_mc_if(uint32_t leader, uint32_t bar,
-                                                       uint16_t cta_mask) {
-  asm volatile(
-      "{\n\t.reg .pred e;\n\t"
-      "setp.ne.b32 e, %2, 0;\n\t"
-      "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 "
-      "[%0], %1;\n\t}" ::"r"(bar),
-      "h"(cta_mask), "r"(leader)
-      : "memory");
-}
-
-// Single-CTA forms issued by the lanes whose `leader` is nonzero (a
-// predicate inside the instruction, no branch around it).
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T (bf16 inputs, fp32 accumulate),
+// A x B with A read from tensor memory, and the commit that arrives once on
+// `bar` when every tcgen05 op issued so far by this thread has completed;
+// each issued by the lanes whose `leader` is nonzero (a predicate inside the
+// instruction, no branch around it).
 __device__ __forceinline__ void umma_ss_if(uint32_t leader, uint32_t d_tmem, uint64_t a_desc,
                                            uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
   asm volatile(

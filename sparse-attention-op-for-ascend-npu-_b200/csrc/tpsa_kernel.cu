@@ -7,31 +7,30 @@
 // BSND paged cache through the block table and writing bf16 output into the
 // caller's buffer.
 //
-// CTA pairs.  The kernel runs as clusters of two CTAs on two SMs that share
-// every tensor-core instruction (tcgen05 cta_group::2, M = 256):
-//   * a work item is (64-token query block, kv head, key-tile range); its
-//     256 rows (64 tokens x 4 GQA heads) are split between the pair: CTA r
-//     owns query heads {4h + 2r, 4h + 2r + 1} (128 rows, one M half);
-//   * each key tile [k0, k0 + w) is split between the pair as the MMA wants
-//     its B operand split along N: CTA r loads keys [k0 + r*w/2, +w/2) of K
-//     (for S = Q K^T) and d-half r of V (for O = P V), so every K/V byte is
-//     loaded once per pair and serves 4 query heads.
-// Roles (384 threads per CTA):
-//   warp 0      K producer (Q of each item, K half-tiles; stores finished
-//               output boxes)
-//   warp 1      CTA 0: tcgen05 MMA issuer; both: TMEM owner
-//   warp 2      CTA 0: work scheduler (global counter, longest items first;
-//               item records into both CTAs' item rings)
-//   warp 3      V producer (V half-tiles)
-//   warps 4-11  two softmax warpgroups.  Key tile gt of the pair's tile
-//               stream belongs to warpgroup gt % 2; both work on the same
-//               rows and pass each row's lazy reference max from tile to
-//               tile, so P of every tile is relative to the reference O is
-//               kept in.  The owner of an item's last tile finishes the item.
-// Tensor memory per CTA (fp32 columns): three S buffers [0,384) and the O
-// accumulator [384,512).  Tile gt uses S buffer gt % 3; its P (bf16 pairs)
-// overwrites columns 64-127 of that buffer and PV(gt) reads it there.  The
-// issuer runs QK up to three tiles ahead of PV across item boundaries.
+// A work item is (64-token query block, kv head, key-tile range).  Its 256
+// rows (64 tokens x 4 GQA heads) are two M=128 query tiles of one CTA:
+// tile 0 holds query heads {4h, 4h+1}, tile 1 heads {4h+2, 4h+3}.  Both read
+// the same K/V tile from shared memory, so every K/V byte loaded serves 4
+// query heads, and both have the same key set.  Softmax warpgroup x owns
+// query tile x for the whole item: its rows' running reference max, row sum
+// and O accumulator never leave it, so the two warpgroups run independently.
+//
+// Roles (384 threads, one CTA per SM, persistent):
+//   warp 0      K producer: Q tiles of each item, K tiles into the K ring
+//   warp 1      tcgen05 MMA issuer (one elected lane) and TMEM owner
+//   warp 2      work scheduler (global counter, longest items first)
+//   warp 3      V producer: V tiles into the V ring
+//   warps 4-7   softmax + epilogue of query tile 0
+//   warps 8-11  softmax + epilogue of query tile 1
+// Tensor memory (512 fp32 columns): S0 [0,128), S1 [128,256), O0 [256,384),
+// O1 [384,512).  P of tile x (bf16 pairs) overwrites columns 64-127 of Sx
+// and PV reads it there.  Per query tile the MMA order is
+//   QK(t) -> softmax(t) -> PV(t) -> QK(t+1)
+// (QK(t+1) may be issued right after PV(t): the tensor pipe runs them in
+// order, so PV(t) has read P before QK(t+1) overwrites Sx), and the issuer
+// interleaves the two tiles: PV0(t), QK0(t+1), PV1(t), QK1(t+1), so one
+// tile's softmax overlaps the other tile's MMAs.  PV(t) runs in two 64-key
+// halves; the first starts as soon as P of keys 0-63 is written.
 //
 // Softmax arithmetic: scores are scaled into the log2 domain with one fused
 // multiply-add, exponentiated with ex2.approx (MUFU), summed in fp32, and
@@ -57,17 +56,16 @@ namespace tpsa {
 
 __device__ uint32_t g_device_status = 0;
 
-// Optional event trace of one CTA pair (build with -DTPSA_TRACE, pair chosen by
-// TPSA_TRACE_CLUSTER; compiled out of
-// the library otherwise).  Each tracing thread owns one buffer and a register
-// counter, so a trace point is two plain stores and a clock read.
+// Optional event trace of one CTA (build with -DTPSA_TRACE; the CTA is
+// TPSA_TRACE_CTA), compiled out of the library otherwise.  Each tracing
+// thread owns one buffer and a register counter, so a trace point is two
+// plain stores and a clock read.
 #ifdef TPSA_TRACE
-#ifndef TPSA_TRACE_CLUSTER
-#define TPSA_TRACE_CLUSTER 0  // CTA pair whose events are recorded
+#ifndef TPSA_TRACE_CTA
+#define TPSA_TRACE_CTA 0  // CTA whose events are recorded
 #endif
-// Roles: 0 K producer, 1 MMA issuer, 2-3 softmax warpgroups of CTA 0,
-// 4 V producer, 5-6 softmax warpgroups of CTA 1.
-constexpr uint32_t kTraceRoles = 7;
+// Roles: 0 K producer, 1 MMA issuer, 2-3 softmax warpgroups, 4 V producer.
+constexpr uint32_t kTraceRoles = 5;
 constexpr uint32_t kTraceCap = 1u << 14;
 __device__ unsigned long long g_trace[kTraceRoles][kTraceCap][2];
 __device__ uint32_t g_trace_n[kTraceRoles];
@@ -77,8 +75,8 @@ __device__ uint32_t g_trace_n[kTraceRoles];
 #endif
 #define TPSA_TR(role, ev, arg)                                                    \
   do {                                                                            \
-    if (((TPSA_TRACE_EVMASK >> (ev)) & 1ull) &&                                   \
-        (blockIdx.x >> 1) == TPSA_TRACE_CLUSTER && tr_n_ < kTraceCap) {           \
+    if (((TPSA_TRACE_EVMASK >> (ev)) & 1ull) && blockIdx.x == TPSA_TRACE_CTA &&   \
+        tr_n_ < kTraceCap) {                                                      \
       g_trace[role][tr_n_][0] = (static_cast<unsigned long long>(ev) << 32) |     \
                                 static_cast<uint32_t>(arg);                        \
       g_trace[role][tr_n_][1] = clock64();                                        \
@@ -98,7 +96,7 @@ __device__ uint32_t g_trace_n[kTraceRoles];
 namespace {
 
 constexpr int kNumThreads = 384;
-constexpr int kSoftmaxWarps = 8;  // two warpgroups, alternate key tiles
+constexpr int kSoftmaxWarps = 8;  // two warpgroups, one per query tile
 constexpr int kFirstSoftmaxWarp = 4;
 // Register split (setmaxnreg): the control warpgroup (warps 0-3) keeps 56
 // registers a thread, the two softmax warpgroups 224, within the launch's
@@ -106,94 +104,60 @@ constexpr int kFirstSoftmaxWarp = 4;
 constexpr uint32_t kControlRegs = 56;
 constexpr uint32_t kSoftmaxRegs = 224;
 static_assert(128 * kControlRegs + 256 * kSoftmaxRegs <= 384 * 168, "register split");
-// Tensor memory (512 columns, lane = row): three S buffers (P, as bf16
-// pairs, over columns 64-127 of each) and the O accumulator shared by both
-// softmax warpgroups.
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kNumSBufs = 3;
-constexpr uint32_t kTmemO = 384;
+constexpr uint32_t kTmemO = 256;  // O0 at 256, O1 at 384 (S0 at 0, S1 at 128)
 constexpr uint64_t kWaitTimeoutNs = 1000000000ull;  // 1 s per wait
 constexpr uint64_t kAbortSettleNs = 200000ull;      // let in-flight TMA land
 constexpr float kRescaleLog2 = 8.0f;  // lazy O rescale threshold (log2 units)
-// Column pairs c (of 16 per 32-column chunk) whose exponentials use the FMA
-// pipe polynomial rather than MUFU ex2: bit c set.  None by default: with
-// two softmax warps per SM sub-partition the MUFU pipe is not the limit
-// (measured: every nonzero mask tried was slower).
-#ifndef TPSA_POLY_MASK
-#define TPSA_POLY_MASK 0u
-#endif
-constexpr uint16_t kPairMask = 0x3;
 
 // Shared memory per CTA (offsets from a 1024-byte aligned base).
-constexpr uint32_t kQHalfBytes = 128 * 128;        // 128 rows x 64 bf16
-constexpr uint32_t kQBytes = 2 * kQHalfBytes;      // one Q buffer (2 d-halves)
-constexpr uint32_t kRingSlotBytes = 16384;         // one key tile's K half, or its V half
-constexpr uint32_t kKHalfBytes = 8192;             // d-half of a K half-tile
-constexpr int kRing = 4;                           // key-tile slots (power of two)
-constexpr uint32_t kOffQ = 0;                      // 2 Q buffers
-constexpr uint32_t kOffK = kOffQ + 2 * kQBytes;     // K ring
-constexpr uint32_t kOffV = kOffK + kRing * kRingSlotBytes;  // V ring
-constexpr uint32_t kOffBar = kOffV + kRing * kRingSlotBytes;
+constexpr uint32_t kQHalfBytes = 128 * 128;           // 128 rows x 64 bf16
+constexpr uint32_t kQTileBytes = 2 * kQHalfBytes;     // one query tile (two d-halves)
+constexpr uint32_t kKvHalfBytes = 128 * 128;          // 128 keys x 64 d
+constexpr uint32_t kKvSlotBytes = 2 * kKvHalfBytes;   // one key tile of K, or of V
+constexpr int kKRing = 2;
+constexpr int kVRing = 2;
+// Output staging: 4 KB per softmax warp (its 32 rows x 64 columns as bf16,
+// 128-byte swizzled), stored to `out` by the warp's own TMA store.
+constexpr uint32_t kOutStageBytes = 32 * 128;
+constexpr uint32_t kOffQ = 0;                                   // [query tile][d half]
+constexpr uint32_t kOffK = kOffQ + 2 * kQTileBytes;              // K ring
+constexpr uint32_t kOffV = kOffK + kKRing * kKvSlotBytes;        // V ring
+constexpr uint32_t kOffOut = kOffV + kVRing * kKvSlotBytes;      // output staging
+constexpr uint32_t kOffBar = kOffOut + 8 * kOutStageBytes;
 
 enum BarId : uint32_t {
-  kBarQFull = 0,                          // [2] CTA 0: both Q halves landed
-  kBarQEmpty = kBarQFull + 2,             // [2] both CTAs: Q buffer free
-  kBarKFull = kBarQEmpty + 2,             // [kRing] CTA 0: K of both CTAs landed
-  kBarKEmpty = kBarKFull + kRing,         // [kRing] both: K slot free (its QK done)
-  kBarVFull = kBarKEmpty + kRing,         // [kRing] CTA 0: V of both CTAs landed
-  kBarVEmpty = kBarVFull + kRing,         // [kRing] both: V slot free (its PV done)
-  kBarSFull = kBarVEmpty + kRing,         // [3] both: S buffer computed
-  kBarPFull = kBarSFull + kNumSBufs,      // [3] CTA 0: P of the tile in the S buffer written
-  kBarPvDone = kBarPFull + kNumSBufs,     // [3] both: PV from the S buffer completed
-  kBarOEmpty = kBarPvDone + kNumSBufs,    // CTA 0: O read by the item's epilogue
-  kBarItemFull = kBarOEmpty + 1,          // [2] both: item index written
-  kBarItemEmpty = kBarItemFull + 2,       // [2] CTA 0: item index consumed
-  kBarTail = kBarItemEmpty + 2,           // per CTA: V tail tile landed
-  kBarDrain = kBarTail + 1,               // CTA 0: all MMAs complete
+  kBarQFull = 0,                        // [2] query tile x landed
+  kBarQEmpty = kBarQFull + 2,           // [2] query tile x free (its last QK done)
+  kBarKFull = kBarQEmpty + 2,           // [kKRing] K tile landed
+  kBarKEmpty = kBarKFull + kKRing,      // [kKRing] K slot free (both QKs done)
+  kBarVFull = kBarKEmpty + kKRing,      // [kVRing] V tile landed (tail rows zeroed)
+  kBarVEmpty = kBarVFull + kVRing,      // [kVRing] V slot free (both PVs done)
+  kBarSFull = kBarVEmpty + kVRing,      // [2] S of tile x computed
+  kBarPFull = kBarSFull + 2,            // [2] P of tile x written (4 warps)
+  kBarPHalf = kBarPFull + 2,            // [2] P of keys 0-63 of tile x written (4 warps)
+  kBarOFull = kBarPHalf + 2,            // [2] the item's last PV of tile x done
+  kBarItemFull = kBarOFull + 2,         // [2] item record written
+  kBarItemEmpty = kBarItemFull + 2,     // [2] item record consumed
+  kBarTail = kBarItemEmpty + 2,         // V producer: a tail tile landed
+  kBarDrain = kBarTail + 1,             // MMA issuer: all MMAs complete
   kNumBars
 };
-// Arrivals: p_full takes one per warp of the tile's softmax warpgroup in
-// both CTAs, o_empty one per warp of the item's finishing warpgroup in both
-// CTAs; item_empty takes the two producers, the MMA issuer and the 8
-// softmax warps of CTA 0 plus the two producers and the 8 softmax warps of
-// CTA 1.
-constexpr uint32_t kPairWgArrivals = kSoftmaxWarps;  // 4 warps x 2 CTAs
-constexpr uint32_t kItemConsumers = 2 * (2 + kSoftmaxWarps) + 1;
-// q_empty: the MMA issuer's commit after the item's last QK.  (The finished
-// item's Q buffer then stages its output rows; the K producer stores them
-// and waits for the store to read the buffer before it loads the next Q.)
-constexpr uint32_t kQEmptyArrivals = 1;
+// item_empty: K producer, V producer, MMA warp, 8 softmax warps.
+constexpr uint32_t kItemConsumers = 3 + kSoftmaxWarps;
 
 constexpr uint32_t kOffItemSlots = (kOffBar + kNumBars * 8 + 15) & ~15u;  // 2 x ItemRec
 constexpr uint32_t kOffTmemSlot = kOffItemSlots + 2 * 64;
 constexpr uint32_t kOffAbort = kOffTmemSlot + 4;
-constexpr uint32_t kOffSplitLast = kOffAbort + 4;  // int32 [2] (by split-item parity)
-// Monotonic uint32 counters in shared memory, one count per warp and event
-// (see softmax_role).
-enum CounterId : uint32_t {
-  kCntPub = 0,                  // [8] row values published by softmax warp (wg * 4 + quad)
-  kCntCon = kCntPub + 8,        // [8] partner values read by softmax warp (wg * 4 + quad)
-  kCntStaged = kCntCon + 8,     // [2] output rows of warpgroup wg staged for its TMA store
-  kCntSplitW = kCntStaged + 2,  // split partial written
-  kCntSplitD,                   // split merge decided (one count per split item)
-  kNumCounters
-};
-constexpr uint32_t kOffCounters = kOffSplitLast + 8;
-// Row values passed between the two warps that hold the same rows in the
-// two softmax warpgroups: float [2 publishers][kChanSlots][128 rows].
-constexpr uint32_t kChanSlots = 4;
-constexpr uint32_t kOffXchg = (kOffCounters + 4 * kNumCounters + 15) & ~15u;
-// Output staging: 2 KB per softmax warp (32 rows x 64 bytes), used to turn
-// row-per-thread results into coalesced global stores.
-constexpr uint32_t kStageBytesPerWarp = 32 * 64;
-constexpr uint32_t kOffStage = (kOffXchg + 2 * kChanSlots * 128 * 4 + 127) & ~127u;
-constexpr uint32_t kSmemUsed = kOffStage + 8 * kStageBytesPerWarp;
+constexpr uint32_t kOffSplitLast = kOffAbort + 4;      // int32 [query tile][2]
+constexpr uint32_t kOffCounters = kOffSplitLast + 16;  // uint32 [4]: split written / decided per tile
+constexpr uint32_t kSmemUsed = kOffCounters + 16;
 constexpr uint32_t kSmemBytes = kSmemUsed + 1024;  // alignment slack
 static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 
 // Workspace control words (first kControlBytes of the workspace, zeroed by
 // the launcher): [0] next work item, [64..] one split counter per
-// (tail block, kv head, pair rank).
+// (tail block, kv head, query tile).
 constexpr int kCtlNextItem = 0;
 constexpr int kCtlSplitBase = 64;
 
@@ -228,13 +192,12 @@ struct KernelArgs {
   unsigned long long* tiles;   // visit mode: [tiles, keys]
 };
 
-struct Shared {
+
+
+struct Smem {
   uint8_t* base;
   uint32_t base_u32;
-  uint32_t rank;  // CTA rank in the pair
   __device__ uint32_t bar(uint32_t id) const { return base_u32 + kOffBar + 8 * id; }
-  // The same barrier in CTA 0 (shared::cluster address).
-  __device__ uint32_t bar0(uint32_t id) const { return ptx::mapa(bar(id), 0); }
   __device__ volatile int* abort_flag() const {
     return reinterpret_cast<volatile int*>(base + kOffAbort);
   }
@@ -242,7 +205,6 @@ struct Shared {
   __device__ uint4* item_slot(uint32_t i) const {
     return reinterpret_cast<uint4*>(base + kOffItemSlots + 64 * i);
   }
-  __device__ uint32_t item_slot_addr(uint32_t i) const { return base_u32 + kOffItemSlots + 64 * i; }
 };
 
 __device__ __forceinline__ void raise_status(uint32_t bits) {
@@ -270,21 +232,15 @@ __device__ __forceinline__ void note_timeout(uint32_t addr, uint32_t arg) {
   } while (0)
 #endif
 
+
+
 // Bounded wait: gives up after kWaitTimeoutNs or as soon as another role of
 // this CTA has aborted; on timeout records TPSA_DEVICE_WAIT_TIMEOUT.
-// kCluster selects a cluster-scope acquire (only needed where the signal
-// carries the peer's st.shared::cluster stores: the item ring).
-template <bool kCluster>
-__device__ __forceinline__ bool try_wait_sel(uint32_t bar, uint32_t parity) {
-  return kCluster ? ptx::mbar_try_wait_cluster(bar, parity) : ptx::mbar_try_wait(bar, parity);
-}
-
-template <bool kCluster>
 __device__ __forceinline__ bool wait_bar_slow(uint32_t bar, uint32_t parity,
                                            volatile int* abort_flag) {
   const uint64_t t0 = ptx::globaltimer_ns();
   while (true) {
-    if (try_wait_sel<kCluster>(bar, parity)) return true;
+    if (ptx::mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
     if (ptx::globaltimer_ns() - t0 > kWaitTimeoutNs) {
       *abort_flag = 1;
@@ -295,10 +251,9 @@ __device__ __forceinline__ bool wait_bar_slow(uint32_t bar, uint32_t parity,
   }
 }
 
-template <bool kCluster = false>
-__device__ __forceinline__ bool wait_bar(const Shared& sh, uint32_t bar, uint32_t parity) {
-  if (try_wait_sel<kCluster>(bar, parity)) return true;
-  return wait_bar_slow<kCluster>(bar, parity, sh.abort_flag());
+__device__ __forceinline__ bool wait(const Smem& sh, uint32_t bar, uint32_t parity) {
+  if (ptx::mbar_try_wait(bar, parity)) return true;
+  return wait_bar_slow(bar, parity, sh.abort_flag());
 }
 
 // Bounded wait used while draining (ignores the abort flag).
@@ -313,9 +268,9 @@ __device__ __forceinline__ void drain_bar(uint32_t bar, uint32_t parity) {
 }
 
 // Bounded wait until the monotonic shared counter `id` reaches `target`
-// (wrap-safe comparison); gives up like wait_bar.
+// (wrap-safe comparison); gives up like wait.
 __device__ __forceinline__ bool wait_count_slow(volatile int* abort_flag, uint32_t addr,
-                                            uint32_t target) {
+                                             uint32_t target) {
   const uint64_t t0 = ptx::globaltimer_ns();
   while (static_cast<int32_t>(ptx::ld_acquire_shared(addr) - target) < 0) {
     if (*abort_flag) return false;
@@ -328,16 +283,12 @@ __device__ __forceinline__ bool wait_count_slow(volatile int* abort_flag, uint32
   }
   return true;
 }
-__device__ __forceinline__ bool wait_count_at(const Shared& sh, uint32_t addr, uint32_t target) {
+
+__device__ __forceinline__ bool wait_count(const Smem& sh, uint32_t id, uint32_t target) {
+  const uint32_t addr = sh.counter(id);
   if (static_cast<int32_t>(ptx::ld_acquire_shared(addr) - target) >= 0) return true;
   return wait_count_slow(sh.abort_flag(), addr, target);
 }
-__device__ __forceinline__ bool wait_count(const Shared& sh, uint32_t id, uint32_t target) {
-  return wait_count_at(sh, sh.counter(id), target);
-}
-
-__device__ __forceinline__ uint32_t ring_slot(uint32_t r) { return r % kRing; }
-__device__ __forceinline__ uint32_t ring_parity(uint32_t r) { return (r / kRing) & 1; }
 
 __device__ __forceinline__ float mufu_exp2(float x) {
   float y;
@@ -423,13 +374,13 @@ __device__ __forceinline__ void poly_exp2_x2(float x0, float x1, float& e0, floa
   e1 = __int_as_float(max(__float_as_int(q1) + (__float_as_int(t1) << 23), 0));
 }
 
+
 // ------------------------------------------------------------ scheduler ring
-// Work items flow from CTA 0's producer to every consumer through a 2-slot
-// ring in each CTA's shared memory.  A slot holds an item record: the item
+// Work items flow from the CTA's scheduler to every consumer through a
+// 2-slot ring in shared memory.  A slot holds an item record: the item
 // index (total_items or above ends the kernel), the decoded item and its
 // block's tile geometry, decoded once by the scheduler so that no consumer
-// repeats that integer arithmetic.  Consumers in CTA 0 release on their own
-// item_empty, consumers in CTA 1 on CTA 0's (remote arrive).
+// repeats that integer arithmetic.
 struct alignas(16) ItemRec {
   int32_t idx;
   tpsa_item it;
@@ -464,15 +415,6 @@ __device__ __forceinline__ ItemRec make_item_rec(const tpsa_plan& p, int32_t idx
   return rec;
 }
 
-__device__ __forceinline__ bool take_item(const Shared& sh, uint32_t n, ItemRec* rec) {
-  const uint32_t slot = n % 2;
-  if (!wait_bar<true>(sh, sh.bar(kBarItemFull + slot), (n / 2) & 1)) return false;
-  const uint4* src = sh.item_slot(slot);
-  uint4* dst = reinterpret_cast<uint4*>(rec);
-#pragma unroll
-  for (int j = 0; j < 4; ++j) dst[j] = src[j];
-  return true;
-}
 
 // The fields of item record n the MMA issuer uses: its index, tile count
 // and narrow-tile bits.
@@ -480,9 +422,22 @@ struct ItemBrief {
   int32_t idx, ntiles;
   uint32_t narrow;
 };
-__device__ __forceinline__ bool take_item_brief(const Shared& sh, uint32_t n, ItemBrief* b) {
+
+__device__ __forceinline__ bool take_item(const Smem& sh, uint32_t n, ItemRec* rec) {
   const uint32_t slot = n % 2;
-  if (!wait_bar<true>(sh, sh.bar(kBarItemFull + slot), (n / 2) & 1)) return false;
+  if (!wait(sh, sh.bar(kBarItemFull + slot), (n / 2) & 1)) return false;
+  const uint4* src = sh.item_slot(slot);
+  uint4* dst = reinterpret_cast<uint4*>(rec);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) dst[j] = src[j];
+  return true;
+}
+
+// The fields of item record n the MMA issuer uses (index, tile count,
+// narrow-tile bits).
+__device__ __forceinline__ bool take_item_brief(const Smem& sh, uint32_t n, ItemBrief* b) {
+  const uint32_t slot = n % 2;
+  if (!wait(sh, sh.bar(kBarItemFull + slot), (n / 2) & 1)) return false;
   const int32_t* w = reinterpret_cast<const int32_t*>(sh.item_slot(slot));
   b->idx = w[offsetof(ItemRec, idx) / 4];
   b->ntiles = w[(offsetof(ItemRec, it) + offsetof(tpsa_item, tile_end)) / 4] -
@@ -491,29 +446,36 @@ __device__ __forceinline__ bool take_item_brief(const Shared& sh, uint32_t n, It
   return true;
 }
 
-__device__ __forceinline__ void release_item(const Shared& sh, uint32_t n) {
-  ptx::mbar_arrive_cluster(sh.bar0(kBarItemEmpty + n % 2));
+__device__ __forceinline__ void release_item(const Smem& sh, uint32_t n) {
+  ptx::mbar_arrive(sh.bar(kBarItemEmpty + n % 2));
 }
 
+// Tile j of an item is 64 keys wide (the others are 128): see ItemRec::narrow.
+__device__ __forceinline__ bool tile_narrow(uint32_t narrow, int32_t j, int32_t ntiles) {
+  return (j < 2 && ((narrow >> j) & 1u)) || (j == ntiles - 1 && (narrow & 4u));
+}
+
+
 // ------------------------------------------------------------ scheduler
-// One thread of CTA 0: takes work items from the grid-wide counter
-// (longest first), decodes each into an item record and publishes it into
-// the pair's two-slot item ring (both CTAs' copies), running up to two items
-// ahead of the slowest consumer.  The index past the last item tells every
-// consumer to stop.
+// One thread: takes items from the grid-wide counter (longest first),
+// decodes each into an item record
+// and publishes it into the CTA's two-slot item ring.  An item is claimed
+// only once its ring slot is free, i.e. once the softmax warpgroups have
+// finished the item two before it: a CTA then holds at most the item it
+// runs and the next one, so CTAs finish the launch within about one item of
+// each other.
 template <bool kVarlen>
-__device__ void scheduler_role(const KernelArgs& a, const Shared& sh) {
+__device__ void scheduler_role(const KernelArgs& a, const Smem& sh) {
   const tpsa_plan& p = a.plan;
-  int32_t next = atomicAdd(a.ctl + kCtlNextItem, 1);
   for (uint32_t n = 0;; ++n) {
     const uint32_t slot = n % 2;
+    if (!wait(sh, sh.bar(kBarItemEmpty + slot), ((n / 2) & 1) ^ 1)) break;
+    const int32_t next = atomicAdd(a.ctl + kCtlNextItem, 1);
+#ifdef TPSA_TRACE
+    if (blockIdx.x < 1024 && next < p.total_items) g_cta_span[blockIdx.x][2] = n + 1;
+#endif
     ItemRec rec;
     if (kVarlen) {
-      // Dispatch order across the launch's requests: first every request's
-      // dense-tail items (the longest), then every request's other items,
-      // so that a later request's long items do not start last.  The record
-      // carries the request-major index (item_base + item within request),
-      // which the consumers use; the terminator carries total_items.
       int32_t q = 0, ridx = 0;
       if (next < p.total_items) {
         if (next < a.tail_total) {
@@ -534,121 +496,58 @@ __device__ void scheduler_role(const KernelArgs& a, const Shared& sh) {
     } else {
       rec = make_item_rec(p, next);
     }
-    if (rec.idx < p.total_items) next = atomicAdd(a.ctl + kCtlNextItem, 1);
-    if (!wait_bar(sh, sh.bar(kBarItemEmpty + slot), ((n / 2) & 1) ^ 1)) break;
     const uint4* words = reinterpret_cast<const uint4*>(&rec);
-    const uint32_t peer = ptx::mapa(sh.item_slot_addr(slot), 1);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      sh.item_slot(slot)[j] = words[j];
-      ptx::st_cluster_v4(peer + 16 * j, words[j]);
-    }
+    for (int j = 0; j < 4; ++j) sh.item_slot(slot)[j] = words[j];
     ptx::mbar_arrive(sh.bar(kBarItemFull + slot));
-    ptx::mbar_arrive_cluster_release(ptx::mapa(sh.bar(kBarItemFull + slot), 1));
     if (rec.idx >= p.total_items) break;
   }
 }
 
 // ------------------------------------------------------------ producers
-// Two single-thread producers per CTA, each following the item ring: the K
-// producer loads Q and the K half-tiles into the K ring (a slot frees when
-// its QK completes), the V producer the V half-tiles into the V ring (a
-// slot frees when its PV completes), so K can run ahead of V by the QK
-// lookahead.  Both CTAs of the pair load their halves with pair TMA loads
-// that complete on CTA 0's full barrier: of K, keys [r*half, (r+1)*half)
-// of the tile, all 128 d; of V, all keys of the tile, d-half r.
-// An item's output box staged in its Q buffer, to be stored by the K producer.
-struct PendingStore {
-  bool stages;          // a full, unsplit block: its epilogue stages the box
-  uint32_t staged;      // staged items up to and including this one
-  int32_t head, token;  // box coordinates in `out` (d is 0 and 64)
-};
-
-// Waits until item `ps` is staged (the finishing warpgroup counts four warps
-// on each d-half counter), TMA-stores its two d-half boxes from Q buffer qb,
-// and waits until the stores have read it.
-__device__ __forceinline__ void flush_store(const Shared& sh, const CUtensorMap* tout,
-                                            PendingStore& ps, uint32_t qb) {
-  if (!ps.stages) return;
-  ps.stages = false;
-  if (!wait_count(sh, kCntStaged + 0, 4 * ps.staged)) return;
-  if (!wait_count(sh, kCntStaged + 1, 4 * ps.staged)) return;
-  const uint32_t src = sh.base_u32 + kOffQ + qb * kQBytes;
-  ptx::tma_store_3d(tout, 0, ps.head, ps.token, src);
-  ptx::tma_store_3d(tout, 64, ps.head, ps.token, src + kQHalfBytes);
-  ptx::bulk_commit_group();
-  ptx::bulk_wait_group_read<0>();
-}
-
+// K side: for each item the first K tile, then the two query tiles (each
+// waits until the previous item's last QK of that tile completed), then the
+// remaining K tiles.  V side: the V tiles.  One thread each.
 template <bool kVarlen>
-__device__ void producer_role(const KernelArgs& a, const Shared& sh, const CUtensorMap* tq,
-                              const CUtensorMap* tk64, const CUtensorMap* tk32,
-                              const CUtensorMap* tv, const CUtensorMap* tout, bool v_side) {
+__device__ void producer_role(const KernelArgs& a, const Smem& sh, const CUtensorMap* tq,
+                              const CUtensorMap* tk128, const CUtensorMap* tk64,
+                              const CUtensorMap* tv, bool v_side) {
   const tpsa_plan& p = a.plan;
-  const uint32_t r = sh.rank;
   if (v_side) {
     ptx::prefetch_tmap(tv);
   } else {
     ptx::prefetch_tmap(tq);
+    ptx::prefetch_tmap(tk128);
     ptx::prefetch_tmap(tk64);
-    ptx::prefetch_tmap(tk32);
   }
-  const uint32_t bar_full = sh.bar0(v_side ? kBarVFull : kBarKFull);
+  const uint32_t bar_full = sh.bar(v_side ? kBarVFull : kBarKFull);
   const uint32_t bar_empty = sh.bar(v_side ? kBarVEmpty : kBarKEmpty);
   const uint32_t ring_base = sh.base_u32 + (v_side ? kOffV : kOffK);
+  const uint32_t ring_n = v_side ? kVRing : kKRing;
   uint32_t ring = 0, q_iter = 0, tail_iter = 0;
-  // K side: the output boxes staged in the two Q buffers, and staged items so far.
-  PendingStore pend0{false, 0, 0, 0}, pend1{false, 0, 0, 0};  // Q buffers 0 and 1
-  uint32_t staged = 0;
   bool ok = true;
   TPSA_TRACE_STATE;
+  const uint32_t trole = v_side ? 4 : 0;
+  (void)trole;
   for (uint32_t n = 0; ok; ++n) {
     ItemRec rec;
     if (!take_item(sh, n, &rec)) break;
     release_item(sh, n);
     if (rec.idx >= p.total_items) break;
-    if (r == 0 && !v_side) TPSA_TR(0, 20, rec.idx);
+    TPSA_TR(trole, 20, rec.idx);
     const tpsa_item& it = rec.it;
     const BlockTiles& bt = rec.bt;
-    // The item's request (a batch-one launch has one, at row and table 0).
     const ReqDesc& rq = a.reqs[kVarlen ? rec.req() : 0];
     const int32_t* table = kVarlen ? a.block_table + rq.table_off : a.block_table;
     const int32_t req_seq_len = kVarlen ? rq.plan.seq_len : p.seq_len;
     const int32_t q_row0 = kVarlen ? rq.q_row0 : 0;
-
     if (!v_side) {
-      // Q: this CTA's 128 rows (64 tokens x query heads 4h + 2r, 4h + 2r + 1).
-      // The buffer last held item n - 2: its QKs completed (q_empty) and its
-      // output, if staged there, is stored first.
-      const uint32_t qb = q_iter % 2;
-      if (q_iter >= 2) {
-        if (qb == 0) {
-          flush_store(sh, tout, pend0, 0);
-        } else {
-          flush_store(sh, tout, pend1, 1);
-        }
-        if (!wait_bar(sh, sh.bar(kBarQEmpty + qb), ((q_iter / 2) - 1) & 1)) break;
+      // The item's query rows into L2 now: the shared-memory copy waits until
+      // the previous item's last QK, and then reads them from L2.
+      for (int32_t c = 0; c < 4; ++c) {
+        ptx::tma_prefetch_3d(tq, (c & 1) * 64, it.kv_head * kGroupSize + 2 * (c >> 1),
+                             q_row0 + it.block * kBlockQ);
       }
-      const bool full_block = !kVarlen || bt.q_end - bt.q_begin == kBlockQ;
-      PendingStore cur;
-      cur.stages = it.num_splits == 1 && full_block;
-      staged += cur.stages ? 1u : 0u;
-      cur.staged = staged;
-      cur.head = it.kv_head * kGroupSize + 2 * static_cast<int32_t>(r);
-      cur.token = q_row0 + it.block * kBlockQ;
-      if (qb == 0) {
-        pend0 = cur;
-      } else {
-        pend1 = cur;
-      }
-      ptx::mbar_arrive_expect_tx_cluster(sh.bar0(kBarQFull + qb), kQBytes);
-      for (int dh = 0; dh < 2; ++dh) {
-        ptx::tma_load_3d_pair(sh.base_u32 + kOffQ + qb * kQBytes + dh * kQHalfBytes, tq, dh * 64,
-                              it.kv_head * kGroupSize + 2 * r, q_row0 + it.block * kBlockQ,
-                              sh.bar0(kBarQFull + qb));
-      }
-      ++q_iter;
-      if (r == 0) TPSA_TR(0, 21, rec.idx);
     }
 
     for (int32_t t = it.tile_begin; t < it.tile_end && ok; ++t) {
@@ -662,66 +561,72 @@ __device__ void producer_role(const KernelArgs& a, const Shared& sh, const CUten
       } else {
         tok = page * kPageSize + (k0 % kPageSize);
       }
-      if (a.tiles != nullptr && r == 0 && !v_side) {
+      if (a.tiles != nullptr && !v_side) {
         atomicAdd(a.tiles, 1ull);
         atomicAdd(a.tiles + 1, static_cast<unsigned long long>(w));
       }
-      const uint32_t s = ring_slot(ring);
-      if (!wait_bar(sh, bar_empty + 8 * s, ring_parity(ring) ^ 1)) { ok = false; break; }
+      const uint32_t s = ring % ring_n;
+      if (!wait(sh, bar_empty + 8 * s, ((ring / ring_n) & 1) ^ 1)) { ok = false; break; }
       ++ring;
-      const uint32_t dst = ring_base + s * kRingSlotBytes;
+      TPSA_TR(trole, 22, t);
+      const uint32_t dst = ring_base + s * kKvSlotBytes;
       if (!v_side) {
-        // Keys at or beyond seq_len (unwritten cache slots of the last page)
-        // only meet masked scores, which select -inf whatever they hold.
-        const int32_t half = w / 2;
-        const CUtensorMap* km = w == kTileKeys ? tk64 : tk32;
-        ptx::mbar_arrive_expect_tx_cluster(bar_full + 8 * s,
-                                           static_cast<uint32_t>(half) * kHeadDim * 2);
+        // Keys at or beyond seq_len (unwritten slots of the last page) only
+        // meet masked scores, which select -inf whatever they hold.
+        const CUtensorMap* km = w == kTileKeys ? tk128 : tk64;
+        ptx::mbar_arrive_expect_tx(bar_full + 8 * s, static_cast<uint32_t>(w) * kHeadDim * 2);
         for (int dh = 0; dh < 2; ++dh) {
-          ptx::tma_load_3d_pair(dst + dh * kKHalfBytes, km, dh * 64, it.kv_head,
-                                tok + static_cast<int32_t>(r) * half, bar_full + 8 * s);
+          ptx::tma_load_3d(dst + dh * kKvHalfBytes, km, dh * 64, it.kv_head, tok,
+                           bar_full + 8 * s);
         }
-      } else if (k0 + w <= req_seq_len) {
-        ptx::mbar_arrive_expect_tx_cluster(bar_full + 8 * s, static_cast<uint32_t>(w) * 64 * 2);
-        for (int sub = 0; sub < w / 64; ++sub) {
-          ptx::tma_load_3d_pair(dst + sub * 8192, tv, static_cast<int32_t>(r) * 64, it.kv_head,
-                                tok + sub * 64, bar_full + 8 * s);
+        if (t == it.tile_begin) {
+          // The item's query tiles, after its first K tile: query tile x
+          // (heads 4h + 2x, 4h + 2x + 1) frees when the previous item's last
+          // QK of that tile completes.
+          for (uint32_t x = 0; x < 2; ++x) {
+            if (q_iter > 0 && !wait(sh, sh.bar(kBarQEmpty + x), (q_iter - 1) & 1)) {
+              ok = false;
+              break;
+            }
+            ptx::mbar_arrive_expect_tx(sh.bar(kBarQFull + x), kQTileBytes);
+            for (int dh = 0; dh < 2; ++dh) {
+              ptx::tma_load_3d(sh.base_u32 + kOffQ + x * kQTileBytes + dh * kQHalfBytes, tq,
+                               dh * 64, it.kv_head * kGroupSize + 2 * static_cast<int32_t>(x),
+                               q_row0 + it.block * kBlockQ, sh.bar(kBarQFull + x));
+            }
+            TPSA_TR(trole, 21, x);
+          }
+          ++q_iter;
         }
       } else {
-        // Values at or beyond seq_len may be unwritten cache slots: load the
-        // tile into this CTA's slot here, zero those rows so P = 0 never
-        // meets a NaN, then release the slot with a plain arrival.
-        ptx::mbar_arrive_expect_tx(sh.bar(kBarTail), static_cast<uint32_t>(w) * 64 * 2);
-        for (int sub = 0; sub < w / 64; ++sub) {
-          ptx::tma_load_3d(dst + sub * 8192, tv, static_cast<int32_t>(r) * 64, it.kv_head,
-                           tok + sub * 64, sh.bar(kBarTail));
+        const bool tail = k0 + w > req_seq_len;
+        // Values at or beyond seq_len may be unwritten cache slots: such a
+        // tile lands on a private barrier, those rows are zeroed (so that
+        // P = 0 never meets a NaN), then the slot is published.
+        const uint32_t lbar = tail ? sh.bar(kBarTail) : bar_full + 8 * s;
+        ptx::mbar_arrive_expect_tx(lbar, static_cast<uint32_t>(w) * kHeadDim * 2);
+        for (int dh = 0; dh < 2; ++dh) {
+          for (int sub = 0; sub < w / 64; ++sub) {
+            ptx::tma_load_3d(dst + dh * kKvHalfBytes + sub * 8192, tv, dh * 64, it.kv_head,
+                             tok + sub * 64, lbar);
+          }
         }
-        if (!wait_bar(sh, sh.bar(kBarTail), tail_iter & 1)) { ok = false; break; }
-        ++tail_iter;
-        for (int32_t row = req_seq_len - k0; row < w; ++row) {
-          uint4* d4 = reinterpret_cast<uint4*>(sh.base + (dst - sh.base_u32) + row * 128);
+        if (tail) {
+          if (!wait(sh, sh.bar(kBarTail), tail_iter & 1)) { ok = false; break; }
+          ++tail_iter;
+          for (int32_t row = req_seq_len - k0; row < w; ++row) {
+            for (int dh = 0; dh < 2; ++dh) {
+              uint4* d4 = reinterpret_cast<uint4*>(sh.base + (dst - sh.base_u32) +
+                                                   dh * kKvHalfBytes + row * 128);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) d4[j] = make_uint4(0, 0, 0, 0);
+              for (int j = 0; j < 8; ++j) d4[j] = make_uint4(0, 0, 0, 0);
+            }
+          }
+          ptx::fence_proxy_async_smem();
+          ptx::mbar_arrive(bar_full + 8 * s);
         }
-        ptx::fence_proxy_async_smem();
-        ptx::mbar_arrive_cluster(bar_full + 8 * s);
-      }
-      if (r == 0) TPSA_TR(v_side ? 4 : 0, 22, t);
-    }
-  }
-  if (!v_side) {
-    // The last two items' outputs, oldest first, complete before the CTA
-    // exits (flush_store gives up if the softmax aborted).
-    if (ok && !*sh.abort_flag()) {
-      if (q_iter % 2 == 0) {
-        flush_store(sh, tout, pend0, 0);
-        flush_store(sh, tout, pend1, 1);
-      } else {
-        flush_store(sh, tout, pend1, 1);
-        flush_store(sh, tout, pend0, 0);
       }
     }
-    ptx::bulk_wait_group<0>();
   }
   if (!ok || *sh.abort_flag()) {
     // Aborted: give in-flight TMA loads time to land before the CTA exits.
@@ -732,243 +637,167 @@ __device__ void producer_role(const KernelArgs& a, const Shared& sh, const CUten
 }
 
 // ------------------------------------------------------------ MMA issuer
-// The whole warp runs this role: operands are computed by every lane (they
-// are warp-uniform) and one elected lane issues each tcgen05 instruction.
-__device__ void mma_role(const KernelArgs& a, const Shared& sh, uint32_t tmem, int lane) {
+// The whole warp runs this role; operands are warp-uniform and one lane,
+// elected once, issues every tcgen05 instruction.
+__device__ void mma_role(const KernelArgs& a, const Smem& sh, uint32_t tmem) {
   const tpsa_plan& p = a.plan;
-  TPSA_TRACE_STATE;
-  // tcgen05.mma issue blocks once about three MMAs are queued, so this
-  // warp's own instructions between MMA batches leave the tensor pipe idle.
-  // The loop below therefore keeps its per-tile work to barrier waits,
-  // commits and additions to operands prepared once: descriptor bases
-  // (32-bit additions to their low word, which holds the start address),
-  // barrier addresses, instruction descriptors and incremental ring
-  // positions.  (Measured: the same loop run by one thread of the warp is
-  // slower.)
-  const uint32_t bar_k_full = sh.bar(kBarKFull), bar_k_empty = sh.bar(kBarKEmpty);
-  const uint32_t bar_v_full = sh.bar(kBarVFull), bar_v_empty = sh.bar(kBarVEmpty);
-  const uint32_t bar_s_full = sh.bar(kBarSFull), bar_p_full = sh.bar(kBarPFull);
-  const uint32_t bar_pv_done = sh.bar(kBarPvDone), bar_q_full = sh.bar(kBarQFull);
-  const uint32_t bar_q_empty = sh.bar(kBarQEmpty), bar_o_empty = sh.bar(kBarOEmpty);
-  // Descriptor start addresses are in 16-byte units, in the low word.
-  const uint64_t q_desc0 = ptx::smem_desc_sw128(sh.base_u32 + kOffQ, 16, 1024);
-  const uint64_t k_desc0 = ptx::smem_desc_sw128(sh.base_u32 + kOffK, 16, 1024);
-  const uint64_t v_desc0 = ptx::smem_desc_sw128(sh.base_u32 + kOffV, kKHalfBytes, 1024);
-  const uint32_t q_hi = static_cast<uint32_t>(q_desc0 >> 32);
-  const uint32_t k_hi = static_cast<uint32_t>(k_desc0 >> 32);
-  const uint32_t v_hi = static_cast<uint32_t>(v_desc0 >> 32);
-  auto desc = [](uint32_t lo, uint32_t hi) { return (static_cast<uint64_t>(hi) << 32) | lo; };
-  constexpr uint32_t kSlotUnits = kRingSlotBytes >> 4;
-  constexpr uint32_t kQUnits = kQBytes >> 4;
-  constexpr uint32_t kIdQk128 = ptx::idesc_bf16_f32(256, 128, 0);
-  constexpr uint32_t kIdQk64 = ptx::idesc_bf16_f32(256, 64, 0);
-  constexpr uint32_t kIdPv = ptx::idesc_bf16_f32(256, 128, 1);
-
-  // One lane, elected once, issues every tcgen05 instruction of this role
-  // under a predicate (an elect.sync per instruction costs more).
   const uint32_t leader = ptx::elect_one();
   auto warp_wait = [&](uint32_t bar, uint32_t parity) -> bool {
-    return __all_sync(0xffffffffu, wait_bar(sh, bar, parity));
+    return __all_sync(0xffffffffu, wait(sh, bar, parity));
   };
+  const uint64_t q_desc0 = ptx::smem_desc_sw128(sh.base_u32 + kOffQ, 16, 1024);
+  const uint64_t k_desc0 = ptx::smem_desc_sw128(sh.base_u32 + kOffK, 16, 1024);
+  const uint64_t v_desc0 = ptx::smem_desc_sw128(sh.base_u32 + kOffV, kKvHalfBytes, 1024);
+  constexpr uint32_t kIdQk128 = ptx::idesc_bf16_f32(128, 128, 0);
+  constexpr uint32_t kIdQk64 = ptx::idesc_bf16_f32(128, 64, 0);
+  constexpr uint32_t kIdPv = ptx::idesc_bf16_f32(128, 128, 1);
 
-  // S(buf) = Q K^T for the key tile in ring slot `slot` (M = 256 over the
-  // pair, N = 128 or 64).
-  auto issue_qk = [&](uint32_t q_lo, uint32_t slot, uint32_t buf, bool narrow) {
-    const uint32_t d = tmem + (buf << 7);
+  // Descriptor start addresses are in 16-byte units in the low word; the
+  // loop adds offsets to 32-bit low words prepared once.
+  const uint32_t q_lo = static_cast<uint32_t>(q_desc0), q_hi = static_cast<uint32_t>(q_desc0 >> 32);
+  const uint32_t k_lo = static_cast<uint32_t>(k_desc0), k_hi = static_cast<uint32_t>(k_desc0 >> 32);
+  const uint32_t v_lo = static_cast<uint32_t>(v_desc0), v_hi = static_cast<uint32_t>(v_desc0 >> 32);
+  auto desc = [](uint32_t lo, uint32_t hi) { return (static_cast<uint64_t>(hi) << 32) | lo; };
+  constexpr uint32_t kHalfUnits = kQHalfBytes >> 4;
+  constexpr uint32_t kQTileUnits = kQTileBytes >> 4;
+  constexpr uint32_t kSlotUnits = kKvSlotBytes >> 4;
+  static_assert(kQHalfBytes == kKvHalfBytes, "Q and K d-halves share offsets");
+  auto commit = [&](uint32_t bar) { ptx::umma_commit_if(leader, bar); };
+  // S_x = Q_x K^T for the K tile in ring slot ks (N = 128 or 64).
+  auto issue_qk = [&](uint32_t x, uint32_t ks, bool narrow) {
+    const uint32_t d = tmem + (x << 7);
     const uint32_t idesc = narrow ? kIdQk64 : kIdQk128;
-    const uint32_t k_lo = static_cast<uint32_t>(k_desc0) + slot * kSlotUnits;
+    const uint32_t qb = q_lo + x * kQTileUnits;
+    const uint32_t kb = k_lo + ks * kSlotUnits;
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-      const uint32_t qo = (k / 4) * (kQHalfBytes >> 4) + (k % 4) * 2;
-      const uint32_t ko = (k / 4) * (kKHalfBytes >> 4) + (k % 4) * 2;
-      ptx::umma_ss_pair_if(leader, d, desc(q_lo + qo, q_hi), desc(k_lo + ko, k_hi), idesc, k > 0 ? 1u : 0u);
+      const uint32_t o = (k / 4) * kHalfUnits + (k % 4) * 2;
+      ptx::umma_ss_if(leader, d, desc(qb + o, q_hi), desc(kb + o, k_hi), idesc, k > 0 ? 1u : 0u);
     }
   };
-  // O += P V: P (bf16 pairs) over columns 64-127 of S buffer buf, V the
-  // d-half of this CTA in ring slot `slot`.
-  auto issue_pv = [&](uint32_t slot, uint32_t buf, bool narrow, bool first) {
-    const uint32_t d = tmem + kTmemO;
-    const uint32_t pa = tmem + (buf << 7) + 64;
-    const uint32_t v_lo = static_cast<uint32_t>(v_desc0) + slot * kSlotUnits;
+  // O_x (+)= P_x V for keys [64 half, 64 half + 64) of the V tile in ring
+  // slot vs.
+  auto issue_pv = [&](uint32_t x, uint32_t vs, uint32_t half, bool first) {
+    const uint32_t d = tmem + kTmemO + (x << 7);
+    const uint32_t pa = tmem + (x << 7) + 64 + half * 32;
+    const uint32_t vb = v_lo + vs * kSlotUnits + half * (8192 >> 4);
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      if (k < 4 || !narrow) {
-        ptx::umma_ts_pair_if(leader, d, pa + k * 8, desc(v_lo + k * (2048 >> 4), v_hi), kIdPv,
-                             (first && k == 0) ? 0u : 1u);
-      }
+    for (int k = 0; k < 4; ++k) {
+      ptx::umma_ts_if(leader, d, pa + k * 8, desc(vb + k * (2048 >> 4), v_hi), kIdPv,
+                      (first && half == 0 && k == 0) ? 0u : 1u);
     }
   };
 
-  // The key tiles of all items form one stream over three S buffers (tile
-  // gt uses buffer gt % 3): after PV(t) this warp issues QK(t + 3), which may
-  // belong to a later item (S buffer t % 3 is free once PV(t), which reads
-  // its P, is issued).  Only the first PV of an item waits for the previous
-  // item's O to be released.  A QK cursor takes items from the ring; each QK
-  // leaves a control word for its tile's PV up to three tiles later.  The QK
-  // cursor stays within one item of the PV cursor: the Q buffer of item k + 2
-  // is released by the epilogue of item k, which needs item k's PVs.
-  enum : uint32_t {
-    kTNarrow = 1u,     // 64-key tile
-    kTFirst = 2u,      // first tile of its item (PV overwrites O)
-    kTItemStart = 4u,  // first tile of an item that is not the first item
-    kTItemOdd = 8u,    // with kTItemStart: the O-empty phase to wait for
-    kTIssued = 16u,    // a QK was issued (no control word otherwise)
-    kTItemShift = 8,   // bits 8 and up: the tile's item number (1-based)
-  };
-  uint32_t slot_q = 0, phase_q = 0, slot_v = 0, phase_v = 0, q_iter = 0;
-  uint32_t sb_q = 0, sb_v = 0, pass_v = 0;  // S buffers of the QK / PV cursors
-  uint32_t n_item = 0;                      // items taken from the ring
-  int32_t q_n = 0, q_ntiles = 0;
-  uint32_t q_narrow = 0, q_qb = 0;
-  uint32_t q_qd = static_cast<uint32_t>(q_desc0);
-  bool q_done = false;
+  TPSA_TRACE_STATE;
+  const bool tr = (threadIdx.x & 31) == 0;
+  uint32_t n_item = 0;
+  uint32_t ks = 0, k_phase = 0;  // K ring cursor of the next QK
+  uint32_t vs = 0, v_phase = 0;  // V ring cursor of the next PV
+  uint32_t p_par = 0;            // P-full phase (same for both tiles)
   bool ok = true;
-  // The next QK is prepared (its item taken, its Q and K waited for, its
-  // control word computed) by plan_qk and issued by fire_qk, so that in the
-  // steady state the QK that follows PV(t) is prepared while this warp waits
-  // for P(t), and PV(t) and QK(t + 3) go to the tensor pipe back to back.
-  uint32_t plan_info = 0;
-  bool plan_narrow = false;
-  // Prepares the next tile's QK; false when none may be issued now (no tile
-  // left, or it starts an item more than one ahead of item `bound`, 0 for
-  // no bound), or when a wait gave up (then ok is cleared).
-  auto plan_qk = [&](uint32_t bound) -> bool {
-    if (q_done) return false;
-    if (q_n == q_ntiles) {
-      if (bound != 0 && n_item > bound) return false;
-      ItemBrief rec;
-      const bool got = take_item_brief(sh, n_item, &rec);
-      if (!__all_sync(0xffffffffu, got)) {
-        ok = false;
-        return false;
+  // Current item.
+  ItemBrief cur;
+  bool got = take_item_brief(sh, n_item, &cur);
+  if (!__all_sync(0xffffffffu, got)) ok = false;
+  __syncwarp();
+  if (ok && (threadIdx.x & 31) == 0) release_item(sh, n_item);
+  if (ok) ++n_item;
+  bool done = !ok || cur.idx >= p.total_items;
+  uint32_t q_iter = 0;
+  if (!done) {
+    // First QKs of the first item.
+    const int32_t nt = cur.ntiles;
+    const bool nar = tile_narrow(cur.narrow, 0, nt);
+    for (uint32_t x = 0; x < 2 && ok; ++x) {
+      if (!warp_wait(sh.bar(kBarQFull + x), 0)) { ok = false; break; }
+      if (x == 0 && !warp_wait(sh.bar(kBarKFull + ks), k_phase)) { ok = false; break; }
+      ptx::tc_fence_after();
+      issue_qk(x, ks, nar);
+      commit(sh.bar(kBarSFull + x));
+      if (nt == 1) commit(sh.bar(kBarQEmpty + x));
+    }
+    commit(sh.bar(kBarKEmpty + ks));
+    ks = (ks + 1) % kKRing;
+    k_phase ^= ks == 0 ? 1u : 0u;
+    ++q_iter;
+  }
+  while (ok && !done) {
+    const int32_t nt = cur.ntiles;
+    ItemBrief nxt;
+    bool nxt_valid = false;
+    for (int32_t j = 0; j < nt && ok; ++j) {
+      const bool nar = tile_narrow(cur.narrow, j, nt);
+      // The QK that follows PV(j) for each tile: tile j + 1 of this item, or
+      // tile 0 of the next item.
+      bool has_next = j + 1 < nt;
+      bool new_item = false;
+      bool next_nar = false, next_last = false;
+      if (has_next) {
+        next_nar = tile_narrow(cur.narrow, j + 1, nt);
+        next_last = j + 1 == nt - 1;
+      } else {
+        const bool g = take_item_brief(sh, n_item, &nxt);
+        if (!__all_sync(0xffffffffu, g)) { ok = false; break; }
+        __syncwarp();
+        if ((threadIdx.x & 31) == 0) release_item(sh, n_item);
+        ++n_item;
+        nxt_valid = nxt.idx < p.total_items;
+        if (tr) TPSA_TR(1, 10, nxt.idx);
+        if (nxt_valid) {
+          const int32_t nn = nxt.ntiles;
+          has_next = true;
+          new_item = true;
+          next_nar = tile_narrow(nxt.narrow, 0, nn);
+          next_last = nn == 1;
+        }
       }
-      __syncwarp();
-      if (lane == 0) release_item(sh, n_item);
-      if (rec.idx >= p.total_items) {
-        q_done = true;
-        return false;
+      for (uint32_t x = 0; x < 2 && ok; ++x) {
+        // PV of keys 0-63 as soon as their P is written, then keys 64-127.
+        if (!warp_wait(sh.bar(kBarPHalf + x), p_par)) { ok = false; break; }
+        if (tr) TPSA_TR(1, 13, x);
+        if (x == 0 && !warp_wait(sh.bar(kBarVFull + vs), v_phase)) { ok = false; break; }
+        if (tr && x == 0) TPSA_TR(1, 14, j);
+        ptx::tc_fence_after();
+        issue_pv(x, vs, 0, j == 0);
+        if (!warp_wait(sh.bar(kBarPFull + x), p_par)) { ok = false; break; }
+        ptx::tc_fence_after();
+        if (!nar) issue_pv(x, vs, 1, false);
+        if (x == 1) commit(sh.bar(kBarVEmpty + vs));
+        if (j == nt - 1) commit(sh.bar(kBarOFull + x));
+        if (has_next) {
+          if (new_item && !warp_wait(sh.bar(kBarQFull + x), q_iter & 1)) { ok = false; break; }
+          if (tr && new_item) TPSA_TR(1, 11, x);
+          if (x == 0 && !warp_wait(sh.bar(kBarKFull + ks), k_phase)) { ok = false; break; }
+          if (tr && x == 0) TPSA_TR(1, 17, j);
+          ptx::tc_fence_after();
+          issue_qk(x, ks, next_nar);
+          if (tr) TPSA_TR(1, 18, x);
+          commit(sh.bar(kBarSFull + x));
+          if (next_last) commit(sh.bar(kBarQEmpty + x));
+        }
       }
-      if (lane == 0) TPSA_TR(1, 10, rec.idx);
-      ++n_item;
-      q_n = 0;
-      q_ntiles = rec.ntiles;
-      q_narrow = rec.narrow;
-      q_qb = q_iter & 1;
-      if (!warp_wait(bar_q_full + 8 * q_qb, (q_iter >> 1) & 1)) {
-        ok = false;
-        return false;
+      if (!ok) break;
+      p_par ^= 1;
+      vs = (vs + 1) % kVRing;
+      v_phase ^= vs == 0 ? 1u : 0u;
+      if (has_next) {
+        commit(sh.bar(kBarKEmpty + ks));
+        ks = (ks + 1) % kKRing;
+        k_phase ^= ks == 0 ? 1u : 0u;
+        if (new_item) ++q_iter;
       }
-      ++q_iter;
-      q_qd = static_cast<uint32_t>(q_desc0) + q_qb * kQUnits;
     }
-    const int32_t last = q_ntiles - 1;
-    plan_narrow = (q_n < 2 && ((q_narrow >> q_n) & 1u)) || (q_n == last && (q_narrow & 4u));
-    plan_info = kTIssued | (plan_narrow ? kTNarrow : 0u) | (q_n == 0 ? kTFirst : 0u) |
-                (q_n == 0 && n_item > 1 ? kTItemStart : 0u) |
-                (((n_item - 1) & 1) ? kTItemOdd : 0u) | (n_item << kTItemShift);
-    if (lane == 0) TPSA_TR(1, 19, sb_q);
-    if (!warp_wait(bar_k_full + 8 * slot_q, phase_q)) {
-      ok = false;
-      return false;
-    }
-    if (lane == 0) TPSA_TR(1, 17, sb_q);
-    return true;
-  };
-  // Issues the planned QK and returns its control word.
-  auto fire_qk = [&]() -> uint32_t {
-    ptx::tc_fence_after();
-    issue_qk(q_qd, slot_q, sb_q, plan_narrow);
-    if (lane == 0) TPSA_TR(1, 18, sb_q);
-    ptx::umma_commit_pair_mc_if(leader, bar_s_full + 8 * sb_q, kPairMask);
-    ptx::umma_commit_pair_mc_if(leader, bar_k_empty + 8 * slot_q, kPairMask);
-    if (q_n == q_ntiles - 1) ptx::umma_commit_pair_mc_if(leader, bar_q_empty + 8 * q_qb, kPairMask);
-    slot_q = (slot_q + 1) & (kRing - 1);
-    phase_q ^= slot_q == 0 ? 1u : 0u;
-    sb_q = sb_q == kNumSBufs - 1 ? 0 : sb_q + 1;
-    ++q_n;
-    return plan_info;
-  };
-
-  // Control words of the (up to three) tiles whose QK is issued and whose
-  // PV is not, oldest first; 0 for none.
-  uint32_t info0 = 0, info1 = 0, info2 = 0;
-  int have = 0;
-  auto push = [&](uint32_t info) {
-    if (have == 0) {
-      info0 = info;
-    } else if (have == 1) {
-      info1 = info;
-    } else {
-      info2 = info;
-    }
-    ++have;
-  };
-  // Issues QKs up to three ahead.  A QK that starts item n_item + 1 waits
-  // until the oldest pending PV is in item n_item: that item's Q buffer is
-  // released by the epilogue of item n_item - 1.
-  auto refill = [&]() {
-    while (ok && have < 3 && plan_qk(have > 0 ? (info0 >> kTItemShift) : 0u)) push(fire_qk());
-  };
-  refill();
-  while (ok && have > 0) {
-    // The QK to follow PV(t), prepared before P(t) is waited for.  Starting
-    // a new item here needs PV(t) itself to be in item n_item or later (the
-    // Q wait may not depend on PV(t)); otherwise refill takes it after PV(t).
-    const bool planned = plan_qk(info0 >> kTItemShift);
-    if (!ok) break;
-    if (lane == 0) TPSA_TR(1, 12, sb_v);
-    if (info0 & kTItemStart) {
-      // O of the previous item (item index k - 1) has been read by its
-      // epilogue: phase (k - 2) & 1 of o_empty.
-      if (!warp_wait(bar_o_empty, (info0 & kTItemOdd) ? 0u : 1u)) { ok = false; break; }
-      if (lane == 0) TPSA_TR(1, 11, sb_v);
-    }
-    if (!warp_wait(bar_p_full + 8 * sb_v, pass_v & 1)) { ok = false; break; }
-    if (lane == 0) TPSA_TR(1, 13, sb_v);
-    if (!warp_wait(bar_v_full + 8 * slot_v, phase_v)) { ok = false; break; }
-    if (lane == 0) TPSA_TR(1, 14, sb_v);
-    ptx::tc_fence_after();
-    issue_pv(slot_v, sb_v, (info0 & kTNarrow) != 0, (info0 & kTFirst) != 0);
-    if (lane == 0) TPSA_TR(1, 15, sb_v);
-    ptx::umma_commit_pair_mc_if(leader, bar_v_empty + 8 * slot_v, kPairMask);
-    ptx::umma_commit_pair_mc_if(leader, bar_pv_done + 8 * sb_v, kPairMask);
-    const uint32_t fired = planned ? fire_qk() : 0u;
-    if (lane == 0) TPSA_TR(1, 16, sb_v);
-    slot_v = (slot_v + 1) & (kRing - 1);
-    phase_v ^= slot_v == 0 ? 1u : 0u;
-    if (sb_v == kNumSBufs - 1) {
-      sb_v = 0;
-      ++pass_v;
-    } else {
-      ++sb_v;
-    }
-    info0 = info1;
-    info1 = info2;
-    info2 = 0;
-    --have;
-    if (fired != 0) push(fired);
-    refill();
-    if (lane == 0) TPSA_TR(1, 23, have);
+    if (!ok || !nxt_valid) break;
+    cur = nxt;
   }
   // All MMAs issued by this warp complete before TMEM is released.
-  ptx::umma_commit_pair_elect(sh.bar(kBarDrain));
-  if (lane == 0) drain_bar(sh.bar(kBarDrain), 0);
+  commit(sh.bar(kBarDrain));
+  if ((threadIdx.x & 31) == 0) drain_bar(sh.bar(kBarDrain), 0);
   __syncwarp();
 }
 
-// ------------------------------------------------------------ softmax
-template <int W>
-__device__ __forceinline__ void load_s(uint32_t taddr, float (&s)[W]) {
-  uint32_t r[W];
-#pragma unroll
-  for (int c = 0; c < W / 32; ++c) {
-    ptx::tmem_ld32(taddr + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&r[32 * c]));
-  }
-  ptx::tmem_wait_ld();
-#pragma unroll
-  for (int c = 0; c < W; ++c) s[c] = __uint_as_float(r[c]);
-}
 
+// ------------------------------------------------------------ softmax
 // Multiplies the 128 O columns of this thread's row by `factor`.
 __device__ __forceinline__ void rescale_o(uint32_t o_addr, float factor) {
 #pragma unroll 1
@@ -1004,40 +833,6 @@ __device__ __forceinline__ float next_ref(float m_ref, float m_tile, float scale
   return move ? m_tile : m_ref;
 }
 
-// Row values passed from one softmax warp to the warp holding the same 32
-// rows in the other warpgroup (warps quad + 4 and quad + 8), in order,
-// through a kChanSlots-deep ring per direction.  Publishing counts on the
-// publisher's counter; reading counts on the reader's, and a publisher
-// reuses a slot only once the reader has counted the value it held.
-struct RowChannel {
-  uint32_t mine, theirs;   // shared addresses of this row in the two rings
-  uint32_t pub_cnt;        // this warp's publication counter; the partner's is
-                           // peer_pub below, the read counters follow at +32 bytes
-  uint32_t peer_pub;
-  uint32_t n_pub, n_read;
-
-  __device__ __forceinline__ bool publish(const Shared& sh, float v) {
-    if (n_pub >= kChanSlots &&
-        !__all_sync(0xffffffffu, wait_count_at(sh, peer_pub + 32, n_pub - kChanSlots + 1))) {
-      return false;
-    }
-    ptx::st_shared_f32(mine + (n_pub % kChanSlots) * 512, v);
-    __syncwarp();
-    if ((threadIdx.x & 31) == 0) ptx::red_release_add_shared(pub_cnt, 1);
-    ++n_pub;
-    return true;
-  }
-  // The partner's next value; false if the wait gave up.
-  __device__ __forceinline__ bool read(const Shared& sh, float* v) {
-    if (!__all_sync(0xffffffffu, wait_count_at(sh, peer_pub, n_read + 1))) return false;
-    *v = ptx::ld_shared_f32(theirs + (n_read % kChanSlots) * 512);
-    __syncwarp();
-    if ((threadIdx.x & 31) == 0) ptx::red_release_add_shared(pub_cnt + 32, 1);
-    ++n_read;
-    return true;
-  }
-};
-
 // Replaces the keys of a 32-key chunk of S (fp32 bits) that are outside the
 // row's key set (bit c of m clear) by -inf.
 __device__ __forceinline__ void mask_chunk(uint32_t (&r)[32], uint32_t m) {
@@ -1049,7 +844,7 @@ __device__ __forceinline__ void mask_chunk(uint32_t (&r)[32], uint32_t m) {
 // pairs stored to tensor memory at p_addr, their sum added to (sum0, sum1).
 // Pair c of the chunk uses the FMA-pipe polynomial when bit c of kPoly is
 // set, MUFU ex2 otherwise.
-template <uint32_t kPoly = TPSA_POLY_MASK>
+template <uint32_t kPoly>
 __device__ __forceinline__ void exp_chunk(const uint32_t (&r)[32], float scale_log2, float neg_mb,
                                           uint32_t p_addr, float& sum0, float& sum1) {
   uint32_t pk[16];
@@ -1083,50 +878,26 @@ __device__ __forceinline__ float chunk_max(const uint32_t (&r)[32]) {
   return fmaxf(max3(mx0, mx1, mx2), mx3);
 }
 
-// Per-row state of the online softmax over one item's tiles, per warpgroup:
-// the reference max as of the last tile this warpgroup knows of, and the
-// warpgroup's partial row sum (over its own tiles) relative to it.
+// Per-row state of the online softmax over one item's tiles: the lazy
+// reference max and the row sum relative to it.
 struct RowState {
   float m_ref;
   float l_part;
 };
 
-// Moves this warpgroup's reference to m (from a tile of the other
-// warpgroup), rescaling the partial sum.  References only grow.
-__device__ __forceinline__ void adopt_ref(RowState& st, float m, float scale_log2) {
-  if (m != st.m_ref) {
-    st.l_part *= st.m_ref == -INFINITY ? 0.0f : mufu_exp2((st.m_ref - m) * scale_log2);
-    st.m_ref = m;
-  }
-}
 
-// Where a tile lives and what its owner needs to know.
+
+// Where a tile lives and what its softmax needs to know.
 struct TileArgs {
   uint32_t s_addr;      // the tile's S buffer (P goes to its columns 64-127)
   uint32_t o_addr;      // O (128 columns)
+  uint32_t half_bar;    // P-half barrier of the tile's query tile
   int32_t k0;           // first key of the tile
   bool wide;            // 128 keys (else 64)
   bool masked;          // some key of the tile is outside some row's key set
   bool first;           // first tile of the item (its PV overwrites O)
-  bool last;            // last tile of the item (its decision is not passed on)
-  uint32_t prev_bar;    // pv_done barrier of the previous tile, and its parity
-  uint32_t prev_parity;
-  uint32_t* trn;        // trace counter of this thread when it records (TPSA_TRACE)
-  uint32_t trole;
 };
-#ifdef TPSA_TRACE
-#define TPSA_TILE_TR(t, ev)                                   \
-  do {                                                        \
-    if ((t).trn != nullptr) {                                 \
-      uint32_t& tr_n_ = *(t).trn;                             \
-      TPSA_TR((t).trole, ev, 0);                              \
-    }                                                         \
-  } while (0)
-#else
-#define TPSA_TILE_TR(t, ev) \
-  do {                      \
-  } while (0)
-#endif
+
 
 // Keeps the visited bits of a 32-key chunk (debug output) and masks it.
 template <bool kVisit>
@@ -1140,106 +911,6 @@ __device__ __forceinline__ void prepare_chunk(uint32_t (&r)[32], bool mk, int32_
   if (mk) mask_chunk(r, m);
 }
 
-// One key tile of this warpgroup, the whole row of this thread: load S,
-// mask, row max; take the reference the previous tile (the other
-// warpgroup's) left, move it if this tile's maxima require, and pass it on;
-// exponentials and P into tensor memory; rescale O (after the previous
-// tile's PV completed) when the reference moved.  P (bf16 pairs) goes to
-// columns 64-127 of the S buffer.  A 64-key tile stays in registers; of a
-// 128-key tile, keys 64-127 stay in registers while keys 0-63 are loaded
-// twice (for the max, then for the exponentials), which keeps 64 of them
-// live at a time: their P lands over S columns 64-127 only after those
-// were read.  Returns false if a wait gave up.
-template <bool kVisit>
-__device__ __forceinline__ bool softmax_tile(const Shared& sh, const tpsa_plan& p,
-                                             const TileArgs& t, int32_t q, bool sparse,
-                                             RowChannel& ch, RowState& st,
-                                             uint32_t* visit_row, int32_t words_per_row) {
-  uint32_t ra[32], rb[32];
-  ptx::tmem_ld32(t.s_addr, ra);
-  ptx::tmem_ld32(t.s_addr + 32, rb);
-  ptx::tmem_wait_ld_regs(ra);
-  ptx::tmem_fence_regs(rb);
-  prepare_chunk<kVisit>(ra, t.masked, q, sparse, t.k0, visit_row, words_per_row);
-  prepare_chunk<kVisit>(rb, t.masked, q, sparse, t.k0 + 32, visit_row, words_per_row);
-  float lm = fmaxf(chunk_max(ra), chunk_max(rb));
-  if (t.wide) {
-    ptx::tmem_ld32(t.s_addr + 64, ra);
-    ptx::tmem_ld32(t.s_addr + 96, rb);
-    ptx::tmem_wait_ld_regs(ra);
-    ptx::tmem_fence_regs(rb);
-    prepare_chunk<kVisit>(ra, t.masked, q, sparse, t.k0 + 64, visit_row, words_per_row);
-    prepare_chunk<kVisit>(rb, t.masked, q, sparse, t.k0 + 96, visit_row, words_per_row);
-    lm = fmaxf(lm, fmaxf(chunk_max(ra), chunk_max(rb)));
-  }
-  TPSA_TILE_TR(t, 30);
-  const float sl2 = p.scale_log2;
-  // Optimistic agreement: the exponentials use this warpgroup's reference
-  // as of its previous tile; the other warpgroup's decision for the tile in
-  // between is read after the reloaded keys 0-63 (it is usually published
-  // by then) and, in the rare case that it changes this tile's reference,
-  // those are redone; keys 64-127, still in registers, follow with the
-  // final reference.
-  float m_new = next_ref(st.m_ref, lm, sl2);
-  bool agreed = t.first;
-  float sum0 = 0.0f, sum1 = 0.0f;
-  const uint32_t p_addr = t.s_addr + 64;
-#pragma unroll 1
-  while (true) {
-    if (t.wide) {
-      const float neg_mb = m_new == -INFINITY ? 0.0f : -m_new * sl2;
-      sum0 = 0.0f;
-      sum1 = 0.0f;
-#pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
-        uint32_t rc[32];
-        ptx::tmem_ld32(t.s_addr + 32 * c, rc);
-        ptx::tmem_wait_ld_regs(rc);
-        if (t.masked) mask_chunk(rc, chunk_mask(q, sparse, t.k0 + 32 * c));
-        exp_chunk(rc, sl2, neg_mb, p_addr + 16 * c, sum0, sum1);
-      }
-    }
-    if (agreed) break;
-    float mp;
-    if (!ch.read(sh, &mp)) return false;
-    agreed = true;
-    adopt_ref(st, mp, sl2);
-    const float m2 = next_ref(st.m_ref, lm, sl2);
-    if (!__any_sync(0xffffffffu, m2 != m_new)) break;
-    m_new = m2;
-  }
-  // The decision is final here: pass it on before the remaining
-  // exponentials, so that the other warpgroup's next tile, which reads it
-  // half-way through, does not wait for them.
-  if (!t.last && !ch.publish(sh, m_new)) return false;
-  TPSA_TILE_TR(t, 31);
-  {
-    const float neg_mb = m_new == -INFINITY ? 0.0f : -m_new * sl2;
-    const uint32_t p_kept = p_addr + (t.wide ? 32 : 0);
-    exp_chunk(ra, sl2, neg_mb, p_kept, sum0, sum1);
-    exp_chunk(rb, sl2, neg_mb, p_kept + 16, sum0, sum1);
-  }
-  TPSA_TILE_TR(t, 32);
-  const bool moved = m_new != st.m_ref;
-  if (__any_sync(0xffffffffu, moved)) {
-    float factor = 1.0f;
-    if (moved) factor = st.m_ref == -INFINITY ? 0.0f : mufu_exp2((st.m_ref - m_new) * sl2);
-    st.l_part *= factor;
-    st.m_ref = m_new;
-    if (!t.first) {
-      // O holds the PVs of the earlier tiles, the last of which has
-      // completed before O is rescaled; this tile's PV is issued only after
-      // this warp publishes P.
-      if (!__all_sync(0xffffffffu, wait_bar(sh, t.prev_bar, t.prev_parity))) return false;
-      ptx::tc_fence_after();
-      rescale_o(t.o_addr, factor);
-    }
-  }
-  st.l_part += sum0 + sum1;
-  ptx::tmem_wait_st();
-  TPSA_TILE_TR(t, 34);
-  return true;
-}
 
 // Writes columns [col, col + 32) of the 32 output rows of a softmax warp as
 // bf16 (values times `scale`).  Each thread holds one row, and its 64 bytes
@@ -1277,72 +948,136 @@ __device__ __forceinline__ void store_rows_bf16(const float (&o)[32], float scal
   __syncwarp();
 }
 
-// One arrival per softmax warp on a CTA-0 barrier.
-__device__ __forceinline__ void warp_arrive0(const Shared& sh, uint32_t id, int lane) {
+
+
+// Pairs of each 32-key chunk whose exponentials use the FMA-pipe polynomial
+// (bit c: pair c; see exp_chunk).  None by default: measured at 8K with the
+// whole row in registers (ms per launch), no pair 0.1140, 0x0001 0.1146,
+// 0x0401 0.1153, 0x1111 0.1179.  (MUFU ex2 runs at 16 per clock per SM, as
+// many exponentials per clock as the tensor pipe needs for this tile shape.)
+#ifndef TPSA_POLY_MASK
+#define TPSA_POLY_MASK 0u
+#endif
+constexpr uint32_t kPolyMask = TPSA_POLY_MASK;
+
+// One key tile of query tile x, the whole row of this thread: load S (all of
+// it into registers), mask, row max, move the lazy reference if this tile's
+// maxima require it (O and the row sum rescaled first), exponentials and P
+// into tensor memory over columns 64-127 of the S buffer.  P of keys 0-63 is
+// published on t.half_bar (the P-half barrier) before the exponentials of
+// keys 64-127, so their PV can start.  O holds the PVs of the earlier tiles
+// of the item, all complete: S of this tile was signalled by a commit issued
+// after the previous PV.  (Keeping keys 64-127 in registers and loading keys
+// 0-63 twice measured 10 % slower at 8K.)
+template <bool kVisit>
+__device__ __forceinline__ void softmax_tile(const TileArgs& t, float sl2, int32_t q, bool sparse,
+                                             RowState& st, uint32_t* visit_row,
+                                             int32_t words_per_row) {
+  uint32_t r0[32], r1[32], r2[32], r3[32];
+  ptx::tmem_ld32(t.s_addr, r0);
+  ptx::tmem_ld32(t.s_addr + 32, r1);
+  if (t.wide) {
+    ptx::tmem_ld32(t.s_addr + 64, r2);
+    ptx::tmem_ld32(t.s_addr + 96, r3);
+  }
+  ptx::tmem_wait_ld_regs(r0);
+  ptx::tmem_fence_regs(r1);
+  ptx::tmem_fence_regs(r2);
+  ptx::tmem_fence_regs(r3);
+  prepare_chunk<kVisit>(r0, t.masked, q, sparse, t.k0, visit_row, words_per_row);
+  prepare_chunk<kVisit>(r1, t.masked, q, sparse, t.k0 + 32, visit_row, words_per_row);
+  float lm = fmaxf(chunk_max(r0), chunk_max(r1));
+  if (t.wide) {
+    prepare_chunk<kVisit>(r2, t.masked, q, sparse, t.k0 + 64, visit_row, words_per_row);
+    prepare_chunk<kVisit>(r3, t.masked, q, sparse, t.k0 + 96, visit_row, words_per_row);
+    lm = fmaxf(lm, fmaxf(chunk_max(r2), chunk_max(r3)));
+  }
+  const float m_new = next_ref(st.m_ref, lm, sl2);
+  const bool moved = m_new != st.m_ref;
+  if (__any_sync(0xffffffffu, moved)) {
+    float factor = 1.0f;
+    if (moved) factor = st.m_ref == -INFINITY ? 0.0f : mufu_exp2((st.m_ref - m_new) * sl2);
+    st.l_part *= factor;
+    st.m_ref = m_new;
+    if (!t.first) rescale_o(t.o_addr, factor);
+  }
+  const float neg_mb = m_new == -INFINITY ? 0.0f : -m_new * sl2;
+  float sum0 = 0.0f, sum1 = 0.0f;
+  const uint32_t p_addr = t.s_addr + 64;
+  exp_chunk<kPolyMask>(r0, sl2, neg_mb, p_addr, sum0, sum1);
+  exp_chunk<kPolyMask>(r1, sl2, neg_mb, p_addr + 16, sum0, sum1);
+  ptx::tmem_wait_st();
+  ptx::tc_fence_before();
   __syncwarp();
-  if (lane == 0) ptx::mbar_arrive_cluster(sh.bar0(id));
+  if ((threadIdx.x & 31) == 0) ptx::mbar_arrive(t.half_bar);
+  if (t.wide) {
+    exp_chunk<kPolyMask>(r2, sl2, neg_mb, p_addr + 32, sum0, sum1);
+    exp_chunk<kPolyMask>(r3, sl2, neg_mb, p_addr + 48, sum0, sum1);
+  }
+  st.l_part += sum0 + sum1;
+  ptx::tmem_wait_st();
 }
 
-// Softmax warpgroup `wg` (warps 4-7: wg 0, warps 8-11: wg 1; warp % 4 is
-// the tensor-memory lane quadrant, so each warpgroup covers all 128 rows).
-// Tile gt of the pair's tile stream (in S buffer gt % 3) belongs to
-// warpgroup gt % 2.  The two warpgroups share the O accumulator and hand
-// each row's lazy reference max from tile to tile through RowChannel, so
-// P of every tile is relative to the reference O is kept in; each keeps a
-// partial row sum over its own tiles.  The warpgroup that owns an item's
-// last tile finishes the item: the other hands over its (reference, partial
-// sum) and goes on to the next item, and the owner normalises and writes
-// all 128 O columns.
+// Softmax warpgroup x (warps 4-7: x = 0, warps 8-11: x = 1) owns query tile
+// x of every item: all its tiles, then the item's epilogue (normalise and
+// store, or write a split partial and merge).
 template <bool kVisit, bool kVarlen>
-__device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tmem) {
+__device__ void softmax_role(const KernelArgs& a, const Smem& sh, uint32_t tmem,
+                             const CUtensorMap* tout) {
   const tpsa_plan& p = a.plan;
-  const uint32_t r = sh.rank;
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
-  const int wg = (warp - kFirstSoftmaxWarp) / 4;
+  const uint32_t x = static_cast<uint32_t>(warp - kFirstSoftmaxWarp) / 4;
   const int quad = warp % 4;
-  const int row = quad * 32 + lane;  // TMEM lane == row of this CTA's M half
+  const int row = quad * 32 + lane;  // TMEM lane == row of query tile x
   const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
   const int32_t hq = p.kv_heads * kGroupSize;
   const bool visit = kVisit && a.visited != nullptr;
-  // Tiles of the pair's stream before the current item.
-  uint32_t g = 0;
-  // Split items so far.
-  uint32_t split_items = 0;
-  RowChannel ch;
-  static_assert(kCntCon == kCntPub + 8, "read counters follow the publication counters");
-  ch.mine = sh.base_u32 + kOffXchg + (wg * kChanSlots * 128 + row) * 4;
-  ch.theirs = sh.base_u32 + kOffXchg + ((1 - wg) * kChanSlots * 128 + row) * 4;
-  ch.pub_cnt = sh.counter(kCntPub + wg * 4 + quad);
-  ch.peer_pub = sh.counter(kCntPub + (1 - wg) * 4 + quad);
-  ch.n_pub = 0;
-  ch.n_read = 0;
-  volatile int* split_last = reinterpret_cast<volatile int*>(sh.base + kOffSplitLast);
+  const uint32_t s_addr = tmem + lane_base + (x << 7);
+  const uint32_t o_addr = tmem + lane_base + kTmemO + (x << 7);
+  const uint32_t bar_s = sh.bar(kBarSFull + x), bar_p = sh.bar(kBarPFull + x);
+  const uint32_t bar_o = sh.bar(kBarOFull + x), bar_ph = sh.bar(kBarPHalf + x);
+  // This warp's output staging (4 KB), stored by its own TMA stores (lane 0
+  // issues them and waits for them to read the buffer before it is reused).
+  const uint32_t wstage = kOffOut + (warp - kFirstSoftmaxWarp) * kOutStageBytes;
+  uint8_t* stage = sh.base + wstage;
+  auto stage_free = [&]() {
+    if (lane == 0) ptx::bulk_wait_group_read<0>();
+    __syncwarp();
+  };
+  volatile int* split_last = reinterpret_cast<volatile int*>(sh.base + kOffSplitLast) + 2 * x;
+  const uint32_t cnt_w = 2 * x, cnt_d = 2 * x + 1;  // split partial written / merge decided
+  uint32_t s_par = 0, o_par = 0, split_items = 0;
   uint32_t tr_sm = 0;  // trace counter (used only with TPSA_TRACE)
+  (void)tr_sm;
+#ifdef TPSA_TRACE
+  const bool tr = row == 0 && blockIdx.x == TPSA_TRACE_CTA;
+#else
+  const bool tr = false;
+#endif
 #define tr_n_ tr_sm
-  const uint32_t o_all = tmem + lane_base + kTmemO;  // O, 128 columns
 
   for (uint32_t n_item = 0;; ++n_item) {
     ItemRec rec;
     const bool got = take_item(sh, n_item, &rec);
     if (!__all_sync(0xffffffffu, got)) break;
     __syncwarp();
-    if (lane == 0) release_item(sh, n_item);
+    // The previous record is released only now that this warp has finished
+    // that item, so the scheduler claims an item when the one two before it
+    // is done.
+    if (lane == 0 && n_item > 0) release_item(sh, n_item - 1);
     if (rec.idx >= p.total_items) break;
-    const uint32_t qb = n_item & 1;  // this item's Q buffer (items alternate)
     const tpsa_item& it = rec.it;
     const BlockTiles& bt = rec.bt;
-    // The item's request (a batch-one launch has one, at row, item, slot and
-    // counter 0).
     const ReqDesc& rq = a.reqs[kVarlen ? rec.req() : 0];
     const tpsa_plan& pr = kVarlen ? rq.plan : p;
     const int32_t q_row0 = kVarlen ? rq.q_row0 : 0;
-    const int32_t ridx = kVarlen ? rec.idx - rq.item_base : rec.idx;  // item within its request
+    const int32_t ridx = kVarlen ? rec.idx - rq.item_base : rec.idx;
     const int32_t tok = bt.q_begin + row / 2;
     const int32_t q = tok < pr.seq_len ? tok : pr.seq_len - 1;
     const bool sparse = row_is_sparse(pr, tok);
     const int32_t qrow = it.block * kBlockQ + row / 2;  // row within the request's chunk
-    const int32_t head = it.kv_head * kGroupSize + 2 * static_cast<int32_t>(r) + (row & 1);
+    const int32_t head = it.kv_head * kGroupSize + 2 * static_cast<int32_t>(x) + (row & 1);
     const bool real_row = qrow < pr.query_tokens;
     uint32_t* visit_row =
         (visit && real_row)
@@ -1351,173 +1086,152 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
     RowState st{-INFINITY, 0.0f};
     bool ok = true;
     const int32_t ntiles = it.tile_end - it.tile_begin;
-    for (int32_t n = (g + wg) & 1; n < ntiles; n += 2) {
-      const uint32_t gt = g + static_cast<uint32_t>(n);
-      const uint32_t sb = gt % kNumSBufs;
+    for (int32_t n = 0; n < ntiles; ++n) {
       int32_t k0, w;
       tile_keys(bt, it.tile_begin + n, &k0, &w);
-      const bool masked = tile_needs_mask(pr, bt, k0, w);
       TileArgs ta;
-      ta.s_addr = tmem + lane_base + (sb << 7);
-      ta.o_addr = o_all;
+      ta.s_addr = s_addr;
+      ta.o_addr = o_addr;
       ta.k0 = k0;
       ta.wide = w > 64;
+      ta.masked = tile_needs_mask(pr, bt, k0, w);
       ta.first = n == 0;
-      ta.last = n == ntiles - 1;
-      ta.prev_bar = sh.bar(kBarPvDone + (gt - 1) % kNumSBufs);
-      ta.prev_parity = ((gt - 1) / kNumSBufs) & 1;
-      ta.trn = row == 0 ? &tr_sm : nullptr;
-      ta.trole = 2 + wg + 3 * r;
-      const bool w_ok = wait_bar(sh, sh.bar(kBarSFull + sb), (gt / kNumSBufs) & 1);
+      ta.half_bar = bar_ph;
+      const bool w_ok = wait(sh, bar_s, s_par);
+      s_par ^= 1;
       if (!__all_sync(0xffffffffu, w_ok)) { ok = false; break; }
-      if (row == 0) TPSA_TR(2 + wg + 3 * r, 1, n);
+      if (tr) TPSA_TR(2 + x, 1, n);
       ptx::tc_fence_after();
-      // One instantiation for masked and unmasked tiles (a uniform branch
-      // around the masking): a second copy of this code would compete with
-      // the MMA issuer's loop for the instruction cache.
-      ta.masked = masked;
-      const bool t_ok =
-          softmax_tile<kVisit>(sh, p, ta, q, sparse, ch, st, visit_row, a.words_per_row);
-      if (!t_ok) { ok = false; break; }
+      softmax_tile<kVisit>(ta, p.scale_log2, q, sparse, st, visit_row, a.words_per_row);
       ptx::tc_fence_before();
-      if (row == 0) TPSA_TR(2 + wg + 3 * r, 3, n);
-      warp_arrive0(sh, kBarPFull + sb, lane);
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(bar_p);
+      if (tr) TPSA_TR(2 + x, 3, n);
     }
     if (!ok) break;
-    g += static_cast<uint32_t>(ntiles);
 
-    // Item end.  The warpgroup that owned the item's last tile (the owner)
-    // finishes the item alone: its reference is final, and the other
-    // warpgroup, if it owned any tile of the item, hands over its reference
-    // and partial row sum and goes on to the next item at once (whose first
-    // tile is its own), so the next item's first P does not wait for this
-    // epilogue.  O is complete once the item's last PV has.
-    const uint32_t gl = g - 1;
-    const bool owner = (gl & 1) == static_cast<uint32_t>(wg);
-    const bool shared_item = ntiles >= 2;
+    // Item end: O_x is complete once the item's last PV of this tile is.
+    const bool w_ok = wait(sh, bar_o, o_par);
+    o_par ^= 1;
+    if (!__all_sync(0xffffffffu, w_ok)) break;
+    ptx::tc_fence_after();
+    if (tr) TPSA_TR(2 + x, 5, rec.idx);
     const bool split = it.num_splits > 1;
     const uint32_t sp_slot = split_items & 1;
     split_items += split ? 1u : 0u;
-    if (!owner) {
-      if (shared_item && !(ch.publish(sh, st.m_ref) && ch.publish(sh, st.l_part))) break;
-      continue;
-    }
-    float l_total = st.l_part;
-    if (shared_item) {
-      float m_peer, l_peer;
-      if (!ch.read(sh, &m_peer) || !ch.read(sh, &l_peer)) break;
-      // The peer's reference is at most the final one (references only grow).
-      if (m_peer != -INFINITY) l_total += l_peer * mufu_exp2((m_peer - st.m_ref) * p.scale_log2);
-    }
-    if (!__all_sync(0xffffffffu, wait_bar(sh, sh.bar(kBarPvDone + gl % kNumSBufs),
-                                          (gl / kNumSBufs) & 1))) {
-      break;
-    }
-    ptx::tc_fence_after();
-    if (row == 0) TPSA_TR(2 + wg + 3 * r, 9, 0);
-    float* slot =
-        a.scratch + static_cast<size_t>((kVarlen ? rq.slot_base : 0) + ridx) * kSlotFloats;
-    constexpr int32_t kSlotRows = 2 * kRowsPerTile;
-    const int32_t srow = static_cast<int32_t>(r) * kRowsPerTile + row;
     // Output rows of this warp: packed token base_q + R / 2, head
     // base_h + R % 2 for warp row R; rows at or past row_end are not written.
     const int32_t base_q = q_row0 + it.block * kBlockQ + quad * 16;
-    const int32_t base_h = it.kv_head * kGroupSize + 2 * static_cast<int32_t>(r);
+    const int32_t base_h = it.kv_head * kGroupSize + 2 * static_cast<int32_t>(x);
     const int32_t row_end = q_row0 + pr.query_tokens;
-    uint8_t* stage = sh.base + kOffStage + (warp - kFirstSoftmaxWarp) * kStageBytesPerWarp;
-    if (kVarlen && !split && bt.q_end - bt.q_begin < kBlockQ) {
-      // A block that ends inside its 64-token box (a request's last block):
-      // a TMA store of the box would also write rows of the next packed
-      // request, so these rows are stored one by one.  (In a batch-one
-      // launch the tensor map's end clips the last box.)
-      const float inv = 1.0f / l_total;
+    if (!split && (!kVarlen || bt.q_end - bt.q_begin == kBlockQ)) {
+      // Two rounds of 64 columns: the warp's 32 rows into its staging
+      // buffer as bf16 (128-byte swizzled rows, the layout the tensor map
+      // stores), then one TMA store of the 16-token x 2-head x 64-column box.
+      // (A batch-one launch's tensor map ends at the last query row, which
+      // clips the last block.)
+      const float inv = 1.0f / st.l_part;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t x[32];
-        ptx::tmem_ld32(o_all + 32 * c, x);
-        ptx::tmem_wait_ld_regs(x);
-        float o[32];
+      for (int h = 0; h < 2; ++h) {
+        uint32_t v0[32], v1[32];
+        ptx::tmem_ld32(o_addr + 64 * h, v0);
+        ptx::tmem_ld32(o_addr + 64 * h + 32, v1);
+        stage_free();
+        ptx::tmem_wait_ld_regs(v0);
+        ptx::tmem_fence_regs(v1);
+        uint8_t* srow = stage + lane * 128;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) o[j] = __uint_as_float(x[j]);
-        store_rows_bf16(o, inv, stage, lane, a.out, base_q, base_h, hq, row_end, 32 * c);
-      }
-      ptx::tc_fence_before();
-      warp_arrive0(sh, kBarOEmpty, lane);
-      if (row == 0) TPSA_TR(2 + wg + 3 * r, 5, 0);
-      continue;
-    }
-    if (!split) {
-      // The 128 output columns, as bf16, into the item's Q buffer, which is
-      // dead (its QKs completed before the last PV) and has the output tile's
-      // shape (per d-half, [64 tokens x 2 heads] rows of 64 d, 128-byte
-      // swizzled as the Q tensor map loads it).
-      const float inv = 1.0f / l_total;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint8_t* dst = sh.base + kOffQ + qb * kQBytes + (c >> 1) * kQHalfBytes + row * 128;
-        uint32_t x[32];
-        ptx::tmem_ld32(o_all + 32 * c, x);
-        ptx::tmem_wait_ld_regs(x);
-#pragma unroll
-        for (int jj = 0; jj < 4; ++jj) {
-          const int j = 4 * (c & 1) + jj;  // 16-byte chunk within the d-half row
-          const uint32_t* v = &x[8 * jj];
-          *reinterpret_cast<uint4*>(dst + ((j ^ (row & 7)) << 4)) = make_uint4(
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t* v = j < 4 ? &v0[8 * j] : &v1[8 * (j - 4)];
+          *reinterpret_cast<uint4*>(srow + ((j ^ (lane & 7)) << 4)) = make_uint4(
               pack_bf16x2(__uint_as_float(v[0]) * inv, __uint_as_float(v[1]) * inv),
               pack_bf16x2(__uint_as_float(v[2]) * inv, __uint_as_float(v[3]) * inv),
               pack_bf16x2(__uint_as_float(v[4]) * inv, __uint_as_float(v[5]) * inv),
               pack_bf16x2(__uint_as_float(v[6]) * inv, __uint_as_float(v[7]) * inv));
         }
+        ptx::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          ptx::tma_store_3d(tout, 64 * h, base_h, base_q, sh.base_u32 + wstage);
+          ptx::bulk_commit_group();
+        }
       }
-      // The K producer stores the staged box (TMA) before it reuses this Q
-      // buffer; it counts four warps per d-half.  Each warp releases O only
-      // after its staged counts: the next item's counts need its PVs, which
-      // need O, so every count of this item lands before any of the next.
-      ptx::fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) {
-        ptx::red_release_add_shared(sh.counter(kCntStaged + 0), 1);
-        ptx::red_release_add_shared(sh.counter(kCntStaged + 1), 1);
+      if (tr) TPSA_TR(2 + x, 6, 0);
+      continue;
+    }
+    if (!split) {
+      // A block that ends inside its 64-token box (a request's last block in
+      // a packed batch): a box store would also write rows of the next
+      // request, so each thread writes its own row: 256 contiguous bytes of
+      // `out`, in two halves of 64 columns.
+      const float inv = 1.0f / st.l_part;
+      uint4* dst = reinterpret_cast<uint4*>(
+          a.out + (static_cast<size_t>(q_row0 + qrow) * hq + head) * kHeadDim);
+#pragma unroll 1
+      for (int h = 0; h < 2; ++h) {
+        uint32_t v0[32], v1[32];
+        ptx::tmem_ld32(o_addr + 64 * h, v0);
+        ptx::tmem_ld32(o_addr + 64 * h + 32, v1);
+        ptx::tmem_wait_ld_regs(v0);
+        ptx::tmem_fence_regs(v1);
+        if (real_row) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            dst[8 * h + j] = make_uint4(
+                pack_bf16x2(__uint_as_float(v0[8 * j]) * inv, __uint_as_float(v0[8 * j + 1]) * inv),
+                pack_bf16x2(__uint_as_float(v0[8 * j + 2]) * inv, __uint_as_float(v0[8 * j + 3]) * inv),
+                pack_bf16x2(__uint_as_float(v0[8 * j + 4]) * inv, __uint_as_float(v0[8 * j + 5]) * inv),
+                pack_bf16x2(__uint_as_float(v0[8 * j + 6]) * inv, __uint_as_float(v0[8 * j + 7]) * inv));
+          }
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            dst[8 * h + 4 + j] = make_uint4(
+                pack_bf16x2(__uint_as_float(v1[8 * j]) * inv, __uint_as_float(v1[8 * j + 1]) * inv),
+                pack_bf16x2(__uint_as_float(v1[8 * j + 2]) * inv, __uint_as_float(v1[8 * j + 3]) * inv),
+                pack_bf16x2(__uint_as_float(v1[8 * j + 4]) * inv, __uint_as_float(v1[8 * j + 5]) * inv),
+                pack_bf16x2(__uint_as_float(v1[8 * j + 6]) * inv, __uint_as_float(v1[8 * j + 7]) * inv));
+          }
+        }
       }
-      ptx::tc_fence_before();
-      warp_arrive0(sh, kBarOEmpty, lane);
-      if (row == 0) TPSA_TR(2 + wg + 3 * r, 5, 0);
+      if (tr) TPSA_TR(2 + x, 6, 0);
       continue;
     }
 
-    // Split item: the fp32 partial (128 columns) into the item's
-    // column-major slot ([128 columns][256 rows], then m[256] and l[256]);
-    // the last split of the block (per CTA of the pair) merges all partials
-    // and writes bf16.  Each split item counts four warps (its owner's).
+    // Split item: the fp32 partial (128 columns) into the item's column-major
+    // slot ([128 columns][256 rows], then m[256] and l[256]; this tile's rows
+    // are 128 x + row); the last split of the block (per query tile) merges
+    // all partials and writes bf16.
+    float* slot =
+        a.scratch + static_cast<size_t>((kVarlen ? rq.slot_base : 0) + ridx) * kSlotFloats;
+    constexpr int32_t kSlotRows = 2 * kRowsPerTile;
+    const int32_t srow = static_cast<int32_t>(x) * kRowsPerTile + row;
 #pragma unroll 1
     for (int c = 0; c < 4; ++c) {
-      uint32_t x[32];
-      ptx::tmem_ld32(o_all + 32 * c, x);
-      ptx::tmem_wait_ld_regs(x);
+      uint32_t v[32];
+      ptx::tmem_ld32(o_addr + 32 * c, v);
+      ptx::tmem_wait_ld_regs(v);
       float* col = slot + static_cast<size_t>(32 * c) * kSlotRows + srow;
 #pragma unroll
-      for (int j = 0; j < 32; ++j) col[j * kSlotRows] = __uint_as_float(x[j]);
+      for (int j = 0; j < 32; ++j) col[j * kSlotRows] = __uint_as_float(v[j]);
     }
     slot[kHeadDim * kSlotRows + srow] = st.m_ref;
-    slot[(kHeadDim + 1) * kSlotRows + srow] = l_total;
+    slot[(kHeadDim + 1) * kSlotRows + srow] = st.l_part;
     __threadfence();
     __syncwarp();
-    if (lane == 0) ptx::red_release_add_shared(sh.counter(kCntSplitW), 1);
+    if (lane == 0) ptx::red_release_add_shared(sh.counter(cnt_w), 1);
     if (row == 0) {
-      if (wait_count(sh, kCntSplitW, 4 * split_items)) {
+      if (wait_count(sh, cnt_w, 4 * split_items)) {
         int32_t* ctr = a.ctl + kCtlSplitBase + (kVarlen ? rq.ctr_base : 0) +
-                       ((it.block - pr.tail_block0) * p.kv_heads + it.kv_head) * 2 + r;
+                       ((it.block - pr.tail_block0) * p.kv_heads + it.kv_head) * 2 +
+                       static_cast<int32_t>(x);
         const int prev = atomicAdd(ctr, 1);
         split_last[sp_slot] = prev == it.num_splits - 1;
-        ptx::red_release_add_shared(sh.counter(kCntSplitD), 1);
+        ptx::red_release_add_shared(sh.counter(cnt_d), 1);
       }
     }
-    const bool decided = __all_sync(0xffffffffu, wait_count(sh, kCntSplitD, split_items));
-    const bool last_split = decided && split_last[sp_slot];
-    ptx::tc_fence_before();
-    warp_arrive0(sh, kBarOEmpty, lane);
+    const bool decided = __all_sync(0xffffffffu, wait_count(sh, cnt_d, split_items));
     if (!decided) break;
-    if (!last_split) continue;
+    if (!split_last[sp_slot]) continue;
     __threadfence();
     const float* first_slot = slot - static_cast<size_t>(it.split) * kSlotFloats;
     const size_t m_off = static_cast<size_t>(kHeadDim) * kSlotRows + srow;
@@ -1533,6 +1247,7 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
       if (ms != -INFINITY) lsum += mufu_exp2((ms - mmax) * p.scale_log2) * __ldcg(sl + l_off);
     }
     const float inv_sum = 1.0f / lsum;
+    stage_free();
 #pragma unroll 1
     for (int c = 0; c < 4; ++c) {
       const int col = 32 * c;
@@ -1551,101 +1266,100 @@ __device__ void softmax_role(const KernelArgs& a, const Shared& sh, uint32_t tme
       store_rows_bf16(acc, inv_sum, stage, lane, a.out, base_q, base_h, hq, row_end, col);
     }
   }
+  // Output stores of this warp complete before the CTA exits.
+  if (lane == 0) ptx::bulk_wait_group<0>();
 }
 #undef tr_n_
 
+
 template <bool kVisit, bool kVarlen>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kNumThreads, 1)
+__global__ void __launch_bounds__(kNumThreads, 1)
     tpsa_paged_kernel(const __grid_constant__ KernelArgs args,
-                      const __grid_constant__ CUtensorMap tmap_q,
-                      const __grid_constant__ CUtensorMap tmap_k64,
-                      const __grid_constant__ CUtensorMap tmap_k32,
-                      const __grid_constant__ CUtensorMap tmap_v,
-                      const __grid_constant__ CUtensorMap tmap_out) {
+                     const __grid_constant__ CUtensorMap tmap_q,
+                     const __grid_constant__ CUtensorMap tmap_k128,
+                     const __grid_constant__ CUtensorMap tmap_k64,
+                     const __grid_constant__ CUtensorMap tmap_v,
+                     const __grid_constant__ CUtensorMap tmap_out) {
   extern __shared__ uint8_t smem_raw[];
-  Shared sh;
+  Smem sh;
   {
     const uint32_t raw = ptx::smem_u32(smem_raw);
     const uint32_t aligned = (raw + 1023u) & ~1023u;
     sh.base = smem_raw + (aligned - raw);
     sh.base_u32 = aligned;
-    sh.rank = ptx::cluster_ctarank();
   }
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; ++i) {
-      ptx::mbar_init(sh.bar(kBarQFull + i), 2);
-      ptx::mbar_init(sh.bar(kBarQEmpty + i), kQEmptyArrivals);
-      ptx::mbar_init(sh.bar(kBarItemFull + i), 1);
-      ptx::mbar_init(sh.bar(kBarItemEmpty + i), kItemConsumers);
+#ifdef TPSA_TRACE
+    if (blockIdx.x < 1024) g_cta_span[blockIdx.x][0] = ptx::globaltimer_ns();
+#endif
+    for (uint32_t x = 0; x < 2; ++x) {
+      ptx::mbar_init(sh.bar(kBarQFull + x), 1);
+      ptx::mbar_init(sh.bar(kBarQEmpty + x), 1);
+      ptx::mbar_init(sh.bar(kBarSFull + x), 1);
+      ptx::mbar_init(sh.bar(kBarPFull + x), 4);
+      ptx::mbar_init(sh.bar(kBarPHalf + x), 4);
+      ptx::mbar_init(sh.bar(kBarOFull + x), 1);
+      ptx::mbar_init(sh.bar(kBarItemFull + x), 1);
+      ptx::mbar_init(sh.bar(kBarItemEmpty + x), kItemConsumers);
     }
-    for (int s = 0; s < kRing; ++s) {
-      ptx::mbar_init(sh.bar(kBarKFull + s), 2);
+    for (int s = 0; s < kKRing; ++s) {
+      ptx::mbar_init(sh.bar(kBarKFull + s), 1);
       ptx::mbar_init(sh.bar(kBarKEmpty + s), 1);
-      ptx::mbar_init(sh.bar(kBarVFull + s), 2);
+    }
+    for (int s = 0; s < kVRing; ++s) {
+      ptx::mbar_init(sh.bar(kBarVFull + s), 1);
       ptx::mbar_init(sh.bar(kBarVEmpty + s), 1);
     }
-    for (uint32_t i = 0; i < kNumSBufs; ++i) {
-      ptx::mbar_init(sh.bar(kBarSFull + i), 1);
-      ptx::mbar_init(sh.bar(kBarPFull + i), kPairWgArrivals);
-      ptx::mbar_init(sh.bar(kBarPvDone + i), 1);
-    }
-    ptx::mbar_init(sh.bar(kBarOEmpty), kPairWgArrivals);
     ptx::mbar_init(sh.bar(kBarTail), 1);
     ptx::mbar_init(sh.bar(kBarDrain), 1);
     *sh.abort_flag() = 0;
-    for (uint32_t i = 0; i < kNumCounters; ++i) {
+    for (uint32_t i = 0; i < 4; ++i) {
       *reinterpret_cast<volatile uint32_t*>(sh.base + kOffCounters + 4 * i) = 0;
     }
     ptx::fence_mbar_init();
   }
   if (warp == 1) {
-    ptx::tmem_alloc_pair(sh.base_u32 + kOffTmemSlot, kTmemCols);
-    ptx::tmem_relinquish_pair();
+    ptx::tmem_alloc(sh.base_u32 + kOffTmemSlot, kTmemCols);
+    ptx::tmem_relinquish();
   }
   ptx::tc_fence_before();
-  ptx::cluster_sync();  // barriers of both CTAs initialised before any remote use
+  __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sh.base + kOffTmemSlot);
 
   if (warp < kFirstSoftmaxWarp) {
     ptx::setmaxnreg_dec<kControlRegs>();
     if (warp == 0) {
-      if (lane == 0) {
-        producer_role<kVarlen>(args, sh, &tmap_q, &tmap_k64, &tmap_k32, &tmap_v, &tmap_out,
-                               false);
-      }
+      if (lane == 0) producer_role<kVarlen>(args, sh, &tmap_q, &tmap_k128, &tmap_k64, &tmap_v, false);
       __syncwarp();
     } else if (warp == 1) {
-      if (sh.rank == 0) mma_role(args, sh, tmem, lane);
-    } else if (warp == 2 && sh.rank == 0) {
-      // The scheduler has a warp of its own: it spins on the item ring, and
-      // a lane of a busy warp would compete with that warp's work.
+      mma_role(args, sh, tmem);
+    } else if (warp == 2) {
       if (lane == 0) scheduler_role<kVarlen>(args, sh);
       __syncwarp();
-    } else if (warp == 3) {
-      if (lane == 0) {
-        producer_role<kVarlen>(args, sh, &tmap_q, &tmap_k64, &tmap_k32, &tmap_v, &tmap_out,
-                               true);
-      }
+    } else {
+      if (lane == 0) producer_role<kVarlen>(args, sh, &tmap_q, &tmap_k128, &tmap_k64, &tmap_v, true);
       __syncwarp();
     }
   } else {
     ptx::setmaxnreg_inc<kSoftmaxRegs>();
-    softmax_role<kVisit, kVarlen>(args, sh, tmem);
+    softmax_role<kVisit, kVarlen>(args, sh, tmem, &tmap_out);
   }
 
   ptx::tc_fence_before();
-  ptx::cluster_sync();  // no remote traffic after this point; MMAs drained
+  __syncthreads();  // MMAs drained, every role done
+#ifdef TPSA_TRACE
+  if (threadIdx.x == 0 && blockIdx.x < 1024) g_cta_span[blockIdx.x][1] = ptx::globaltimer_ns();
+#endif
   if (warp == 1) {
     ptx::tc_fence_after();
-    ptx::tmem_dealloc_pair(tmem, kTmemCols);
+    ptx::tmem_dealloc(tmem, kTmemCols);
   }
 }
 
-#include "tpsa_solo_kernel.cuh"
 
 // ================================================================ host side
 thread_local std::string t_last_error;
@@ -1656,7 +1370,7 @@ tpsa_status fail(tpsa_status s, const std::string& msg) {
 }
 
 // Dense-tail blocks longer than this fraction of the average work per CTA
-// pair are split into several items (merged in-kernel).
+// are split into several items (merged in-kernel).
 #ifndef TPSA_SPLIT_FACTOR
 #define TPSA_SPLIT_FACTOR 0.7
 #endif
@@ -1664,30 +1378,29 @@ constexpr double kSplitFactor = TPSA_SPLIT_FACTOR;
 
 // Split threshold (tiles per item) for the dense-tail blocks of a plan.  The
 // B = tail blocks x kv heads longest items, each cut into ns pieces of
-// ceil(T / ns) tiles, go first to the CTA pairs (longest first), so the
-// busiest pair carries ceil(B ns / P) pieces; the short items fill the other
-// pairs.  The estimated makespan, in tiles, is
+// ceil(T / ns) tiles, go first to the P CTAs (longest first), so the
+// busiest CTA carries ceil(B ns / P) pieces; the short items fill the other
+// CTAs.  The estimated makespan, in tiles, is
 //   max(ceil(B ns / P) (ceil(T / ns) + c), (total + B ns c) / P)
 // with c the per-piece cost of a partial write and its share of the merge
 // (kSplitPieceTiles); the smallest ns with the least estimate wins.  ns is
-// at most what a threshold of kSplitFactor times the average work per pair
+// at most what a threshold of kSplitFactor times the average work per CTA
 // gives, so no plan needs more split slots than that rule (the static-scratch
-// entry point's limit rests on it).  (That rule alone cut the 128K-context
-// tail into 5 pieces: 80 pieces for 74 pairs, six pairs with two.)
+// entry point's limit rests on it).
 constexpr double kSplitPieceTiles = 2.0;
 // `longest`: tiles of the longest dense-tail block; `tail`: dense-tail
 // (block, head) items before splitting; `tiles`: all tiles of the launch.
-int32_t choose_split_counts(int32_t longest, int64_t tail, int64_t tiles, int32_t pairs) {
+int32_t choose_split_counts(int32_t longest, int64_t tail, int64_t tiles, int32_t ctas) {
   if (tail == 0 || longest == 0) return 1 << 30;
   const int32_t by_fraction = max_i(kMinSplitTiles, static_cast<int32_t>(
-      kSplitFactor * static_cast<double>(tiles) / pairs));
+      kSplitFactor * static_cast<double>(tiles) / ctas));
   const int32_t ns_max = min_i(64, ceil_div(longest, by_fraction));
   double best = 0.0;
   int32_t best_ns = 1;
   for (int32_t ns = 1; ns <= ns_max; ++ns) {
     const double piece = static_cast<double>(ceil_div(longest, ns)) + kSplitPieceTiles;
-    const double rounds = static_cast<double>((tail * ns + pairs - 1) / pairs);
-    const double avg = (static_cast<double>(tiles) + kSplitPieceTiles * tail * ns) / pairs;
+    const double rounds = static_cast<double>((tail * ns + ctas - 1) / ctas);
+    const double avg = (static_cast<double>(tiles) + kSplitPieceTiles * tail * ns) / ctas;
     const double est = std::max(rounds * piece, avg);
     if (ns == 1 || est < best - 1e-9) {
       best = est;
@@ -1697,29 +1410,15 @@ int32_t choose_split_counts(int32_t longest, int64_t tail, int64_t tiles, int32_
   return best_ns == 1 ? (1 << 30) : ceil_div(longest, best_ns);
 }
 
-int32_t choose_split(const tpsa_plan& p, int32_t b0, int64_t tiles, int32_t pairs) {
+int32_t choose_split(const tpsa_plan& p, int32_t b0, int64_t tiles, int32_t ctas) {
   int32_t longest = 0;
   for (int32_t b = b0; b < p.num_blocks; ++b) longest = max_i(longest, block_tiles(p, b).count);
   return choose_split_counts(longest, static_cast<int64_t>(p.num_blocks - b0) * p.kv_heads, tiles,
-                             pairs);
+                             ctas);
 }
 
 tpsa_status cuda_fail(cudaError_t e, const char* what) {
   return fail(TPSA_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
-}
-
-// Kernel form: one CTA per item (tpsa_solo_kernel, the default) or CTA pairs
-// (tpsa_paged_kernel, selected by TPSA_KERNEL=pair in the environment; kept
-// as the measured comparison).  Read once per process.
-enum class Form { kPair, kSolo };
-
-Form kernel_form() {
-  static const Form form = [] {
-    const char* e = std::getenv("TPSA_KERNEL");
-    if (e != nullptr && std::strcmp(e, "pair") == 0) return Form::kPair;
-    return Form::kSolo;
-  }();
-  return form;
 }
 
 struct DeviceState {
@@ -1727,14 +1426,8 @@ struct DeviceState {
   int sm_count = 0;
   int major = 0;
   bool attr_set = false;
-  int max_pairs = 0;  // co-resident CTA pairs (clusters of 2)
-  int max_solo = 0;   // co-resident solo CTAs
-  // Parallel workers of the current kernel form (CTA pairs or solo CTAs)
-  // and CTAs per worker.
-  int workers() const { return kernel_form() == Form::kSolo ? max_solo : max_pairs; }
+  int max_ctas = 0;  // co-resident CTAs of the kernel (one per SM)
 };
-
-int ctas_per_worker() { return kernel_form() == Form::kSolo ? 1 : 2; }
 
 std::mutex g_mutex;
 DeviceState g_devices[64];
@@ -1767,30 +1460,12 @@ tpsa_status device_state(DeviceState** out) {
     e = cudaFuncSetAttribute(tpsa_paged_kernel<false, true>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(2 * (st.sm_count / 2), 1, 1);
-    cfg.blockDim = dim3(kNumThreads, 1, 1);
-    cfg.dynamicSmemBytes = kSmemBytes;
-    int clusters = 0;
-    e = cudaOccupancyMaxActiveClusters(&clusters, tpsa_paged_kernel<false, false>, &cfg);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveClusters");
-    if (clusters <= 0) return fail(TPSA_ERR_CUDA, "no CTA pair fits on this device");
-    st.max_pairs = clusters;
-    e = cudaFuncSetAttribute(tpsa_solo_kernel<false, false>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, solo::kSmemBytes);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
-    e = cudaFuncSetAttribute(tpsa_solo_kernel<true, false>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, solo::kSmemBytes);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
-    e = cudaFuncSetAttribute(tpsa_solo_kernel<false, true>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, solo::kSmemBytes);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
     int per_sm = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tpsa_solo_kernel<false, false>,
-                                                      solo::kNumThreads, solo::kSmemBytes);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tpsa_paged_kernel<false, false>,
+                                                      kNumThreads, kSmemBytes);
     if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
-    if (per_sm <= 0) return fail(TPSA_ERR_CUDA, "the solo kernel does not fit on an SM");
-    st.max_solo = per_sm * st.sm_count;
+    if (per_sm <= 0) return fail(TPSA_ERR_CUDA, "the kernel does not fit on an SM");
+    st.max_ctas = per_sm * st.sm_count;
     st.attr_set = true;
   }
   *out = &st;
@@ -1844,13 +1519,11 @@ tpsa_status encode_map(CUtensorMap* map, const void* base, uint64_t d1, uint64_t
   return TPSA_OK;
 }
 
-// `pairs`: parallel workers the launch runs (CTA pairs, or single CTAs for the
-// solo kernel, ctas_per_worker() CTAs each); each worker runs one item at a
-// time.
+// `ctas`: co-resident CTAs the launch runs; each runs one item at a time.
 // `split_override` > 0 replaces the split threshold derived from this
 // request's own work (a varlen launch derives it from the whole launch).
 tpsa_status build_plan(int64_t query_tokens, int64_t query_start, int64_t seq_len,
-                       int64_t prompt_len, int32_t kv_heads, int32_t pairs,
+                       int64_t prompt_len, int32_t kv_heads, int32_t ctas,
                        float scale, tpsa_plan* p, int32_t split_override = 0) {
   if (p == nullptr) return fail(TPSA_ERR_INVALID_ARGUMENT, "plan pointer is NULL");
   if (!(kv_heads == 1 || kv_heads == 2 || kv_heads == 4 || kv_heads == 8)) {
@@ -1871,7 +1544,7 @@ tpsa_status build_plan(int64_t query_tokens, int64_t query_start, int64_t seq_le
   if (prompt_len > static_cast<int64_t>(UINT32_MAX)) {
     return fail(TPSA_ERR_INVALID_ARGUMENT, "prompt lengths above UINT32_MAX are unsupported");
   }
-  if (pairs <= 0) return fail(TPSA_ERR_INVALID_ARGUMENT, "sm_count must be positive");
+  if (ctas <= 0) return fail(TPSA_ERR_INVALID_ARGUMENT, "sm_count must be positive");
   std::memset(p, 0, sizeof(*p));
   p->query_tokens = static_cast<int32_t>(query_tokens);
   p->query_start = static_cast<int32_t>(query_start);
@@ -1889,7 +1562,7 @@ tpsa_status build_plan(int64_t query_tokens, int64_t query_start, int64_t seq_le
   int64_t tiles = 0;
   for (int32_t b = 0; b < p->num_blocks; ++b) tiles += block_tiles(*p, b).count;
   tiles *= kv_heads;
-  int32_t split = split_override > 0 ? split_override : choose_split(*p, b0, tiles, pairs);
+  int32_t split = split_override > 0 ? split_override : choose_split(*p, b0, tiles, ctas);
   if (split < kMinSplitTiles) split = kMinSplitTiles;
   // The in-kernel merge keeps per-split weights for at most 64 splits.
   for (int32_t b = b0; b < p->num_blocks; ++b) {
@@ -1907,7 +1580,7 @@ tpsa_status build_plan(int64_t query_tokens, int64_t query_start, int64_t seq_le
   }
   p->tail_items = static_cast<int32_t>(tail_items);
   p->total_items = static_cast<int32_t>(tail_items + static_cast<int64_t>(b0) * kv_heads);
-  p->grid = ctas_per_worker() * (p->total_items < pairs ? p->total_items : pairs);
+  p->grid = p->total_items < ctas ? p->total_items : ctas;
   p->total_tiles = tiles;
   p->workspace_bytes = kControlBytes + (any_split ? tail_items * kSlotBytes : 0);
   return TPSA_OK;
@@ -1937,7 +1610,7 @@ tpsa_status launch(const void* query, const void* key_cache, const void* value_c
   if (st != TPSA_OK) return st;
   KernelArgs args;
   std::memset(&args, 0, sizeof(args));
-  st = build_plan(query_tokens, query_start, seq_len, prompt_len, kv_heads, dev->workers(),
+  st = build_plan(query_tokens, query_start, seq_len, prompt_len, kv_heads, dev->max_ctas,
                   scale, &args.plan);
   if (st != TPSA_OK) return st;
   const tpsa_plan& p = args.plan;
@@ -1952,19 +1625,20 @@ tpsa_status launch(const void* query, const void* key_cache, const void* value_c
       return fail(TPSA_ERR_INVALID_ARGUMENT, "tensors must be 16-byte aligned");
     }
   }
-  CUtensorMap tq, tk64, tk32, tv;
+  CUtensorMap tq, tk128, tk64, tv, tout;
   const uint64_t hq = static_cast<uint64_t>(kv_heads) * kGroupSize;
   const uint64_t cache_tokens = static_cast<uint64_t>(num_pages) * kPageSize;
   st = encode_map(&tq, query, hq, static_cast<uint64_t>(query_tokens), 2, kBlockQ);
   if (st != TPSA_OK) return st;
-  st = encode_map(&tk64, key_cache, kv_heads, cache_tokens, 1, 64);
+  st = encode_map(&tk128, key_cache, kv_heads, cache_tokens, 1, 128);
   if (st != TPSA_OK) return st;
-  st = encode_map(&tk32, key_cache, kv_heads, cache_tokens, 1, 32);
+  st = encode_map(&tk64, key_cache, kv_heads, cache_tokens, 1, 64);
   if (st != TPSA_OK) return st;
   st = encode_map(&tv, value_cache, kv_heads, cache_tokens, 1, 64);
   if (st != TPSA_OK) return st;
-  CUtensorMap tout;  // output tile stores: the Q tile's shape over `out`
-  st = encode_map(&tout, out, hq, static_cast<uint64_t>(query_tokens), 2, kBlockQ);
+  // Output boxes of one softmax warp: 16 tokens x 2 heads x 64 columns.  The
+  // map's extent ends at the last query row, which clips the last block.
+  st = encode_map(&tout, out, hq, static_cast<uint64_t>(query_tokens), 2, 16);
   if (st != TPSA_OK) return st;
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -1982,25 +1656,11 @@ tpsa_status launch(const void* query, const void* key_cache, const void* value_c
   args.tiles = reinterpret_cast<unsigned long long*>(tile_counter);
   args.words_per_row = (p.seq_len + 31) / 32;
 
-  const bool visit = visited != nullptr || tile_counter != nullptr;
-  if (kernel_form() == Form::kSolo) {
-    CUtensorMap tk128, tout16;  // whole 128-key K tiles; one softmax warp's output box
-    st = encode_map(&tk128, key_cache, kv_heads, cache_tokens, 1, 128);
-    if (st != TPSA_OK) return st;
-    st = encode_map(&tout16, out, hq, static_cast<uint64_t>(query_tokens), 2, 16);
-    if (st != TPSA_OK) return st;
-    if (visit) {
-      tpsa_solo_kernel<true, false><<<p.grid, solo::kNumThreads, solo::kSmemBytes, s>>>(
-          args, tq, tk128, tk64, tv, tout16);
-    } else {
-      tpsa_solo_kernel<false, false><<<p.grid, solo::kNumThreads, solo::kSmemBytes, s>>>(
-          args, tq, tk128, tk64, tv, tout16);
-    }
-  } else if (visit) {
-    tpsa_paged_kernel<true, false><<<p.grid, kNumThreads, kSmemBytes, s>>>(args, tq, tk64, tk32,
+  if (visited != nullptr || tile_counter != nullptr) {
+    tpsa_paged_kernel<true, false><<<p.grid, kNumThreads, kSmemBytes, s>>>(args, tq, tk128, tk64,
                                                                             tv, tout);
   } else {
-    tpsa_paged_kernel<false, false><<<p.grid, kNumThreads, kSmemBytes, s>>>(args, tq, tk64, tk32,
+    tpsa_paged_kernel<false, false><<<p.grid, kNumThreads, kSmemBytes, s>>>(args, tq, tk128, tk64,
                                                                              tv, tout);
   }
   e = cudaGetLastError();
@@ -2021,7 +1681,7 @@ struct BatchLaunch {
 
 tpsa_status build_batch(int32_t first, int32_t count, const int64_t* cu_seqlens_q,
                         const int64_t* seq_lens, const int64_t* prompt_lens, int32_t kv_heads,
-                        int32_t pairs, float scale, int64_t table_cols, BatchLaunch* b) {
+                        int32_t ctas, float scale, int64_t table_cols, BatchLaunch* b) {
   std::memset(&b->args, 0, sizeof(b->args));
   KernelArgs& a = b->args;
   int64_t tiles = 0, tail_items = 0;
@@ -2031,7 +1691,7 @@ tpsa_status build_batch(int32_t first, int32_t count, const int64_t* cu_seqlens_
     const int64_t tq = cu_seqlens_q[r + 1] - cu_seqlens_q[r];
     tpsa_plan probe;
     tpsa_status st = build_plan(tq, seq_lens[r] - tq, seq_lens[r], prompt_lens[r], kv_heads,
-                                pairs, scale, &probe, 1 << 30);
+                                ctas, scale, &probe, 1 << 30);
     if (st != TPSA_OK) return st;
     tiles += probe.total_tiles;
     tail_items += static_cast<int64_t>(probe.num_blocks - probe.tail_block0) * kv_heads;
@@ -2041,7 +1701,7 @@ tpsa_status build_batch(int32_t first, int32_t count, const int64_t* cu_seqlens_
   }
   // One split threshold for the launch, from the makespan estimate over all
   // requests' dense-tail items (which are dispatched first).
-  int32_t split = choose_split_counts(longest, tail_items, tiles, pairs);
+  int32_t split = choose_split_counts(longest, tail_items, tiles, ctas);
   if (split < kMinSplitTiles) split = kMinSplitTiles;
   int32_t items = 0, slots = 0, counters = 0, tail = 0, rest = 0;
   for (int32_t i = 0; i < count; ++i) {
@@ -2049,7 +1709,7 @@ tpsa_status build_batch(int32_t first, int32_t count, const int64_t* cu_seqlens_
     const int64_t tq = cu_seqlens_q[r + 1] - cu_seqlens_q[r];
     ReqDesc& d = a.reqs[i];
     tpsa_status st = build_plan(tq, seq_lens[r] - tq, seq_lens[r], prompt_lens[r], kv_heads,
-                                pairs, scale, &d.plan, split);
+                                ctas, scale, &d.plan, split);
     if (st != TPSA_OK) return st;
     d.item_base = items;
     d.tail_base = tail;
@@ -2072,7 +1732,7 @@ tpsa_status build_batch(int32_t first, int32_t count, const int64_t* cu_seqlens_
   a.plan.query_tokens = static_cast<int32_t>(cu_seqlens_q[first + count] - cu_seqlens_q[first]);
   a.plan.total_items = items;
   a.plan.total_tiles = tiles;
-  a.plan.grid = ctas_per_worker() * (items < pairs ? items : pairs);
+  a.plan.grid = items < ctas ? items : ctas;
   const int64_t ctl = (int64_t{kCtlSplitBase} + counters) * 4;
   b->ctl_bytes = std::max<int64_t>(kControlBytes, (ctl + 255) / 256 * 256);
   b->workspace_bytes = b->ctl_bytes + static_cast<int64_t>(slots) * kSlotBytes;
@@ -2103,7 +1763,7 @@ tpsa_status check_batch(int32_t batch, const int64_t* cu_seqlens_q, const int64_
 }
 
 tpsa_status varlen_workspace(int32_t batch, const int64_t* cu_seqlens_q, const int64_t* seq_lens,
-                             const int64_t* prompt_lens, int32_t kv_heads, int32_t pairs,
+                             const int64_t* prompt_lens, int32_t kv_heads, int32_t ctas,
                              uint64_t* bytes) {
   tpsa_status st = check_batch(batch, cu_seqlens_q, seq_lens, prompt_lens);
   if (st != TPSA_OK) return st;
@@ -2111,7 +1771,7 @@ tpsa_status varlen_workspace(int32_t batch, const int64_t* cu_seqlens_q, const i
   int64_t most = kControlBytes;
   for (int32_t first = 0; first < batch; first += kMaxReqs) {
     const int32_t count = std::min(kMaxReqs, batch - first);
-    st = build_batch(first, count, cu_seqlens_q, seq_lens, prompt_lens, kv_heads, pairs,
+    st = build_batch(first, count, cu_seqlens_q, seq_lens, prompt_lens, kv_heads, ctas,
                      1.0f, 1, b.get());
     if (st != TPSA_OK) return st;
     most = std::max(most, b->workspace_bytes);
@@ -2160,23 +1820,18 @@ tpsa_status launch_varlen(const void* query, const void* key_cache, const void* 
     return fail(TPSA_ERR_INVALID_ARGUMENT, "kv_heads must be 1, 2, 4 or 8");
   }
   const uint64_t total_rows = static_cast<uint64_t>(cu_seqlens_q[batch]);
-  CUtensorMap tq, tk64, tk32, tv, tout;
+  CUtensorMap tq, tk128, tk64, tv, tout;
   const uint64_t hq = static_cast<uint64_t>(kv_heads) * kGroupSize;
   const uint64_t cache_tokens = static_cast<uint64_t>(num_pages) * kPageSize;
   st = encode_map(&tq, query, hq, total_rows, 2, kBlockQ);
   if (st != TPSA_OK) return st;
-  st = encode_map(&tk64, key_cache, kv_heads, cache_tokens, 1, 64);
+  st = encode_map(&tk128, key_cache, kv_heads, cache_tokens, 1, 128);
   if (st != TPSA_OK) return st;
-  st = encode_map(&tk32, key_cache, kv_heads, cache_tokens, 1, 32);
+  st = encode_map(&tk64, key_cache, kv_heads, cache_tokens, 1, 64);
   if (st != TPSA_OK) return st;
   st = encode_map(&tv, value_cache, kv_heads, cache_tokens, 1, 64);
   if (st != TPSA_OK) return st;
-  st = encode_map(&tout, out, hq, total_rows, 2, kBlockQ);
-  if (st != TPSA_OK) return st;
-  CUtensorMap tk128, tout16;  // solo kernel: whole 128-key K tiles, one warp's output box
-  st = encode_map(&tk128, key_cache, kv_heads, cache_tokens, 1, 128);
-  if (st != TPSA_OK) return st;
-  st = encode_map(&tout16, out, hq, total_rows, 2, 16);
+  st = encode_map(&tout, out, hq, total_rows, 2, 16);
   if (st != TPSA_OK) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   std::unique_ptr<BatchLaunch> b(new BatchLaunch);
@@ -2185,7 +1840,7 @@ tpsa_status launch_varlen(const void* query, const void* key_cache, const void* 
   for (int32_t first = 0; first < batch; first += kMaxReqs) {
     const int32_t count = std::min(kMaxReqs, batch - first);
     st = build_batch(first, count, cu_seqlens_q, seq_lens, prompt_lens, kv_heads,
-                     dev->workers(), scale, table_cols, b.get());
+                     dev->max_ctas, scale, table_cols, b.get());
     if (st != TPSA_OK) return st;
     if (workspace_bytes < static_cast<uint64_t>(b->workspace_bytes)) {
       return fail(TPSA_ERR_WORKSPACE, "workspace smaller than tpsa_varlen_workspace_size()");
@@ -2198,13 +1853,8 @@ tpsa_status launch_varlen(const void* query, const void* key_cache, const void* 
     args.scratch = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + b->ctl_bytes);
     cudaError_t e = cudaMemsetAsync(workspace, 0, static_cast<size_t>(b->ctl_bytes), s);
     if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(workspace)");
-    if (kernel_form() == Form::kSolo) {
-      tpsa_solo_kernel<false, true><<<args.plan.grid, solo::kNumThreads, solo::kSmemBytes, s>>>(
-          args, tq, tk128, tk64, tv, tout16);
-    } else {
-      tpsa_paged_kernel<false, true><<<args.plan.grid, kNumThreads, kSmemBytes, s>>>(
-          args, tq, tk64, tk32, tv, tout);
-    }
+    tpsa_paged_kernel<false, true><<<args.plan.grid, kNumThreads, kSmemBytes, s>>>(
+        args, tq, tk128, tk64, tv, tout);
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
   }
@@ -2281,14 +1931,14 @@ tpsa_status tpsa_make_plan(int64_t query_tokens, int64_t query_start, int64_t se
                            int64_t prompt_len, int32_t kv_heads, int32_t sm_count,
                            float scale, tpsa_plan* plan) {
   t_last_error.clear();
-  int32_t pairs = sm_count / ctas_per_worker();  // workers of the kernel form
+  int32_t ctas = sm_count;  // one CTA per SM
   if (sm_count <= 0) {
     DeviceState* dev = nullptr;
     tpsa_status st = device_state(&dev);
     if (st != TPSA_OK) return st;
-    pairs = dev->workers();
+    ctas = dev->max_ctas;
   }
-  return build_plan(query_tokens, query_start, seq_len, prompt_len, kv_heads, pairs, scale,
+  return build_plan(query_tokens, query_start, seq_len, prompt_len, kv_heads, ctas, scale,
                     plan);
 }
 
@@ -2350,7 +2000,7 @@ tpsa_status tpsa_varlen_workspace_size(int32_t batch, const int64_t* cu_seqlens_
   tpsa_status st = device_state(&dev);
   if (st != TPSA_OK) return st;
   return varlen_workspace(batch, cu_seqlens_q, seq_lens, prompt_lens, TPSA_KV_HEADS,
-                          dev->workers(), bytes);
+                          dev->max_ctas, bytes);
 }
 
 tpsa_status tpsa_varlen_workspace_size_heads(int32_t batch, const int64_t* cu_seqlens_q,
@@ -2365,7 +2015,7 @@ tpsa_status tpsa_varlen_workspace_size_heads(int32_t batch, const int64_t* cu_se
   tpsa_status st = device_state(&dev);
   if (st != TPSA_OK) return st;
   return varlen_workspace(batch, cu_seqlens_q, seq_lens, prompt_lens, kv_heads,
-                          dev->workers(), bytes);
+                          dev->max_ctas, bytes);
 }
 
 tpsa_status tpsa_paged_attention_varlen(const void* query, const void* key_cache,
@@ -2430,7 +2080,7 @@ tpsa_status tpsa_paged_attention_static_scratch(const void* query, const void* k
   tpsa_status st = device_state(&dev);
   if (st != TPSA_OK) return st;
   tpsa_plan p;
-  st = build_plan(query_tokens, query_start, seq_len, prompt_len, TPSA_KV_HEADS, dev->workers(),
+  st = build_plan(query_tokens, query_start, seq_len, prompt_len, TPSA_KV_HEADS, dev->max_ctas,
                   scale, &p);
   if (st != TPSA_OK) return st;
   if (static_cast<uint64_t>(p.workspace_bytes) > kStaticScratchBytes) {
@@ -2449,7 +2099,7 @@ tpsa_status tpsa_paged_attention_static_scratch(const void* query, const void* k
 }
 
 #ifdef TPSA_TRACE
-// Copies role `role`'s events of the last launch into out (2 x uint64 each).
+// Copies {start ns, end ns, items} of the first `ctas` CTAs of the last launch.
 TPSA_API void tpsa_debug_spans(unsigned long long* out, uint32_t ctas) {
   cudaDeviceSynchronize();
   cudaMemcpyFromSymbol(out, g_cta_span, sizeof(unsigned long long) * 3 * (ctas < 1024 ? ctas : 1024));
@@ -2460,12 +2110,11 @@ TPSA_API void tpsa_debug_timeout(uint32_t* out5) {
   cudaMemcpyFromSymbol(out5, g_timeout_site, sizeof(uint32_t) * 5);
 }
 
+// Copies role `role`'s events of the last launch into out (2 x uint64 each).
 TPSA_API uint32_t tpsa_debug_trace(uint32_t role, unsigned long long* out, uint32_t max_events) {
   uint32_t n[kTraceRoles] = {};
   cudaDeviceSynchronize();
-  if (role >= kTraceRoles) {  // softmax sub-phase buffers of CTA role - 4
-    return 0;
-  }
+  if (role >= kTraceRoles) return 0;
   cudaMemcpyFromSymbol(n, g_trace_n, sizeof(n));
   uint32_t c = n[role] < max_events ? n[role] : max_events;
   cudaMemcpyFromSymbol(out, g_trace, sizeof(unsigned long long) * 2 * c,
