@@ -108,7 +108,8 @@ def lib() -> ctypes.CDLL:
         h.tpsa_make_plan.argtypes = [_i64, _i64, _i64, _i64, _i32, _i32, _f32, ctypes.POINTER(Plan)]
         h.tpsa_plan_item.argtypes = [ctypes.POINTER(Plan), _i32, ctypes.POINTER(Item)]
         h.tpsa_plan_tile.argtypes = [ctypes.POINTER(Plan), _i32, _i32, ctypes.POINTER(_i32),
-                                     ctypes.POINTER(_i32), ctypes.POINTER(_i32)]
+                                     ctypes.POINTER(_i32), ctypes.POINTER(_i32),
+                                     ctypes.POINTER(_i32)]
         h.tpsa_workspace_size.argtypes = [_i64, _i64, _i64, _i64, ctypes.POINTER(_u64)]
         h.tpsa_paged_attention.argtypes = _ATTN + [_vp, _u64, _vp]
         h.tpsa_paged_attention_heads.argtypes = _ATTN + [_i32, _vp, _u64, _vp]
@@ -155,11 +156,12 @@ def plan_item(plan: Plan, item: int) -> Item:
     return out
 
 
-def plan_tile(plan: Plan, block: int, tile: int) -> tuple[int, int, bool]:
-    k0, w, m = _i32(), _i32(), _i32()
+def plan_tile(plan: Plan, block: int, tile: int) -> tuple[int, int, bool, int]:
+    """(first key, key count, needs mask, first key of keys 64-127)."""
+    k0, w, up, m = _i32(), _i32(), _i32(), _i32()
     check(lib().tpsa_plan_tile(ctypes.byref(plan), block, tile, ctypes.byref(k0), ctypes.byref(w),
-                               ctypes.byref(m)))
-    return k0.value, w.value, bool(m.value)
+                               ctypes.byref(up), ctypes.byref(m)))
+    return k0.value, w.value, bool(m.value), up.value
 
 
 def workspace_size(query_tokens: int, query_start: int, seq_len: int, prompt_len: int) -> int:

@@ -550,17 +550,26 @@ __device__ void producer_role(const KernelArgs& a, const Smem& sh, const CUtenso
       }
     }
 
+    // Cache row (page * 128 + slot) of logical key k; a block-table entry
+    // outside the cache is flagged and points fully out of bounds, where
+    // TMA fills zeros.
+    auto cache_row = [&](int32_t k) -> int32_t {
+      const int32_t page = __ldg(table + k / kPageSize);
+      if (page < 0 || page >= a.num_pages) {
+        raise_status(TPSA_DEVICE_BAD_PAGE);
+        return -kPageSize;
+      }
+      return page * kPageSize + (k % kPageSize);
+    };
     for (int32_t t = it.tile_begin; t < it.tile_end && ok; ++t) {
       int32_t k0, w;
       tile_keys(bt, t, &k0, &w);
-      const int32_t page = __ldg(table + k0 / kPageSize);
-      int32_t tok;
-      if (page < 0 || page >= a.num_pages) {
-        raise_status(TPSA_DEVICE_BAD_PAGE);
-        tok = -kPageSize;  // fully out of bounds: TMA fills zeros
-      } else {
-        tok = page * kPageSize + (k0 % kPageSize);
-      }
+      // Keys 0-63 of the tile start at k0, keys 64-127 at k_up (the band
+      // edge of a composite tile, else k0 + 64 in the same page).
+      const int32_t k_up = upper_key(bt, t, k0);
+      const bool split_halves = w == kTileKeys && k_up != k0 + kKeyGrain;
+      const int32_t tok = cache_row(k0);
+      const int32_t tok_up = split_halves ? cache_row(k_up) : tok + kKeyGrain;
       if (a.tiles != nullptr && !v_side) {
         atomicAdd(a.tiles, 1ull);
         atomicAdd(a.tiles + 1, static_cast<unsigned long long>(w));
@@ -573,11 +582,15 @@ __device__ void producer_role(const KernelArgs& a, const Smem& sh, const CUtenso
       if (!v_side) {
         // Keys at or beyond seq_len (unwritten slots of the last page) only
         // meet masked scores, which select -inf whatever they hold.
-        const CUtensorMap* km = w == kTileKeys ? tk128 : tk64;
+        const CUtensorMap* km = w == kTileKeys && !split_halves ? tk128 : tk64;
         ptx::mbar_arrive_expect_tx(bar_full + 8 * s, static_cast<uint32_t>(w) * kHeadDim * 2);
         for (int dh = 0; dh < 2; ++dh) {
           ptx::tma_load_3d(dst + dh * kKvHalfBytes, km, dh * 64, it.kv_head, tok,
                            bar_full + 8 * s);
+          if (split_halves) {
+            ptx::tma_load_3d(dst + dh * kKvHalfBytes + 64 * 128, tk64, dh * 64, it.kv_head, tok_up,
+                             bar_full + 8 * s);
+          }
         }
         if (t == it.tile_begin) {
           // The item's query tiles, after its first K tile: query tile x
@@ -599,7 +612,8 @@ __device__ void producer_role(const KernelArgs& a, const Smem& sh, const CUtenso
           ++q_iter;
         }
       } else {
-        const bool tail = k0 + w > req_seq_len;
+        const bool tail = k0 + min_i(w, kKeyGrain) > req_seq_len ||
+                          (w > kKeyGrain && k_up + kKeyGrain > req_seq_len);
         // Values at or beyond seq_len may be unwritten cache slots: such a
         // tile lands on a private barrier, those rows are zeroed (so that
         // P = 0 never meets a NaN), then the slot is published.
@@ -608,13 +622,15 @@ __device__ void producer_role(const KernelArgs& a, const Smem& sh, const CUtenso
         for (int dh = 0; dh < 2; ++dh) {
           for (int sub = 0; sub < w / 64; ++sub) {
             ptx::tma_load_3d(dst + dh * kKvHalfBytes + sub * 8192, tv, dh * 64, it.kv_head,
-                             tok + sub * 64, lbar);
+                             sub == 0 ? tok : tok_up, lbar);
           }
         }
         if (tail) {
           if (!wait(sh, sh.bar(kBarTail), tail_iter & 1)) { ok = false; break; }
           ++tail_iter;
-          for (int32_t row = req_seq_len - k0; row < w; ++row) {
+          for (int32_t row = 0; row < w; ++row) {
+            const int32_t key = row < kKeyGrain ? k0 + row : k_up + row - kKeyGrain;
+            if (key < req_seq_len) continue;
             for (int dh = 0; dh < 2; ++dh) {
               uint4* d4 = reinterpret_cast<uint4*>(sh.base + (dst - sh.base_u32) +
                                                    dh * kKvHalfBytes + row * 128);
@@ -892,7 +908,8 @@ struct TileArgs {
   uint32_t s_addr;      // the tile's S buffer (P goes to its columns 64-127)
   uint32_t o_addr;      // O (128 columns)
   uint32_t half_bar;    // P-half barrier of the tile's query tile
-  int32_t k0;           // first key of the tile
+  int32_t k0;           // first key of the tile (keys 0-63)
+  int32_t k_up;         // first key of keys 64-127 of a 128-key tile
   bool wide;            // 128 keys (else 64)
   bool masked;          // some key of the tile is outside some row's key set
   bool first;           // first tile of the item (its PV overwrites O)
@@ -988,8 +1005,8 @@ __device__ __forceinline__ void softmax_tile(const TileArgs& t, float sl2, int32
   prepare_chunk<kVisit>(r1, t.masked, q, sparse, t.k0 + 32, visit_row, words_per_row);
   float lm = fmaxf(chunk_max(r0), chunk_max(r1));
   if (t.wide) {
-    prepare_chunk<kVisit>(r2, t.masked, q, sparse, t.k0 + 64, visit_row, words_per_row);
-    prepare_chunk<kVisit>(r3, t.masked, q, sparse, t.k0 + 96, visit_row, words_per_row);
+    prepare_chunk<kVisit>(r2, t.masked, q, sparse, t.k_up, visit_row, words_per_row);
+    prepare_chunk<kVisit>(r3, t.masked, q, sparse, t.k_up + 32, visit_row, words_per_row);
     lm = fmaxf(lm, fmaxf(chunk_max(r2), chunk_max(r3)));
   }
   const float m_new = next_ref(st.m_ref, lm, sl2);
@@ -1093,6 +1110,7 @@ __device__ void softmax_role(const KernelArgs& a, const Smem& sh, uint32_t tmem,
       ta.s_addr = s_addr;
       ta.o_addr = o_addr;
       ta.k0 = k0;
+      ta.k_up = upper_key(bt, it.tile_begin + n, k0);
       ta.wide = w > 64;
       ta.masked = tile_needs_mask(pr, bt, k0, w);
       ta.first = n == 0;
@@ -1951,9 +1969,11 @@ tpsa_status tpsa_plan_item(const tpsa_plan* plan, int32_t item, tpsa_item* out) 
 }
 
 tpsa_status tpsa_plan_tile(const tpsa_plan* plan, int32_t block, int32_t tile,
-                           int32_t* key_begin, int32_t* key_count, int32_t* needs_mask) {
+                           int32_t* key_begin, int32_t* key_count, int32_t* upper_begin,
+                           int32_t* needs_mask) {
   if (plan == nullptr || key_begin == nullptr || key_count == nullptr ||
-      needs_mask == nullptr || block < 0 || block >= plan->num_blocks) {
+      upper_begin == nullptr || needs_mask == nullptr || block < 0 ||
+      block >= plan->num_blocks) {
     return fail(TPSA_ERR_INVALID_ARGUMENT, "block index out of range");
   }
   const BlockTiles bt = block_tiles(*plan, block);
@@ -1964,6 +1984,7 @@ tpsa_status tpsa_plan_tile(const tpsa_plan* plan, int32_t block, int32_t tile,
   tile_keys(bt, tile, &k0, &w);
   *key_begin = k0;
   *key_count = w;
+  *upper_begin = upper_key(bt, tile, k0);
   *needs_mask = tile_needs_mask(*plan, bt, k0, w) ? 1 : 0;
   return TPSA_OK;
 }

@@ -5,13 +5,18 @@
 // kernel runs as two M=128 tensor-core tiles (query heads {4h, 4h+1} and
 // {4h+2, 4h+3}) that read the same key tiles.
 //
-// Key tiles are page-contained runs of 64 or 128 keys.  For each block the
-// tiles cover exactly the union of the rows' key sets rounded out to 64-key
-// granularity, so keys that no row of the block uses are never loaded:
+// Key tiles are runs of 64 or 128 keys, each 64-key half inside one page.
+// For each block the tiles cover exactly the union of the rows' key sets
+// rounded out to 64-key granularity, so keys that no row of the block uses
+// are never loaded:
 //   * a block whose rows are all sparse (reference operator/op_kernel/
 //     triangle_schedule.h:101-142, BuildTileSchedule "fullySparse") reads the
 //     sink page prefix [0, 64) plus the local band [qBegin - 512, qEnd);
-//     when the band starts inside page 0 the two are merged into one range;
+//     when the band starts inside page 0 the two are merged into one range.
+//     The band is 576 keys (4.5 pages) long, so one of its ends is a 64-key
+//     edge; tile 0 joins the sink prefix with that edge into one 128-key
+//     composite tile (keys [0, 64) and [edge, edge + 64)), so the block runs
+//     one 128-key tile where it would run two 64-key tiles;
 //   * any other block reads the dense range [0, qEnd).
 // A block straddling sparse_begin or sparse_end is not cut into spans as the
 // reference does (triangle_schedule.h:74-99); it reads the dense range and
@@ -59,12 +64,13 @@ TPSA_HD int32_t max_i(int32_t a, int32_t b) { return a > b ? a : b; }
 struct BlockTiles {
   int32_t q_begin;    // absolute position of the block's first row
   int32_t q_end;      // one past its last real row (<= seq_len)
-  int32_t sink;       // 1: tile 0 is the separate sink tile [0, 64)
+  int32_t sink;       // 1: tile 0 is the sink tile [0, 64); 2: tile 0 is the
+                      // composite tile [0, 64) + [edge, edge + 64)
   int32_t key_begin;  // 64-aligned start of the contiguous key range
   int32_t key_end;    // 64-aligned end of the contiguous key range
   int32_t count;      // number of key tiles
   int32_t all_dense;  // every row of the block is a dense row
-  int32_t all_sparse; // every row of the block is a sparse row
+  int32_t edge;       // with sink == 2: first key of the band edge in tile 0
 };
 
 // Row q is sparse iff sparse_begin <= q < sparse_end (reference
@@ -81,29 +87,41 @@ TPSA_HD BlockTiles block_tiles(const tpsa_plan& p, int32_t block) {
   const int32_t sparse_hi = min_i(t.q_end, p.sparse_end);
   t.all_dense = sparse_lo >= sparse_hi ? 1 : 0;
   const bool all_sparse = t.q_begin >= p.sparse_begin && t.q_end <= p.sparse_end;
-  t.all_sparse = all_sparse ? 1 : 0;
   t.key_end = ceil_div(t.q_end, kKeyGrain) * kKeyGrain;
   t.sink = 0;
   t.key_begin = 0;
+  t.edge = 0;
   if (all_sparse) {
     // q_begin >= 521, so the band start q_begin - 512 is positive.
     const int32_t band = ((t.q_begin - kLocalWindow) / kKeyGrain) * kKeyGrain;
     if (band >= kTileKeys) {
       t.sink = 1;
       t.key_begin = band;
+      // A band end half-way through a page becomes the upper half of tile 0.
+      if (t.key_begin % kTileKeys != 0) {
+        t.sink = 2;
+        t.edge = t.key_begin;
+        t.key_begin += kKeyGrain;
+      } else if (t.key_end % kTileKeys != 0) {
+        t.sink = 2;
+        t.edge = t.key_end - kKeyGrain;
+        t.key_end -= kKeyGrain;
+      }
     }
   }
-  t.count = t.sink + ceil_div(t.key_end, kTileKeys) - t.key_begin / kTileKeys;
+  t.count = (t.sink != 0 ? 1 : 0) + ceil_div(t.key_end, kTileKeys) - t.key_begin / kTileKeys;
   return t;
 }
 
-// Keys [*k0, *k0 + *width) of tile `tile` of a block.
+// Tile `tile` of a block: *width keys, the first 64 (or all of a 64-key
+// tile) from *k0 on; keys 64-127 of a 128-key tile start at
+// upper_key(t, tile, *k0), which is *k0 + 64 except for the composite tile.
 TPSA_HD void tile_keys(const BlockTiles& t, int32_t tile, int32_t* k0,
                        int32_t* width) {
-  if (t.sink) {
+  if (t.sink != 0) {
     if (tile == 0) {
       *k0 = 0;
-      *width = kKeyGrain;
+      *width = t.sink == 2 ? kTileKeys : kKeyGrain;
       return;
     }
     tile -= 1;
@@ -115,8 +133,14 @@ TPSA_HD void tile_keys(const BlockTiles& t, int32_t tile, int32_t* k0,
   *width = end - start;
 }
 
-// True when some real row of the block excludes some key of [k0, k0 + w).
-// Conservative for blocks that mix dense and sparse rows.
+TPSA_HD int32_t upper_key(const BlockTiles& t, int32_t tile, int32_t k0) {
+  return (t.sink == 2 && tile == 0) ? t.edge : k0 + kKeyGrain;
+}
+
+// True when some real row of the block excludes some key of [k0, k0 + w)
+// (the composite tile always has excluded keys: only keys 0-7 of its lower
+// half are in the sparse rows' sets).  Conservative for blocks that mix
+// dense and sparse rows.
 TPSA_HD bool tile_needs_mask(const tpsa_plan& p, const BlockTiles& t,
                              int32_t k0, int32_t w) {
   if (k0 + w - 1 > t.q_begin) return true;  // causal edge of the first row

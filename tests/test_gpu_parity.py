@@ -129,7 +129,7 @@ def test_visited_key_set_bit_exact(tm, cuda_device, query_start, tq, seq, prompt
     for i in range(plan.total_items):
         it = tm._native.plan_item(plan, i)
         for t in range(it.tile_begin, it.tile_end):
-            _, w, _ = tm._native.plan_tile(plan, it.block, t)
+            _, w, _, _ = tm._native.plan_tile(plan, it.block, t)
             n_tiles += 1
             n_keys += w
     assert int(tiles[0]) == n_tiles and int(tiles[1]) == n_keys

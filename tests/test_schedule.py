@@ -31,7 +31,7 @@ def test_library_exports_every_declared_symbol(tm):
     lib = tm._native.lib()
     for name in declared:
         assert hasattr(lib, name)
-    assert lib.tpsa_abi_version() == 1
+    assert lib.tpsa_abi_version() == 2
 
 
 def test_adapter_library_is_built(tm):
@@ -73,8 +73,9 @@ CASES = [
 
 @pytest.mark.parametrize("q0,tq,seq,prompt", CASES)
 def test_tile_schedule_covers_exact_key_sets(tm, q0, tq, seq, prompt):
-    """Per block: tiles are page-contained, cover every visible key, and load
-    no key outside the 64-rounded union of the block's key sets."""
+    """Per block: each 64-key half of a tile is page-contained, the tiles
+    cover every visible key, and they load no key outside the 64-rounded
+    union of the block's key sets."""
     plan = tm._native.make_plan(tq, q0, seq, prompt, 8, SM)
     assert plan.num_blocks == -(-tq // 64)
     for b in range(plan.num_blocks):
@@ -85,13 +86,19 @@ def test_tile_schedule_covers_exact_key_sets(tm, q0, tq, seq, prompt):
         loaded = []
         while True:
             try:
-                k0, w, masked = tm._native.plan_tile(plan, b, t)
+                k0, w, masked, up = tm._native.plan_tile(plan, b, t)
             except tm.TpsaError:
                 break
-            assert w in (64, 128) and k0 % 64 == 0
-            assert k0 // 128 == (k0 + w - 1) // 128, "tile crosses a page"
-            assert k0 + w <= -(-seq // 128) * 128, "tile beyond the block table"
-            keys = np.arange(k0, k0 + w)
+            assert w in (64, 128) and k0 % 64 == 0 and up % 64 == 0
+            halves = [k0] if w == 64 else [k0, up]
+            if w == 128 and up != k0 + 64:
+                # the composite tile of a sparse block: sink prefix + band edge
+                assert k0 == 0 and t == 0 and up >= 128
+            else:
+                assert k0 // 128 == (k0 + w - 1) // 128, "tile crosses a page"
+            for h in halves:
+                assert h + 64 <= -(-seq // 128) * 128, "tile beyond the block table"
+            keys = np.concatenate([np.arange(h, h + 64) for h in halves])
             vis = o.visible_mask(rows, keys, seq, prompt)
             if not masked:
                 assert vis.all(), f"unmasked tile {k0}+{w} hides keys of block {b}"
@@ -152,13 +159,13 @@ def test_long_tail_blocks_are_split_and_run_first(tm):
     assert plan.total_tiles / SM >= longest
 
 
-@pytest.mark.parametrize("seq, pieces", [(8192, 2), (32768, 4), (65536, 6), (131072, 7)])
+@pytest.mark.parametrize("seq, pieces", [(8192, 2), (32768, 5), (65536, 6), (131072, 8)])
 def test_tail_split_count_fits_the_ctas(tm, seq, pieces):
     """BASELINE config 3 (8192-row chunk ending an N-token prompt): the 16
     dense-tail (block, head) items are cut into as many pieces as the
-    makespan estimate picks for 148 single-CTA workers: at 128K 7 pieces
-    (112 pieces of 147 tiles, one per CTA, beside an average of 152 tiles
-    per CTA), never more pieces than CTAs."""
+    makespan estimate picks for 148 CTAs: at 128K 8 pieces (128 pieces of
+    128 tiles, one per CTA, beside an average of 145 tiles per CTA), never
+    more pieces than CTAs."""
     plan = tm._native.make_plan(8192, seq - 8192, seq, seq, 8, SM)
     tail_blocks = (plan.num_blocks - plan.tail_block0) * 8
     assert plan.tail_items == tail_blocks * pieces
