@@ -153,3 +153,20 @@ TORCH_LIBRARY_IMPL(trianglemix, CUDA, ops) {
   ops.impl("triangle_paged_sparse_attention.out",
            &trianglemix_b200::triangle_paged_sparse_attention_out);
 }
+
+// The name the reference registers from its in-tree vLLM-Ascend build
+// (README.md:34-36 of the reference: torch.ops._C_ascend.
+// npu_triangle_paged_sparse_attention, an out-variant operator), bound to the
+// same out implementation: same arguments, same gates, caller-owned output.
+TORCH_LIBRARY_FRAGMENT(_C_ascend, ops) {
+  ops.def(
+      "npu_triangle_paged_sparse_attention("
+      "Tensor query, Tensor key_cache, Tensor value_cache, "
+      "Tensor block_table, int query_start, int seq_len, "
+      "int prompt_len, float scale, *, Tensor(a!) out) -> Tensor(a!)");
+}
+
+TORCH_LIBRARY_IMPL(_C_ascend, CUDA, ops) {
+  ops.impl("npu_triangle_paged_sparse_attention",
+           &trianglemix_b200::triangle_paged_sparse_attention_out);
+}

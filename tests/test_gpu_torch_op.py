@@ -33,6 +33,23 @@ def test_out_variant_writes_caller_buffer(adapter, cuda_device):
     assert_close(out.cpu(), oracle_attention(q, k, v, table, 0, 1300, 1300, SCALE), "out variant")
 
 
+def test_c_ascend_alias_is_the_out_operator(adapter, cuda_device):
+    """torch.ops._C_ascend.npu_triangle_paged_sparse_attention, the name of the
+    reference's in-tree registration (README.md:34-36 of the reference), writes
+    the caller's buffer and applies the same gates."""
+    (q, k, v, table), (qd, kd, vd, td) = _inputs(cuda_device)
+    out = torch.full_like(qd, float("nan"))
+    ptr = out.data_ptr()
+    res = torch.ops._C_ascend.npu_triangle_paged_sparse_attention(
+        qd, kd, vd, td, 0, 1300, 1300, SCALE, out=out)
+    torch.cuda.synchronize()
+    assert res.data_ptr() == ptr
+    assert_close(out.cpu(), oracle_attention(q, k, v, table, 0, 1300, 1300, SCALE), "_C_ascend")
+    with pytest.raises(RuntimeError, match="query must be BF16"):
+        torch.ops._C_ascend.npu_triangle_paged_sparse_attention(
+            qd.float(), kd, vd, td, 0, 1300, 1300, SCALE, out=out)
+
+
 def test_functional_variant_and_workspace_size(adapter, cuda_device):
     (q, k, v, table), (qd, kd, vd, td) = _inputs(cuda_device)
     out = torch.ops.trianglemix_reference.triangle_paged_sparse_attention(qd, kd, vd, td, 0, 1300,

@@ -209,3 +209,21 @@ def test_varlen_metadata_gates_on_host(tm, cu, seq_lens, prompt_lens, message):
                                                1 << 20, None)
     assert st == 1  # TPSA_ERR_INVALID_ARGUMENT
     assert message in nat.lib().tpsa_last_error().decode()
+
+
+def test_adapter_registers_the_reference_schemas(tm):
+    """Loading the adapter (no GPU needed) registers the reference's operator
+    names and schemas (operator/torch_adapter/triangle_paged_attention_torch.cpp
+    :265-297, README.md:34-36 of the reference)."""
+    import torch
+
+    tm.load_adapter()
+    args = ("(Tensor query, Tensor key_cache, Tensor value_cache, Tensor block_table, "
+            "int query_start, int seq_len, int prompt_len, float scale")
+    out = ", *, Tensor(a!) out) -> Tensor(a!)"
+    assert str(torch.ops.trianglemix.triangle_paged_sparse_attention.out._schema) == (
+        "trianglemix::triangle_paged_sparse_attention.out" + args + out)
+    assert str(torch.ops._C_ascend.npu_triangle_paged_sparse_attention.default._schema) == (
+        "_C_ascend::npu_triangle_paged_sparse_attention" + args + out)
+    assert str(torch.ops.trianglemix_reference.triangle_paged_sparse_attention.default._schema) == (
+        "trianglemix_reference::triangle_paged_sparse_attention" + args + ") -> Tensor")
