@@ -16,7 +16,15 @@ FlashAttention backend:
   ``vllm.v1.attention.backends.flash_attn.FlashAttentionImpl.forward``.  In
   vLLM's v1 engine the KV cache write is a separate step, so ``forward`` only
   reads the paged cache ``[2, num_blocks, block_size, kv_heads, head_size]``,
-  which is this kernel's BSND layout when ``block_size`` is 128.
+  which is this kernel's BSND layout when ``block_size`` is 128;
+* ``install_vllm_metadata_patch`` puts each step's host lengths and the
+  scheduler's final prompt lengths on vLLM's FlashAttention metadata (the
+  reference attaches the runner's prompt lengths the same way,
+  plugin.py:523-570, 946);
+* ``register`` is the ``vllm.general_plugins`` entry point (pyproject.toml;
+  reference setup.py:292-294, plugin.py:1705-1741): it installs both, with
+  the configuration read from ``additional_config.trianglemix`` when vLLM
+  builds its first attention layer.
 
 Differences from the reference, both enabled by this kernel: a packed batch
 of prefills is direct when every request is eligible (one varlen launch),
@@ -27,6 +35,9 @@ fallback, plugin.py:1251-1253).
 
 from __future__ import annotations
 
+import contextvars
+import logging
+import os
 import threading
 import time
 from typing import Any, Callable, Sequence
@@ -34,12 +45,51 @@ from typing import Any, Callable, Sequence
 import torch
 
 from . import _native
-from .config import PluginConfig
+from .config import PluginConfig, coerce_bool, resolve_plugin_config
 from .kernel import (SUPPORTED_CACHE_BLOCK_SIZE, SUPPORTED_HEAD_SIZE, extract_layer_index)
 from .planning import FallbackReason, TriangleBatchPlan, build_batch_plan
 from .stats import TriangleMixRuntimeStats, runtime_stats
 
 GROUP_SIZE = 4  # query heads per KV head (GQA 4:1)
+logger = logging.getLogger(__name__)
+
+# Attributes this module puts on vLLM's FlashAttention metadata (host lists).
+QUERY_START_ATTR = "trianglemix_query_start_loc"
+SEQ_LENS_ATTR = "trianglemix_seq_lens"
+PROMPT_LENS_ATTR = "trianglemix_prompt_lens"
+
+
+def _int_list(value: Any) -> list[int] | None:
+    """A host integer sequence as a list, or None (device tensors are not read)."""
+    if value is None:
+        return None
+    if isinstance(value, torch.Tensor):
+        if value.device.type != "cpu":
+            return None
+        value = value.tolist()
+    try:
+        out = [int(x) for x in value]
+    except (TypeError, ValueError):
+        return None
+    return out or None
+
+
+def metadata_prompt_lens(metadata: Any) -> tuple[list[int] | None, str]:
+    """The scheduler's final prompt length of each request of a step, and where
+    it came from; ``(None, "missing")`` when the metadata carries none.
+
+    Same order of sources as the reference (plugin.py:523-570): fields of the
+    metadata itself, then the lengths this module attached from the model
+    runner's input batch.
+    """
+    for name in ("prompt_lens_list", "prompt_lens_cpu", "num_prompt_tokens_cpu"):
+        value = _int_list(getattr(metadata, name, None))
+        if value:
+            return value, f"metadata:{name}"
+    value = _int_list(getattr(metadata, PROMPT_LENS_ATTR, None))
+    if value:
+        return value, "runner"
+    return None, "missing"
 
 
 def step_state(query_lens: Sequence[int], seq_lens: Sequence[int]) -> tuple[str, int]:
@@ -66,7 +116,7 @@ class TriangleMixRouter:
         self.config = config
         self.stats = stats if stats is not None else runtime_stats()
         self.stats.configure(config.stats_recent_capacity, config.stats_log_interval)
-        self._workspaces: dict[tuple[int, int], torch.Tensor] = {}
+        self._workspaces: dict[int, torch.Tensor] = {}  # one buffer per device
         self._lock = threading.Lock()
         self._plans: dict[int, tuple[Any, TriangleBatchPlan]] = {}
 
@@ -76,15 +126,20 @@ class TriangleMixRouter:
 
     def plan_step(self, *, query_lens: Sequence[int], seq_lens: Sequence[int],
                   prompt_lens: Sequence[int] | None = None) -> TriangleBatchPlan:
-        """The step's plan from host lengths (prompt_lens default to seq_lens)."""
-        query_lens = [int(x) for x in query_lens]
-        seq_lens = [int(x) for x in seq_lens]
-        prompts = [int(x) for x in prompt_lens] if prompt_lens is not None else list(seq_lens)
+        """The step's plan from host lengths, for a caller that knows each
+        request's whole prompt (prompt_lens default to seq_lens)."""
+        return self._plan([int(x) for x in query_lens], [int(x) for x in seq_lens],
+                          prompt_lens if prompt_lens is not None else seq_lens)
+
+    def _plan(self, query_lens: list[int], seq_lens: list[int],
+              prompt_lens: Sequence[int] | None) -> TriangleBatchPlan:
+        """The step's plan (prompt_lens None: missing, the step falls back)."""
         state, decodes = step_state(query_lens, seq_lens)
         ends, total = [], 0
         for q in query_lens:
             total += q
             ends.append(total)
+        prompts = [int(x) for x in prompt_lens] if prompt_lens is not None else None
         plan = build_batch_plan(state_name=state, cumulative_query_ends=ends, seq_lens=seq_lens,
                                 prompt_lens=prompts, num_decodes=decodes,
                                 num_prefills=len(query_lens) - decodes, config=self.config.kernel)
@@ -96,21 +151,31 @@ class TriangleMixRouter:
                           ) -> TriangleBatchPlan:
         """One plan per metadata object (shared by all layers of a step).
 
-        The lengths are read to the host once per step (``query_start_loc``
-        and ``seq_lens`` of vLLM's FlashAttention metadata).  Prompt lengths
-        come from ``prompt_lens_provider(metadata)``; without one, each
-        request's prompt is taken to end at its sequence end.
+        Lengths come from the host lists ``install_vllm_metadata_patch`` puts
+        on the metadata; without them ``query_start_loc`` and ``seq_lens`` are
+        read from the device once per step.  Prompt lengths come from the
+        metadata (``metadata_prompt_lens``), else from
+        ``prompt_lens_provider(metadata)``.  With no prompt length the step
+        falls back with ``missing_metadata``, as the reference does
+        (plugin.py:523-570): a chunk's sparse range depends on where the
+        prompt ends, which the sequence end does not tell.
         """
         key = id(metadata)
         with self._lock:
             hit = self._plans.get(key)
             if hit is not None and hit[0] is metadata:
                 return hit[1]
-        starts = [int(x) for x in metadata.query_start_loc.tolist()]
-        seq_lens = [int(x) for x in metadata.seq_lens.tolist()]
+        starts = _int_list(getattr(metadata, QUERY_START_ATTR, None))
+        if starts is None:
+            starts = [int(x) for x in metadata.query_start_loc.tolist()]
+        seq_lens = _int_list(getattr(metadata, SEQ_LENS_ATTR, None))
+        if seq_lens is None:
+            seq_lens = [int(x) for x in metadata.seq_lens.tolist()]
         query_lens = [b - a for a, b in zip(starts, starts[1:])]
-        prompts = prompt_lens_provider(metadata) if prompt_lens_provider is not None else None
-        plan = self.plan_step(query_lens=query_lens, seq_lens=seq_lens, prompt_lens=prompts)
+        prompts, _ = metadata_prompt_lens(metadata)
+        if prompts is None and prompt_lens_provider is not None:
+            prompts = _int_list(prompt_lens_provider(metadata))
+        plan = self._plan(query_lens, seq_lens, prompts)
         with self._lock:
             if len(self._plans) > 64:
                 self._plans.clear()
@@ -163,9 +228,11 @@ class TriangleMixRouter:
 
     # ------------------------------------------------------------ launch
     def _workspace(self, device: torch.device, nbytes: int) -> torch.Tensor:
-        key = (device.index or 0, nbytes)
+        """The device's one workspace, grown (never shrunk) to the largest
+        size a step has needed, so the router holds one buffer per device."""
+        key = device.index or 0
         ws = self._workspaces.get(key)
-        if ws is None:
+        if ws is None or ws.numel() < nbytes:
             ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=device)
             self._workspaces[key] = ws
         return ws
@@ -255,6 +322,16 @@ def install_vllm_flash_attention_hook(router: TriangleMixRouter, *, impl_cls: ty
             return original(self, layer, query, key, value, kv_cache, attn_metadata, output,
                              output_scale, output_block_scale)
         plan = router.plan_for_metadata(attn_metadata, prompt_lens_provider)
+        if (int(getattr(self, "dcp_world_size", 1) or 1) > 1
+                or int(getattr(self, "pcp_world_size", 1) or 1) > 1):
+            # Context parallelism shards the KV cache across ranks, so this
+            # rank's cache holds part of each sequence (reference
+            # plugin.py:1254-1256 falls back the same way).
+            router.stats.record_layer_fallback(plan_id=plan.plan_id,
+                                               layer_index=extract_layer_index(name),
+                                               reason=FallbackReason.CONTEXT_PARALLEL)
+            return original(self, layer, query, key, value, kv_cache, attn_metadata, output,
+                            output_scale, output_block_scale)
         key_cache, value_cache = kv_cache.unbind(0)
         rows = int(getattr(attn_metadata, "num_actual_tokens", query.shape[0]))
         q = query[:rows]
@@ -287,3 +364,191 @@ def uninstall_vllm_flash_attention_hook(impl_cls: type | None = None) -> bool:
     impl_cls.forward = original
     delattr(impl_cls, _HOOK_ATTR)
     return True
+
+
+# ------------------------------------------------------------ step metadata
+# The model runner's prompt lengths of the step being built (set around
+# GPUModelRunner._build_attention_metadata, read by the metadata builder).
+_STEP_PROMPTS: contextvars.ContextVar[tuple[int, ...] | None] = contextvars.ContextVar(
+    "trianglemix_step_prompts", default=None)
+_META_ATTR = "_trianglemix_original_build"
+_RUNNER_ATTR = "_trianglemix_original_build_attention_metadata"
+
+
+def install_vllm_metadata_patch(*, builder_cls: type | None = None,
+                                runner_cls: type | None = None) -> bool:
+    """Put host lengths and final prompt lengths on each FlashAttention metadata.
+
+    ``runner_cls._build_attention_metadata`` (vLLM's GPUModelRunner) is
+    wrapped to publish ``input_batch.num_prompt_tokens`` of the step's
+    requests, the scheduler's final prompt lengths, while it builds the
+    step's metadata; ``builder_cls.build`` (FlashAttentionMetadataBuilder) is
+    wrapped to copy them, with the host copies of ``query_start_loc`` and
+    ``seq_lens`` that the common metadata already holds, onto the metadata it
+    returns.  The hook then plans a step without reading the device.  Returns
+    False when vLLM is not importable.
+    """
+    if builder_cls is None or runner_cls is None:
+        try:
+            from vllm.v1.attention.backends.flash_attn import FlashAttentionMetadataBuilder
+            from vllm.v1.worker.gpu_model_runner import GPUModelRunner
+        except Exception:
+            return False
+        builder_cls = builder_cls or FlashAttentionMetadataBuilder
+        runner_cls = runner_cls or GPUModelRunner
+    build = getattr(builder_cls, _META_ATTR, None) or builder_cls.build
+    prepare = getattr(runner_cls, _RUNNER_ATTR, None) or runner_cls._build_attention_metadata
+
+    def build_with_lengths(self, common_prefix_len, common_attn_metadata, *args, **kwargs):
+        meta = build(self, common_prefix_len, common_attn_metadata, *args, **kwargs)
+        try:
+            n = int(common_attn_metadata.num_reqs)
+            starts = common_attn_metadata.query_start_loc_cpu[:n + 1].tolist()
+            setattr(meta, QUERY_START_ATTR, starts)
+            seqs = getattr(common_attn_metadata, "_seq_lens_cpu", None)
+            if isinstance(seqs, torch.Tensor) and seqs.device.type == "cpu":
+                setattr(meta, SEQ_LENS_ATTR, seqs[:n].tolist())
+            prompts = _STEP_PROMPTS.get()
+            if prompts is not None and len(prompts) >= n:
+                setattr(meta, PROMPT_LENS_ATTR, list(prompts[:n]))
+        except Exception:  # metadata of another shape: plan from the device instead
+            runtime_stats().record_runtime_error(stage="metadata_lengths")
+        return meta
+
+    def build_attention_metadata(self, num_tokens, num_reqs, *args, **kwargs):
+        prompts = None
+        batch = getattr(self, "input_batch", None)
+        counts = getattr(batch, "num_prompt_tokens", None)
+        if counts is not None:
+            prompts = tuple(int(x) for x in counts[:int(num_reqs)])
+        token = _STEP_PROMPTS.set(prompts)
+        try:
+            return prepare(self, num_tokens, num_reqs, *args, **kwargs)
+        finally:
+            _STEP_PROMPTS.reset(token)
+
+    setattr(builder_cls, _META_ATTR, build)
+    builder_cls.build = build_with_lengths
+    setattr(runner_cls, _RUNNER_ATTR, prepare)
+    runner_cls._build_attention_metadata = build_attention_metadata
+    return True
+
+
+def uninstall_vllm_metadata_patch(*, builder_cls: type | None = None,
+                                  runner_cls: type | None = None) -> bool:
+    if builder_cls is None or runner_cls is None:
+        try:
+            from vllm.v1.attention.backends.flash_attn import FlashAttentionMetadataBuilder
+            from vllm.v1.worker.gpu_model_runner import GPUModelRunner
+        except Exception:
+            return False
+        builder_cls = builder_cls or FlashAttentionMetadataBuilder
+        runner_cls = runner_cls or GPUModelRunner
+    done = False
+    for cls, attr, name in ((builder_cls, _META_ATTR, "build"),
+                            (runner_cls, _RUNNER_ATTR, "_build_attention_metadata")):
+        original = getattr(cls, attr, None)
+        if original is not None:
+            setattr(cls, name, original)
+            delattr(cls, attr)
+            done = True
+    return done
+
+
+# ------------------------------------------------------------ vLLM plugin entry
+_REGISTER_LOCK = threading.Lock()
+_ROUTER: TriangleMixRouter | None = None
+_INIT_ATTR = "_trianglemix_original_init"
+
+
+def registered_router() -> TriangleMixRouter | None:
+    """The router ``register`` installed in this process, if any."""
+    return _ROUTER
+
+
+def _strict_from_environment() -> bool:
+    value = os.getenv("VLLM_ASCEND_TRIANGLE_MIX_STRICT")
+    try:
+        return coerce_bool(value, name="strict") if value is not None else False
+    except ValueError:
+        return False
+
+
+def _configure_from_vllm(router: TriangleMixRouter, impl_cls: type) -> None:
+    """Wrap ``impl_cls.__init__`` so that the first attention layer vLLM
+    builds (while its configuration is current) sets the router's
+    configuration from ``additional_config.trianglemix``."""
+    original = getattr(impl_cls, _INIT_ATTR, None) or impl_cls.__init__
+    state = {"done": False}
+
+    def __init__(self, *args, **kwargs):
+        original(self, *args, **kwargs)
+        if state["done"]:
+            return
+        state["done"] = True
+        try:
+            from vllm.config import get_current_vllm_config
+
+            config = resolve_plugin_config(get_current_vllm_config())
+        except Exception:
+            runtime_stats().record_runtime_error(stage="plugin_config")
+            if router.config.strict or _strict_from_environment():
+                raise
+            logger.warning("TriangleMix configuration could not be read; the stock "
+                           "attention path stays active", exc_info=True)
+            return
+        router.config = config
+        router.stats.configure(config.stats_recent_capacity, config.stats_log_interval)
+
+    setattr(impl_cls, _INIT_ATTR, original)
+    impl_cls.__init__ = __init__
+
+
+def register() -> None:
+    """vLLM ``general_plugins`` entry point (declared in pyproject.toml).
+
+    Installs the FlashAttention hook and the metadata patch once per process
+    (reference plugin.py:1705-1741).  The configuration starts from the
+    environment and is replaced by ``additional_config.trianglemix`` when vLLM
+    builds its first FlashAttention layer; the path is off unless enabled.
+    A failure leaves vLLM's own attention in place, or raises with
+    ``strict``.
+    """
+    global _ROUTER
+    with _REGISTER_LOCK:
+        if _ROUTER is not None:
+            return
+        try:
+            from vllm.v1.attention.backends.flash_attn import FlashAttentionImpl
+
+            router = TriangleMixRouter(resolve_plugin_config(None))
+            _configure_from_vllm(router, FlashAttentionImpl)
+            if not install_vllm_flash_attention_hook(router, impl_cls=FlashAttentionImpl):
+                raise RuntimeError("FlashAttentionImpl could not be hooked")
+            install_vllm_metadata_patch()
+        except Exception:
+            runtime_stats().record_runtime_error(stage="plugin_register")
+            if _strict_from_environment():
+                raise
+            logger.warning("TriangleMix plugin could not hook vLLM; the stock attention "
+                           "path stays active", exc_info=True)
+            return
+        _ROUTER = router
+
+
+def unregister() -> bool:
+    """Undo ``register`` in this process (vLLM's own attention path returns)."""
+    global _ROUTER
+    with _REGISTER_LOCK:
+        if _ROUTER is None:
+            return False
+        from vllm.v1.attention.backends.flash_attn import FlashAttentionImpl
+
+        uninstall_vllm_flash_attention_hook(FlashAttentionImpl)
+        uninstall_vllm_metadata_patch()
+        original = getattr(FlashAttentionImpl, _INIT_ATTR, None)
+        if original is not None:
+            FlashAttentionImpl.__init__ = original
+            delattr(FlashAttentionImpl, _INIT_ATTR)
+        _ROUTER = None
+        return True

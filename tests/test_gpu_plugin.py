@@ -66,7 +66,9 @@ def test_hook_varlen_batch_matches_oracle(cuda_device):
         meta = types.SimpleNamespace(
             query_start_loc=torch.tensor(cu, dtype=torch.int32, device=cuda_device),
             seq_lens=torch.tensor([s for _, s, _ in specs], dtype=torch.int32, device=cuda_device),
-            num_actual_tokens=cu[-1], block_table=tables.to(cuda_device), causal=True)
+            num_actual_tokens=cu[-1], block_table=tables.to(cuda_device), causal=True,
+            # the scheduler's final prompt lengths, as the metadata patch attaches them
+            trianglemix_prompt_lens=[p for _, _, p in specs])
         out = torch.zeros(cu[-1], 32 * 128, dtype=torch.bfloat16, device=cuda_device)
         layer = types.SimpleNamespace(layer_name="model.layers.0.self_attn.attn")
         Impl().forward(layer, q.to(cuda_device), None, None, kv, meta, out)
