@@ -25,8 +25,6 @@ SUPPORTED_KV_HEADS = 8
 SUPPORTED_SINK_TOKENS = 8
 SUPPORTED_LOCAL_WINDOW = 512
 SUPPORTED_LAST_ROWS = 128
-DEFAULT_BLOCK_M = 32
-DEFAULT_BLOCK_N = 512
 
 
 @dataclass(frozen=True)
@@ -274,22 +272,25 @@ def triangle_direct_paged_attention(*, query: torch.Tensor, key_cache: torch.Ten
     return output
 
 
-def estimate_tile_counts(seq_len: int, config: TriangleMixConfig, block_m: int = DEFAULT_BLOCK_M,
-                         block_n: int = DEFAULT_BLOCK_N) -> tuple[int, int]:
-    """Theoretical ``(triangle, dense)`` full-prompt QK tile counts (reference kernel.py:492-522)."""
+def estimate_tile_counts(seq_len: int, config: TriangleMixConfig) -> tuple[int, int]:
+    """``(triangle, dense)`` key-tile counts of one KV head for a full prompt of
+    ``seq_len`` tokens run as one chunk, in this kernel's tiling.
+
+    The reference's helper (kernel.py:492-522) counts its own 32-row x
+    512-key tiles; here ``triangle`` is the plan this library launches
+    (``tpsa_make_plan``: 64-token blocks, 128- and 64-key tiles, the sink and
+    band edge of a sparse block in one composite tile) and ``dense`` the tiles
+    the same blocks would run over their whole causal prefix.
+    """
     if seq_len < 0:
         raise ValueError("seq_len must be non-negative")
-    if block_m <= 0 or block_n <= 0:
-        raise ValueError("block sizes must be positive")
-    tri = dense = 0
-    start = triangle_streaming_start(config)
-    for q_lo in range(0, seq_len, block_m):
-        q_hi = min(seq_len, q_lo + block_m)
-        dense += math.ceil(q_hi / block_n)
-        if q_hi <= start:
-            tri += math.ceil(q_hi / block_n)
-            continue
-        sink_tiles = math.ceil(config.sink_tokens / block_n)
-        local_lo = max(config.sink_tokens, q_lo - config.local_window)
-        tri += sink_tiles + max(0, math.ceil(q_hi / block_n) - local_lo // block_n)
-    return tri, dense
+    if (config.sink_tokens, config.local_window, config.last_rows) != (8, 512, 128):
+        raise ValueError("the kernel's geometry is sink 8, window 512, dense tail 128")
+    if seq_len == 0:
+        return 0, 0
+    triangle = _native.make_plan(seq_len, 0, seq_len, seq_len, 1, 148).total_tiles
+    dense = 0
+    for q_lo in range(0, seq_len, 64):
+        keys = -(-min(seq_len, q_lo + 64) // 64) * 64
+        dense += -(-keys // 128)
+    return triangle, dense

@@ -14,7 +14,7 @@ Outputs (next to this script):
   reference_cases.npz   reference outputs (float32) of the stored rows
   intervals.json        reference ``selected_intervals`` over a grid of rows
 
-Usage:  python tests/golden/make_golden.py [--reference /root/reference]
+Usage:  python tests/golden/make_golden.py --reference <reference checkout>
 """
 
 from __future__ import annotations
@@ -74,7 +74,8 @@ def pick_rows(case: dict) -> list[int]:
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", type=Path, default=Path("/root/reference"))
+    ap.add_argument("--reference", type=Path, required=True,
+                    help="root of the reference project checkout")
     args = ap.parse_args()
     ref = load_reference(args.reference)
     torch.set_num_threads(8)

@@ -227,3 +227,12 @@ def test_adapter_registers_the_reference_schemas(tm):
         "_C_ascend::npu_triangle_paged_sparse_attention" + args + out)
     assert str(torch.ops.trianglemix_reference.triangle_paged_sparse_attention.default._schema) == (
         "trianglemix_reference::triangle_paged_sparse_attention" + args + ") -> Tensor")
+
+
+def test_estimate_tile_counts_is_this_kernels_plan(tm):
+    cfg = tm.TriangleMixConfig(enabled=True, layer_indices=frozenset({1}))
+    tri, dense = tm.estimate_tile_counts(8192, cfg)
+    assert tri == tm._native.make_plan(8192, 0, 8192, 8192, 8, SM).total_tiles // 8
+    assert dense == sum(-(-(64 * (b + 1)) // 128) for b in range(128))
+    assert tri < dense
+    assert tm.estimate_tile_counts(0, cfg) == (0, 0)
