@@ -667,13 +667,228 @@ def run_ttft(args) -> None:
     print(json.dumps(line), flush=True)
 
 
-def workload_config(args) -> dict:
-    name = "prefill_8k" if args.seq_len == 8192 else f"prefill_{args.seq_len // 1024}k_q{args.query_tokens}"
-    return {"workload": name, "seq_len": args.seq_len, "query_tokens": args.query_tokens,
-            "query_start": args.seq_len - args.query_tokens, "prompt_len": args.seq_len,
-            "geometry": "Qwen3-8B attention (Hq=32, Hkv=8, D=128, page 128)",
-            "parallelism": f"kv-head partition x{args.gpus}", "layers_per_step": args.gpus,
+def workload_config(args, seq: int | None = None, tq: int | None = None) -> dict:
+    seq = args.seq_len if seq is None else seq
+    tq = args.query_tokens if tq is None else tq
+    name = "prefill_8k" if seq == 8192 and tq == 8192 else f"prefill_{seq // 1024}k_q{tq}"
+    world = args.gpus
+    return {"workload": name, "seq_len": seq, "query_tokens": tq, "query_start": seq - tq,
+            "prompt_len": seq, "geometry": "Qwen3-8B attention (Hq=32, Hkv=8, D=128, page 128)",
+            "parallelism": (f"kv-head partition x{world}: each rank runs its {KV_HEADS // world} "
+                            f"KV heads of the one layer" if world > 1 else "one GPU, all 8 KV heads"),
+            "layers_per_step": 1,
             "l2": "flushed between timed steps (256 MiB write)"}
+
+
+class Timer:
+    """Steps timed with CUDA events on the launching stream, L2 flushed
+    between steps (outside the events), clocks sampled during the timing."""
+
+    def __init__(self, tm, dev, local: int, world: int):
+        self.tm, self.dev, self.local, self.world = tm, dev, local, world
+        self.stream = torch.cuda.current_stream(dev)
+        self.flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+
+    def barrier(self):
+        if self.world > 1:
+            torch.distributed.barrier()
+
+    def max_over_ranks(self, ms: float) -> float:
+        if self.world == 1:
+            return ms
+        t = torch.tensor([ms], device=self.dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+    def all_ranks(self, ms: float) -> list[float]:
+        if self.world == 1:
+            return [ms]
+        t = torch.tensor([ms], device=self.dev)
+        out = [torch.empty_like(t) for _ in range(self.world)]
+        torch.distributed.all_gather(out, t)
+        return [float(x.item()) for x in out]
+
+    def run(self, step, steps: int, warmup: int) -> tuple[float, dict]:
+        """(mean ms per step on this rank, clocks during the timed steps)."""
+        for _ in range(warmup):
+            self.flush.fill_(1.0)
+            step()
+        torch.cuda.synchronize(self.dev)
+        status = self.tm._native.device_status(self.local)
+        if status:
+            raise RuntimeError(f"device status {status:#x} after warm-up")
+        sampler = ClockSampler(self.local)
+        sampler.start()
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        self.barrier()
+        torch.cuda.synchronize(self.dev)
+        for i in range(steps):
+            self.flush.fill_(float(i))  # evict L2 between steps (outside the timed events)
+            starts[i].record(self.stream)
+            step()
+            ends[i].record(self.stream)
+        torch.cuda.synchronize(self.dev)
+        self.barrier()
+        clocks = sampler.stop()
+        status = self.tm._native.device_status(self.local)
+        if status:
+            raise RuntimeError(f"device status {status:#x} after timing")
+        times = [a.elapsed_time(b) for a, b in zip(starts, ends)]
+        return sum(times) / len(times), clocks
+
+
+def layer_flops(tq: int, seq: int) -> float:
+    return 4.0 * HEAD_DIM * QUERY_HEADS * effective_pairs(seq - tq, tq, seq, seq)
+
+
+def roofline_record(flops: float, kernel_ms: float, workload: str, heads: int,
+                    kernel: str) -> dict:
+    peaks, peak_kind = load_peaks()
+    achieved = flops / (kernel_ms * 1e-3) / 1e12
+    rec = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
+           "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"], "traffic": None,
+           "peak_source": f"{peak_kind} bf16_tflops (burst)", "kernel": kernel,
+           "kernel_ms": kernel_ms,
+           "algorithmic": "4*128*heads*pairs effective FLOPs per launch"}
+    traffic = profiled_traffic(workload, heads)
+    if traffic is not None:
+        rec["traffic"] = traffic["bytes"]
+        rec["traffic_unit"] = "bytes/launch (ncu dram read+write)"
+        rec["traffic_source"] = traffic["source"]
+    return rec
+
+
+def measure_layer(tm, timer: Timer, args, tq: int, seq: int, rank: int, world: int,
+                  e2e: bool) -> dict:
+    """One layer per step: the full 8-head layer on one GPU, or this rank's
+    8/N-KV-head slice of it (one tpsa_paged_attention_heads launch)."""
+    dev = timer.dev
+    q0 = seq - tq
+    heads = KV_HEADS // world
+    host = make_inputs(tq, seq, 0, rank, world)
+    q, k, v, table = (t.to(dev) for t in host)
+    out = torch.empty_like(q)
+    plan = tm._native.make_plan(tq, q0, seq, seq, heads, 0, SCALE)
+    ws = torch.empty(max(plan.workspace_bytes, 256), dtype=torch.uint8, device=dev)
+    stream = timer.stream
+
+    def launch(q_, k_, v_, t_, o_):
+        tm._native.paged_attention(q_, k_, v_, t_, o_, q0, seq, seq, SCALE,
+                                   kv_heads=heads if world > 1 else None, workspace=ws,
+                                   stream=stream.cuda_stream)
+
+    ms_rank, clocks = timer.run(lambda: launch(q, k, v, table, out), args.steps, args.warmup)
+    per_rank = timer.all_ranks(ms_rank)
+    ms = max(per_rank)
+    flops = layer_flops(tq, seq)
+    rec = {"workload": workload_config(args, seq, tq)["workload"], "ms_per_layer": ms,
+           "value": flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s (effective)",
+           "clocks": clocks,
+           "roofline": roofline_record(flops * heads / KV_HEADS, ms_rank,
+                                       workload_config(args, seq, tq)["workload"], heads,
+                                       "tpsa_paged_kernel<false, false>"),
+           "plan": {"grid": plan.grid, "items": plan.total_items, "split_tiles": plan.split_tiles,
+                    "tiles": plan.total_tiles}}
+    if world > 1:
+        rec["per_rank_kernel_ms"] = per_rank
+    if e2e:
+        rec["e2e"] = measure_e2e(tm, timer, args, host, launch, flops, world)
+    rec["_out"] = out
+    return rec
+
+
+def measure_e2e(tm, timer: Timer, args, host, launch, flops: float, world: int) -> dict:
+    """The same layer through the public API with pinned host buffers: every
+    step copies its inputs host -> device and its output back inside the
+    timing.  Steps are pipelined as a serving loop runs them: step i + 1's
+    inputs go up on a copy stream (into the other of two device buffers) while
+    step i computes and its output comes down."""
+    dev, stream = timer.dev, timer.stream
+    host = tuple(t.pin_memory() for t in host)
+    hout = torch.empty_like(host[0]).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in host)
+    d2h = hout.numel() * hout.element_size()
+    tq, seq = args.query_tokens, args.seq_len
+    q0 = seq - tq
+    if world == 1:
+        tm.load_adapter()
+    copy_stream = torch.cuda.Stream(dev)
+    dbufs = [tuple(torch.empty_like(t, device=dev) for t in host) for _ in range(2)]
+    ready = [torch.cuda.Event() for _ in range(2)]
+    free = [torch.cuda.Event() for _ in range(2)]
+    for ev in free:
+        ev.record(stream)
+
+    def e2e_step(i):
+        b = i % 2
+        with torch.cuda.stream(copy_stream):
+            copy_stream.wait_event(free[b])
+            for h, d in zip(host, dbufs[b]):
+                d.copy_(h, non_blocking=True)
+            ready[b].record(copy_stream)
+        stream.wait_event(ready[b])
+        dq, dk, dv, dt = dbufs[b]
+        if world == 1:
+            o = torch.ops.trianglemix_reference.triangle_paged_sparse_attention(
+                dq, dk, dv, dt, q0, seq, seq, SCALE)
+        else:
+            o = torch.empty_like(dq)
+            launch(dq, dk, dv, dt, o)
+        hout.copy_(o, non_blocking=True)
+        free[b].record(stream)
+
+    for i in range(args.warmup):
+        e2e_step(i)
+    torch.cuda.synchronize(dev)
+    timer.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    copy_stream.wait_event(e0)
+    for i in range(args.steps):
+        e2e_step(i)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = timer.max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    return {"value": flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s (effective)", "ms_per_step": ms,
+            "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
+            "path": ("torch.ops.trianglemix_reference.triangle_paged_sparse_attention"
+                     if world == 1 else
+                     "C ABI tpsa_paged_attention_heads, each rank its KV-head slice"),
+            "pipelining": "step i+1's H2D (copy stream, second device buffer) overlaps "
+                          "step i's kernel and D2H"}
+
+
+def measure_concurrent(tm, timer: Timer, args, rank: int, world: int) -> dict:
+    """N concurrent requests (one layer each) at tensor parallelism N: each rank
+    runs its 8/N KV heads of all N requests as one varlen launch over one page
+    pool, as a serving engine with one KV pool per layer would."""
+    dev = timer.dev
+    tq, seq = args.query_tokens, args.seq_len
+    heads = KV_HEADS // world
+    per_req = [make_inputs(tq, seq, j, rank, world) for j in range(world)]
+    pages = per_req[0][1].shape[0]
+    q = torch.cat([x[0] for x in per_req]).to(dev)
+    k = torch.cat([x[1] for x in per_req]).to(dev)
+    v = torch.cat([x[2] for x in per_req]).to(dev)
+    table = torch.cat([x[3] + j * pages for j, x in enumerate(per_req)]).to(dev)
+    out = torch.empty_like(q)
+    cu = [tq * j for j in range(world + 1)]
+    seqs = [seq] * world
+    ws = torch.empty(tm._native.varlen_workspace_size(cu, seqs, seqs, kv_heads=heads),
+                     dtype=torch.uint8, device=dev)
+
+    def step():
+        tm._native.paged_attention_varlen(q, k, v, table, out, cu, seqs, seqs, SCALE,
+                                          kv_heads=heads, workspace=ws,
+                                          stream=timer.stream.cuda_stream)
+
+    ms_rank, _ = timer.run(step, args.steps, args.warmup)
+    ms = timer.max_over_ranks(ms_rank)
+    return {"what": f"{world} concurrent requests of one layer at tensor parallelism {world}: "
+                    f"each rank its {heads} KV heads of every request, one varlen launch",
+            "ms_per_step": ms, "value": world * layer_flops(tq, seq) / (ms * 1e-3) / 1e12,
+            "unit": "TFLOP/s (effective, all requests)", "scaling": "weak"}
 
 
 def main() -> None:
@@ -687,6 +902,8 @@ def main() -> None:
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-32k", action="store_true",
+                    help="skip the second record (the last 8192-token chunk of a 32K prompt)")
     ap.add_argument("--batch", type=int, default=0,
                     help="BASELINE config 4: a packed batch of this many prompts (one GPU)")
     ap.add_argument("--crossover", action="store_true",
@@ -696,7 +913,7 @@ def main() -> None:
                     help="BASELINE config 2: Qwen3-8B prefill TTFT, TriangleMix layers against "
                          "all-dense (one GPU)")
     ap.add_argument("--validate", action="store_true",
-                    help="N > 1: all-gather the head slices of layer 0 over NCCL and compare "
+                    help="N > 1: all-gather the layer's head slices over NCCL and compare "
                          "them with a full-layer run on rank 0 (outside the timing)")
     args = ap.parse_args()
     if args.query_tokens is None:
@@ -739,194 +956,41 @@ def main() -> None:
         import torch.distributed as dist
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    timer = Timer(tm, dev, local, world)
     tq, seq = args.query_tokens, args.seq_len
-    q0 = seq - tq
-    heads_per_rank = KV_HEADS // world
-    layers = world  # weak scaling: N layers per step for N ranks
-    # Each rank: `layers` layers x its kv-head slice.  Distinct seeds per layer.
-    rank_inputs = []
-    for layer in range(layers):
-        q, k, v, table = make_inputs(tq, seq, layer, rank, world)
-        rank_inputs.append((q, k, v, table))
-    cu = [tq * j for j in range(layers + 1)]
-    seq_lens = [seq] * layers
-    if world > 1:
-        # The rank's head slices of its N layers live in one page pool (layer
-        # j's pages after layer j - 1's, its block table offset to them) and
-        # run as the N requests of one launch, which is as large as a full
-        # 8-head layer on one GPU.
-        pages = rank_inputs[0][1].shape[0]
-        rank_inputs = [(torch.cat([x[0] for x in rank_inputs]),
-                        torch.cat([x[1] for x in rank_inputs]),
-                        torch.cat([x[2] for x in rank_inputs]),
-                        torch.cat([x[3] + j * pages for j, x in enumerate(rank_inputs)]))]
-    dev_inputs = [tuple(t.to(dev) for t in x) for x in rank_inputs]
-    outs = [torch.empty_like(x[0]) for x in dev_inputs]
-    plan = tm._native.make_plan(tq, q0, seq, seq, heads_per_rank, 0, SCALE)
-    if world > 1:
-        ws = torch.empty(tm._native.varlen_workspace_size(cu, seq_lens, seq_lens,
-                                                          kv_heads=heads_per_rank),
-                         dtype=torch.uint8, device=dev)
-    else:
-        ws = (torch.empty(plan.workspace_bytes, dtype=torch.uint8, device=dev)
-              if plan.workspace_bytes else None)
-    stream = torch.cuda.current_stream(dev)
-    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
-
-    def launch(q, k, v, table, out):
-        if world > 1:
-            tm._native.paged_attention_varlen(q, k, v, table, out, cu, seq_lens, seq_lens, SCALE,
-                                              kv_heads=heads_per_rank, workspace=ws,
-                                              stream=stream.cuda_stream)
-        else:
-            tm._native.paged_attention(q, k, v, table, out, q0, seq, seq, SCALE,
-                                       workspace=ws, stream=stream.cuda_stream)
-
-    def step():
-        for (q, k, v, table), out in zip(dev_inputs, outs):
-            launch(q, k, v, table, out)
-
-    def barrier():
-        if world > 1:
-            torch.distributed.barrier()
-
-    for _ in range(args.warmup):
-        flush.fill_(1.0)
-        step()
-    torch.cuda.synchronize(dev)
-    status = tm._native.device_status(local)
-    if status:
-        raise RuntimeError(f"device status {status:#x} after warm-up")
-
-    sampler = ClockSampler(local)
-    sampler.start()
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    barrier()
-    torch.cuda.synchronize(dev)
-    for i in range(args.steps):
-        flush.fill_(float(i))  # evict L2 between steps (outside the timed events)
-        starts[i].record(stream)
-        step()
-        ends[i].record(stream)
-    torch.cuda.synchronize(dev)
-    barrier()
-    clocks = sampler.stop()
-    times = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    ms_rank = sum(times) / len(times)
-    kernel_ms = ms_rank  # one launch per step on every rank
-    if world > 1:
-        t = torch.tensor([ms_rank], device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms_step = float(t.item())
-    else:
-        ms_step = ms_rank
-    pairs = effective_pairs(q0, tq, seq, seq)
-    flops_layer = 4.0 * HEAD_DIM * QUERY_HEADS * pairs  # all 32 heads
-    value = flops_layer * layers / (ms_step * 1e-3) / 1e12
-
-    # End to end through the public API with pinned host buffers: at N = 1 the
-    # reference-facing torch op on the full layer; at N > 1 each rank's head
-    # slices through the C ABI (tpsa_paged_attention_heads).  Every step
-    # copies the inputs host -> device and the output back inside the timing.
-    e2e = None
-    if not args.no_e2e:
-        host = [tuple(t.pin_memory() for t in x) for x in rank_inputs]
-        houts = [torch.empty_like(x[0]).pin_memory() for x in host]
-        h2d = sum(t.numel() * t.element_size() for x in host for t in x)
-        d2h = sum(o.numel() * o.element_size() for o in houts)
-        if world == 1:
-            tm.load_adapter()
-
-        # Steps are pipelined as a serving loop would run them: step i + 1's
-        # inputs go host -> device on a copy stream (into the other of two
-        # device buffers) while step i computes and its output comes back on
-        # the launching stream; the two directions use separate copy engines.
-        copy_stream = torch.cuda.Stream(dev)
-        dbufs = [[tuple(torch.empty_like(t, device=dev) for t in x) for x in host]
-                 for _ in range(2)]
-        ready = [torch.cuda.Event() for _ in range(2)]
-        free = [torch.cuda.Event() for _ in range(2)]
-        for ev in free:
-            ev.record(stream)
-
-        def e2e_step(i):
-            b = i % 2
-            with torch.cuda.stream(copy_stream):
-                copy_stream.wait_event(free[b])
-                for (hq, hk, hv, ht), dbuf in zip(host, dbufs[b]):
-                    for h, d in zip((hq, hk, hv, ht), dbuf):
-                        d.copy_(h, non_blocking=True)
-                ready[b].record(copy_stream)
-            stream.wait_event(ready[b])
-            for (dq, dk, dv, dt), hout in zip(dbufs[b], houts):
-                if world == 1:
-                    o = torch.ops.trianglemix_reference.triangle_paged_sparse_attention(
-                        dq, dk, dv, dt, q0, seq, seq, SCALE)
-                else:
-                    o = torch.empty_like(dq)
-                    launch(dq, dk, dv, dt, o)
-                hout.copy_(o, non_blocking=True)
-            free[b].record(stream)
-
-        for i in range(args.warmup):
-            e2e_step(i)
-        torch.cuda.synchronize(dev)
-        barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        copy_stream.wait_event(e0)
-        for i in range(args.steps):
-            e2e_step(i)
-        e1.record(stream)
-        torch.cuda.synchronize(dev)
-        e2e_ms = e0.elapsed_time(e1) / args.steps
-        if world > 1:
-            t = torch.tensor([e2e_ms], device=dev)
-            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-            e2e_ms = float(t.item())
-        e2e = {"value": flops_layer * layers / (e2e_ms * 1e-3) / 1e12,
-               "unit": "TFLOP/s (effective)", "ms_per_step": e2e_ms,
-               "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
-               "path": ("torch.ops.trianglemix_reference.triangle_paged_sparse_attention"
-                        if world == 1 else
-                        "C ABI tpsa_paged_attention_varlen_heads, one launch per rank"),
-               "pipelining": "step i+1's H2D (copy stream, second device buffer) overlaps "
-                             "step i's kernel and D2H"}
+    # Headline: one layer per step (on N GPUs, split by KV head: strong scaling).
+    head = measure_layer(tm, timer, args, tq, seq, rank, world, e2e=not args.no_e2e)
+    out = head.pop("_out")
     check = None
     if args.validate and world > 1:
-        check = validate_shards(tm, rank, world, dev, outs[0][:tq], q0, seq, tq)
-    status = tm._native.device_status(local)
-    if status:
-        raise RuntimeError(f"device status {status:#x} after timing")
+        check = validate_shards(tm, rank, world, dev, out, seq - tq, seq, tq)
+    del out
+    points = []
+    if not args.no_32k and (seq, tq) == (8192, 8192):
+        # The "@32K" point of the metric: the last 8192-token chunk of a
+        # 32768-token prompt, measured the same way.
+        p32 = measure_layer(tm, timer, args, 8192, 32768, rank, world, e2e=False)
+        p32.pop("_out")
+        points.append(p32)
+    concurrent = measure_concurrent(tm, timer, args, rank, world) if world > 1 else None
 
-    peaks, peak_kind = load_peaks()
-    achieved = flops_layer * layers * heads_per_rank / KV_HEADS / (kernel_ms * 1e-3) / 1e12
-    roofline = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
-                "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
-                "traffic": None,
-                "peak_source": f"{peak_kind} bf16_tflops (burst)",
-                "kernel": "tpsa_paged_kernel<false, false>" if world == 1 else
-                          "tpsa_paged_kernel<false, true> (layers x head slice per launch)",
-                "kernel_ms": kernel_ms,
-                "algorithmic": "4*128*heads*pairs effective FLOPs per launch"}
-    traffic = profiled_traffic(workload_config(args)["workload"], heads_per_rank * layers)
-    if traffic is not None:
-        roofline["traffic"] = traffic["bytes"]
-        roofline["traffic_unit"] = "bytes/launch (ncu dram read+write)"
-        roofline["traffic_source"] = traffic["source"]
-    line = {"metric": METRIC, "value": value, "unit": "TFLOP/s (effective)", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
-            "ms_per_layer": ms_step / layers, "higher_is_better": True, "scaling": "weak",
+    line = {"metric": METRIC, "value": head["value"], "unit": "TFLOP/s (effective)",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": head["ms_per_layer"], "ms_per_layer": head["ms_per_layer"],
+            "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) bf16)",
             "config": workload_config(args), "gpu_launches": args.steps,
-            "clocks": clocks, "roofline": roofline, "e2e": e2e,
-            "plan": {"grid": plan.grid, "items": plan.total_items, "split_tiles": plan.split_tiles,
-                     "tiles": plan.total_tiles}}
+            "clocks": head["clocks"], "roofline": head["roofline"], "e2e": head.get("e2e"),
+            "plan": head["plan"]}
+    if world > 1:
+        line["per_rank_kernel_ms"] = head["per_rank_kernel_ms"]
+        line["concurrent_requests"] = concurrent
+    if points:
+        line["points"] = points
     if check is not None:
         line["validation"] = check
     if rank == 0 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(tq, seq, q0, seq, args.cpu_budget)
+        line["cpu_baseline"] = cpu_baseline(tq, seq, seq - tq, seq, args.cpu_budget)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -321,6 +321,19 @@ TPSA_API tpsa_status tpsa_paged_attention_static_scratch(
  */
 TPSA_API tpsa_status tpsa_device_status(int32_t device, uint32_t* status_bits);
 
+/*
+ * Test hook for the bounded waits (no reference counterpart).  The next
+ * single-request launch on the calling thread (tpsa_paged_attention and its
+ * _heads / _visit / _static_scratch forms) runs in probe mode: in every CTA
+ * the scheduler waits on a barrier that nothing arrives on, with a limit of
+ * `limit_ns` instead of 1 s, before it claims any work.  The wait runs out,
+ * the kernel records TPSA_DEVICE_WAIT_TIMEOUT and every role leaves through
+ * its abort path; no load, MMA or output store is issued, so `out` keeps its
+ * contents.  The launch itself returns TPSA_OK; tpsa_device_status reports
+ * the bit.  limit_ns: 0 disarms, else 1000 (1 us) to 100000000 (100 ms).
+ */
+TPSA_API tpsa_status tpsa_debug_wait_probe(uint32_t limit_ns);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

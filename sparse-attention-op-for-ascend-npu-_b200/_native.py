@@ -44,6 +44,7 @@ EXPORTED_SYMBOLS = (
     "tpsa_paged_attention_varlen",
     "tpsa_varlen_workspace_size_heads",
     "tpsa_paged_attention_varlen_heads",
+    "tpsa_debug_wait_probe",
 )
 
 
@@ -115,6 +116,7 @@ def lib() -> ctypes.CDLL:
         h.tpsa_paged_attention_heads.argtypes = _ATTN + [_i32, _vp, _u64, _vp]
         h.tpsa_paged_attention_visit.argtypes = _ATTN + [_i32, _vp, _u64, _vp, _vp, _vp]
         h.tpsa_device_status.argtypes = [_i32, ctypes.POINTER(ctypes.c_uint32)]
+        h.tpsa_debug_wait_probe.argtypes = [ctypes.c_uint32]
         h.tpsa_paged_attention_static_scratch.argtypes = _ATTN + [_vp]
         _p64 = ctypes.POINTER(_i64)
         h.tpsa_varlen_workspace_size.argtypes = [_i32, _p64, _p64, _p64, ctypes.POINTER(_u64)]
@@ -130,7 +132,7 @@ def lib() -> ctypes.CDLL:
                      "tpsa_paged_attention_visit", "tpsa_device_status",
                      "tpsa_paged_attention_static_scratch", "tpsa_varlen_workspace_size",
                      "tpsa_paged_attention_varlen", "tpsa_varlen_workspace_size_heads",
-                     "tpsa_paged_attention_varlen_heads"):
+                     "tpsa_paged_attention_varlen_heads", "tpsa_debug_wait_probe"):
             getattr(h, name).restype = ctypes.c_int
         _LIB = h
         return h
@@ -217,6 +219,14 @@ def paged_attention_varlen(query, key_cache, value_cache, block_tables, out, cu_
         check(lib().tpsa_paged_attention_varlen(*common, *ws))
     else:
         check(lib().tpsa_paged_attention_varlen_heads(*common, kv_heads, *ws))
+
+
+def debug_wait_probe(limit_ns: int) -> None:
+    """Test hook: the next single-request launch on this thread waits, in
+    every CTA, on a barrier nothing arrives on with a limit of ``limit_ns``
+    before claiming work; it issues no load or store and leaves
+    TPSA_DEVICE_WAIT_TIMEOUT in the device status word.  0 disarms."""
+    check(lib().tpsa_debug_wait_probe(limit_ns))
 
 
 def device_status(device: int = 0) -> int:

@@ -141,6 +141,7 @@ enum BarId : uint32_t {
   kBarItemEmpty = kBarItemFull + 2,     // [2] item record consumed
   kBarTail = kBarItemEmpty + 2,         // V producer: a tail tile landed
   kBarDrain = kBarTail + 1,             // MMA issuer: all MMAs complete
+  kBarProbe = kBarDrain + 1,            // test hook: never arrived on
   kNumBars
 };
 // item_empty: K producer, V producer, MMA warp, 8 softmax warps.
@@ -190,6 +191,7 @@ struct KernelArgs {
   int32_t words_per_row;       // visit mode
   uint32_t* visited;           // visit mode
   unsigned long long* tiles;   // visit mode: [tiles, keys]
+  uint32_t probe_wait_ns;      // test hook (0 = off): see scheduler_role
 };
 
 
@@ -234,15 +236,17 @@ __device__ __forceinline__ void note_timeout(uint32_t addr, uint32_t arg) {
 
 
 
-// Bounded wait: gives up after kWaitTimeoutNs or as soon as another role of
-// this CTA has aborted; on timeout records TPSA_DEVICE_WAIT_TIMEOUT.
+// Bounded wait: gives up after limit_ns or as soon as another role of this
+// CTA has aborted; on timeout it sets the CTA's abort flag and records
+// TPSA_DEVICE_WAIT_TIMEOUT.
 __device__ __forceinline__ bool wait_bar_slow(uint32_t bar, uint32_t parity,
-                                           volatile int* abort_flag) {
+                                           volatile int* abort_flag,
+                                           uint64_t limit_ns = kWaitTimeoutNs) {
   const uint64_t t0 = ptx::globaltimer_ns();
   while (true) {
     if (ptx::mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (ptx::globaltimer_ns() - t0 > kWaitTimeoutNs) {
+    if (ptx::globaltimer_ns() - t0 > limit_ns) {
       *abort_flag = 1;
       raise_status(TPSA_DEVICE_WAIT_TIMEOUT);
       TPSA_NOTE_TIMEOUT(bar, parity);
@@ -464,9 +468,19 @@ __device__ __forceinline__ bool tile_narrow(uint32_t narrow, int32_t j, int32_t 
 // finished the item two before it: a CTA then holds at most the item it
 // runs and the next one, so CTAs finish the launch within about one item of
 // each other.
+//
+// Test hook (probe_wait_ns != 0): before claiming anything, the scheduler
+// waits on kBarProbe, which nothing arrives on, with that short limit.  The
+// wait runs out, sets the abort flag and TPSA_DEVICE_WAIT_TIMEOUT; the other
+// roles, all still waiting for their first item record, leave through their
+// abort paths.  No item is claimed, so no load, MMA or store is ever issued.
 template <bool kVarlen>
 __device__ void scheduler_role(const KernelArgs& a, const Smem& sh) {
   const tpsa_plan& p = a.plan;
+  if (a.probe_wait_ns != 0) {
+    wait_bar_slow(sh.bar(kBarProbe), 0, sh.abort_flag(), a.probe_wait_ns);
+    return;
+  }
   for (uint32_t n = 0;; ++n) {
     const uint32_t slot = n % 2;
     if (!wait(sh, sh.bar(kBarItemEmpty + slot), ((n / 2) & 1) ^ 1)) break;
@@ -1333,6 +1347,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     }
     ptx::mbar_init(sh.bar(kBarTail), 1);
     ptx::mbar_init(sh.bar(kBarDrain), 1);
+    ptx::mbar_init(sh.bar(kBarProbe), 1);
     *sh.abort_flag() = 0;
     for (uint32_t i = 0; i < 4; ++i) {
       *reinterpret_cast<volatile uint32_t*>(sh.base + kOffCounters + 4 * i) = 0;
@@ -1381,6 +1396,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 
 // ================================================================ host side
 thread_local std::string t_last_error;
+// Test hook armed by tpsa_debug_wait_probe: the limit of the probe wait of
+// the next launch on this thread (0 = none).
+thread_local uint32_t t_probe_wait_ns = 0;
 
 tpsa_status fail(tpsa_status s, const std::string& msg) {
   t_last_error = "[TPSA] " + msg;
@@ -1673,6 +1691,8 @@ tpsa_status launch(const void* query, const void* key_cache, const void* value_c
   args.visited = visited;
   args.tiles = reinterpret_cast<unsigned long long*>(tile_counter);
   args.words_per_row = (p.seq_len + 31) / 32;
+  args.probe_wait_ns = t_probe_wait_ns;
+  t_probe_wait_ns = 0;
 
   if (visited != nullptr || tile_counter != nullptr) {
     tpsa_paged_kernel<true, false><<<p.grid, kNumThreads, kSmemBytes, s>>>(args, tq, tk128, tk64,
@@ -2143,6 +2163,15 @@ TPSA_API uint32_t tpsa_debug_trace(uint32_t role, unsigned long long* out, uint3
   return c;
 }
 #endif
+
+tpsa_status tpsa_debug_wait_probe(uint32_t limit_ns) {
+  t_last_error.clear();
+  if (limit_ns != 0 && (limit_ns < 1000u || limit_ns > 100000000u)) {
+    return fail(TPSA_ERR_INVALID_ARGUMENT, "probe limit must be 0 or in [1 us, 100 ms]");
+  }
+  t_probe_wait_ns = limit_ns;
+  return TPSA_OK;
+}
 
 tpsa_status tpsa_device_status(int32_t device, uint32_t* status_bits) {
   t_last_error.clear();

@@ -62,6 +62,16 @@ def test_scale_and_head_gates(tm):
             tm._native.make_plan(10, 0, 10, 10, kvh, SM)
 
 
+def test_wait_probe_limit_gate(tm):
+    """The test hook takes 0 (disarm) or a limit in [1 us, 100 ms]; arming
+    and disarming touch no device."""
+    for bad in (1, 999, 100_000_001, 2 ** 32 - 1):
+        with pytest.raises(tm.TpsaError, match="probe limit"):
+            tm._native.debug_wait_probe(bad)
+    tm._native.debug_wait_probe(200_000)
+    tm._native.debug_wait_probe(0)
+
+
 CASES = [
     (0, 1, 1, 1024), (0, 5, 5, 2048), (250, 5, 255, 2048), (519, 4, 523, 2048), (500, 65, 565, 2048),
     (766, 35, 801, 2048), (894, 4, 898, 1024), (1023, 1, 1024, 1024), (0, 4096, 4096, 4096),
