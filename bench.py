@@ -334,56 +334,119 @@ def run_batch(args) -> None:
 CROSSOVER_PROMPTS = ((2869, 512), (4096, 512), (6144, 512), (8192, 512), (8320, 2048))
 
 
-def dense_paged_attention(kind: str, tq: int, seq: int, dev):
-    """The stock dense path a non-selected layer takes: causal GQA attention
-    of one chunk over its whole cached context (bottom-right aligned: row i
-    of the chunk sees keys <= seq - tq + i).  Neither library reads 128-token
-    pages (FlashAttention-2's paged mode needs 256-token pages), so the
-    context is first gathered from the pages; the gather is part of the
-    timed call.  kind "fa2": flash_attn varlen; "sdpa": torch
-    scaled_dot_product_attention (backend chosen by torch).
-    Returns fn(q, k_cache, v_cache, table) -> out."""
-    npages = math.ceil(seq / PAGE)
+def flashinfer_paged_prefill(tq: int, seq: int, table, dev):
+    """FlashInfer's paged prefill over the same 128-token pages (NHD, the
+    BSND cache as is, no gather): causal, bottom-right aligned, GQA 4:1.
+    Planned once here; returns fn(q, k_cache, v_cache, out)."""
+    import flashinfer
 
-    def gather(k_cache, v_cache, table):
+    npages = math.ceil(seq / PAGE)
+    ws = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    wrapper = flashinfer.BatchPrefillWithPagedKVCacheWrapper(ws, "NHD")
+    i32 = dict(dtype=torch.int32, device=dev)
+    wrapper.plan(torch.tensor([0, tq], **i32), torch.tensor([0, npages], **i32),
+                 table[0, :npages].to(**i32).contiguous(),
+                 torch.tensor([seq - (npages - 1) * PAGE], **i32),
+                 QUERY_HEADS, KV_HEADS, HEAD_DIM, PAGE, causal=True, sm_scale=SCALE,
+                 q_data_type=torch.bfloat16, kv_data_type=torch.bfloat16)
+
+    def run(q, k_cache, v_cache, out):
+        wrapper.run(q, (k_cache, v_cache), out=out)
+        return out
+    return run
+
+
+def fa2_gathered(tq: int, seq: int, dev):
+    """flash_attn 2 varlen over the context gathered from the pages
+    (FlashAttention-2's own paged mode needs 256-token pages); the gather is
+    part of the timed call.  Returns fn(q, k_cache, v_cache, table)."""
+    from flash_attn import flash_attn_varlen_func
+
+    npages = math.ceil(seq / PAGE)
+    cu_q = torch.tensor([0, tq], dtype=torch.int32, device=dev)
+    cu_k = torch.tensor([0, seq], dtype=torch.int32, device=dev)
+
+    def run(q, k_cache, v_cache, table):
         pages = table[0, :npages].long()
         kc = k_cache.index_select(0, pages).reshape(-1, KV_HEADS, HEAD_DIM)[:seq]
         vc = v_cache.index_select(0, pages).reshape(-1, KV_HEADS, HEAD_DIM)[:seq]
-        return kc, vc
-
-    if kind == "fa2":
-        from flash_attn import flash_attn_varlen_func
-
-        cu_q = torch.tensor([0, tq], dtype=torch.int32, device=dev)
-        cu_k = torch.tensor([0, seq], dtype=torch.int32, device=dev)
-
-        def run(q, k_cache, v_cache, table):
-            kc, vc = gather(k_cache, v_cache, table)
-            return flash_attn_varlen_func(q, kc, vc, cu_q, cu_k, tq, seq, softmax_scale=SCALE,
-                                          causal=True)
-        return run
-
-    from torch.nn.attention.bias import causal_lower_right
-    import torch.nn.functional as F
-
-    mask = causal_lower_right(tq, seq)
-
-    def run(q, k_cache, v_cache, table):
-        kc, vc = gather(k_cache, v_cache, table)
-        o = F.scaled_dot_product_attention(q.transpose(0, 1).unsqueeze(0),
-                                           kc.transpose(0, 1).unsqueeze(0),
-                                           vc.transpose(0, 1).unsqueeze(0),
-                                           attn_mask=mask, scale=SCALE, enable_gqa=True)
-        return o[0].transpose(0, 1)
+        return flash_attn_varlen_func(q, kc, vc, cu_q, cu_k, tq, seq, softmax_scale=SCALE,
+                                      causal=True)
     return run
+
+
+def stock_dense(tq: int, seq: int, table, dev) -> tuple[str, object]:
+    """The dense paged attention a non-selected layer takes: FlashInfer's
+    paged prefill at page 128 when it builds on this box, else flash_attn 2
+    over the gathered context.  Returns (name, fn(q, k_cache, v_cache, table))."""
+    try:
+        fi = flashinfer_paged_prefill(tq, seq, table, dev)
+        return "flashinfer_p128", lambda q, k, v, t: fi(q, k, v, torch.empty_like(q))
+    except Exception:  # the flash_attn path is the recorded fallback
+        fa2 = fa2_gathered(tq, seq, dev)
+        return "fa2_gathered", fa2
+
+
+class CallTimer:
+    """Device time of one call: replayed from a CUDA graph (host launch cost
+    kept out) when the call can be captured, else launched eagerly; L2 is
+    flushed (256 MiB write) before every timed call, outside its events."""
+
+    def __init__(self, dev, errors: list):
+        self.dev = dev
+        self.stream = torch.cuda.current_stream(dev)
+        self.flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+        self.errors = errors
+
+    def prepare(self, name: str, fn, warmup: int):
+        side = torch.cuda.Stream(self.dev)
+        side.wait_stream(self.stream)
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                fn()
+        self.stream.wait_stream(side)
+        torch.cuda.synchronize(self.dev)
+        graph = torch.cuda.CUDAGraph()
+        try:
+            with torch.cuda.graph(graph):
+                fn()
+            torch.cuda.synchronize(self.dev)
+            return ("graph", graph)
+        except RuntimeError as exc:
+            self.errors.append(f"{name}: not captured ({str(exc).splitlines()[0]}); timed eagerly")
+            torch.cuda.synchronize(self.dev)
+            return ("eager", fn)
+
+    def sample(self, prepared, iterations: int) -> float:
+        kind, obj = prepared
+        call = obj.replay if kind == "graph" else obj
+        events = []
+        for i in range(iterations):
+            self.flush.fill_(float(i))
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(self.stream)
+            call()
+            e1.record(self.stream)
+            events.append((e0, e1))
+        torch.cuda.synchronize(self.dev)
+        ms = sorted(a.elapsed_time(b) for a, b in events)
+        return ms[len(ms) // 2]
 
 
 def run_crossover(args) -> None:
     """BASELINE config 1 on one GPU: every chunk of each chunked prefill timed
-    through this library (C ABI, batch-one) and through the dense baseline on
-    the same inputs; the planner's quantities per chunk (sparse rows, saved
-    QK pairs per head, reference kernel.py:185-269) beside the two times, so
-    that the direct-route thresholds can be calibrated for B200."""
+    through this library (C ABI, batch-one) against dense causal paged
+    attention on the same inputs.  Comparators: FlashInfer's paged prefill at
+    page 128 (the stock dense paged attention of a serving engine on B200),
+    this kernel's all-dense control (tpsa_paged_attention_dense), and
+    flash_attn 2 over a gathered context.  Arms are timed in alternating
+    order (ABCD on even repeats, DCBA on odd ones, the reference crossover's
+    AB/BA scheme, operator/tests/npu_v2_crossover.py:233-305); each cell
+    reports medians, the robust bound min(dense) / max(sparse), and the
+    planner's quantities (sparse rows, saved QK pairs per head, reference
+    kernel.py:185-269) so the direct-route thresholds can be calibrated."""
+    import statistics
+
     from __graft_entry__ import load_package
 
     tm = load_package()
@@ -391,110 +454,109 @@ def run_crossover(args) -> None:
     cfg = kernel.TriangleMixConfig(enabled=True, layer_indices=frozenset())
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    stream = torch.cuda.current_stream(dev)
-    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
     errors: list[str] = []
-
-    def timed(fn) -> float | None:
-        """Median device time of one call, replayed from a CUDA graph so that
-        host launch overhead stays out of it; None if the call cannot be
-        captured (its error is recorded)."""
-        side = torch.cuda.Stream(dev)
-        side.wait_stream(stream)
-        with torch.cuda.stream(side):
-            for _ in range(args.warmup):
-                fn()
-        stream.wait_stream(side)
-        torch.cuda.synchronize(dev)
-        graph = torch.cuda.CUDAGraph()
-        try:
-            with torch.cuda.graph(graph):
-                fn()
-        except RuntimeError as exc:
-            errors.append(str(exc).splitlines()[0])
-            torch.cuda.synchronize(dev)
-            return None
-        for _ in range(3):
-            flush.fill_(1.0)
-            graph.replay()
-        torch.cuda.synchronize(dev)
-        ms = []
-        for i in range(args.steps):
-            flush.fill_(float(i))
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            graph.replay()
-            e1.record(stream)
-            torch.cuda.synchronize(dev)
-            ms.append(e0.elapsed_time(e1))
-        ms.sort()
-        del graph
-        return ms[len(ms) // 2]
-
+    timer = CallTimer(dev, errors)
+    repeats = max(2, args.repeats)
+    iterations = max(3, args.steps)
     rows = []
     sampler = ClockSampler(0)
     sampler.start()
+    cell = 0
     for prompt, chunk in CROSSOVER_PROMPTS:
         q, k, v, table = make_inputs(prompt, prompt, seed=0)
         qd, kd, vd, td = q.to(dev), k.to(dev), v.to(dev), table.to(dev)
-        out = torch.empty_like(qd)
+        out_s, out_d, out_f = (torch.empty_like(qd) for _ in range(3))
         per_prompt = {"prompt_len": prompt, "chunk": chunk, "chunks": []}
         for q0 in range(0, prompt, chunk):
             tq = min(chunk, prompt - q0)
             seq = q0 + tq
             span = kernel.triangle_sparse_span(query_len=tq, seq_len=seq, prompt_len=prompt,
                                                config=cfg)
-            ws = torch.empty(tm._native.make_plan(tq, q0, seq, prompt).workspace_bytes,
-                             dtype=torch.uint8, device=dev)
-            qc, oc = qd[q0:seq], out[q0:seq]
-
-            def sparse_call():
-                tm._native.paged_attention(qc, kd, vd, td, oc, q0, seq, prompt, SCALE,
-                                           workspace=ws)
-
-            ms_sparse = timed(sparse_call)
-            fa2 = dense_paged_attention("fa2", tq, seq, dev)
-            sdpa = dense_paged_attention("sdpa", tq, seq, dev)
-            ms_fa2 = timed(lambda: fa2(qc, kd, vd, td))
-            ms_sdpa = timed(lambda: sdpa(qc, kd, vd, td))
-            dense_ms = [m for m in (ms_fa2, ms_sdpa) if m is not None]
-            ms_dense = min(dense_ms) if dense_ms else float("inf")
-            per_prompt["chunks"].append({
-                "query_start": q0, "query_len": tq, "seq_len": seq,
-                "sparse_rows": span.sparse_rows, "saved_qk": span.saved_qk,
-                "split": span.is_split, "ms_sparse": ms_sparse, "ms_dense": ms_dense,
-                "ms_dense_fa2": ms_fa2, "ms_dense_sdpa": ms_sdpa,
-                "eligible_reference_thresholds": kernel.triangle_direct_eligible(
-                    query_len=tq, seq_len=seq, prompt_len=prompt, config=cfg)})
-        c = per_prompt["chunks"]
-        per_prompt["ms_sparse_all"] = sum(x["ms_sparse"] for x in c)
-        per_prompt["ms_dense_all"] = sum(x["ms_dense"] for x in c)
-        per_prompt["ms_routed"] = sum(min(x["ms_sparse"], x["ms_dense"]) if x["sparse_rows"]
-                                      else x["ms_dense"] for x in c)
+            ws_s = torch.empty(max(256, tm._native.make_plan(tq, q0, seq, prompt).workspace_bytes),
+                               dtype=torch.uint8, device=dev)
+            ws_d = torch.empty(max(256, tm._native.dense_workspace_size(tq, q0, seq)),
+                               dtype=torch.uint8, device=dev)
+            qc = qd[q0:seq]
+            os_, od, of = out_s[q0:seq], out_d[q0:seq], out_f[q0:seq]
+            arms = {
+                "sparse": lambda: tm._native.paged_attention(qc, kd, vd, td, os_, q0, seq, prompt,
+                                                             SCALE, workspace=ws_s),
+                "dense_own": lambda: tm._native.paged_attention_dense(qc, kd, vd, td, od, q0, seq,
+                                                                      SCALE, workspace=ws_d),
+            }
+            try:
+                fi = flashinfer_paged_prefill(tq, seq, td, dev)
+                arms["flashinfer_p128"] = lambda: fi(qc, kd, vd, of)
+            except Exception as exc:  # recorded; the other arms still run
+                if not any(e.startswith("flashinfer") for e in errors):
+                    errors.append(f"flashinfer: {type(exc).__name__}: {str(exc).splitlines()[0]}")
+            try:
+                fa2 = fa2_gathered(tq, seq, dev)
+                arms["fa2_gathered"] = lambda: fa2(qc, kd, vd, td)
+            except Exception as exc:
+                if not any(e.startswith("flash_attn") for e in errors):
+                    errors.append(f"flash_attn: {type(exc).__name__}: {str(exc).splitlines()[0]}")
+            prepared = {n: timer.prepare(n, fn, args.warmup) for n, fn in arms.items()}
+            samples: dict[str, list[float]] = {n: [] for n in arms}
+            names = list(arms)
+            for r in range(repeats):
+                order = names if (cell + r) % 2 == 0 else names[::-1]
+                for n in order:
+                    samples[n].append(timer.sample(prepared[n], iterations))
+            cell += 1
+            med = {n: statistics.median(v) for n, v in samples.items()}
+            rec = {"query_start": q0, "query_len": tq, "seq_len": seq,
+                   "sparse_rows": span.sparse_rows, "saved_qk": span.saved_qk,
+                   "split": span.is_split, "ms": med,
+                   "timing": {n: prepared[n][0] for n in arms},
+                   "eligible_reference_thresholds": kernel.triangle_direct_eligible(
+                       query_len=tq, seq_len=seq, prompt_len=prompt, config=cfg)}
+            for n in arms:
+                if n != "sparse":
+                    rec[f"speedup_vs_{n}"] = med[n] / med["sparse"]
+                    rec[f"robust_vs_{n}"] = min(samples[n]) / max(samples["sparse"])
+            if "flashinfer_p128" in arms:
+                # Both dense arms compute the same causal attention.
+                d = (out_d[q0:seq].float() - out_f[q0:seq].float()).abs()
+                rec["dense_own_vs_flashinfer"] = {"max_abs": float(d.max()),
+                                                  "mean_abs": float(d.mean())}
+            per_prompt["chunks"].append(rec)
+            del prepared
+        for n in ("sparse", "dense_own", "flashinfer_p128", "fa2_gathered"):
+            if all(n in x["ms"] for x in per_prompt["chunks"]):
+                per_prompt[f"ms_{n}_all"] = sum(x["ms"][n] for x in per_prompt["chunks"])
         rows.append(per_prompt)
     clocks = sampler.stop()
     status = tm._native.device_status(0)
     if status:
         raise RuntimeError(f"device status {status:#x}")
-    chunks = [x for r in rows for x in r["chunks"] if x["sparse_rows"] > 0]
-    wins = [x for x in chunks if x["ms_sparse"] < x["ms_dense"]]
-    losses = [x for x in chunks if x["ms_sparse"] >= x["ms_dense"]]
-    # Smallest saved-QK threshold above which every measured chunk is faster
-    # through this library.
-    threshold = (max(x["saved_qk"] for x in losses) + 1) if losses else 0
+    stock = "flashinfer_p128" if all("flashinfer_p128" in x["ms"] for r in rows
+                                     for x in r["chunks"]) else "fa2_gathered"
+    calibration = {}
+    for ref_arm in (stock, "dense_own"):
+        chunks = [x for r in rows for x in r["chunks"] if x["sparse_rows"] > 0 and ref_arm in x["ms"]]
+        losses = [x for x in chunks if x["ms"]["sparse"] >= x["ms"][ref_arm]]
+        calibration[ref_arm] = {
+            "chunks_with_sparse_rows": len(chunks),
+            "sparse_faster": len(chunks) - len(losses),
+            "robust_sparse_faster": sum(1 for x in chunks if x[f"robust_vs_{ref_arm}"] > 1.0),
+            # Smallest saved-QK threshold above which every measured chunk
+            # is faster through this library.
+            "min_saved_qk_all_faster": (max(x["saved_qk"] for x in losses) + 1) if losses else 0,
+            "losing_chunks": [(x["query_start"], x["seq_len"], x["saved_qk"]) for x in losses]}
     line = {"metric": "TriangleMix chunked-prefill crossover (BASELINE config 1)",
-            "unit": "ms per prompt (sum over chunks)", "n_gpus": 1, "steps": args.steps,
-            "warmup": args.warmup, "data": "synthetic (seeded N(0,1) bf16)",
-            "dense_baseline": "faster of flash_attn 2 varlen and torch SDPA (causal bottom-right, "
-                              "GQA) over the context gathered from 128-token pages, gather timed",
-            "timing": "CUDA graph replay per call, L2 flushed between calls (256 MiB write), "
-                      "median of steps",
-            "errors": errors,
-            "clocks": clocks, "prompts": rows,
-            "calibration": {"chunks_with_sparse_rows": len(chunks), "sparse_faster": len(wins),
-                            "min_saved_qk_all_faster": threshold,
-                            "losing_chunks": [(x["query_start"], x["seq_len"], x["saved_qk"])
-                                              for x in losses]}}
+            "unit": "ms per call (median)", "n_gpus": 1, "iterations": iterations,
+            "repeats": repeats, "warmup": args.warmup, "data": "synthetic (seeded N(0,1) bf16)",
+            "stock_dense": stock,
+            "arms": {"sparse": "tpsa_paged_attention (TriangleMix key sets)",
+                     "dense_own": "tpsa_paged_attention_dense (same kernel, every row dense)",
+                     "flashinfer_p128": "flashinfer BatchPrefillWithPagedKVCacheWrapper, NHD, "
+                                        "page 128, causal",
+                     "fa2_gathered": "flash_attn 2 varlen over the context gathered from the "
+                                     "pages, gather timed"},
+            "timing": "per call: CUDA graph replay (else eager), L2 flushed before every call; "
+                      "sample = median of iterations; arms in alternating order per repeat",
+            "errors": errors, "clocks": clocks, "prompts": rows, "calibration": calibration}
     print(json.dumps(line), flush=True)
 
 
@@ -571,7 +633,8 @@ class Qwen3Prefill:
             x = self.embed[ids[p0:seq]]
             direct = kernel.triangle_direct_eligible(query_len=tq, seq_len=seq, prompt_len=prompt,
                                                      config=cfg)
-            dense = dense_paged_attention("fa2", tq, seq, dev)
+            dense_name, dense = stock_dense(tq, seq, self.table, dev)
+            counts["dense_kind"] = dense_name
             for li in range(c["layers"]):
                 lw = self.layers[li]
                 hdn = self.rmsnorm(x, self.norm_in[li])
@@ -623,7 +686,7 @@ def run_ttft(args) -> None:
                         generator=torch.Generator().manual_seed(0)).pin_memory()
 
     def one(mode: str) -> tuple[float, dict]:
-        counts = {"direct": 0, "dense": 0}
+        counts = {"direct": 0, "dense": 0, "dense_kind": None}
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize(dev)
         e0.record(stream)
@@ -659,7 +722,7 @@ def run_ttft(args) -> None:
                                 "MLP 12288, vocab 151936, QK-norm, RoPE 1e6)",
                        "prompt": TTFT_PROMPT, "chunk": TTFT_CHUNK, "triangle_layers": TTFT_LAYERS,
                        "thresholds": "b200 profile", "kv_cache": "paged, page 128, random table",
-                       "dense_attention": "flash_attn 2 varlen over the gathered paged context"},
+                       "dense_attention": counts["dense"].get("dense_kind")},
             "ttft_ms": {"triangle": med["triangle"], "dense": med["dense"],
                         "speedup": med["dense"] / med["triangle"]},
             "runs_ms": times, "attention_calls_per_prefill": counts, "clocks": clocks,
@@ -909,6 +972,8 @@ def main() -> None:
     ap.add_argument("--crossover", action="store_true",
                     help="BASELINE config 1: chunked-prefill sweep against the dense baseline "
                          "(one GPU)")
+    ap.add_argument("--repeats", type=int, default=5,
+                    help="--crossover: alternating-order repeats per chunk")
     ap.add_argument("--ttft", action="store_true",
                     help="BASELINE config 2: Qwen3-8B prefill TTFT, TriangleMix layers against "
                          "all-dense (one GPU)")

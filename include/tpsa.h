@@ -196,6 +196,25 @@ TPSA_API tpsa_status tpsa_paged_attention_heads(
     void* workspace, uint64_t workspace_bytes, void* stream);
 
 /*
+ * All-dense control: the same kernel and launch with no sparse rows, i.e.
+ * plain causal attention of the chunk over its whole paged context (row
+ * query_start + i reads keys [0, query_start + i]).  This is the dense
+ * comparator of the chunked-prefill crossover and of all-dense timing runs;
+ * no reference counterpart (the reference's dense path is the stock paged
+ * attention).  Arguments and gates are tpsa_paged_attention's without
+ * prompt_len; the workspace size comes from tpsa_dense_workspace_size.
+ */
+TPSA_API tpsa_status tpsa_dense_workspace_size(int64_t query_tokens, int64_t query_start,
+                                      int64_t seq_len, uint64_t* bytes);
+
+TPSA_API tpsa_status tpsa_paged_attention_dense(
+    const void* query, const void* key_cache, const void* value_cache,
+    const int32_t* block_table, void* out, int64_t query_tokens,
+    int64_t num_pages, int64_t table_cols, int64_t query_start,
+    int64_t seq_len, float scale, void* workspace, uint64_t workspace_bytes,
+    void* stream);
+
+/*
  * Packed ragged batch (varlen): `batch` requests whose query rows are packed
  * back to back, each computed exactly as one tpsa_paged_attention call on
  * its own rows.  Same semantics as the reference's packed-batch helper

@@ -45,6 +45,8 @@ EXPORTED_SYMBOLS = (
     "tpsa_varlen_workspace_size_heads",
     "tpsa_paged_attention_varlen_heads",
     "tpsa_debug_wait_probe",
+    "tpsa_dense_workspace_size",
+    "tpsa_paged_attention_dense",
 )
 
 
@@ -117,6 +119,9 @@ def lib() -> ctypes.CDLL:
         h.tpsa_paged_attention_visit.argtypes = _ATTN + [_i32, _vp, _u64, _vp, _vp, _vp]
         h.tpsa_device_status.argtypes = [_i32, ctypes.POINTER(ctypes.c_uint32)]
         h.tpsa_debug_wait_probe.argtypes = [ctypes.c_uint32]
+        h.tpsa_dense_workspace_size.argtypes = [_i64, _i64, _i64, ctypes.POINTER(_u64)]
+        h.tpsa_paged_attention_dense.argtypes = [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64,
+                                                 _i64, _f32, _vp, _u64, _vp]
         h.tpsa_paged_attention_static_scratch.argtypes = _ATTN + [_vp]
         _p64 = ctypes.POINTER(_i64)
         h.tpsa_varlen_workspace_size.argtypes = [_i32, _p64, _p64, _p64, ctypes.POINTER(_u64)]
@@ -132,7 +137,8 @@ def lib() -> ctypes.CDLL:
                      "tpsa_paged_attention_visit", "tpsa_device_status",
                      "tpsa_paged_attention_static_scratch", "tpsa_varlen_workspace_size",
                      "tpsa_paged_attention_varlen", "tpsa_varlen_workspace_size_heads",
-                     "tpsa_paged_attention_varlen_heads", "tpsa_debug_wait_probe"):
+                     "tpsa_paged_attention_varlen_heads", "tpsa_debug_wait_probe",
+                     "tpsa_dense_workspace_size", "tpsa_paged_attention_dense"):
             getattr(h, name).restype = ctypes.c_int
         _LIB = h
         return h
@@ -170,6 +176,30 @@ def workspace_size(query_tokens: int, query_start: int, seq_len: int, prompt_len
     out = _u64()
     check(lib().tpsa_workspace_size(query_tokens, query_start, seq_len, prompt_len, ctypes.byref(out)))
     return out.value
+
+
+def dense_workspace_size(query_tokens: int, query_start: int, seq_len: int) -> int:
+    out = _u64()
+    check(lib().tpsa_dense_workspace_size(query_tokens, query_start, seq_len, ctypes.byref(out)))
+    return out.value
+
+
+def paged_attention_dense(query, key_cache, value_cache, block_table, out, query_start: int,
+                          seq_len: int, scale: float, *, workspace=None, stream=None) -> None:
+    """The all-dense control (plain causal attention over the paged context)
+    through the C ABI; a workspace is allocated when none is given."""
+    import torch
+
+    if stream is None:
+        stream = torch.cuda.current_stream(query.device).cuda_stream
+    if workspace is None:
+        nbytes = dense_workspace_size(query.shape[0], query_start, seq_len)
+        workspace = torch.empty(nbytes, dtype=torch.uint8, device=query.device)
+    check(lib().tpsa_paged_attention_dense(
+        query.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(), block_table.data_ptr(),
+        out.data_ptr(), query.shape[0], key_cache.shape[0], block_table.shape[-1], query_start,
+        seq_len, scale, workspace.data_ptr(), workspace.numel() * workspace.element_size(),
+        stream))
 
 
 def _int64_array(values) -> ctypes.Array:

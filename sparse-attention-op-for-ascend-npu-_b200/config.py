@@ -38,11 +38,14 @@ def coerce_bool(value: object, *, name: str) -> bool:
 # Direct-route thresholds (planner gates, reference kernel.py:240-269) per
 # device.  "910b" holds the reference's values, calibrated on Ascend 910B3.
 # "b200" comes from the BASELINE config 1 sweep on one B200 (bench.py
-# --crossover): every chunk with sparse rows (181 to 2048 of them, 127 K to
-# 13.6 M skipped QK pairs per head) ran 2.0x to 14.5x faster through this
-# library than the faster of FlashAttention-2 and torch SDPA over the same
-# paged context, so no saved-pairs minimum is kept; chunks below 128 sparse
-# rows were not measured and keep the reference's floor.
+# --crossover, arms in alternating order): every chunk with sparse rows (181
+# to 2048 of them, 127 K to 13.6 M skipped QK pairs per head) ran 2.2x to
+# 21.7x faster through this library than FlashInfer's paged prefill over the
+# same 128-token pages, also by the robust bound min(dense) / max(sparse).
+# Against this kernel's own all-dense mode the only chunk without a gain is
+# the 309-row last chunk of a 2869-token prompt (181 sparse rows, 1.00x), so
+# no saved-pairs minimum is kept; chunks below 128 sparse rows were not
+# measured and keep the reference's floor.
 THRESHOLD_PROFILES: dict[str, dict[str, int]] = {
     "910b": {"min_seq_len": 0, "min_sparse_rows": 128, "min_saved_qk": 913_152,
              "split_min_sparse_rows": 192, "split_min_saved_qk": 1_299_264},

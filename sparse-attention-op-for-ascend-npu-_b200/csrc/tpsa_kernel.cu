@@ -1560,7 +1560,8 @@ tpsa_status encode_map(CUtensorMap* map, const void* base, uint64_t d1, uint64_t
 // request's own work (a varlen launch derives it from the whole launch).
 tpsa_status build_plan(int64_t query_tokens, int64_t query_start, int64_t seq_len,
                        int64_t prompt_len, int32_t kv_heads, int32_t ctas,
-                       float scale, tpsa_plan* p, int32_t split_override = 0) {
+                       float scale, tpsa_plan* p, int32_t split_override = 0,
+                       bool dense = false) {
   if (p == nullptr) return fail(TPSA_ERR_INVALID_ARGUMENT, "plan pointer is NULL");
   if (!(kv_heads == 1 || kv_heads == 2 || kv_heads == 4 || kv_heads == 8)) {
     return fail(TPSA_ERR_INVALID_ARGUMENT, "kv_heads must be 1, 2, 4 or 8");
@@ -1588,6 +1589,10 @@ tpsa_status build_plan(int64_t query_tokens, int64_t query_start, int64_t seq_le
   p->sparse_begin = kSparseBegin;
   const int64_t se = prompt_len - kDenseTail > 0 ? prompt_len - kDenseTail : 0;
   p->sparse_end = static_cast<int32_t>(se < seq_len ? se : seq_len);
+  // All-dense control: no sparse rows, every row reads [0, q].  Every block
+  // then counts as a dense-tail block (longest first, split when the
+  // counters allow).
+  if (dense) p->sparse_end = 0;
   p->kv_heads = kv_heads;
   p->num_blocks = ceil_div(p->query_tokens, kBlockQ);
   p->scale = scale;
@@ -1627,7 +1632,7 @@ tpsa_status launch(const void* query, const void* key_cache, const void* value_c
                    int64_t num_pages, int64_t table_cols, int64_t query_start,
                    int64_t seq_len, int64_t prompt_len, float scale, int32_t kv_heads,
                    void* workspace, uint64_t workspace_bytes, uint32_t* visited,
-                   uint64_t* tile_counter, void* stream) {
+                   uint64_t* tile_counter, void* stream, bool dense = false) {
   t_last_error.clear();
   if (query == nullptr || key_cache == nullptr || value_cache == nullptr ||
       block_table == nullptr || out == nullptr) {
@@ -1647,7 +1652,7 @@ tpsa_status launch(const void* query, const void* key_cache, const void* value_c
   KernelArgs args;
   std::memset(&args, 0, sizeof(args));
   st = build_plan(query_tokens, query_start, seq_len, prompt_len, kv_heads, dev->max_ctas,
-                  scale, &args.plan);
+                  scale, &args.plan, 0, dense);
   if (st != TPSA_OK) return st;
   const tpsa_plan& p = args.plan;
   if (workspace == nullptr || workspace_bytes < static_cast<uint64_t>(p.workspace_bytes)) {
@@ -2030,6 +2035,32 @@ tpsa_status tpsa_paged_attention(const void* query, const void* key_cache,
   return launch(query, key_cache, value_cache, block_table, out, query_tokens, num_pages,
                 table_cols, query_start, seq_len, prompt_len, scale, TPSA_KV_HEADS,
                 workspace, workspace_bytes, nullptr, nullptr, stream);
+}
+
+tpsa_status tpsa_dense_workspace_size(int64_t query_tokens, int64_t query_start,
+                                      int64_t seq_len, uint64_t* bytes) {
+  t_last_error.clear();
+  if (bytes == nullptr) return fail(TPSA_ERR_INVALID_ARGUMENT, "bytes pointer is NULL");
+  DeviceState* dev = nullptr;
+  tpsa_status st = device_state(&dev);
+  if (st != TPSA_OK) return st;
+  tpsa_plan p;
+  st = build_plan(query_tokens, query_start, seq_len, seq_len, TPSA_KV_HEADS, dev->max_ctas,
+                  1.0f, &p, 0, true);
+  if (st != TPSA_OK) return st;
+  *bytes = static_cast<uint64_t>(p.workspace_bytes);
+  return TPSA_OK;
+}
+
+tpsa_status tpsa_paged_attention_dense(const void* query, const void* key_cache,
+                                       const void* value_cache, const int32_t* block_table,
+                                       void* out, int64_t query_tokens, int64_t num_pages,
+                                       int64_t table_cols, int64_t query_start,
+                                       int64_t seq_len, float scale, void* workspace,
+                                       uint64_t workspace_bytes, void* stream) {
+  return launch(query, key_cache, value_cache, block_table, out, query_tokens, num_pages,
+                table_cols, query_start, seq_len, seq_len, scale, TPSA_KV_HEADS, workspace,
+                workspace_bytes, nullptr, nullptr, stream, true);
 }
 
 tpsa_status tpsa_varlen_workspace_size(int32_t batch, const int64_t* cu_seqlens_q,
