@@ -954,6 +954,50 @@ def measure_concurrent(tm, timer: Timer, args, rank: int, world: int) -> dict:
             "unit": "TFLOP/s (effective, all requests)", "scaling": "weak"}
 
 
+def run_rank_sweep(args) -> None:
+    """One GPU: the launch each rank of an N-GPU KV-head partition runs, for
+    N = 1, 2, 4, 8 (ranks 0 and N - 1; the slices are equal in work), at the
+    headline context and at 32K/q8K.  Predicts the strong-scaling headline
+    of `--gpus N` without N GPUs: the N-GPU step time is the max over ranks
+    of these launches."""
+    from __graft_entry__ import load_package
+
+    tm = load_package()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    timer = Timer(tm, dev, 0, 1)
+    rows = []
+    for seq, tq in ((args.seq_len, args.query_tokens), (32768, 8192)):
+        base = None
+        for world in (1, 2, 4, 8):
+            heads = KV_HEADS // world
+            per_rank = []
+            for rank in sorted({0, world - 1}):
+                q, k, v, table = (t.to(dev) for t in make_inputs(tq, seq, 0, rank, world))
+                out = torch.empty_like(q)
+                plan = tm._native.make_plan(tq, seq - tq, seq, seq, heads, 0, SCALE)
+                ws = torch.empty(max(plan.workspace_bytes, 256), dtype=torch.uint8, device=dev)
+
+                def step():
+                    tm._native.paged_attention(q, k, v, table, out, seq - tq, seq, seq, SCALE,
+                                               kv_heads=heads if world > 1 else None,
+                                               workspace=ws)
+
+                ms, clocks = timer.run(step, args.steps, args.warmup)
+                per_rank.append(ms)
+            ms = max(per_rank)
+            base = ms if world == 1 else base
+            rows.append({"workload": workload_config(args, seq, tq)["workload"], "n": world,
+                         "kv_heads_per_rank": heads, "ms_per_rank": per_rank,
+                         "value": layer_flops(tq, seq) / (ms * 1e-3) / 1e12,
+                         "efficiency": base / (world * ms), "items": plan.total_items,
+                         "split_tiles": plan.split_tiles, "clocks": clocks})
+    print(json.dumps({"metric": "KV-head partition: per-rank launch on one B200",
+                      "unit": "TFLOP/s (effective, whole layer)", "steps": args.steps,
+                      "warmup": args.warmup, "data": "synthetic (seeded N(0,1) bf16)",
+                      "rows": rows}), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -977,6 +1021,9 @@ def main() -> None:
     ap.add_argument("--ttft", action="store_true",
                     help="BASELINE config 2: Qwen3-8B prefill TTFT, TriangleMix layers against "
                          "all-dense (one GPU)")
+    ap.add_argument("--rank-sweep", action="store_true",
+                    help="one GPU: time the launch each rank of an N-GPU KV-head partition "
+                         "runs, N = 1, 2, 4, 8")
     ap.add_argument("--validate", action="store_true",
                     help="N > 1: all-gather the layer's head slices over NCCL and compare "
                          "them with a full-layer run on rank 0 (outside the timing)")
@@ -1008,6 +1055,11 @@ def main() -> None:
         if world != 1:
             ap.error("--batch runs on one GPU")
         run_batch(args)
+        return
+    if args.rank_sweep:
+        if world != 1:
+            ap.error("--rank-sweep runs on one GPU")
+        run_rank_sweep(args)
         return
 
     from __graft_entry__ import load_package

@@ -68,6 +68,17 @@ __device__ __forceinline__ void red_release_add_shared(uint32_t addr, uint32_t v
   asm volatile("red.release.cta.shared::cta.add.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
 }
 
+// Counters in global memory shared by CTAs: release add, acquire load.
+__device__ __forceinline__ void red_release_add_global(int32_t* addr, int32_t v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ int32_t ld_acquire_global(const int32_t* addr) {
+  int32_t v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+  return v;
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

@@ -142,6 +142,7 @@ enum BarId : uint32_t {
   kBarTail = kBarItemEmpty + 2,         // V producer: a tail tile landed
   kBarDrain = kBarTail + 1,             // MMA issuer: all MMAs complete
   kBarProbe = kBarDrain + 1,            // test hook: never arrived on
+  kBarPieceDone = kBarProbe + 1,        // softmax warps: a split piece merged
   kNumBars
 };
 // item_empty: K producer, V producer, MMA warp, 8 softmax warps.
@@ -192,6 +193,7 @@ struct KernelArgs {
   uint32_t* visited;           // visit mode
   unsigned long long* tiles;   // visit mode: [tiles, keys]
   uint32_t probe_wait_ns;      // test hook (0 = off): see scheduler_role
+  int32_t coop_merge;          // split pieces merge together (softmax_role)
 };
 
 
@@ -216,6 +218,15 @@ __device__ __forceinline__ void raise_status(uint32_t bits) {
 #ifdef TPSA_TRACE
 // Start and end (globaltimer ns) and items run of every CTA of the last launch.
 __device__ unsigned long long g_cta_span[1024][3];
+// Per CTA, softmax warpgroup and item (first 8): {idx | splits << 32,
+// globaltimer before taking the item, after taking it, after O is complete,
+// and for a split piece after its partial is written, after the wait for the
+// other pieces, after the merge}.
+__device__ unsigned long long g_item_trace[1024][2][8][8];
+#define TPSA_ITEM_REC(n, f, v)                                          \
+  do {                                                                  \
+    if (row == 0 && blockIdx.x < 1024 && (n) < 8) g_item_trace[blockIdx.x][x][n][f] = (v); \
+  } while (0)
 // First wait that gave up: {set, block, thread, shared offset, parity or target}.
 __device__ uint32_t g_timeout_site[5];
 extern __shared__ uint8_t smem_raw[];
@@ -231,6 +242,9 @@ __device__ __forceinline__ void note_timeout(uint32_t addr, uint32_t arg) {
 #else
 #define TPSA_NOTE_TIMEOUT(addr, arg) \
   do {                               \
+  } while (0)
+#define TPSA_ITEM_REC(n, f, v) \
+  do {                         \
   } while (0)
 #endif
 
@@ -292,6 +306,25 @@ __device__ __forceinline__ bool wait_count(const Smem& sh, uint32_t id, uint32_t
   const uint32_t addr = sh.counter(id);
   if (static_cast<int32_t>(ptx::ld_acquire_shared(addr) - target) >= 0) return true;
   return wait_count_slow(sh.abort_flag(), addr, target);
+}
+
+// Bounded wait until the global counter at `addr` (written by other CTAs
+// with release adds) reaches `target`; gives up like wait.  Polls back off
+// with a short sleep so that waiting CTAs do not flood the L2 slice.
+__device__ __noinline__ bool wait_global_count(const Smem& sh, const int32_t* addr,
+                                               int32_t target) {
+  const uint64_t t0 = ptx::globaltimer_ns();
+  while (ptx::ld_acquire_global(addr) < target) {
+    if (*sh.abort_flag()) return false;
+    if (ptx::globaltimer_ns() - t0 > kWaitTimeoutNs) {
+      *sh.abort_flag() = 1;
+      raise_status(TPSA_DEVICE_WAIT_TIMEOUT);
+      TPSA_NOTE_TIMEOUT(0u, static_cast<uint32_t>(target) | 0x80000000u);
+      return false;
+    }
+    __nanosleep(64);
+  }
+  return true;
 }
 
 __device__ __forceinline__ float mufu_exp2(float x) {
@@ -425,6 +458,8 @@ __device__ __forceinline__ ItemRec make_item_rec(const tpsa_plan& p, int32_t idx
 struct ItemBrief {
   int32_t idx, ntiles;
   uint32_t narrow;
+  bool piece;  // a split piece of a cooperative-merge launch: the scheduler
+               // publishes the next item only after this one is merged
 };
 
 __device__ __forceinline__ bool take_item(const Smem& sh, uint32_t n, ItemRec* rec) {
@@ -439,7 +474,8 @@ __device__ __forceinline__ bool take_item(const Smem& sh, uint32_t n, ItemRec* r
 
 // The fields of item record n the MMA issuer uses (index, tile count,
 // narrow-tile bits).
-__device__ __forceinline__ bool take_item_brief(const Smem& sh, uint32_t n, ItemBrief* b) {
+__device__ __forceinline__ bool take_item_brief(const Smem& sh, uint32_t n, ItemBrief* b,
+                                                bool coop) {
   const uint32_t slot = n % 2;
   if (!wait(sh, sh.bar(kBarItemFull + slot), (n / 2) & 1)) return false;
   const int32_t* w = reinterpret_cast<const int32_t*>(sh.item_slot(slot));
@@ -447,6 +483,7 @@ __device__ __forceinline__ bool take_item_brief(const Smem& sh, uint32_t n, Item
   b->ntiles = w[(offsetof(ItemRec, it) + offsetof(tpsa_item, tile_end)) / 4] -
               w[(offsetof(ItemRec, it) + offsetof(tpsa_item, tile_begin)) / 4];
   b->narrow = static_cast<uint32_t>(w[offsetof(ItemRec, narrow) / 4]);
+  b->piece = coop && w[(offsetof(ItemRec, it) + offsetof(tpsa_item, num_splits)) / 4] > 1;
   return true;
 }
 
@@ -481,6 +518,7 @@ __device__ void scheduler_role(const KernelArgs& a, const Smem& sh) {
     wait_bar_slow(sh.bar(kBarProbe), 0, sh.abort_flag(), a.probe_wait_ns);
     return;
   }
+  uint32_t piece_par = 0;
   for (uint32_t n = 0;; ++n) {
     const uint32_t slot = n % 2;
     if (!wait(sh, sh.bar(kBarItemEmpty + slot), ((n / 2) & 1) ^ 1)) break;
@@ -515,6 +553,12 @@ __device__ void scheduler_role(const KernelArgs& a, const Smem& sh) {
     for (int j = 0; j < 4; ++j) sh.item_slot(slot)[j] = words[j];
     ptx::mbar_arrive(sh.bar(kBarItemFull + slot));
     if (rec.idx >= p.total_items) break;
+    // A split piece waits for the other pieces of its block (softmax_role):
+    // claim nothing more until it is merged.
+    if (a.coop_merge && rec.it.num_splits > 1) {
+      if (!wait(sh, sh.bar(kBarPieceDone), piece_par)) break;
+      piece_par ^= 1u;
+    }
   }
 }
 
@@ -727,20 +771,21 @@ __device__ void mma_role(const KernelArgs& a, const Smem& sh, uint32_t tmem) {
   bool ok = true;
   // Current item.
   ItemBrief cur;
-  bool got = take_item_brief(sh, n_item, &cur);
+  bool got = take_item_brief(sh, n_item, &cur, a.coop_merge != 0);
   if (!__all_sync(0xffffffffu, got)) ok = false;
   __syncwarp();
   if (ok && (threadIdx.x & 31) == 0) release_item(sh, n_item);
   if (ok) ++n_item;
   bool done = !ok || cur.idx >= p.total_items;
   uint32_t q_iter = 0;
-  if (!done) {
-    // First QKs of the first item.
-    const int32_t nt = cur.ntiles;
-    const bool nar = tile_narrow(cur.narrow, 0, nt);
-    for (uint32_t x = 0; x < 2 && ok; ++x) {
-      if (!warp_wait(sh.bar(kBarQFull + x), 0)) { ok = false; break; }
-      if (x == 0 && !warp_wait(sh.bar(kBarKFull + ks), k_phase)) { ok = false; break; }
+  // First QKs of an item that no PV precedes: the launch's first item, and
+  // the item after a split piece.
+  auto first_qks = [&](const ItemBrief& it) -> bool {
+    const int32_t nt = it.ntiles;
+    const bool nar = tile_narrow(it.narrow, 0, nt);
+    for (uint32_t x = 0; x < 2; ++x) {
+      if (!warp_wait(sh.bar(kBarQFull + x), q_iter & 1)) return false;
+      if (x == 0 && !warp_wait(sh.bar(kBarKFull + ks), k_phase)) return false;
       ptx::tc_fence_after();
       issue_qk(x, ks, nar);
       commit(sh.bar(kBarSFull + x));
@@ -750,7 +795,9 @@ __device__ void mma_role(const KernelArgs& a, const Smem& sh, uint32_t tmem) {
     ks = (ks + 1) % kKRing;
     k_phase ^= ks == 0 ? 1u : 0u;
     ++q_iter;
-  }
+    return true;
+  };
+  if (!done) ok = first_qks(cur);
   while (ok && !done) {
     const int32_t nt = cur.ntiles;
     ItemBrief nxt;
@@ -765,8 +812,8 @@ __device__ void mma_role(const KernelArgs& a, const Smem& sh, uint32_t tmem) {
       if (has_next) {
         next_nar = tile_narrow(cur.narrow, j + 1, nt);
         next_last = j + 1 == nt - 1;
-      } else {
-        const bool g = take_item_brief(sh, n_item, &nxt);
+      } else if (!cur.piece) {
+        const bool g = take_item_brief(sh, n_item, &nxt, a.coop_merge != 0);
         if (!__all_sync(0xffffffffu, g)) { ok = false; break; }
         __syncwarp();
         if ((threadIdx.x & 31) == 0) release_item(sh, n_item);
@@ -816,6 +863,17 @@ __device__ void mma_role(const KernelArgs& a, const Smem& sh, uint32_t tmem) {
         k_phase ^= ks == 0 ? 1u : 0u;
         if (new_item) ++q_iter;
       }
+    }
+    if (ok && cur.piece) {
+      // The next item is published once this piece is merged, which needs
+      // its last PVs (issued above): take it only now.
+      const bool g = take_item_brief(sh, n_item, &nxt, a.coop_merge != 0);
+      if (!__all_sync(0xffffffffu, g)) break;
+      __syncwarp();
+      if ((threadIdx.x & 31) == 0) release_item(sh, n_item);
+      ++n_item;
+      nxt_valid = nxt.idx < p.total_items;
+      if (nxt_valid) ok = first_qks(nxt);
     }
     if (!ok || !nxt_valid) break;
     cur = nxt;
@@ -943,41 +1001,6 @@ __device__ __forceinline__ void prepare_chunk(uint32_t (&r)[32], bool mk, int32_
 }
 
 
-// Writes columns [col, col + 32) of the 32 output rows of a softmax warp as
-// bf16 (values times `scale`).  Each thread holds one row, and its 64 bytes
-// are one half of a 128-byte line of `out`; storing them directly would make
-// every store instruction touch 32 lines.  The warp instead passes the rows
-// through its 2 KB staging buffer (16-byte chunks XOR-swizzled so both the
-// writes and the reads are bank-conflict free) and each store instruction
-// then writes 64 contiguous bytes of 8 rows.  Warp row R is query token
-// base_q + R / 2, head base_h + R % 2; rows at or past query_tokens are not
-// written.  All 32 lanes must call this.
-__device__ __forceinline__ void store_rows_bf16(const float (&o)[32], float scale, uint8_t* stage,
-                                                int lane, __nv_bfloat16* out, int32_t base_q,
-                                                int32_t base_h, int32_t hq, int32_t query_tokens,
-                                                int32_t col) {
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const uint4 v = make_uint4(pack_bf16x2(o[8 * j] * scale, o[8 * j + 1] * scale),
-                               pack_bf16x2(o[8 * j + 2] * scale, o[8 * j + 3] * scale),
-                               pack_bf16x2(o[8 * j + 4] * scale, o[8 * j + 5] * scale),
-                               pack_bf16x2(o[8 * j + 6] * scale, o[8 * j + 7] * scale));
-    *reinterpret_cast<uint4*>(stage + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) = v;
-  }
-  __syncwarp();
-  const int c = lane & 3;
-#pragma unroll
-  for (int jj = 0; jj < 4; ++jj) {
-    const int rr = 8 * jj + (lane >> 2);
-    const uint4 v = *reinterpret_cast<const uint4*>(stage + rr * 64 + ((c ^ ((rr >> 1) & 3)) << 4));
-    const int32_t q = base_q + (rr >> 1);
-    if (q < query_tokens) {
-      *reinterpret_cast<uint4*>(out + (static_cast<size_t>(q) * hq + base_h + (rr & 1)) * kHeadDim +
-                                col + 8 * c) = v;
-    }
-  }
-  __syncwarp();
-}
 
 
 
@@ -1090,8 +1113,12 @@ __device__ void softmax_role(const KernelArgs& a, const Smem& sh, uint32_t tmem,
 
   for (uint32_t n_item = 0;; ++n_item) {
     ItemRec rec;
+    TPSA_ITEM_REC(n_item, 1, ptx::globaltimer_ns());
     const bool got = take_item(sh, n_item, &rec);
     if (!__all_sync(0xffffffffu, got)) break;
+    TPSA_ITEM_REC(n_item, 2, ptx::globaltimer_ns());
+    TPSA_ITEM_REC(n_item, 0, static_cast<unsigned long long>(rec.idx) |
+                                 (static_cast<unsigned long long>(rec.it.num_splits) << 32));
     __syncwarp();
     // The previous record is released only now that this warp has finished
     // that item, so the scheduler claims an item when the one two before it
@@ -1147,15 +1174,15 @@ __device__ void softmax_role(const KernelArgs& a, const Smem& sh, uint32_t tmem,
     o_par ^= 1;
     if (!__all_sync(0xffffffffu, w_ok)) break;
     ptx::tc_fence_after();
+    TPSA_ITEM_REC(n_item, 3, ptx::globaltimer_ns());
     if (tr) TPSA_TR(2 + x, 5, rec.idx);
     const bool split = it.num_splits > 1;
     const uint32_t sp_slot = split_items & 1;
     split_items += split ? 1u : 0u;
     // Output rows of this warp: packed token base_q + R / 2, head
-    // base_h + R % 2 for warp row R; rows at or past row_end are not written.
+    // base_h + R % 2 for warp row R (the tensor map clips rows past the end).
     const int32_t base_q = q_row0 + it.block * kBlockQ + quad * 16;
     const int32_t base_h = it.kv_head * kGroupSize + 2 * static_cast<int32_t>(x);
-    const int32_t row_end = q_row0 + pr.query_tokens;
     if (!split && (!kVarlen || bt.q_end - bt.q_begin == kBlockQ)) {
       // Two rounds of 64 columns: the warp's 32 rows into its staging
       // buffer as bf16 (128-byte swizzled rows, the layout the tensor map
@@ -1231,8 +1258,15 @@ __device__ void softmax_role(const KernelArgs& a, const Smem& sh, uint32_t tmem,
 
     // Split item: the fp32 partial (128 columns) into the item's column-major
     // slot ([128 columns][256 rows], then m[256] and l[256]; this tile's rows
-    // are 128 x + row); the last split of the block (per query tile) merges
-    // all partials and writes bf16.
+    // are 128 x + row).  Every piece of the block then merges a slice of the
+    // tile's rows: once all pieces have published their partials (a global
+    // counter per block, kv head and query tile reaches 4 warps x pieces),
+    // piece s merges rows [s r, (s + 1) r), r = ceil(128 / pieces), reading
+    // every piece's values of those rows only, so the merge and its L2
+    // traffic are spread over the pieces' CTAs.  The scheduler claims
+    // nothing while its CTA holds a split piece: a waiting piece's partners
+    // are running on other CTAs or not yet claimed, and the CTAs that hold
+    // no piece of a block with unclaimed pieces keep claiming.
     float* slot =
         a.scratch + static_cast<size_t>((kVarlen ? rq.slot_base : 0) + ridx) * kSlotFloats;
     constexpr int32_t kSlotRows = 2 * kRowsPerTile;
@@ -1250,53 +1284,128 @@ __device__ void softmax_role(const KernelArgs& a, const Smem& sh, uint32_t tmem,
     slot[(kHeadDim + 1) * kSlotRows + srow] = st.l_part;
     __threadfence();
     __syncwarp();
-    if (lane == 0) ptx::red_release_add_shared(sh.counter(cnt_w), 1);
-    if (row == 0) {
-      if (wait_count(sh, cnt_w, 4 * split_items)) {
-        int32_t* ctr = a.ctl + kCtlSplitBase + (kVarlen ? rq.ctr_base : 0) +
-                       ((it.block - pr.tail_block0) * p.kv_heads + it.kv_head) * 2 +
-                       static_cast<int32_t>(x);
-        const int prev = atomicAdd(ctr, 1);
-        split_last[sp_slot] = prev == it.num_splits - 1;
-        ptx::red_release_add_shared(sh.counter(cnt_d), 1);
+    TPSA_ITEM_REC(n_item, 4, ptx::globaltimer_ns());
+    const int32_t ns = it.num_splits;
+    int32_t* ctr = a.ctl + kCtlSplitBase + (kVarlen ? rq.ctr_base : 0) +
+                   ((it.block - pr.tail_block0) * p.kv_heads + it.kv_head) * 2 +
+                   static_cast<int32_t>(x);
+    int32_t slice = 0, rows_per = kRowsPerTile;
+    if (a.coop_merge) {
+      bool all_in = true;
+      if (lane == 0) {
+        ptx::red_release_add_global(ctr, 1);
+        all_in = wait_global_count(sh, ctr, 4 * ns);
+      }
+      if (!__all_sync(0xffffffffu, __shfl_sync(0xffffffffu, all_in, 0))) break;
+      __syncwarp();  // lane 0's acquire orders the other lanes' loads too
+      slice = it.split;
+      rows_per = (kRowsPerTile + ns - 1) / ns;
+      TPSA_ITEM_REC(n_item, 5, ptx::globaltimer_ns());
+    } else {
+      // The last piece to finish merges all rows of the tile.
+      if (lane == 0) ptx::red_release_add_shared(sh.counter(cnt_w), 1);
+      if (row == 0) {
+        if (wait_count(sh, cnt_w, 4 * split_items)) {
+          const int prev = atomicAdd(ctr, 1);
+          split_last[sp_slot] = prev == ns - 1;
+          ptx::red_release_add_shared(sh.counter(cnt_d), 1);
+        }
+      }
+      const bool decided = __all_sync(0xffffffffu, wait_count(sh, cnt_d, split_items));
+      if (!decided) break;
+      if (!split_last[sp_slot]) continue;
+      __threadfence();
+    }
+
+    // This thread's share of the merge: row slot `t % cw` of the slice and
+    // columns [cw (t / cw), cw (t / cw + 1)), cw = the slice's rows rounded up
+    // to a power of two (cw row slots x 128 / cw column groups = 128 threads;
+    // the whole tile is one slice of 128 rows, one thread per row).  The
+    // partials come from L2 (other CTAs just wrote them): the pieces' m and
+    // l 8 at a time, then per 16 columns 2 pieces' values per round.  (Kept
+    // inline and small: a merge out of line, or with more loads per round,
+    // measured 2 to 4 % slower at 8 kv heads, and staging the weights of
+    // narrow slices in shared memory to load more pieces per round was
+    // slower too.)
+    int32_t cw = 1;
+    while (cw < rows_per) cw <<= 1;
+    const int32_t t = row;
+    const int32_t mr = slice * rows_per + (t & (cw - 1));  // row of tile x
+    const int32_t mc0 = (t / cw) * cw;                        // first column
+    const int32_t mqrow = it.block * kBlockQ + mr / 2;
+    if ((t & (cw - 1)) < rows_per && mr < kRowsPerTile && mqrow < pr.query_tokens) {
+      const int32_t msrow = static_cast<int32_t>(x) * kRowsPerTile + mr;
+      const float* first_slot = slot - static_cast<size_t>(it.split) * kSlotFloats;
+      const size_t m_off = static_cast<size_t>(kHeadDim) * kSlotRows + msrow;
+      const size_t l_off = static_cast<size_t>(kHeadDim + 1) * kSlotRows + msrow;
+      float mmax = -INFINITY;
+#pragma unroll 1
+      for (int32_t sp0 = 0; sp0 < ns; sp0 += 8) {
+        float mv[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          mv[u] = sp0 + u < ns ? __ldcg(first_slot + (sp0 + u) * kSlotFloats + m_off) : -INFINITY;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) mmax = fmaxf(mmax, mv[u]);
+      }
+      float lsum = 0.0f;
+#pragma unroll 1
+      for (int32_t sp0 = 0; sp0 < ns; sp0 += 8) {
+        float mv[8], lv[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const bool in = sp0 + u < ns;
+          const float* sl = first_slot + (sp0 + u) * kSlotFloats;
+          mv[u] = in ? __ldcg(sl + m_off) : -INFINITY;
+          lv[u] = in ? __ldcg(sl + l_off) : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          if (mv[u] != -INFINITY) lsum += mufu_exp2((mv[u] - mmax) * p.scale_log2) * lv[u];
+        }
+      }
+      const float inv_sum = 1.0f / lsum;
+      const int32_t mhead = it.kv_head * kGroupSize + 2 * static_cast<int32_t>(x) + (mr & 1);
+      uint32_t* orow = reinterpret_cast<uint32_t*>(
+          a.out + (static_cast<size_t>(q_row0 + mqrow) * hq + mhead) * kHeadDim + mc0);
+      const int32_t cw16 = cw < 16 ? cw : 16;
+#pragma unroll 1
+      for (int32_t c0 = 0; c0 < cw; c0 += 16) {
+        float acc[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) acc[j] = 0.0f;
+#pragma unroll 1
+        for (int32_t sp0 = 0; sp0 < ns; sp0 += 2) {
+          float val[2][16], wgt[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const bool in = sp0 + u < ns;
+            const float* sl = first_slot + (sp0 + u) * kSlotFloats;
+            wgt[u] = in ? __ldcg(sl + m_off) : -INFINITY;
+            const float* colp = sl + static_cast<size_t>(mc0 + c0) * kSlotRows + msrow;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              val[u][j] = (in && j < cw16) ? __ldcg(colp + j * kSlotRows) : 0.0f;
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const float w =
+                wgt[u] == -INFINITY ? 0.0f : mufu_exp2((wgt[u] - mmax) * p.scale_log2);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) acc[j] += w * val[u][j];
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (2 * j < cw16) orow[c0 / 2 + j] = pack_bf16x2(acc[2 * j] * inv_sum, acc[2 * j + 1] * inv_sum);
+        }
       }
     }
-    const bool decided = __all_sync(0xffffffffu, wait_count(sh, cnt_d, split_items));
-    if (!decided) break;
-    if (!split_last[sp_slot]) continue;
-    __threadfence();
-    const float* first_slot = slot - static_cast<size_t>(it.split) * kSlotFloats;
-    const size_t m_off = static_cast<size_t>(kHeadDim) * kSlotRows + srow;
-    const size_t l_off = static_cast<size_t>(kHeadDim + 1) * kSlotRows + srow;
-    float mmax = -INFINITY;
-    for (int32_t sp = 0; sp < it.num_splits; ++sp) {
-      mmax = fmaxf(mmax, __ldcg(first_slot + sp * kSlotFloats + m_off));
-    }
-    float lsum = 0.0f;
-    for (int32_t sp = 0; sp < it.num_splits; ++sp) {
-      const float* sl = first_slot + sp * kSlotFloats;
-      const float ms = __ldcg(sl + m_off);
-      if (ms != -INFINITY) lsum += mufu_exp2((ms - mmax) * p.scale_log2) * __ldcg(sl + l_off);
-    }
-    const float inv_sum = 1.0f / lsum;
-    stage_free();
-#pragma unroll 1
-    for (int c = 0; c < 4; ++c) {
-      const int col = 32 * c;
-      float acc[32];
-#pragma unroll
-      for (int j = 0; j < 32; ++j) acc[j] = 0.0f;
-#pragma unroll 1
-      for (int32_t sp = 0; sp < it.num_splits; ++sp) {
-        const float* sl = first_slot + sp * kSlotFloats;
-        const float ms = __ldcg(sl + m_off);
-        const float wgt = ms == -INFINITY ? 0.0f : mufu_exp2((ms - mmax) * p.scale_log2);
-        const float* colp = sl + static_cast<size_t>(col) * kSlotRows + srow;
-#pragma unroll
-        for (int j = 0; j < 32; ++j) acc[j] += wgt * __ldcg(colp + j * kSlotRows);
-      }
-      store_rows_bf16(acc, inv_sum, stage, lane, a.out, base_q, base_h, hq, row_end, col);
-    }
+    __syncwarp();
+    TPSA_ITEM_REC(n_item, 6, ptx::globaltimer_ns());
+    if (a.coop_merge && lane == 0) ptx::mbar_arrive(sh.bar(kBarPieceDone));
   }
   // Output stores of this warp complete before the CTA exits.
   if (lane == 0) ptx::bulk_wait_group<0>();
@@ -1348,6 +1457,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     ptx::mbar_init(sh.bar(kBarTail), 1);
     ptx::mbar_init(sh.bar(kBarDrain), 1);
     ptx::mbar_init(sh.bar(kBarProbe), 1);
+    ptx::mbar_init(sh.bar(kBarPieceDone), kSoftmaxWarps);
     *sh.abort_flag() = 0;
     for (uint32_t i = 0; i < 4; ++i) {
       *reinterpret_cast<volatile uint32_t*>(sh.base + kOffCounters + 4 * i) = 0;
@@ -1444,6 +1554,19 @@ int32_t choose_split_counts(int32_t longest, int64_t tail, int64_t tiles, int32_
     }
   }
   return best_ns == 1 ? (1 << 30) : ceil_div(longest, best_ns);
+}
+
+// Merge mode of a launch's split pieces.  With few items per CTA (a head
+// slice of a multi-GPU partition, short prompts) the pieces run side by side
+// and the last one's merge of every partial is the launch's tail, so all
+// pieces of a block merge together, each a slice of the rows.  With many
+// items per CTA the last piece merges alone: the others leave at once and
+// their CTAs take the next item.  Measured at 8K and 32K/q8K (8 to 1 kv
+// heads): the cooperative merge loses about 6 % at 7 items per CTA and gains
+// 2 to 40 % at 3.6 or fewer.
+constexpr int64_t kCoopItemsPerCta = 4;
+bool coop_merge(int64_t items, int32_t grid) {
+  return items <= kCoopItemsPerCta * static_cast<int64_t>(grid);
 }
 
 int32_t choose_split(const tpsa_plan& p, int32_t b0, int64_t tiles, int32_t ctas) {
@@ -1605,10 +1728,13 @@ tpsa_status build_plan(int64_t query_tokens, int64_t query_start, int64_t seq_le
   tiles *= kv_heads;
   int32_t split = split_override > 0 ? split_override : choose_split(*p, b0, tiles, ctas);
   if (split < kMinSplitTiles) split = kMinSplitTiles;
-  // The in-kernel merge keeps per-split weights for at most 64 splits.
+  // At most 64 pieces per block, and fewer than the CTAs: the pieces of a
+  // block wait for one another before merging, which needs them to run at
+  // once.
+  const int32_t max_pieces = min_i(64, ctas);
   for (int32_t b = b0; b < p->num_blocks; ++b) {
     const int32_t c = block_tiles(*p, b).count;
-    if (ceil_div(c, split) > 64) split = ceil_div(c, 64);
+    if (ceil_div(c, split) > max_pieces) split = ceil_div(c, max_pieces);
   }
   if ((p->num_blocks - b0) * kv_heads * 2 > kMaxSplitCounters) split = 1 << 30;
   p->split_tiles = split;
@@ -1697,6 +1823,7 @@ tpsa_status launch(const void* query, const void* key_cache, const void* value_c
   args.tiles = reinterpret_cast<unsigned long long*>(tile_counter);
   args.words_per_row = (p.seq_len + 31) / 32;
   args.probe_wait_ns = t_probe_wait_ns;
+  args.coop_merge = coop_merge(p.total_items, p.grid) ? 1 : 0;
   t_probe_wait_ns = 0;
 
   if (visited != nullptr || tile_counter != nullptr) {
@@ -1776,6 +1903,7 @@ tpsa_status build_batch(int32_t first, int32_t count, const int64_t* cu_seqlens_
   a.plan.total_items = items;
   a.plan.total_tiles = tiles;
   a.plan.grid = items < ctas ? items : ctas;
+  a.coop_merge = coop_merge(items, a.plan.grid) ? 1 : 0;
   const int64_t ctl = (int64_t{kCtlSplitBase} + counters) * 4;
   b->ctl_bytes = std::max<int64_t>(kControlBytes, (ctl + 255) / 256 * 256);
   b->workspace_bytes = b->ctl_bytes + static_cast<int64_t>(slots) * kSlotBytes;
@@ -2175,6 +2303,12 @@ tpsa_status tpsa_paged_attention_static_scratch(const void* query, const void* k
 TPSA_API void tpsa_debug_spans(unsigned long long* out, uint32_t ctas) {
   cudaDeviceSynchronize();
   cudaMemcpyFromSymbol(out, g_cta_span, sizeof(unsigned long long) * 3 * (ctas < 1024 ? ctas : 1024));
+}
+
+TPSA_API void tpsa_debug_items(unsigned long long* out, uint32_t ctas) {
+  cudaDeviceSynchronize();
+  cudaMemcpyFromSymbol(out, g_item_trace,
+                       sizeof(unsigned long long) * 128 * (ctas < 1024 ? ctas : 1024));
 }
 
 TPSA_API void tpsa_debug_timeout(uint32_t* out5) {

@@ -47,7 +47,7 @@ constexpr int32_t kBlockQ = 64;        // query tokens per block
 constexpr int32_t kRowsPerTile = 128;  // rows of one tensor-core M tile
 constexpr int32_t kTileKeys = 128;     // widest key tile (one page)
 constexpr int32_t kKeyGrain = 64;      // key tiles are multiples of this
-constexpr int32_t kMinSplitTiles = 8;  // never split below this many tiles
+constexpr int32_t kMinSplitTiles = 4;  // never split below this many tiles
 constexpr int32_t kMaxSeqLen = 1 << 30;
 // Partial result of one split item: 256 rows x (128 O values + m + l), fp32.
 constexpr int64_t kSlotFloats = 2 * kRowsPerTile * (kHeadDim + 2);

@@ -79,6 +79,34 @@ def test_bench_layer_matches_oracle(tm, cuda_device, seq, tq):
     check_rows(out, q, k, v, table, q0, seq, seq, rows, f"bench layer {seq}/{tq}")
 
 
+@pytest.mark.parametrize("seq,world,rank", [(8192, 8, 0), (8192, 4, 1), (32768, 8, 7),
+                                             (32768, 2, 1)],
+                         ids=["8k_1head", "8k_2heads", "32k_1head", "32k_4heads"])
+def test_bench_head_slice_matches_oracle(tm, cuda_device, seq, world, rank):
+    """One rank's KV-head slice of the bench layer (bench.py at --gpus N):
+    the launches with few items per CTA, whose split pieces merge
+    cooperatively (each piece a slice of the rows), checked on the sampled
+    rows, the whole dense tail included."""
+    tq = 8192
+    q0 = seq - tq
+    heads = 8 // world
+    q, k, v, table = bench.make_inputs(tq, seq, 0, rank, world)
+    plan = tm._native.make_plan(tq, q0, seq, seq, heads, 0, SCALE)
+    assert plan.workspace_bytes > 2048, "expected split dense-tail items"
+    dev = cuda_device
+    qd, kd, vd, td = (t.to(dev) for t in (q, k, v, table))
+    out = torch.empty_like(qd)
+    ws = torch.empty(plan.workspace_bytes, dtype=torch.uint8, device=dev)
+    tm._native.paged_attention(qd, kd, vd, td, out, q0, seq, seq, SCALE, kv_heads=heads,
+                               workspace=ws)
+    torch.cuda.synchronize(dev)
+    assert tm._native.device_status(dev.index or 0) == 0
+    out = out.cpu()
+    assert torch.isfinite(out.float()).all()
+    rows = sample_rows(tq, q0, seq)
+    check_rows(out, q, k, v, table, q0, seq, seq, rows, f"head slice {seq} rank {rank}/{world}")
+
+
 def test_bench_32k_visited_set_bit_exact(tm, cuda_device):
     """Visited keys of the 32K / 8K-chunk plan (split tail) equal the key sets."""
     seq, tq = 32768, 8192
