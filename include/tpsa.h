@@ -160,10 +160,22 @@ TPSA_API tpsa_status tpsa_workspace_size(int64_t query_tokens, int64_t query_sta
  *                any input; written in place
  *   workspace    device scratch of at least tpsa_workspace_size() bytes,
  *                256-byte aligned, never NULL.  Its contents need not be
- *                initialised: each call clears the 2 KiB of control words
- *                with cudaMemsetAsync on `stream` before the kernel.  Calls
- *                sharing one workspace must be ordered on one stream.
+ *                initialised.  Calls sharing one workspace must be ordered
+ *                on one stream.
  *   stream       cudaStream_t
+ *
+ * Control words (the work-item counter and the split-KV counters, which
+ * start every launch at zero) live in a library-owned 4 KiB block per
+ * stream, one of 128 per device in a module-global array: the first call on
+ * a stream clears its block with cudaMemsetAsync on that stream, and the
+ * last CTA of every launch zeroes it again before it exits, so later calls
+ * issue only the kernel.  Streams are told apart by cudaStreamGetId.  While
+ * `stream` is being captured into a CUDA graph, or once 128 streams of a
+ * device hold blocks, a call keeps its control words in the first 2 KiB of
+ * `workspace` instead and clears them with cudaMemsetAsync before the
+ * kernel (a captured graph then carries that memset and may be replayed on
+ * any stream).  The block addresses are looked up once per device; after
+ * cudaDeviceReset in the same process they are stale.
  *
  * Gates (reference op_host :133-238): table_cols >= ceil(seq_len / 128),
  * num_pages > 0, query_start + query_tokens == seq_len, prompt_len >= seq_len,

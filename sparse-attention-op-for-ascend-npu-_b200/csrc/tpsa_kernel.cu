@@ -153,14 +153,19 @@ constexpr uint32_t kOffTmemSlot = kOffItemSlots + 2 * 64;
 constexpr uint32_t kOffAbort = kOffTmemSlot + 4;
 constexpr uint32_t kOffSplitLast = kOffAbort + 4;      // int32 [query tile][2]
 constexpr uint32_t kOffCounters = kOffSplitLast + 16;  // uint32 [4]: split written / decided per tile
-constexpr uint32_t kSmemUsed = kOffCounters + 16;
+constexpr uint32_t kOffLastCta = kOffCounters + 16;    // int32: this CTA finished the launch last
+constexpr uint32_t kSmemUsed = kOffLastCta + 16;
 constexpr uint32_t kSmemBytes = kSmemUsed + 1024;  // alignment slack
 static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 
-// Workspace control words (first kControlBytes of the workspace, zeroed by
-// the launcher): [0] next work item, [64..] one split counter per
-// (tail block, kv head, query tile).
+// Control words: [0] next work item, [1] CTAs that have finished, [64..] one
+// split counter per (tail block, kv head, query tile).  They start every
+// launch at zero.  Either they live in a library-owned control block of the
+// launching stream, which the last CTA of each launch zeroes again on its
+// way out (KernelArgs::ctl_reset_words), or in the first bytes of the
+// caller's workspace, which the launcher clears before the kernel.
 constexpr int kCtlNextItem = 0;
+constexpr int kCtlExited = 1;
 constexpr int kCtlSplitBase = 64;
 
 // One request of a launch (a batch-one call is a launch of one request).
@@ -194,6 +199,7 @@ struct KernelArgs {
   unsigned long long* tiles;   // visit mode: [tiles, keys]
   uint32_t probe_wait_ns;      // test hook (0 = off): see scheduler_role
   int32_t coop_merge;          // split pieces merge together (softmax_role)
+  int32_t ctl_reset_words;     // > 0: the last CTA zeroes ctl[0, ctl_reset_words)
 };
 
 
@@ -966,6 +972,84 @@ __device__ __forceinline__ float chunk_max(const uint32_t (&r)[32]) {
   return fmaxf(max3(mx0, mx1, mx2), mx3);
 }
 
+// Split-KV merge of one row over `ns` pieces' partials (column-major slots
+// of kSlotFloats floats; this row's m at m_off, its O values at col_off +
+// column * 2 kRowsPerTile), for columns [0, cw) of the thread's column
+// group, written as bf16 pairs to orow.  Each round loads kCw columns of
+// 32 / kCw pieces (32 independent L2 loads), so that a narrow column group
+// (a slice of few rows over many pieces) needs ns kCw / 32 rounds, not
+// ns / 2.  mmax and inv_sum come from merge_row_stats.
+template <int kCw>
+__device__ __forceinline__ void merge_columns(const float* first_slot, size_t m_off,
+                                              size_t col_off, int32_t ns, int32_t cw,
+                                              float mmax, float sl2, float inv_sum,
+                                              uint32_t* orow) {
+  constexpr int kPr = 32 / kCw;  // pieces per round
+  constexpr size_t kColStride = 2 * kRowsPerTile;
+#pragma unroll 1
+  for (int32_t c0 = 0; c0 < cw; c0 += kCw) {
+    float acc[kCw];
+#pragma unroll
+    for (int j = 0; j < kCw; ++j) acc[j] = 0.0f;
+#pragma unroll 1
+    for (int32_t sp0 = 0; sp0 < ns; sp0 += kPr) {
+      float val[kPr][kCw], wgt[kPr];
+#pragma unroll
+      for (int u = 0; u < kPr; ++u) {
+        const bool in = sp0 + u < ns;
+        const float* sl = first_slot + static_cast<size_t>(sp0 + u) * kSlotFloats;
+        wgt[u] = in ? __ldcg(sl + m_off) : -INFINITY;
+        const float* colp = sl + col_off + static_cast<size_t>(c0) * kColStride;
+#pragma unroll
+        for (int j = 0; j < kCw; ++j) val[u][j] = in ? __ldcg(colp + j * kColStride) : 0.0f;
+      }
+#pragma unroll
+      for (int u = 0; u < kPr; ++u) {
+        const float w = wgt[u] == -INFINITY ? 0.0f : mufu_exp2((wgt[u] - mmax) * sl2);
+#pragma unroll
+        for (int j = 0; j < kCw; ++j) acc[j] += w * val[u][j];
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kCw / 2; ++j) {
+      orow[c0 / 2 + j] = pack_bf16x2(acc[2 * j] * inv_sum, acc[2 * j + 1] * inv_sum);
+    }
+  }
+}
+
+// Row max and row sum of one row over `ns` pieces' (m, l) in one pass of
+// 8 pieces per round (an online log-sum-exp: the sum is rescaled when the
+// max grows).  Returns 1 / sum through inv_sum.
+__device__ __forceinline__ float merge_row_stats(const float* first_slot, size_t m_off,
+                                                 size_t l_off, int32_t ns, float sl2,
+                                                 float* inv_sum) {
+  float mmax = -INFINITY, lsum = 0.0f;
+#pragma unroll 1
+  for (int32_t sp0 = 0; sp0 < ns; sp0 += 8) {
+    float mv[8], lv[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const bool in = sp0 + u < ns;
+      const float* sl = first_slot + static_cast<size_t>(sp0 + u) * kSlotFloats;
+      mv[u] = in ? __ldcg(sl + m_off) : -INFINITY;
+      lv[u] = in ? __ldcg(sl + l_off) : 0.0f;
+    }
+    float bm = mmax;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) bm = fmaxf(bm, mv[u]);
+    if (bm != -INFINITY) {
+      if (bm != mmax) lsum = mmax == -INFINITY ? 0.0f : lsum * mufu_exp2((mmax - bm) * sl2);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (mv[u] != -INFINITY) lsum += mufu_exp2((mv[u] - bm) * sl2) * lv[u];
+      }
+      mmax = bm;
+    }
+  }
+  *inv_sum = 1.0f / lsum;
+  return mmax;
+}
+
 // Per-row state of the online softmax over one item's tiles: the lazy
 // reference max and the row sum relative to it.
 struct RowState {
@@ -1322,11 +1406,12 @@ __device__ void softmax_role(const KernelArgs& a, const Smem& sh, uint32_t tmem,
     // to a power of two (cw row slots x 128 / cw column groups = 128 threads;
     // the whole tile is one slice of 128 rows, one thread per row).  The
     // partials come from L2 (other CTAs just wrote them): the pieces' m and
-    // l 8 at a time, then per 16 columns 2 pieces' values per round.  (Kept
-    // inline and small: a merge out of line, or with more loads per round,
-    // measured 2 to 4 % slower at 8 kv heads, and staging the weights of
-    // narrow slices in shared memory to load more pieces per round was
-    // slower too.)
+    // l 8 at a time in one online pass, then 32 values per round, min(cw, 16)
+    // columns of 32 / min(cw, 16) pieces, so a narrow slice over many pieces
+    // (a one-head launch: 43 pieces of 3 rows at 32K) takes few rounds of L2
+    // latency.  (A full-width slice keeps 2 pieces x 16 columns per round: a
+    // merge out of line, or with more loads per round, measured 2 to 4 %
+    // slower at 8 kv heads.)
     int32_t cw = 1;
     while (cw < rows_per) cw <<= 1;
     const int32_t t = row;
@@ -1338,69 +1423,20 @@ __device__ void softmax_role(const KernelArgs& a, const Smem& sh, uint32_t tmem,
       const float* first_slot = slot - static_cast<size_t>(it.split) * kSlotFloats;
       const size_t m_off = static_cast<size_t>(kHeadDim) * kSlotRows + msrow;
       const size_t l_off = static_cast<size_t>(kHeadDim + 1) * kSlotRows + msrow;
-      float mmax = -INFINITY;
-#pragma unroll 1
-      for (int32_t sp0 = 0; sp0 < ns; sp0 += 8) {
-        float mv[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          mv[u] = sp0 + u < ns ? __ldcg(first_slot + (sp0 + u) * kSlotFloats + m_off) : -INFINITY;
-        }
-#pragma unroll
-        for (int u = 0; u < 8; ++u) mmax = fmaxf(mmax, mv[u]);
-      }
-      float lsum = 0.0f;
-#pragma unroll 1
-      for (int32_t sp0 = 0; sp0 < ns; sp0 += 8) {
-        float mv[8], lv[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const bool in = sp0 + u < ns;
-          const float* sl = first_slot + (sp0 + u) * kSlotFloats;
-          mv[u] = in ? __ldcg(sl + m_off) : -INFINITY;
-          lv[u] = in ? __ldcg(sl + l_off) : 0.0f;
-        }
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          if (mv[u] != -INFINITY) lsum += mufu_exp2((mv[u] - mmax) * p.scale_log2) * lv[u];
-        }
-      }
-      const float inv_sum = 1.0f / lsum;
+      float inv_sum;
+      const float mmax = merge_row_stats(first_slot, m_off, l_off, ns, p.scale_log2, &inv_sum);
       const int32_t mhead = it.kv_head * kGroupSize + 2 * static_cast<int32_t>(x) + (mr & 1);
       uint32_t* orow = reinterpret_cast<uint32_t*>(
           a.out + (static_cast<size_t>(q_row0 + mqrow) * hq + mhead) * kHeadDim + mc0);
-      const int32_t cw16 = cw < 16 ? cw : 16;
-#pragma unroll 1
-      for (int32_t c0 = 0; c0 < cw; c0 += 16) {
-        float acc[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) acc[j] = 0.0f;
-#pragma unroll 1
-        for (int32_t sp0 = 0; sp0 < ns; sp0 += 2) {
-          float val[2][16], wgt[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const bool in = sp0 + u < ns;
-            const float* sl = first_slot + (sp0 + u) * kSlotFloats;
-            wgt[u] = in ? __ldcg(sl + m_off) : -INFINITY;
-            const float* colp = sl + static_cast<size_t>(mc0 + c0) * kSlotRows + msrow;
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              val[u][j] = (in && j < cw16) ? __ldcg(colp + j * kSlotRows) : 0.0f;
-            }
-          }
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const float w =
-                wgt[u] == -INFINITY ? 0.0f : mufu_exp2((wgt[u] - mmax) * p.scale_log2);
-#pragma unroll
-            for (int j = 0; j < 16; ++j) acc[j] += w * val[u][j];
-          }
-        }
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          if (2 * j < cw16) orow[c0 / 2 + j] = pack_bf16x2(acc[2 * j] * inv_sum, acc[2 * j + 1] * inv_sum);
-        }
+      const size_t col_off = static_cast<size_t>(mc0) * kSlotRows + msrow;
+      if (cw >= 16) {
+        merge_columns<16>(first_slot, m_off, col_off, ns, cw, mmax, p.scale_log2, inv_sum, orow);
+      } else if (cw == 8) {
+        merge_columns<8>(first_slot, m_off, col_off, ns, cw, mmax, p.scale_log2, inv_sum, orow);
+      } else if (cw == 4) {
+        merge_columns<4>(first_slot, m_off, col_off, ns, cw, mmax, p.scale_log2, inv_sum, orow);
+      } else {
+        merge_columns<2>(first_slot, m_off, col_off, ns, cw, mmax, p.scale_log2, inv_sum, orow);
       }
     }
     __syncwarp();
@@ -1497,6 +1533,24 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 #ifdef TPSA_TRACE
   if (threadIdx.x == 0 && blockIdx.x < 1024) g_cta_span[blockIdx.x][1] = ptx::globaltimer_ns();
 #endif
+  if (args.ctl_reset_words > 0) {
+    // Control words of a library-owned block: the last CTA to finish zeroes
+    // them for the next launch on the stream.  Every other CTA has made its
+    // last claim and its last split-counter update before counting itself
+    // out (the fence orders them before the count).
+    volatile int* last = reinterpret_cast<volatile int*>(sh.base + kOffLastCta);
+    if (threadIdx.x == 0) {
+      __threadfence();
+      const int done = atomicAdd(args.ctl + kCtlExited, 1);
+      *last = done == static_cast<int>(gridDim.x) - 1 ? 1 : 0;
+      __threadfence();
+    }
+    __syncthreads();
+    if (*last) {
+      __threadfence();
+      for (int32_t i = threadIdx.x; i < args.ctl_reset_words; i += kNumThreads) args.ctl[i] = 0;
+    }
+  }
   if (warp == 1) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem, kTmemCols);
@@ -1631,6 +1685,76 @@ tpsa_status device_state(DeviceState** out) {
   return TPSA_OK;
 }
 
+// ------------------------------------------------ stream control blocks
+// The control words of a launch (scheduler counter, exit counter, split
+// counters) start at zero.  Instead of clearing them with a memset before
+// every kernel (a separate operation of a few microseconds on the stream),
+// each stream that calls the library gets a control block of its own in a
+// module-global array; the block is cleared once when the stream first gets
+// it, and the last CTA of every launch zeroes it again before exiting.
+// Launches on one stream run one after another, so they never share a block
+// at the same time.  Streams are told apart by cudaStreamGetId, which is
+// unique for the life of the context (a destroyed stream's handle may be
+// reused, its id is not).  A launch falls back to control words in the
+// caller's workspace, cleared by cudaMemsetAsync, when the stream is being
+// captured into a CUDA graph (a graph may be replayed on any stream), when
+// all blocks are taken, or when the launch needs more words than a block
+// holds.
+constexpr int kCtlBlocks = 128;
+constexpr int32_t kCtlBlockWords = 1024;  // 4 KiB; a 16-request launch needs at most 832
+struct CtlBlocks {
+  int32_t* base = nullptr;  // device address of g_ctl_blocks on this device
+  unsigned long long stream_id[kCtlBlocks] = {};
+  int used = 0;
+};
+CtlBlocks g_ctl[64];  // per device ordinal, guarded by g_mutex
+
+}  // namespace
+
+static __device__ __align__(256) int32_t g_ctl_blocks[kCtlBlocks * kCtlBlockWords];
+
+namespace {
+
+// The control block of `stream` for a launch of `words` control words, or
+// nullptr in *ctl when the launch must use its workspace instead.  The first
+// launch of a stream clears its block on that stream.
+tpsa_status stream_ctl_block(cudaStream_t stream, int64_t words, int32_t** ctl) {
+  *ctl = nullptr;
+  if (words > kCtlBlockWords) return TPSA_OK;
+  cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+  cudaError_t e = cudaStreamIsCapturing(stream, &capture);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamIsCapturing");
+  if (capture != cudaStreamCaptureStatusNone) return TPSA_OK;
+  unsigned long long id = 0;
+  e = cudaStreamGetId(stream, &id);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamGetId");
+  int dev = 0;
+  e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(TPSA_ERR_CUDA, "device ordinal out of range");
+  std::lock_guard<std::mutex> lock(g_mutex);
+  CtlBlocks& cb = g_ctl[dev];
+  if (cb.base == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_ctl_blocks);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(control blocks)");
+    cb.base = static_cast<int32_t*>(p);
+  }
+  for (int i = 0; i < cb.used; ++i) {
+    if (cb.stream_id[i] == id) {
+      *ctl = cb.base + static_cast<size_t>(i) * kCtlBlockWords;
+      return TPSA_OK;
+    }
+  }
+  if (cb.used == kCtlBlocks) return TPSA_OK;
+  int32_t* block = cb.base + static_cast<size_t>(cb.used) * kCtlBlockWords;
+  e = cudaMemsetAsync(block, 0, kCtlBlockWords * sizeof(int32_t), stream);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(control block)");
+  cb.stream_id[cb.used++] = id;
+  *ctl = block;
+  return TPSA_OK;
+}
+
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
                                   const cuuint32_t*, CUtensorMapInterleave,
@@ -1758,7 +1882,8 @@ tpsa_status launch(const void* query, const void* key_cache, const void* value_c
                    int64_t num_pages, int64_t table_cols, int64_t query_start,
                    int64_t seq_len, int64_t prompt_len, float scale, int32_t kv_heads,
                    void* workspace, uint64_t workspace_bytes, uint32_t* visited,
-                   uint64_t* tile_counter, void* stream, bool dense = false) {
+                   uint64_t* tile_counter, void* stream, bool dense = false,
+                   bool ctl_in_workspace = false) {
   t_last_error.clear();
   if (query == nullptr || key_cache == nullptr || value_cache == nullptr ||
       block_table == nullptr || out == nullptr) {
@@ -1814,11 +1939,23 @@ tpsa_status launch(const void* query, const void* key_cache, const void* value_c
   args.block_table = block_table;
   args.out = static_cast<__nv_bfloat16*>(out);
   args.num_pages = static_cast<int32_t>(num_pages);
-  args.ctl = static_cast<int32_t*>(workspace);
   args.scratch = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kControlBytes);
-  // The work-item counter and split counters start at zero every launch.
-  cudaError_t e = cudaMemsetAsync(workspace, 0, kControlBytes, s);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(workspace)");
+  // The work-item counter and split counters start at zero every launch: in
+  // the stream's control block (left at zero by the previous launch), else
+  // in the workspace, cleared here.
+  args.ctl = nullptr;
+  if (!ctl_in_workspace) {
+    st = stream_ctl_block(s, kControlBytes / 4, &args.ctl);
+    if (st != TPSA_OK) return st;
+  }
+  cudaError_t e = cudaSuccess;
+  if (args.ctl != nullptr) {
+    args.ctl_reset_words = kControlBytes / 4;
+  } else {
+    args.ctl = static_cast<int32_t*>(workspace);
+    e = cudaMemsetAsync(workspace, 0, kControlBytes, s);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(workspace)");
+  }
   args.visited = visited;
   args.tiles = reinterpret_cast<unsigned long long*>(tile_counter);
   args.words_per_row = (p.seq_len + 31) / 32;
@@ -2020,10 +2157,17 @@ tpsa_status launch_varlen(const void* query, const void* key_cache, const void* 
     args.block_table = block_tables;
     args.out = static_cast<__nv_bfloat16*>(out);
     args.num_pages = static_cast<int32_t>(num_pages);
-    args.ctl = static_cast<int32_t*>(workspace);
     args.scratch = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + b->ctl_bytes);
-    cudaError_t e = cudaMemsetAsync(workspace, 0, static_cast<size_t>(b->ctl_bytes), s);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(workspace)");
+    st = stream_ctl_block(s, b->ctl_bytes / 4, &args.ctl);
+    if (st != TPSA_OK) return st;
+    cudaError_t e = cudaSuccess;
+    if (args.ctl != nullptr) {
+      args.ctl_reset_words = static_cast<int32_t>(b->ctl_bytes / 4);
+    } else {
+      args.ctl = static_cast<int32_t*>(workspace);
+      e = cudaMemsetAsync(workspace, 0, static_cast<size_t>(b->ctl_bytes), s);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(workspace)");
+    }
     tpsa_paged_kernel<false, true><<<args.plan.grid, kNumThreads, kSmemBytes, s>>>(
         args, tq, tk128, tk64, tv, tout);
     e = cudaGetLastError();
@@ -2295,7 +2439,7 @@ tpsa_status tpsa_paged_attention_static_scratch(const void* query, const void* k
   if (st != TPSA_OK) return st;
   return launch(query, key_cache, value_cache, block_table, out, query_tokens, num_pages,
                 table_cols, query_start, seq_len, prompt_len, scale, TPSA_KV_HEADS, scratch,
-                kStaticScratchBytes, nullptr, nullptr, stream);
+                kStaticScratchBytes, nullptr, nullptr, stream, false, true);
 }
 
 #ifdef TPSA_TRACE
