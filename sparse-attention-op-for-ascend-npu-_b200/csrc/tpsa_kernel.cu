@@ -119,6 +119,9 @@ constexpr int kKRing = 2;
 constexpr int kVRing = 2;
 // Output staging: 4 KB per softmax warp (its 32 rows x 64 columns as bf16,
 // 128-byte swizzled), stored to `out` by the warp's own TMA store.
+// (Measured: giving this space to a third K slot, with the staging in the K
+// slot of the item's last tile, was 3.5 % slower at 8K, although the K loads
+// then run a tile further ahead.)
 constexpr uint32_t kOutStageBytes = 32 * 128;
 constexpr uint32_t kOffQ = 0;                                   // [query tile][d half]
 constexpr uint32_t kOffK = kOffQ + 2 * kQTileBytes;              // K ring
@@ -571,14 +574,20 @@ __device__ void scheduler_role(const KernelArgs& a, const Smem& sh) {
 // ------------------------------------------------------------ producers
 // K side: for each item the first K tile, then the two query tiles (each
 // waits until the previous item's last QK of that tile completed), then the
-// remaining K tiles.  V side: the V tiles.  One thread each.
+// remaining K tiles.  V side: the V tiles.  One thread each.  A 128-key tile
+// from one page is one 128-row box per 64-column half (tk128 / tv128); a
+// 64-key tile, or the two halves of a composite tile, 64-row boxes.
+// (Measured at 8K: 128-row V boxes and no L2 prefetch of the query rows, 2.7 %
+// faster than 64-row V boxes with the prefetch; L2 prefetches of the next
+// item's K/V tiles were 10 % slower.)
 template <bool kVarlen>
 __device__ void producer_role(const KernelArgs& a, const Smem& sh, const CUtensorMap* tq,
                               const CUtensorMap* tk128, const CUtensorMap* tk64,
-                              const CUtensorMap* tv, bool v_side) {
+                              const CUtensorMap* tv, const CUtensorMap* tv128, bool v_side) {
   const tpsa_plan& p = a.plan;
   if (v_side) {
     ptx::prefetch_tmap(tv);
+    ptx::prefetch_tmap(tv128);
   } else {
     ptx::prefetch_tmap(tq);
     ptx::prefetch_tmap(tk128);
@@ -605,14 +614,6 @@ __device__ void producer_role(const KernelArgs& a, const Smem& sh, const CUtenso
     const int32_t* table = kVarlen ? a.block_table + rq.table_off : a.block_table;
     const int32_t req_seq_len = kVarlen ? rq.plan.seq_len : p.seq_len;
     const int32_t q_row0 = kVarlen ? rq.q_row0 : 0;
-    if (!v_side) {
-      // The item's query rows into L2 now: the shared-memory copy waits until
-      // the previous item's last QK, and then reads them from L2.
-      for (int32_t c = 0; c < 4; ++c) {
-        ptx::tma_prefetch_3d(tq, (c & 1) * 64, it.kv_head * kGroupSize + 2 * (c >> 1),
-                             q_row0 + it.block * kBlockQ);
-      }
-    }
 
     // Cache row (page * 128 + slot) of logical key k; a block-table entry
     // outside the cache is flagged and points fully out of bounds, where
@@ -684,9 +685,13 @@ __device__ void producer_role(const KernelArgs& a, const Smem& sh, const CUtenso
         const uint32_t lbar = tail ? sh.bar(kBarTail) : bar_full + 8 * s;
         ptx::mbar_arrive_expect_tx(lbar, static_cast<uint32_t>(w) * kHeadDim * 2);
         for (int dh = 0; dh < 2; ++dh) {
-          for (int sub = 0; sub < w / 64; ++sub) {
-            ptx::tma_load_3d(dst + dh * kKvHalfBytes + sub * 8192, tv, dh * 64, it.kv_head,
-                             sub == 0 ? tok : tok_up, lbar);
+          if (w == kTileKeys && !split_halves) {
+            ptx::tma_load_3d(dst + dh * kKvHalfBytes, tv128, dh * 64, it.kv_head, tok, lbar);
+          } else {
+            for (int sub = 0; sub < w / 64; ++sub) {
+              ptx::tma_load_3d(dst + dh * kKvHalfBytes + sub * 8192, tv, dh * 64, it.kv_head,
+                               sub == 0 ? tok : tok_up, lbar);
+            }
           }
         }
         if (tail) {
@@ -1261,13 +1266,14 @@ __device__ void softmax_role(const KernelArgs& a, const Smem& sh, uint32_t tmem,
     TPSA_ITEM_REC(n_item, 3, ptx::globaltimer_ns());
     if (tr) TPSA_TR(2 + x, 5, rec.idx);
     const bool split = it.num_splits > 1;
+    const bool staged_store = !split && (!kVarlen || bt.q_end - bt.q_begin == kBlockQ);
     const uint32_t sp_slot = split_items & 1;
     split_items += split ? 1u : 0u;
     // Output rows of this warp: packed token base_q + R / 2, head
     // base_h + R % 2 for warp row R (the tensor map clips rows past the end).
     const int32_t base_q = q_row0 + it.block * kBlockQ + quad * 16;
     const int32_t base_h = it.kv_head * kGroupSize + 2 * static_cast<int32_t>(x);
-    if (!split && (!kVarlen || bt.q_end - bt.q_begin == kBlockQ)) {
+    if (staged_store) {
       // Two rounds of 64 columns: the warp's 32 rows into its staging
       // buffer as bf16 (128-byte swizzled rows, the layout the tensor map
       // stores), then one TMA store of the 16-token x 2-head x 64-column box.
@@ -1456,6 +1462,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
                      const __grid_constant__ CUtensorMap tmap_k128,
                      const __grid_constant__ CUtensorMap tmap_k64,
                      const __grid_constant__ CUtensorMap tmap_v,
+                     const __grid_constant__ CUtensorMap tmap_v128,
                      const __grid_constant__ CUtensorMap tmap_out) {
   extern __shared__ uint8_t smem_raw[];
   Smem sh;
@@ -1512,7 +1519,10 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   if (warp < kFirstSoftmaxWarp) {
     ptx::setmaxnreg_dec<kControlRegs>();
     if (warp == 0) {
-      if (lane == 0) producer_role<kVarlen>(args, sh, &tmap_q, &tmap_k128, &tmap_k64, &tmap_v, false);
+      if (lane == 0) {
+        producer_role<kVarlen>(args, sh, &tmap_q, &tmap_k128, &tmap_k64, &tmap_v, &tmap_v128,
+                               false);
+      }
       __syncwarp();
     } else if (warp == 1) {
       mma_role(args, sh, tmem);
@@ -1520,7 +1530,10 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       if (lane == 0) scheduler_role<kVarlen>(args, sh);
       __syncwarp();
     } else {
-      if (lane == 0) producer_role<kVarlen>(args, sh, &tmap_q, &tmap_k128, &tmap_k64, &tmap_v, true);
+      if (lane == 0) {
+        producer_role<kVarlen>(args, sh, &tmap_q, &tmap_k128, &tmap_k64, &tmap_v, &tmap_v128,
+                               true);
+      }
       __syncwarp();
     }
   } else {
@@ -1917,7 +1930,7 @@ tpsa_status launch(const void* query, const void* key_cache, const void* value_c
       return fail(TPSA_ERR_INVALID_ARGUMENT, "tensors must be 16-byte aligned");
     }
   }
-  CUtensorMap tq, tk128, tk64, tv, tout;
+  CUtensorMap tq, tk128, tk64, tv, tv128, tout;
   const uint64_t hq = static_cast<uint64_t>(kv_heads) * kGroupSize;
   const uint64_t cache_tokens = static_cast<uint64_t>(num_pages) * kPageSize;
   st = encode_map(&tq, query, hq, static_cast<uint64_t>(query_tokens), 2, kBlockQ);
@@ -1927,6 +1940,8 @@ tpsa_status launch(const void* query, const void* key_cache, const void* value_c
   st = encode_map(&tk64, key_cache, kv_heads, cache_tokens, 1, 64);
   if (st != TPSA_OK) return st;
   st = encode_map(&tv, value_cache, kv_heads, cache_tokens, 1, 64);
+  if (st != TPSA_OK) return st;
+  st = encode_map(&tv128, value_cache, kv_heads, cache_tokens, 1, 128);
   if (st != TPSA_OK) return st;
   // Output boxes of one softmax warp: 16 tokens x 2 heads x 64 columns.  The
   // map's extent ends at the last query row, which clips the last block.
@@ -1965,10 +1980,10 @@ tpsa_status launch(const void* query, const void* key_cache, const void* value_c
 
   if (visited != nullptr || tile_counter != nullptr) {
     tpsa_paged_kernel<true, false><<<p.grid, kNumThreads, kSmemBytes, s>>>(args, tq, tk128, tk64,
-                                                                            tv, tout);
+                                                                            tv, tv128, tout);
   } else {
     tpsa_paged_kernel<false, false><<<p.grid, kNumThreads, kSmemBytes, s>>>(args, tq, tk128, tk64,
-                                                                             tv, tout);
+                                                                             tv, tv128, tout);
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
@@ -2128,7 +2143,7 @@ tpsa_status launch_varlen(const void* query, const void* key_cache, const void* 
     return fail(TPSA_ERR_INVALID_ARGUMENT, "kv_heads must be 1, 2, 4 or 8");
   }
   const uint64_t total_rows = static_cast<uint64_t>(cu_seqlens_q[batch]);
-  CUtensorMap tq, tk128, tk64, tv, tout;
+  CUtensorMap tq, tk128, tk64, tv, tv128, tout;
   const uint64_t hq = static_cast<uint64_t>(kv_heads) * kGroupSize;
   const uint64_t cache_tokens = static_cast<uint64_t>(num_pages) * kPageSize;
   st = encode_map(&tq, query, hq, total_rows, 2, kBlockQ);
@@ -2138,6 +2153,8 @@ tpsa_status launch_varlen(const void* query, const void* key_cache, const void* 
   st = encode_map(&tk64, key_cache, kv_heads, cache_tokens, 1, 64);
   if (st != TPSA_OK) return st;
   st = encode_map(&tv, value_cache, kv_heads, cache_tokens, 1, 64);
+  if (st != TPSA_OK) return st;
+  st = encode_map(&tv128, value_cache, kv_heads, cache_tokens, 1, 128);
   if (st != TPSA_OK) return st;
   st = encode_map(&tout, out, hq, total_rows, 2, 16);
   if (st != TPSA_OK) return st;
@@ -2169,7 +2186,7 @@ tpsa_status launch_varlen(const void* query, const void* key_cache, const void* 
       if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(workspace)");
     }
     tpsa_paged_kernel<false, true><<<args.plan.grid, kNumThreads, kSmemBytes, s>>>(
-        args, tq, tk128, tk64, tv, tout);
+        args, tq, tk128, tk64, tv, tv128, tout);
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
   }
