@@ -187,3 +187,30 @@ def test_bad_page_is_flagged_not_faulted(tm, cuda_device):
     assert status & tm._native.DEVICE_WAIT_TIMEOUT == 0
     assert torch.isfinite(out.float()).all()
     assert tm._native.device_status(0) == 0  # reading cleared it
+
+
+@pytest.mark.parametrize("spike_key", [200, 760])
+def test_reference_moves_in_upper_half_of_tile(tm, cuda_device, spike_key):
+    """A key whose score exceeds every earlier key's by far more than the
+    lazy reference threshold (2^8 after scaling), in keys 64-127 of a tile
+    that is not the first of its item: the softmax's reference max moves on
+    that tile, and O and the row sum accumulated so far are rescaled (to
+    zero here).  Every row that sees the key follows its value row; all rows
+    are checked against the oracle."""
+    seq = 1024
+    gen = torch.Generator().manual_seed(31 + spike_key)
+    pages = seq // 128
+    table = torch.randperm(2 * pages, generator=gen)[:pages].to(torch.int32).view(1, -1)
+    u = torch.randn(128, generator=gen)
+    q = (u + 0.1 * torch.randn(seq, 32, 128, generator=gen)).to(torch.bfloat16)
+    k = (0.1 * torch.randn(2 * pages, 128, 8, 128, generator=gen)).to(torch.bfloat16)
+    v = torch.randn(2 * pages, 128, 8, 128, generator=gen).to(torch.bfloat16)
+    page, off = divmod(spike_key, 128)
+    assert off % 128 >= 64, "the spike must sit in keys 64-127 of a page-aligned tile"
+    k[table[0, page], off] = (8.0 * u / u.norm() * 11.3).to(torch.bfloat16)
+    out = run_cabi(tm, q, k, v, table, 0, seq, seq, cuda_device)
+    ref = oracle_attention(q, k, v, table, 0, seq, seq, SCALE)
+    assert_close(out, ref, f"spike at key {spike_key}")
+    # The rows that see the spike follow its value row.
+    row = spike_key + 10
+    assert float((out[row].float() - v[table[0, page], off].float().repeat_interleave(4, 0)).abs().max()) < 0.05
