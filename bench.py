@@ -730,6 +730,134 @@ def run_ttft(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+# Qwen3-8B's architecture for vLLM's dummy-weight loader (random weights, no
+# checkpoint): the public model configuration's shape fields.
+QWEN3_8B_VLLM_CONFIG = {
+    "architectures": ["Qwen3ForCausalLM"], "model_type": "qwen3", "hidden_size": 4096,
+    "intermediate_size": 12288, "num_hidden_layers": 36, "num_attention_heads": 32,
+    "num_key_value_heads": 8, "head_dim": 128, "max_position_embeddings": 40960,
+    "rms_norm_eps": 1e-6, "rope_theta": 1000000.0, "vocab_size": 151936,
+    "torch_dtype": "bfloat16", "tie_word_embeddings": False, "hidden_act": "silu",
+    "attention_bias": False, "attention_dropout": 0.0, "rope_scaling": None,
+    "sliding_window": None, "use_sliding_window": False, "max_window_layers": 36,
+    "bos_token_id": 151643, "eos_token_id": 151645}
+
+
+def ttft_vllm_worker(mode: str, runs: int, warmup: int) -> None:
+    """One process of the live-engine TTFT: a vLLM 0.22 engine (in this
+    process) with a random-init Qwen3-8B, the plugin registered, TriangleMix
+    on (``triangle``) or off (``dense``); prints one JSON line with the TTFT
+    of each timed run (wall time of ``generate`` with one output token for
+    the 8320-token prompt: five 2048-token prefill steps and the sample)."""
+    import tempfile
+
+    os.environ["VLLM_ENABLE_V1_MULTIPROCESSING"] = "0"  # the hook lives in this process
+    os.environ.setdefault("VLLM_USE_FLASHINFER_SAMPLER", "0")
+    from __graft_entry__ import load_package
+
+    tm = load_package()
+    tm.plugin.register()
+    model_dir = tempfile.mkdtemp(prefix="qwen3_8b_config_")
+    Path(model_dir, "config.json").write_text(json.dumps(QWEN3_8B_VLLM_CONFIG))
+    from vllm import LLM, SamplingParams
+
+    section = {"enabled": mode == "triangle", "layers": TTFT_LAYERS, "threshold_profile": "b200"}
+    llm = LLM(model=model_dir, load_format="dummy", skip_tokenizer_init=True, enforce_eager=True,
+              dtype="bfloat16", max_model_len=TTFT_PROMPT + 128, block_size=PAGE,
+              max_num_batched_tokens=TTFT_CHUNK, enable_chunked_prefill=True,
+              enable_prefix_caching=False, gpu_memory_utilization=0.6,
+              attention_backend="TRITON_ATTN", seed=0,
+              additional_config={"trianglemix": section})
+    ids = torch.randint(0, QWEN3_8B["vocab"], (TTFT_PROMPT,),
+                        generator=torch.Generator().manual_seed(0)).tolist()
+    params = SamplingParams(max_tokens=1, temperature=0.0, detokenize=False)
+    prompt = [{"prompt_token_ids": ids}]
+    for _ in range(warmup):
+        llm.generate(prompt, params, use_tqdm=False)
+    router = tm.plugin.registered_router()
+    before = dict(router.stats.snapshot()["counters"]) if router else {}
+    times = []
+    for _ in range(runs):
+        t0 = time.perf_counter()
+        out = llm.generate(prompt, params, use_tqdm=False)
+        times.append((time.perf_counter() - t0) * 1e3)
+        assert len(out[0].outputs[0].token_ids) == 1
+    after = router.stats.snapshot()["counters"] if router else {}
+    per_prefill = {k: (after.get(k, 0) - before.get(k, 0)) / runs for k in sorted(after)
+                   if after.get(k, 0) != before.get(k, 0) and not k.endswith("_ns")}
+    print("TTFT_VLLM " + json.dumps({"mode": mode, "ttft_ms": times,
+                                     "per_prefill": per_prefill,
+                                     "status": tm._native.device_status(0)}), flush=True)
+
+
+def run_ttft_vllm(args) -> None:
+    """BASELINE config 2 through a live vLLM engine: TTFT of one 8320-token
+    prompt (chunk 2048, block 128) with TriangleMix on layers 5, 7, 10, 15-35
+    against vLLM's own attention on every layer.  Rounds of four processes
+    in D-S-S-D / S-D-D-S order, each a fresh engine timing ``--steps`` runs
+    after ``--warmup`` (reference ttft_abba.py:73-197: alternating process
+    order and a bootstrap over rounds).  vLLM 0.22's FlashAttention extension
+    is not built in this image, so its attention backend here is the Triton
+    one (``TRITON_ATTN``), which the plugin hooks like FlashAttention."""
+    import random
+    import subprocess
+
+    rounds = max(1, args.rounds)
+    per_mode: dict[str, list[float]] = {"dense": [], "triangle": []}
+    per_round: list[dict[str, list[float]]] = []
+    counts = {}
+    for r in range(rounds):
+        order = ("dense", "triangle", "triangle", "dense") if r % 2 == 0 else \
+            ("triangle", "dense", "dense", "triangle")
+        got: dict[str, list[float]] = {"dense": [], "triangle": []}
+        for mode in order:
+            res = subprocess.run([sys.executable, str(Path(__file__).resolve()),
+                                  "--ttft-vllm-worker", mode, "--steps", str(args.steps),
+                                  "--warmup", str(args.warmup)],
+                                 capture_output=True, text=True, timeout=900)
+            lines = [ln for ln in res.stdout.splitlines() if ln.startswith("TTFT_VLLM ")]
+            if res.returncode != 0 or not lines:
+                raise RuntimeError(f"vLLM worker ({mode}) failed:\n{res.stdout[-2000:]}\n"
+                                   f"{res.stderr[-4000:]}")
+            rec = json.loads(lines[-1][len("TTFT_VLLM "):])
+            if rec["status"]:
+                raise RuntimeError(f"device status {rec['status']:#x} in the {mode} worker")
+            med = sorted(rec["ttft_ms"])[len(rec["ttft_ms"]) // 2]
+            got[mode].append(med)
+            per_mode[mode].append(med)
+            counts[mode] = rec["per_prefill"]
+        per_round.append(got)
+    med = {m: sorted(v)[len(v) // 2] for m, v in per_mode.items()}
+    # Bootstrap over rounds of the ratio of per-mode means (a round keeps its
+    # pair of processes per mode together).
+    rng = random.Random(0)
+    ratios = []
+    for _ in range(2000):
+        pick = [per_round[rng.randrange(rounds)] for _ in range(rounds)]
+        d = sum(sum(x["dense"]) for x in pick) / sum(len(x["dense"]) for x in pick)
+        t = sum(sum(x["triangle"]) for x in pick) / sum(len(x["triangle"]) for x in pick)
+        ratios.append(d / t)
+    ratios.sort()
+    line = {"metric": METRIC, "workload": "ttft_qwen3_8b_8320_c2048_vllm",
+            "value": med["triangle"], "unit": "ms TTFT", "higher_is_better": False,
+            "n_gpus": 1, "rounds": rounds, "runs_per_process": args.steps, "warmup": args.warmup,
+            "data": "synthetic (vLLM dummy-weight Qwen3-8B, uniform random token ids)",
+            "dtype": "bf16",
+            "config": {"engine": "vLLM 0.22, one process per run set, enforce_eager, prefix "
+                                 "caching off, chunked prefill 2048, block 128",
+                       "stock_attention": "TRITON_ATTN (vLLM's FlashAttention extension is not "
+                                          "built in this image)",
+                       "triangle_layers": TTFT_LAYERS, "thresholds": "b200 profile",
+                       "prompt": TTFT_PROMPT, "chunk": TTFT_CHUNK},
+            "ttft_ms": {"triangle": med["triangle"], "dense": med["dense"],
+                        "speedup": med["dense"] / med["triangle"],
+                        "speedup_ci95": [ratios[int(0.025 * len(ratios))],
+                                         ratios[int(0.975 * len(ratios)) - 1]]},
+            "process_medians_ms": per_mode, "attention_calls_per_prefill": counts,
+            "order": "D-S-S-D / S-D-D-S rounds of fresh engine processes"}
+    print(json.dumps(line), flush=True)
+
+
 def workload_config(args, seq: int | None = None, tq: int | None = None) -> dict:
     seq = args.seq_len if seq is None else seq
     tq = args.query_tokens if tq is None else tq
@@ -1021,6 +1149,12 @@ def main() -> None:
     ap.add_argument("--ttft", action="store_true",
                     help="BASELINE config 2: Qwen3-8B prefill TTFT, TriangleMix layers against "
                          "all-dense (one GPU)")
+    ap.add_argument("--ttft-vllm", action="store_true",
+                    help="BASELINE config 2 through a live vLLM engine: D-S-S-D rounds of "
+                         "engine processes (one GPU)")
+    ap.add_argument("--rounds", type=int, default=2, help="--ttft-vllm: D-S-S-D rounds")
+    ap.add_argument("--ttft-vllm-worker", choices=("dense", "triangle"), default=None,
+                    help=argparse.SUPPRESS)
     ap.add_argument("--rank-sweep", action="store_true",
                     help="one GPU: time the launch each rank of an N-GPU KV-head partition "
                          "runs, N = 1, 2, 4, 8")
@@ -1050,6 +1184,14 @@ def main() -> None:
         if world != 1:
             ap.error("--ttft runs on one GPU")
         run_ttft(args)
+        return
+    if args.ttft_vllm_worker:
+        ttft_vllm_worker(args.ttft_vllm_worker, args.steps, args.warmup)
+        return
+    if args.ttft_vllm:
+        if world != 1:
+            ap.error("--ttft-vllm runs on one GPU")
+        run_ttft_vllm(args)
         return
     if args.batch:
         if world != 1:

@@ -222,7 +222,7 @@ def varlen_workspace_size(cu_seqlens_q, seq_lens, prompt_lens, *, kv_heads=None)
 
 def paged_attention_varlen(query, key_cache, value_cache, block_tables, out, cu_seqlens_q,
                            seq_lens, prompt_lens, scale: float, *, kv_heads=None,
-                           workspace=None, stream=None) -> None:
+                           workspace=None, stream=None, value_offset_pages: int = 0) -> None:
     """Packed ragged batch through the C ABI.
 
     ``query``/``out`` are packed ``[cu_seqlens_q[-1], 32, 128]`` CUDA tensors and
@@ -230,7 +230,8 @@ def paged_attention_varlen(query, key_cache, value_cache, block_tables, out, cu_
     metadata (``cu_seqlens_q``, ``seq_lens``, ``prompt_lens``) are host integer
     sequences.  With ``kv_heads`` the head-slice form runs (``[rows, 4*kv_heads,
     128]`` queries, ``kv_heads``-head caches).  A workspace is allocated from
-    torch when none is given.
+    torch when none is given.  ``value_offset_pages`` > 0 reads V that many
+    pages past the start of ``value_cache`` (see ``paged_attention``).
     """
     import torch
 
@@ -240,7 +241,8 @@ def paged_attention_varlen(query, key_cache, value_cache, block_tables, out, cu_
     if workspace is None:
         nbytes = varlen_workspace_size(cu_seqlens_q, seq_lens, prompt_lens, kv_heads=kv_heads)
         workspace = torch.empty(nbytes, dtype=torch.uint8, device=query.device)
-    common = (query.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(),
+    common = (query.data_ptr(), key_cache.data_ptr(),
+              _value_ptr(value_cache, value_offset_pages),
               block_tables.data_ptr(), out.data_ptr(), batch, _int64_array(cu_seqlens_q),
               _int64_array(seq_lens), _int64_array(prompt_lens), key_cache.shape[0],
               block_tables.shape[-1], scale)
@@ -267,10 +269,27 @@ def device_status(device: int = 0) -> int:
     return bits.value
 
 
+def _value_ptr(value_cache, offset_pages: int) -> int:
+    """Address of V: ``offset_pages`` cache pages past ``value_cache``'s start.
+
+    vLLM's Triton backend stores a block's K and V pages next to each other
+    (``[num_blocks, 2, 128, heads, 128]``).  Viewed as ``2 * num_blocks``
+    pages, block b's K page is page 2b and its V page is 2b + 1: the launch
+    passes that view as both caches, the block table doubled, and V one page
+    further, so that V of table entry 2b is page 2b + 1.
+    """
+    page_bytes = value_cache[0].numel() * value_cache.element_size()
+    return value_cache.data_ptr() + offset_pages * page_bytes
+
+
 def paged_attention(query, key_cache, value_cache, block_table, out, query_start: int,
                     seq_len: int, prompt_len: int, scale: float, *, kv_heads: int | None = None,
-                    workspace=None, stream=None, visited=None, tile_counter=None) -> None:
-    """Launch through the C ABI with torch CUDA tensors (no checks beyond the ABI's)."""
+                    workspace=None, stream=None, visited=None, tile_counter=None,
+                    value_offset_pages: int = 0) -> None:
+    """Launch through the C ABI with torch CUDA tensors (no checks beyond the ABI's).
+
+    ``value_offset_pages`` > 0 reads V that many pages past the start of
+    ``value_cache`` (an interleaved K/V page layout, ``_value_ptr``)."""
     import torch
 
     if stream is None:
@@ -278,9 +297,9 @@ def paged_attention(query, key_cache, value_cache, block_table, out, query_start
     h = lib()
     ws_ptr = workspace.data_ptr() if workspace is not None else None
     ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
-    common = (query.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(), block_table.data_ptr(),
-              out.data_ptr(), query.shape[0], key_cache.shape[0], block_table.shape[-1],
-              query_start, seq_len, prompt_len, scale)
+    common = (query.data_ptr(), key_cache.data_ptr(), _value_ptr(value_cache, value_offset_pages),
+              block_table.data_ptr(), out.data_ptr(), query.shape[0], key_cache.shape[0],
+              block_table.shape[-1], query_start, seq_len, prompt_len, scale)
     if visited is not None:
         check(h.tpsa_paged_attention_visit(*common, kv_heads or key_cache.shape[2], ws_ptr, ws_bytes,
                                            visited.data_ptr(), tile_counter.data_ptr(), stream))

@@ -17,10 +17,15 @@ FlashAttention backend:
   vLLM's v1 engine the KV cache write is a separate step, so ``forward`` only
   reads the paged cache ``[2, num_blocks, block_size, kv_heads, head_size]``,
   which is this kernel's BSND layout when ``block_size`` is 128;
+  ``install_vllm_triton_attention_hook`` does the same for vLLM's Triton
+  backend, whose cache ``[num_blocks, 2, block_size, kv_heads, head_size]``
+  the kernel reads in place as interleaved K and V pages;
 * ``install_vllm_metadata_patch`` puts each step's host lengths and the
-  scheduler's final prompt lengths on vLLM's FlashAttention metadata (the
+  scheduler's final prompt lengths on the backend's metadata (the
   reference attaches the runner's prompt lengths the same way,
-  plugin.py:523-570, 946);
+  plugin.py:523-570, 946); ``install_vllm_v2_runner_patch`` publishes the
+  prompt lengths from vLLM's V2 model runner (the default for Qwen3 in vLLM
+  0.22);
 * ``register`` is the ``vllm.general_plugins`` entry point (pyproject.toml;
   reference setup.py:292-294, plugin.py:1705-1741): it installs both, with
   the configuration read from ``additional_config.trianglemix`` when vLLM
@@ -238,7 +243,7 @@ class TriangleMixRouter:
         return ws
 
     def _launch(self, plan: TriangleBatchPlan, query, key_cache, value_cache, block_table,
-                out) -> int:
+                out, value_offset_pages: int = 0) -> int:
         reqs = plan.requests[:plan.batch_size]
         scale = SUPPORTED_HEAD_SIZE ** -0.5
         stream = torch.cuda.current_stream(query.device).cuda_stream
@@ -251,7 +256,7 @@ class TriangleMixRouter:
                                     r.q_begin, r.seq_len, r.prompt_len, scale,
                                     kv_heads=kv_heads,
                                     workspace=self._workspace(query.device, nbytes),
-                                    stream=stream)
+                                    stream=stream, value_offset_pages=value_offset_pages)
             return 1
         cu = plan.cu_seqlens_q
         seqs = [r.seq_len for r in reqs]
@@ -260,17 +265,19 @@ class TriangleMixRouter:
         _native.paged_attention_varlen(query, key_cache, value_cache, block_table, out, cu, seqs,
                                        prompts, scale,
                                        workspace=self._workspace(query.device, nbytes),
-                                       stream=stream)
+                                       stream=stream, value_offset_pages=value_offset_pages)
         return -(-plan.batch_size // 16)
 
     def attend(self, plan: TriangleBatchPlan, layer_name: str, query: torch.Tensor,
                key_cache: torch.Tensor, value_cache: torch.Tensor, block_table: torch.Tensor,
                out: torch.Tensor, *, causal: bool = True,
-               unsupported_features: bool = False) -> bool:
+               unsupported_features: bool = False, value_offset_pages: int = 0) -> bool:
         """Run the kernel into ``out`` if the call qualifies; False: run the stock backend.
 
         With ``strict`` configured, a launch error raises instead of falling
-        back (reference plugin.py:1406-1535).
+        back (reference plugin.py:1406-1535).  ``value_offset_pages`` = 1 with
+        one interleaved page view as both caches reads vLLM's
+        ``[num_blocks, 2, ...]`` cache (``_native._value_ptr``).
         """
         layer_index = extract_layer_index(layer_name)
         reason = self.dispatch_reason(plan, query, key_cache, value_cache, block_table, out,
@@ -281,7 +288,8 @@ class TriangleMixRouter:
             return False
         started = time.perf_counter_ns()
         try:
-            launches = self._launch(plan, query, key_cache, value_cache, block_table, out)
+            launches = self._launch(plan, query, key_cache, value_cache, block_table, out,
+                                    value_offset_pages)
         except Exception:
             self.stats.record_runtime_error(stage="direct_launch")
             if self.config.strict:
@@ -297,22 +305,36 @@ class TriangleMixRouter:
 
 
 _HOOK_ATTR = "_trianglemix_original_forward"
+# The doubled block table of an interleaved-cache step, kept on its metadata.
+INTERLEAVED_TABLE_ATTR = "trianglemix_interleaved_block_table"
 
 
-def install_vllm_flash_attention_hook(router: TriangleMixRouter, *, impl_cls: type | None = None,
-                                      prompt_lens_provider: Callable[[Any], Sequence[int]]
-                                      | None = None) -> bool:
-    """Wrap FlashAttentionImpl.forward so selected layers take the TriangleMix kernel.
+def interleaved_pages(kv_cache: torch.Tensor) -> torch.Tensor | None:
+    """vLLM's ``[num_blocks, 2, block_size, kv_heads, head_size]`` cache (the
+    Triton backend's) as ``2 * num_blocks`` pages: block b's K page is page
+    2b and its V page 2b + 1.  None when the cache has another shape or is
+    not contiguous."""
+    if kv_cache.dim() != 5 or kv_cache.shape[1] != 2 or not kv_cache.is_contiguous():
+        return None
+    return kv_cache.view(kv_cache.shape[0] * 2, *kv_cache.shape[2:])
 
-    ``impl_cls`` defaults to vLLM's ``FlashAttentionImpl``; returns False when
-    vLLM is not importable.  Installing twice replaces the router.
-    """
-    if impl_cls is None:
-        try:
-            from vllm.v1.attention.backends.flash_attn import FlashAttentionImpl as impl_cls
-        except Exception:  # vLLM absent or incompatible: nothing to hook
-            return False
-    original = getattr(impl_cls, _HOOK_ATTR, None) or impl_cls.forward
+
+def interleaved_block_table(metadata: Any) -> torch.Tensor:
+    """The step's block table with every entry doubled (block b -> K page 2b),
+    computed once per metadata object and shared by the step's layers."""
+    table = getattr(metadata, INTERLEAVED_TABLE_ATTR, None)
+    if table is None:
+        table = metadata.block_table * 2
+        setattr(metadata, INTERLEAVED_TABLE_ATTR, table)
+    return table
+
+
+def _wrap_forward(router: TriangleMixRouter, original: Callable, interleaved: bool,
+                  prompt_lens_provider: Callable[[Any], Sequence[int]] | None) -> Callable:
+    """A backend ``forward`` that runs selected layers through ``router`` and
+    everything else (and every call the kernel cannot take) through
+    ``original``.  ``interleaved``: the cache is ``[num_blocks, 2, ...]``
+    (vLLM's Triton backend), else ``[2, num_blocks, ...]`` (FlashAttention)."""
 
     def forward(self, layer, query, key, value, kv_cache, attn_metadata, output,
                 output_scale=None, output_block_scale=None):
@@ -320,19 +342,31 @@ def install_vllm_flash_attention_hook(router: TriangleMixRouter, *, impl_cls: ty
         if (attn_metadata is None or output_scale is not None or output_block_scale is not None
                 or not router.selects(name)):
             return original(self, layer, query, key, value, kv_cache, attn_metadata, output,
-                             output_scale, output_block_scale)
+                            output_scale, output_block_scale)
         plan = router.plan_for_metadata(attn_metadata, prompt_lens_provider)
+        reason = None
         if (int(getattr(self, "dcp_world_size", 1) or 1) > 1
                 or int(getattr(self, "pcp_world_size", 1) or 1) > 1):
             # Context parallelism shards the KV cache across ranks, so this
             # rank's cache holds part of each sequence (reference
             # plugin.py:1254-1256 falls back the same way).
+            reason = FallbackReason.CONTEXT_PARALLEL
+        elif interleaved:
+            pages = interleaved_pages(kv_cache)
+            if pages is None:
+                reason = FallbackReason.KV_CACHE_UNSUPPORTED
+            else:
+                key_cache = value_cache = pages
+                table, offset = interleaved_block_table(attn_metadata), 1
+        else:
+            key_cache, value_cache = kv_cache.unbind(0)
+            table, offset = attn_metadata.block_table, 0
+        if reason is not None:
             router.stats.record_layer_fallback(plan_id=plan.plan_id,
                                                layer_index=extract_layer_index(name),
-                                               reason=FallbackReason.CONTEXT_PARALLEL)
+                                               reason=reason)
             return original(self, layer, query, key, value, kv_cache, attn_metadata, output,
                             output_scale, output_block_scale)
-        key_cache, value_cache = kv_cache.unbind(0)
         rows = int(getattr(attn_metadata, "num_actual_tokens", query.shape[0]))
         q = query[:rows]
         out = output[:rows].view(rows, q.shape[1], -1)
@@ -340,16 +374,47 @@ def install_vllm_flash_attention_hook(router: TriangleMixRouter, *, impl_cls: ty
                   or getattr(self, "alibi_slopes", None) is not None
                   or bool(getattr(self, "logits_soft_cap", 0) or 0)
                   or getattr(self, "sinks", None) is not None)
-        if router.attend(plan, name, q, key_cache, value_cache, attn_metadata.block_table, out,
+        if router.attend(plan, name, q, key_cache, value_cache, table, out,
                          causal=bool(getattr(attn_metadata, "causal", True)),
-                         unsupported_features=extras):
+                         unsupported_features=extras, value_offset_pages=offset):
             return output
         return original(self, layer, query, key, value, kv_cache, attn_metadata, output,
                         output_scale, output_block_scale)
 
+    return forward
+
+
+def _install_hook(router, impl_cls, interleaved, prompt_lens_provider) -> bool:
+    original = getattr(impl_cls, _HOOK_ATTR, None) or impl_cls.forward
     setattr(impl_cls, _HOOK_ATTR, original)
-    impl_cls.forward = forward
+    impl_cls.forward = _wrap_forward(router, original, interleaved, prompt_lens_provider)
     return True
+
+
+def _uninstall_hook(impl_cls) -> bool:
+    original = getattr(impl_cls, _HOOK_ATTR, None)
+    if original is None:
+        return False
+    impl_cls.forward = original
+    delattr(impl_cls, _HOOK_ATTR)
+    return True
+
+
+def install_vllm_flash_attention_hook(router: TriangleMixRouter, *, impl_cls: type | None = None,
+                                      prompt_lens_provider: Callable[[Any], Sequence[int]]
+                                      | None = None) -> bool:
+    """Wrap FlashAttentionImpl.forward so selected layers take the TriangleMix kernel.
+
+    ``impl_cls`` defaults to vLLM's ``FlashAttentionImpl`` (cache
+    ``[2, num_blocks, block_size, kv_heads, head_size]``); returns False when
+    vLLM is not importable.  Installing twice replaces the router.
+    """
+    if impl_cls is None:
+        try:
+            from vllm.v1.attention.backends.flash_attn import FlashAttentionImpl as impl_cls
+        except Exception:  # vLLM absent or incompatible: nothing to hook
+            return False
+    return _install_hook(router, impl_cls, False, prompt_lens_provider)
 
 
 def uninstall_vllm_flash_attention_hook(impl_cls: type | None = None) -> bool:
@@ -358,12 +423,35 @@ def uninstall_vllm_flash_attention_hook(impl_cls: type | None = None) -> bool:
             from vllm.v1.attention.backends.flash_attn import FlashAttentionImpl as impl_cls
         except Exception:
             return False
-    original = getattr(impl_cls, _HOOK_ATTR, None)
-    if original is None:
-        return False
-    impl_cls.forward = original
-    delattr(impl_cls, _HOOK_ATTR)
-    return True
+    return _uninstall_hook(impl_cls)
+
+
+def install_vllm_triton_attention_hook(router: TriangleMixRouter, *, impl_cls: type | None = None,
+                                       prompt_lens_provider: Callable[[Any], Sequence[int]]
+                                       | None = None) -> bool:
+    """Wrap TritonAttentionImpl.forward (vLLM's Triton backend) the same way.
+
+    Its cache is ``[num_blocks, 2, block_size, kv_heads, head_size]``: a
+    block's K and V pages are adjacent.  The kernel reads it in place as
+    ``2 * num_blocks`` pages with the block table doubled and V one page past
+    K (``interleaved_pages``, ``_native._value_ptr``).  Returns False when
+    vLLM is not importable.
+    """
+    if impl_cls is None:
+        try:
+            from vllm.v1.attention.backends.triton_attn import TritonAttentionImpl as impl_cls
+        except Exception:
+            return False
+    return _install_hook(router, impl_cls, True, prompt_lens_provider)
+
+
+def uninstall_vllm_triton_attention_hook(impl_cls: type | None = None) -> bool:
+    if impl_cls is None:
+        try:
+            from vllm.v1.attention.backends.triton_attn import TritonAttentionImpl as impl_cls
+        except Exception:
+            return False
+    return _uninstall_hook(impl_cls)
 
 
 # ------------------------------------------------------------ step metadata
@@ -377,7 +465,7 @@ _RUNNER_ATTR = "_trianglemix_original_build_attention_metadata"
 
 def install_vllm_metadata_patch(*, builder_cls: type | None = None,
                                 runner_cls: type | None = None) -> bool:
-    """Put host lengths and final prompt lengths on each FlashAttention metadata.
+    """Put host lengths and final prompt lengths on each step's attention metadata.
 
     ``runner_cls._build_attention_metadata`` (vLLM's GPUModelRunner) is
     wrapped to publish ``input_batch.num_prompt_tokens`` of the step's
@@ -455,6 +543,87 @@ def uninstall_vllm_metadata_patch(*, builder_cls: type | None = None,
     return done
 
 
+# vLLM's V2 model runner (vllm/v1/worker/gpu, the default for Qwen3 in vLLM
+# 0.22) builds a step's attention metadata in ModelState.prepare_attn from its
+# InputBatch; the scheduler's prompt lengths are in the runner's
+# req_states.prompt_len, indexed by the batch's idx_mapping_np.
+_V2_RUNNER: contextvars.ContextVar[Any] = contextvars.ContextVar("trianglemix_v2_runner",
+                                                                 default=None)
+_V2_EXEC_ATTR = "_trianglemix_original_execute_model"
+_V2_PREP_ATTR = "_trianglemix_original_prepare_attn"
+
+
+def install_vllm_v2_runner_patch(*, runner_cls: type | None = None,
+                                 state_cls: type | None = None) -> bool:
+    """Publish the final prompt lengths of each V2-runner step to the metadata
+    builder patch (``install_vllm_metadata_patch``).
+
+    ``runner_cls.execute_model`` is wrapped to make the runner visible while
+    it runs; ``state_cls.prepare_attn`` is wrapped to read the prompt length
+    of each batch row and publish them while the metadata is built.  Returns
+    False when vLLM's V2 runner is not importable.
+    """
+    if runner_cls is None or state_cls is None:
+        try:
+            from vllm.v1.worker.gpu.model_runner import GPUModelRunner as V2Runner
+            from vllm.v1.worker.gpu.model_states.default import DefaultModelState
+        except Exception:
+            return False
+        runner_cls = runner_cls or V2Runner
+        state_cls = state_cls or DefaultModelState
+    execute = getattr(runner_cls, _V2_EXEC_ATTR, None) or runner_cls.execute_model
+    prepare = getattr(state_cls, _V2_PREP_ATTR, None) or state_cls.prepare_attn
+
+    def execute_model(self, *args, **kwargs):
+        token = _V2_RUNNER.set(self)
+        try:
+            return execute(self, *args, **kwargs)
+        finally:
+            _V2_RUNNER.reset(token)
+
+    def prepare_attn(self, input_batch, *args, **kwargs):
+        prompts = None
+        runner = _V2_RUNNER.get()
+        if runner is not None:
+            try:
+                rows = input_batch.idx_mapping_np[:int(input_batch.num_reqs)]
+                prompts = tuple(int(x) for x in runner.req_states.prompt_len.np[rows])
+            except Exception:  # another runner layout: the step falls back
+                runtime_stats().record_runtime_error(stage="v2_prompt_lengths")
+        token = _STEP_PROMPTS.set(prompts)
+        try:
+            return prepare(self, input_batch, *args, **kwargs)
+        finally:
+            _STEP_PROMPTS.reset(token)
+
+    setattr(runner_cls, _V2_EXEC_ATTR, execute)
+    runner_cls.execute_model = execute_model
+    setattr(state_cls, _V2_PREP_ATTR, prepare)
+    state_cls.prepare_attn = prepare_attn
+    return True
+
+
+def uninstall_vllm_v2_runner_patch(*, runner_cls: type | None = None,
+                                   state_cls: type | None = None) -> bool:
+    if runner_cls is None or state_cls is None:
+        try:
+            from vllm.v1.worker.gpu.model_runner import GPUModelRunner as V2Runner
+            from vllm.v1.worker.gpu.model_states.default import DefaultModelState
+        except Exception:
+            return False
+        runner_cls = runner_cls or V2Runner
+        state_cls = state_cls or DefaultModelState
+    done = False
+    for cls, attr, name in ((runner_cls, _V2_EXEC_ATTR, "execute_model"),
+                            (state_cls, _V2_PREP_ATTR, "prepare_attn")):
+        original = getattr(cls, attr, None)
+        if original is not None:
+            setattr(cls, name, original)
+            delattr(cls, attr)
+            done = True
+    return done
+
+
 # ------------------------------------------------------------ vLLM plugin entry
 _REGISTER_LOCK = threading.Lock()
 _ROUTER: TriangleMixRouter | None = None
@@ -504,36 +673,78 @@ def _configure_from_vllm(router: TriangleMixRouter, impl_cls: type) -> None:
     impl_cls.__init__ = __init__
 
 
+# vLLM attention backends the plugin hooks: (module, impl class, metadata
+# builder class, cache layout interleaved).  FlashAttention is vLLM's CUDA
+# default; the Triton backend runs where vLLM's FlashAttention extension is
+# not built (as in this image).
+_BACKENDS = (
+    ("vllm.v1.attention.backends.flash_attn", "FlashAttentionImpl",
+     "FlashAttentionMetadataBuilder", False),
+    ("vllm.v1.attention.backends.triton_attn", "TritonAttentionImpl",
+     "TritonAttentionMetadataBuilder", True),
+)
+_HOOKED: list[tuple[type, type]] = []  # (impl class, builder class) hooked by register
+
+
 def register() -> None:
     """vLLM ``general_plugins`` entry point (declared in pyproject.toml).
 
-    Installs the FlashAttention hook and the metadata patch once per process
+    Installs the forward hook and the metadata patch on each of vLLM's
+    FlashAttention and Triton backends that imports, once per process
     (reference plugin.py:1705-1741).  The configuration starts from the
     environment and is replaced by ``additional_config.trianglemix`` when vLLM
-    builds its first FlashAttention layer; the path is off unless enabled.
+    builds its first hooked attention layer; the path is off unless enabled.
     A failure leaves vLLM's own attention in place, or raises with
     ``strict``.
     """
+    import importlib
+
     global _ROUTER
     with _REGISTER_LOCK:
         if _ROUTER is not None:
             return
+        hooked: list[tuple[type, type]] = []
         try:
-            from vllm.v1.attention.backends.flash_attn import FlashAttentionImpl
+            from vllm.v1.worker.gpu_model_runner import GPUModelRunner
 
             router = TriangleMixRouter(resolve_plugin_config(None))
-            _configure_from_vllm(router, FlashAttentionImpl)
-            if not install_vllm_flash_attention_hook(router, impl_cls=FlashAttentionImpl):
-                raise RuntimeError("FlashAttentionImpl could not be hooked")
-            install_vllm_metadata_patch()
+            for module, impl_name, builder_name, interleaved in _BACKENDS:
+                try:
+                    mod = importlib.import_module(module)
+                    impl_cls, builder_cls = getattr(mod, impl_name), getattr(mod, builder_name)
+                except Exception:  # this vLLM build lacks the backend
+                    continue
+                _configure_from_vllm(router, impl_cls)
+                _install_hook(router, impl_cls, interleaved, None)
+                if not install_vllm_metadata_patch(builder_cls=builder_cls,
+                                                   runner_cls=GPUModelRunner):
+                    raise RuntimeError(f"{builder_name} could not be patched")
+                hooked.append((impl_cls, builder_cls))
+            if not hooked:
+                raise RuntimeError("no vLLM attention backend could be hooked")
+            install_vllm_v2_runner_patch()
         except Exception:
+            for impl_cls, builder_cls in hooked:
+                _unhook(impl_cls, builder_cls)
             runtime_stats().record_runtime_error(stage="plugin_register")
             if _strict_from_environment():
                 raise
             logger.warning("TriangleMix plugin could not hook vLLM; the stock attention "
                            "path stays active", exc_info=True)
             return
+        _HOOKED[:] = hooked
         _ROUTER = router
+
+
+def _unhook(impl_cls: type, builder_cls: type) -> None:
+    from vllm.v1.worker.gpu_model_runner import GPUModelRunner
+
+    _uninstall_hook(impl_cls)
+    uninstall_vllm_metadata_patch(builder_cls=builder_cls, runner_cls=GPUModelRunner)
+    original = getattr(impl_cls, _INIT_ATTR, None)
+    if original is not None:
+        impl_cls.__init__ = original
+        delattr(impl_cls, _INIT_ATTR)
 
 
 def unregister() -> bool:
@@ -542,13 +753,9 @@ def unregister() -> bool:
     with _REGISTER_LOCK:
         if _ROUTER is None:
             return False
-        from vllm.v1.attention.backends.flash_attn import FlashAttentionImpl
-
-        uninstall_vllm_flash_attention_hook(FlashAttentionImpl)
-        uninstall_vllm_metadata_patch()
-        original = getattr(FlashAttentionImpl, _INIT_ATTR, None)
-        if original is not None:
-            FlashAttentionImpl.__init__ = original
-            delattr(FlashAttentionImpl, _INIT_ATTR)
+        for impl_cls, builder_cls in _HOOKED:
+            _unhook(impl_cls, builder_cls)
+        _HOOKED.clear()
+        uninstall_vllm_v2_runner_patch()
         _ROUTER = None
         return True

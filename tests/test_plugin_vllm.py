@@ -190,3 +190,139 @@ def test_router_keeps_one_workspace_per_device():
         assert ws.numel() >= n
     assert len(r._workspaces) == 1
     assert r._workspaces[0].numel() == 3 << 20
+
+
+vllm_triton = pytest.importorskip("vllm.v1.attention.backends.triton_attn")
+
+
+def test_register_hooks_the_triton_backend_too():
+    impl, builder = vllm_triton.TritonAttentionImpl, vllm_triton.TritonAttentionMetadataBuilder
+    originals = (impl.forward, impl.__init__, builder.build)
+    forward_params = list(inspect.signature(impl.forward).parameters)
+    tm.plugin.register()
+    try:
+        assert impl.forward is not originals[0] and impl._trianglemix_original_forward is originals[0]
+        assert impl.__init__ is not originals[1] and builder.build is not originals[2]
+        assert list(inspect.signature(impl.forward).parameters) == forward_params
+        # The Triton backend's cache shape, which the hook reads in place.
+        assert vllm_triton.TritonAttentionBackend.get_kv_cache_shape(10, 128, 8, 128) == \
+            (10, 2, 128, 8, 128)
+        fields = {f.name for f in __import__("dataclasses").fields(vllm_triton.TritonAttentionMetadata)}
+        assert {"query_start_loc", "seq_lens", "block_table", "num_actual_tokens"} <= fields
+    finally:
+        assert tm.plugin.unregister()
+    assert (impl.forward, impl.__init__, builder.build) == originals
+
+
+def test_interleaved_pages_view_and_doubled_table():
+    kv = torch.arange(3 * 2 * 4 * 2 * 3, dtype=torch.float32).view(3, 2, 4, 2, 3)
+    pages = tm.plugin.interleaved_pages(kv)
+    assert pages.shape == (6, 4, 2, 3) and pages.data_ptr() == kv.data_ptr()
+    for b in range(3):
+        assert torch.equal(pages[2 * b], kv[b, 0]) and torch.equal(pages[2 * b + 1], kv[b, 1])
+    assert tm.plugin.interleaved_pages(kv.transpose(0, 1)) is None
+    assert tm.plugin.interleaved_pages(torch.zeros(2, 3, 4, 2, 3)) is None
+    m = types.SimpleNamespace(block_table=torch.tensor([[4, 0, 7]], dtype=torch.int32))
+    table = tm.plugin.interleaved_block_table(m)
+    assert table.dtype == torch.int32 and table.tolist() == [[8, 0, 14]]
+    assert tm.plugin.interleaved_block_table(m) is table  # once per step's metadata
+
+
+class CaptureRouter:
+    """Router stand-in that records what the hook hands to ``attend``."""
+
+    def __init__(self):
+        self.seen = None
+        self.stats = tm.stats.TriangleMixRuntimeStats()
+
+    def selects(self, name):
+        return True
+
+    def plan_for_metadata(self, metadata, provider=None):
+        return types.SimpleNamespace(plan_id=1)
+
+    def attend(self, plan, name, q, key_cache, value_cache, table, out, **kw):
+        self.seen = (key_cache, value_cache, table, kw)
+        return True
+
+
+def test_triton_hook_passes_the_interleaved_cache():
+    r = CaptureRouter()
+    assert tm.plugin.install_vllm_triton_attention_hook(r, impl_cls=FakeImpl)
+    try:
+        impl = FakeImpl()
+        m = types.SimpleNamespace(num_actual_tokens=256,
+                                  block_table=torch.tensor([[3, 1]], dtype=torch.int32))
+        q = torch.zeros(256, 32, 128, dtype=torch.bfloat16)
+        kv = torch.zeros(4, 2, 128, 8, 128, dtype=torch.bfloat16)
+        out = torch.zeros(256, 32 * 128, dtype=torch.bfloat16)
+        layer = types.SimpleNamespace(layer_name="model.layers.3.self_attn.attn")
+        assert impl.forward(layer, q, None, None, kv, m, out) is out
+        assert impl.calls == 0  # the kernel path took the call
+        key_cache, value_cache, table, kw = r.seen
+        assert key_cache.shape == (8, 128, 8, 128) and value_cache is key_cache
+        assert key_cache.data_ptr() == kv.data_ptr()
+        assert table.tolist() == [[6, 2]] and kw["value_offset_pages"] == 1
+        # A cache of another layout goes to the stock path with a reason.
+        impl.forward(layer, q, None, None, kv.transpose(0, 1).contiguous().transpose(0, 1), m, out)
+        assert impl.calls == 1
+        assert r.stats.snapshot()["counters"]["layer_fia_reason:kv_cache_unsupported"] == 1
+    finally:
+        assert tm.plugin.uninstall_vllm_triton_attention_hook(impl_cls=FakeImpl)
+
+
+class FakeV2State:
+    """Builds the step's metadata in prepare_attn, as vLLM's V2 ModelState does."""
+
+    common = None
+
+    def prepare_attn(self, input_batch, cudagraph_mode, block_tables, slot_mappings,
+                     attn_groups, kv_cache_config, for_capture=False):
+        return FakeBuilder().build(common_prefix_len=0, common_attn_metadata=self.common)
+
+
+class FakeV2Runner:
+    def __init__(self, prompt_lens, common):
+        self.req_states = types.SimpleNamespace(
+            prompt_len=types.SimpleNamespace(np=np.array(prompt_lens, dtype=np.int32)))
+        self.model_state = FakeV2State()
+        self.model_state.common = common
+
+    def execute_model(self, input_batch):
+        return self.model_state.prepare_attn(input_batch, None, (), None, [], None)
+
+
+def test_v2_runner_patch_carries_prompt_lengths_in_batch_order():
+    common = types.SimpleNamespace(num_reqs=2, query_start_loc_cpu=torch.tensor([0, 2048, 2176]),
+                                   _seq_lens_cpu=torch.tensor([4096, 8320]))
+    assert tm.plugin.install_vllm_metadata_patch(builder_cls=FakeBuilder, runner_cls=FakeRunner)
+    assert tm.plugin.install_vllm_v2_runner_patch(runner_cls=FakeV2Runner, state_cls=FakeV2State)
+    try:
+        runner = FakeV2Runner([9000, 8320, 4096], common)
+        # Batch rows 0 and 1 are request states 2 and 0.
+        batch = types.SimpleNamespace(num_reqs=2, idx_mapping_np=np.array([2, 0]))
+        meta = runner.execute_model(batch)
+        assert meta.trianglemix_prompt_lens == [4096, 9000]
+        # prepare_attn outside execute_model (a capture or dummy run): none.
+        plain = runner.model_state.prepare_attn(batch, None, (), None, [], None)
+        assert not hasattr(plain, "trianglemix_prompt_lens")
+    finally:
+        assert tm.plugin.uninstall_vllm_v2_runner_patch(runner_cls=FakeV2Runner,
+                                                        state_cls=FakeV2State)
+        assert tm.plugin.uninstall_vllm_metadata_patch(builder_cls=FakeBuilder,
+                                                       runner_cls=FakeRunner)
+
+
+def test_register_patches_vllm_v2_runner():
+    v2_runner = pytest.importorskip("vllm.v1.worker.gpu.model_runner")
+    v2_state = pytest.importorskip("vllm.v1.worker.gpu.model_states.default")
+    runner, state = v2_runner.GPUModelRunner, v2_state.DefaultModelState
+    originals = (runner.execute_model, state.prepare_attn)
+    assert list(inspect.signature(state.prepare_attn).parameters)[:2] == ["self", "input_batch"]
+    tm.plugin.register()
+    try:
+        assert runner.execute_model is not originals[0]
+        assert state.prepare_attn is not originals[1]
+    finally:
+        assert tm.plugin.unregister()
+    assert (runner.execute_model, state.prepare_attn) == originals
