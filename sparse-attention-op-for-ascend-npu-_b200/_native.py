@@ -278,6 +278,8 @@ def _value_ptr(value_cache, offset_pages: int) -> int:
     passes that view as both caches, the block table doubled, and V one page
     further, so that V of table entry 2b is page 2b + 1.
     """
+    if not offset_pages:
+        return value_cache.data_ptr()
     page_bytes = value_cache[0].numel() * value_cache.element_size()
     return value_cache.data_ptr() + offset_pages * page_bytes
 
