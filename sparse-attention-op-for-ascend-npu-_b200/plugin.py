@@ -321,12 +321,16 @@ def interleaved_pages(kv_cache: torch.Tensor) -> torch.Tensor | None:
 
 def interleaved_block_table(metadata: Any) -> torch.Tensor:
     """The step's block table with every entry doubled (block b -> K page 2b),
-    computed once per metadata object and shared by the step's layers."""
-    table = getattr(metadata, INTERLEAVED_TABLE_ATTR, None)
-    if table is None:
-        table = metadata.block_table * 2
-        setattr(metadata, INTERLEAVED_TABLE_ATTR, table)
-    return table
+    computed once per metadata object and shared by the step's layers.  The
+    cached copy is kept with the table it was made from, so a metadata copy
+    that carries another block table (vLLM's ``update_block_table``) gets its
+    own."""
+    source = metadata.block_table
+    cached = getattr(metadata, INTERLEAVED_TABLE_ATTR, None)
+    if cached is None or cached[0] is not source:
+        cached = (source, source * 2)
+        setattr(metadata, INTERLEAVED_TABLE_ATTR, cached)
+    return cached[1]
 
 
 def _wrap_forward(router: TriangleMixRouter, original: Callable, interleaved: bool,

@@ -226,6 +226,12 @@ def test_interleaved_pages_view_and_doubled_table():
     table = tm.plugin.interleaved_block_table(m)
     assert table.dtype == torch.int32 and table.tolist() == [[8, 0, 14]]
     assert tm.plugin.interleaved_block_table(m) is table  # once per step's metadata
+    # A shallow copy with another block table (vLLM's update_block_table).
+    import copy
+    m2 = copy.copy(m)
+    m2.block_table = torch.tensor([[1, 2, 3]], dtype=torch.int32)
+    assert tm.plugin.interleaved_block_table(m2).tolist() == [[2, 4, 6]]
+    assert tm.plugin.interleaved_block_table(m) is table
 
 
 class CaptureRouter:
