@@ -58,6 +58,33 @@ from .stats import TriangleMixRuntimeStats, runtime_stats
 GROUP_SIZE = 4  # query heads per KV head (GQA 4:1)
 logger = logging.getLogger(__name__)
 
+
+class _NvtxRange:
+    """An NVTX range on the host timeline (``trianglemix.plan``,
+    ``trianglemix.attend``), so a profiler shows where the router spends
+    host time; a no-op where NVTX is unavailable."""
+
+    __slots__ = ("name", "pushed")
+
+    def __init__(self, name: str):
+        self.name, self.pushed = name, False
+
+    def __enter__(self):
+        try:
+            torch.cuda.nvtx.range_push(self.name)
+            self.pushed = True
+        except Exception:
+            pass
+        return self
+
+    def __exit__(self, *exc):
+        if self.pushed:
+            try:
+                torch.cuda.nvtx.range_pop()
+            except Exception:
+                pass
+        return False
+
 # Attributes this module puts on vLLM's FlashAttention metadata (host lists).
 QUERY_START_ATTR = "trianglemix_query_start_loc"
 SEQ_LENS_ATTR = "trianglemix_seq_lens"
@@ -180,7 +207,8 @@ class TriangleMixRouter:
         prompts, _ = metadata_prompt_lens(metadata)
         if prompts is None and prompt_lens_provider is not None:
             prompts = _int_list(prompt_lens_provider(metadata))
-        plan = self._plan(query_lens, seq_lens, prompts)
+        with _NvtxRange("trianglemix.plan"):
+            plan = self._plan(query_lens, seq_lens, prompts)
         with self._lock:
             if len(self._plans) > 64:
                 self._plans.clear()
@@ -288,8 +316,9 @@ class TriangleMixRouter:
             return False
         started = time.perf_counter_ns()
         try:
-            launches = self._launch(plan, query, key_cache, value_cache, block_table, out,
-                                    value_offset_pages)
+            with _NvtxRange("trianglemix.attend"):
+                launches = self._launch(plan, query, key_cache, value_cache, block_table, out,
+                                        value_offset_pages)
         except Exception:
             self.stats.record_runtime_error(stage="direct_launch")
             if self.config.strict:

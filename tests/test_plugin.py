@@ -255,3 +255,21 @@ def test_hook_routes_only_selected_layers_and_falls_back():
     finally:
         assert tm.plugin.uninstall_vllm_flash_attention_hook(impl_cls=FakeImpl)
     assert not hasattr(FakeImpl, "_trianglemix_original_forward")
+
+
+def test_nvtx_ranges_are_balanced_and_never_raise(monkeypatch):
+    calls = []
+    monkeypatch.setattr(torch.cuda.nvtx, "range_push", lambda name: calls.append(("push", name)))
+    monkeypatch.setattr(torch.cuda.nvtx, "range_pop", lambda: calls.append(("pop",)))
+    with tm.plugin._NvtxRange("trianglemix.attend"):
+        pass
+    assert calls == [("push", "trianglemix.attend"), ("pop",)]
+
+    def broken(name):
+        raise RuntimeError("no NVTX")
+
+    monkeypatch.setattr(torch.cuda.nvtx, "range_push", broken)
+    calls.clear()
+    with tm.plugin._NvtxRange("trianglemix.plan"):
+        pass
+    assert calls == []  # nothing pushed, nothing popped
