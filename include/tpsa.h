@@ -38,7 +38,10 @@
 extern "C" {
 #endif
 
-#define TPSA_ABI_VERSION 2
+/* 3: tpsa_plan_tile reports the 80-key composite tile (band edge, then
+ * the sink slice [0, 16)); 2 reported a 128-key one (sink prefix, then the
+ * band edge). */
+#define TPSA_ABI_VERSION 3
 
 /* Fixed geometry (reference operator/op_kernel/triangle_schedule.h:14-21). */
 #define TPSA_QUERY_HEADS 32
@@ -123,13 +126,14 @@ TPSA_API tpsa_status tpsa_plan_item(const tpsa_plan* plan, int32_t item,
                            tpsa_item* out);
 
 /*
- * Key tile `tile` of query block `block`: *key_count keys (64 or 128).  The
- * first 64 (all of a 64-key tile) are [*key_begin, *key_begin + 64); keys
- * 64-127 of a 128-key tile are [*upper_begin, *upper_begin + 64), which is
- * *key_begin + 64 except for the composite tile of a sparse block (the sink
- * page prefix [0, 64) joined with the band's 64-key edge).  No 64-key half
- * crosses a page.  *needs_mask is 1 when some row of the block excludes some
- * key of the tile (causal / window / sink boundary).
+ * Key tile `tile` of query block `block`: *key_count keys (64, 80 or 128).
+ * The first 64 (all of a 64-key tile) are [*key_begin, *key_begin + 64); the
+ * rest follow from *upper_begin on: keys 64-127 of a 128-key tile are
+ * [*key_begin + 64, *key_begin + 128), and the 80-key composite tile of a
+ * sparse block (tile 0) is the band's 64-key edge followed by the sink
+ * slice [0, 16) (*upper_begin = 0).  No 64-key half crosses a page.
+ * *needs_mask is 1 when some row of the block excludes some key of the tile
+ * (causal / window / sink boundary; always for the composite tile).
  */
 TPSA_API tpsa_status tpsa_plan_tile(const tpsa_plan* plan, int32_t block, int32_t tile,
                            int32_t* key_begin, int32_t* key_count,

@@ -216,7 +216,6 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr,
       : "memory");
 }
 
-
 // TMA tile store from this CTA's shared memory (bulk async-group completion).
 __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, int32_t c0, int32_t c1,
                                              int32_t c2, uint32_t src) {

@@ -14,9 +14,9 @@
 //     sink page prefix [0, 64) plus the local band [qBegin - 512, qEnd);
 //     when the band starts inside page 0 the two are merged into one range.
 //     The band is 576 keys (4.5 pages) long, so one of its ends is a 64-key
-//     edge; tile 0 joins the sink prefix with that edge into one 128-key
-//     composite tile (keys [0, 64) and [edge, edge + 64)), so the block runs
-//     one 128-key tile where it would run two 64-key tiles;
+//     edge; tile 0 joins that edge with the first 16 keys of the sink page
+//     into one 80-key composite tile (keys [edge, edge + 64) then [0, 16)),
+//     so the block runs one 80-key tile where it would run two 64-key tiles;
 //   * any other block reads the dense range [0, qEnd).
 // A block straddling sparse_begin or sparse_end is not cut into spans as the
 // reference does (triangle_schedule.h:74-99); it reads the dense range and
@@ -47,6 +47,11 @@ constexpr int32_t kBlockQ = 64;        // query tokens per block
 constexpr int32_t kRowsPerTile = 128;  // rows of one tensor-core M tile
 constexpr int32_t kTileKeys = 128;     // widest key tile (one page)
 constexpr int32_t kKeyGrain = 64;      // key tiles are multiples of this
+// A composite tile: a 64-key band edge, then the first kSinkSlice keys of
+// page 0 (the smallest N step of an M = 128 MMA that holds the sink).
+constexpr int32_t kSinkSlice = 16;
+constexpr int32_t kCompositeKeys = kKeyGrain + kSinkSlice;  // 80
+static_assert(kSinkTokens <= kSinkSlice, "the sink fits the composite tile's sink slice");
 constexpr int32_t kMinSplitTiles = 4;  // never split below this many tiles
 constexpr int32_t kMaxSeqLen = 1 << 30;
 // Partial result of one split item: 256 rows x (128 O values + m + l), fp32.
@@ -65,7 +70,7 @@ struct BlockTiles {
   int32_t q_begin;    // absolute position of the block's first row
   int32_t q_end;      // one past its last real row (<= seq_len)
   int32_t sink;       // 1: tile 0 is the sink tile [0, 64); 2: tile 0 is the
-                      // composite tile [0, 64) + [edge, edge + 64)
+                      // composite tile [edge, edge + 64) + [0, 16)
   int32_t key_begin;  // 64-aligned start of the contiguous key range
   int32_t key_end;    // 64-aligned end of the contiguous key range
   int32_t count;      // number of key tiles
@@ -97,7 +102,8 @@ TPSA_HD BlockTiles block_tiles(const tpsa_plan& p, int32_t block) {
     if (band >= kTileKeys) {
       t.sink = 1;
       t.key_begin = band;
-      // A band end half-way through a page becomes the upper half of tile 0.
+      // A band end half-way through a page becomes the lower 64 keys of
+      // tile 0.
       if (t.key_begin % kTileKeys != 0) {
         t.sink = 2;
         t.edge = t.key_begin;
@@ -113,15 +119,16 @@ TPSA_HD BlockTiles block_tiles(const tpsa_plan& p, int32_t block) {
   return t;
 }
 
-// Tile `tile` of a block: *width keys, the first 64 (or all of a 64-key
-// tile) from *k0 on; keys 64-127 of a 128-key tile start at
-// upper_key(t, tile, *k0), which is *k0 + 64 except for the composite tile.
+// Tile `tile` of a block: *width keys (64, 80 or 128), the first 64 (or all
+// of a 64-key tile) from *k0 on; the keys after the first 64 start at
+// upper_key(t, tile, *k0): *k0 + 64 in a 128-key tile, key 0 in the 80-key
+// composite tile (whose first 64 keys are the band edge).
 TPSA_HD void tile_keys(const BlockTiles& t, int32_t tile, int32_t* k0,
                        int32_t* width) {
   if (t.sink != 0) {
     if (tile == 0) {
-      *k0 = 0;
-      *width = t.sink == 2 ? kTileKeys : kKeyGrain;
+      *k0 = t.sink == 2 ? t.edge : 0;
+      *width = t.sink == 2 ? kCompositeKeys : kKeyGrain;
       return;
     }
     tile -= 1;
@@ -134,15 +141,16 @@ TPSA_HD void tile_keys(const BlockTiles& t, int32_t tile, int32_t* k0,
 }
 
 TPSA_HD int32_t upper_key(const BlockTiles& t, int32_t tile, int32_t k0) {
-  return (t.sink == 2 && tile == 0) ? t.edge : k0 + kKeyGrain;
+  return (t.sink == 2 && tile == 0) ? 0 : k0 + kKeyGrain;
 }
 
-// True when some real row of the block excludes some key of [k0, k0 + w)
-// (the composite tile always has excluded keys: only keys 0-7 of its lower
-// half are in the sparse rows' sets).  Conservative for blocks that mix
-// dense and sparse rows.
+// True when some real row of the block excludes some key of the tile that
+// starts at k0 and is w keys wide (the composite tile always has excluded
+// keys: only keys 0-7 of its sink slice are in the sparse rows' sets).
+// Conservative for blocks that mix dense and sparse rows.
 TPSA_HD bool tile_needs_mask(const tpsa_plan& p, const BlockTiles& t,
                              int32_t k0, int32_t w) {
+  if (w == kCompositeKeys) return true;
   if (k0 + w - 1 > t.q_begin) return true;  // causal edge of the first row
   if (t.all_dense) return false;
   const int32_t last_sparse = min_i(t.q_end, p.sparse_end) - 1;

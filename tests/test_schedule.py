@@ -31,7 +31,7 @@ def test_library_exports_every_declared_symbol(tm):
     lib = tm._native.lib()
     for name in declared:
         assert hasattr(lib, name)
-    assert lib.tpsa_abi_version() == 2
+    assert lib.tpsa_abi_version() == 3
 
 
 def test_adapter_library_is_built(tm):
@@ -99,16 +99,19 @@ def test_tile_schedule_covers_exact_key_sets(tm, q0, tq, seq, prompt):
                 k0, w, masked, up = tm._native.plan_tile(plan, b, t)
             except tm.TpsaError:
                 break
-            assert w in (64, 128) and k0 % 64 == 0 and up % 64 == 0
-            halves = [k0] if w == 64 else [k0, up]
-            if w == 128 and up != k0 + 64:
-                # the composite tile of a sparse block: sink prefix + band edge
-                assert k0 == 0 and t == 0 and up >= 128
+            assert w in (64, 80, 128) and k0 % 64 == 0 and up % 64 == 0
+            if w == 80:
+                # the composite tile of a sparse block: the band's 64-key edge
+                # and the first 16 keys of the sink page, always masked
+                assert t == 0 and k0 >= 128 and up == 0 and masked
+                runs = [(k0, 64), (0, 16)]
             else:
+                assert up == k0 + 64
                 assert k0 // 128 == (k0 + w - 1) // 128, "tile crosses a page"
-            for h in halves:
-                assert h + 64 <= -(-seq // 128) * 128, "tile beyond the block table"
-            keys = np.concatenate([np.arange(h, h + 64) for h in halves])
+                runs = [(k0, w)]
+            for h, n in runs:
+                assert h + n <= -(-seq // 128) * 128, "tile beyond the block table"
+            keys = np.concatenate([np.arange(h, h + n) for h, n in runs])
             vis = o.visible_mask(rows, keys, seq, prompt)
             if not masked:
                 assert vis.all(), f"unmasked tile {k0}+{w} hides keys of block {b}"
