@@ -326,13 +326,11 @@ TPSA_API tpsa_status tpsa_paged_attention_visit(
  * tpsa_paged_attention with a caller workspace for those shapes.  The call
  * makes no cudaMalloc or cudaFree and uses no allocating library routine.
  *
- * Set-up: the first call on a device (with that device current) looks up
- * the array's device address with cudaGetSymbolAddress and caches it.  That
- * lookup also makes the CUDA runtime load this library's device globals on
- * the device.  Make the first call on each device before any stream capture.
- * The cached address belongs to the device's primary context: after
- * cudaDeviceReset on that device it is stale, so do not call this entry
- * point on a device that has been reset in this process.
+ * Set-up: every call looks up the array's device address on the current
+ * device with cudaGetSymbolAddress; the library keeps no address between
+ * calls.  The first lookup on a device also makes the CUDA runtime load the
+ * library's device globals there: make the first call on each device before
+ * any stream capture.
  *
  * Sharing: every call on a device uses the same array, and the array keeps
  * the previous call's contents.  Each call clears the control words that

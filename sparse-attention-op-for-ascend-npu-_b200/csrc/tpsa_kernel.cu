@@ -1771,13 +1771,18 @@ tpsa_status stream_ctl_block(cudaStream_t stream, int64_t words, int32_t** ctl) 
   e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   if (dev < 0 || dev >= 64) return fail(TPSA_ERR_CUDA, "device ordinal out of range");
+  // The array's address is looked up on every call (cheap once the module
+  // is loaded): after a device reset the module loads again in a new
+  // context, possibly at another address, and its blocks start from zero,
+  // so a changed address starts the device's table afresh.
+  void* p = nullptr;
+  e = cudaGetSymbolAddress(&p, g_ctl_blocks);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(control blocks)");
   std::lock_guard<std::mutex> lock(g_mutex);
   CtlBlocks& cb = g_ctl[dev];
-  if (cb.base == nullptr) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_ctl_blocks);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(control blocks)");
+  if (cb.base != static_cast<int32_t*>(p)) {
     cb.base = static_cast<int32_t*>(p);
+    cb.used = 0;
   }
   for (int i = 0; i < cb.used; ++i) {
     if (cb.stream_id[i] == id) {
@@ -2240,13 +2245,11 @@ tpsa_status launch_varlen(const void* query, const void* key_cache, const void* 
 // count stays near one piece per CTA, so no plan needs more than 144 partial
 // slots (18.3 MiB; query chunks of 64 to 16384 rows over contexts to 4M).
 constexpr uint64_t kStaticScratchBytes = uint64_t{24} << 20;
-constexpr int kMaxScratchDevices = 64;
-std::mutex g_scratch_mutex;
-void* g_scratch_ptr[kMaxScratchDevices] = {};
 
-// Device address of the static scratch on the current device.  The first
-// call on a device looks the address up (cudaGetSymbolAddress, which also
-// makes the runtime load this module's device globals there) and caches it.
+// Device address of the static scratch on the current device, looked up on
+// every call (cudaGetSymbolAddress; the first call on a device also makes
+// the runtime load this module's device globals there), so that it stays
+// right after a device reset, which loads the module again.
 tpsa_status static_scratch_address(void** ptr);
 
 }  // namespace
@@ -2256,21 +2259,11 @@ static __device__ __align__(256) uint8_t g_static_scratch[kStaticScratchBytes];
 namespace {
 
 tpsa_status static_scratch_address(void** ptr) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
-  if (dev < 0 || dev >= kMaxScratchDevices) {
-    return fail(TPSA_ERR_CUDA, "device ordinal out of range");
-  }
-  std::lock_guard<std::mutex> lock(g_scratch_mutex);
-  if (g_scratch_ptr[dev] == nullptr) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_static_scratch);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(static scratch)");
-    if (p == nullptr) return fail(TPSA_ERR_CUDA, "static scratch has no device address");
-    g_scratch_ptr[dev] = p;
-  }
-  *ptr = g_scratch_ptr[dev];
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(static scratch)");
+  if (p == nullptr) return fail(TPSA_ERR_CUDA, "static scratch has no device address");
+  *ptr = p;
   return TPSA_OK;
 }
 
