@@ -113,6 +113,7 @@ def test_long_context_split_tail(tm, cuda_device, seq):
     (0, 2048, 2048, 2048),
     (1536, 512, 2048, 8320),    # intermediate chunk, no tail
     (3000, 1096, 4096, 4096),   # unaligned chunk start reaching the tail
+    (1088, 92, 1180, 4000),     # composite tile whose band edge passes seq_len
 ])
 def test_visited_key_set_bit_exact(tm, cuda_device, query_start, tq, seq, prompt):
     """Keys entering each (row, head) softmax equal the reference key set exactly."""
@@ -137,6 +138,29 @@ def test_visited_key_set_bit_exact(tm, cuda_device, query_start, tq, seq, prompt
         want[::32].view(np.uint8)).sum())
     ref = oracle_attention(q, k, v, table, query_start, seq, prompt, SCALE)
     assert_close(out, ref, "visit-mode output")
+
+
+@pytest.mark.parametrize("query_start,tq,seq,prompt", [
+    (0, 1100, 1100, 1100),      # one chunk: the last page is written up to key 1099
+    (1088, 92, 1180, 4000),     # intermediate chunk: the last sparse block's
+                                # composite tile reads its band edge [1152, 1216)
+])
+def test_unwritten_cache_slots_never_reach_the_output(tm, cuda_device, query_start, tq, seq,
+                                                      prompt):
+    """Cache slots at or beyond seq_len hold whatever the serving engine left
+    there; here NaN in K and V.  The kernel masks their scores and zeroes
+    their values in shared memory, so the output equals the oracle's on the
+    clean cache (and has no NaN)."""
+    q, k, v, table = baseline_inputs(tq, seq, seed=9)
+    ref = oracle_attention(q, k, v, table, query_start, seq, prompt, SCALE)
+    k_bad, v_bad = k.clone(), v.clone()
+    pages = table[0].tolist()
+    for key in range(seq, len(pages) * 128):
+        k_bad[pages[key // 128], key % 128] = float("nan")
+        v_bad[pages[key // 128], key % 128] = float("nan")
+    out = run_cabi(tm, q, k_bad, v_bad, table, query_start, seq, prompt, cuda_device)
+    assert not torch.isnan(out.float()).any()
+    assert_close(out, ref, f"NaN beyond seq_len {seq}")
 
 
 def test_page_placement_invariance_bit_exact(tm, cuda_device):
