@@ -127,3 +127,27 @@ def test_varlen_heads_packs_layer_slices(tm, cuda_device, kv_heads):
         ref = oracle_attention(qs[j], ks[j], vs[j], tables[j].view(1, -1), seq - rows, seq, seq,
                                SCALE)
         assert_close(out[cu[j]:cu[j + 1]], ref.to(torch.bfloat16), f"layer {j} of {layers}")
+
+
+def test_varlen_unwritten_slots_never_reach_the_output(tm, cuda_device):
+    """Each request's cache slots at or beyond its seq_len, and the pool's
+    unused pages, hold NaN in K and V; every request still matches the
+    oracle on the clean pool (one request's last sparse block runs a
+    composite tile whose band edge passes its seq_len)."""
+    specs = MIXED + [(92, 1180, 4000)]
+    q, k, v, tables, per_request, cu = varlen_inputs(specs, seed=23)
+    k_bad, v_bad = k.clone(), v.clone()
+    used = set()
+    for (_, seq, _), row in zip(specs, per_request):
+        pages = row[0].tolist()
+        used.update(pages)
+        for key in range(seq, len(pages) * 128):
+            k_bad[pages[key // 128], key % 128] = float("nan")
+            v_bad[pages[key // 128], key % 128] = float("nan")
+    for page in set(range(k.shape[0])) - used:
+        k_bad[page] = float("nan")
+        v_bad[page] = float("nan")
+    out = _run_varlen(tm, cuda_device, q, k_bad, v_bad, tables, cu, [s for _, s, _ in specs],
+                      [p for _, _, p in specs])
+    assert not torch.isnan(out.float()).any()
+    _check_against_oracle(out, q, k, v, per_request, cu, specs, "NaN beyond seq_len")
