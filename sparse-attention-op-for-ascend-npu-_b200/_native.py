@@ -12,6 +12,8 @@ from pathlib import Path
 
 PKG_DIR = Path(__file__).resolve().parent
 LIB_PATH = PKG_DIR / "libtpsa.so"
+# TPSA_ABI_VERSION of the header this binding follows (include/tpsa.h).
+ABI_VERSION = 3
 ADAPTER_PATH = PKG_DIR / "_tpsa_torch.so"
 
 TPSA_OK = 0
@@ -105,6 +107,10 @@ def lib() -> ctypes.CDLL:
             raise RuntimeError(f"{LIB_PATH} is missing; build it with build.py")
         h = ctypes.CDLL(str(LIB_PATH))
         h.tpsa_abi_version.restype = _i32
+        found = h.tpsa_abi_version()
+        if found != ABI_VERSION:
+            raise RuntimeError(f"{LIB_PATH} has ABI version {found}, this binding expects "
+                               f"{ABI_VERSION}; rebuild it with build.py")
         h.tpsa_status_string.argtypes = [ctypes.c_int]
         h.tpsa_status_string.restype = ctypes.c_char_p
         h.tpsa_last_error.restype = ctypes.c_char_p

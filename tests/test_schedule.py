@@ -31,7 +31,8 @@ def test_library_exports_every_declared_symbol(tm):
     lib = tm._native.lib()
     for name in declared:
         assert hasattr(lib, name)
-    assert lib.tpsa_abi_version() == 3
+    define = re.search(r"#define TPSA_ABI_VERSION (\d+)", header)
+    assert define and lib.tpsa_abi_version() == int(define.group(1)) == tm._native.ABI_VERSION
 
 
 def test_adapter_library_is_built(tm):
