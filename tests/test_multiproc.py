@@ -64,7 +64,7 @@ def _rank_main(rank: int, world: int, port: int, seq: int, result_q) -> None:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_kv_head_partition_gather_matches_full_layer(world):
     ctx = mp.get_context("spawn")
     result_q = ctx.Queue()
